@@ -1,0 +1,400 @@
+"""Benchmark of the B200 fused-MoE operator (one JSON line on rank 0).
+
+Default workload: the Mixtral-8x7B-shaped MoE layer (H=4096, I=14336, E=8,
+top-2, bf16) on T=4096 tokens per GPU -- the configuration the headline
+metric (fused-MoE layer tokens/s and TFLOP/s) is quoted on. A step is one
+forward of the operator: routing (softmax/top-k/renormalise) + align +
+gather + gate-up GEMM (SiLU fused) + down GEMM (top-k weight fused) + top-k
+sum, over one batch of synthetic tokens (N(0,1) activations, N(0,1/fan_in)
+weights, N(0,1) router logits).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload mixtral|qwen3|dsv3-fp8|qwen3-int8] [--tokens T]
+
+`value` is device time (CUDA events, inputs resident in HBM, L2 flushed
+between steps outside the timed windows, max over ranks); `e2e` is the same
+metric through ModelNew.forward with pinned host inputs, including the H2D
+copies of hidden states and router logits and the D2H copy of the output.
+`--impl reference` times the reference's CPU torch path (base.py:35-76,
+restated in the oracle) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+
+WORKLOADS = {
+    # name: (H, I, E, k, quant, default T, logit bias std)
+    "mixtral": (4096, 14336, 8, 2, "none", 4096, 0.0),
+    "qwen3": (2048, 768, 128, 8, "none", 8192, 0.5),
+    "dsv3-fp8": (7168, 2048, 256, 8, "fp8", 4096, 0.0),
+    "qwen3-int8": (2048, 768, 128, 8, "int8", 8192, 0.5),
+}
+METRIC = "fused-MoE layer tokens/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixtral")
+    ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (0 = workload default)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def flops_per_token(H, I, k):
+    # gate-up 2*H*2I + down 2*I*H multiply-adds per routed row
+    return 6 * H * I * k
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        if not getattr(self, "lines", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm, smax, power, reasons = [], [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        busy = [s for s, p in zip(sm, power) if p > 0.3 * max(power)] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(smax),
+                "power_w_max": max(power), "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference's torch path on the host cores
+# ---------------------------------------------------------------------------
+
+def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1):
+    """tokens/s of base.py's forward (oracle restatement) on the host CPU."""
+    import torch
+    from oracle import moe_oracle as orc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    hidden = torch.randn(sample_tokens, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(sample_tokens, E, generator=g)
+    if bias:
+        logits = logits + torch.randn(E, generator=g) * bias
+    # base.py keeps fp32 master weights and casts them on every call
+    w1 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
+    w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
+    times = []
+    for i in range(warmup + repeats):
+        t0 = time.perf_counter()
+        orc.model_forward_native(hidden, logits, w1, w2, k)
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    med = statistics.median(times)
+    return sample_tokens / med, med, torch.get_num_threads()
+
+
+def cpu_sample_tokens(H, I, E):
+    # keep one CPU call around a second or two: bigger layers get fewer tokens
+    per_token = 6 * H * I * 2
+    return int(max(16, min(512, 2e10 / per_token)))
+
+
+def run_reference(args, H, I, E, k, quant, T, bias, rank):
+    """--impl reference: the reference's CPU torch path, rank 0 only."""
+    if rank != 0:
+        return
+    sample = cpu_sample_tokens(H, I, E)
+    rate, med, cores = cpu_reference_rate(H, I, E, k, quant, bias, sample,
+                                          repeats=max(1, args.steps), warmup=max(0, args.warmup))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(args.workload, H, I, E, k, quant, T, args.gpus),
+        "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens per step of the {args.workload} layer, "
+                                   "base.py forward restated in torch-CPU bf16 with the "
+                                   "per-call fp32->bf16 weight casts"},
+        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(name, H, I, E, k, quant, T, n):
+    return {"workload": f"{name} MoE layer H={H} I={I} E={E} top-{k} "
+                        f"{'bf16' if quant == 'none' else quant + ' W8A8'}, {T} tokens/GPU",
+            "hidden": H, "intermediate": I, "experts": E, "top_k": k, "quant": quant,
+            "tokens_per_gpu": T, "global_tokens": T * n,
+            "parallelism": "replicas" if n > 1 else "single",
+            "l2": f"flushed between steps ({L2_FLUSH_BYTES >> 20} MB write) outside the "
+                  "timed windows; weights also exceed L2"}
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+
+def main():
+    args = parse_args()
+    H, I, E, k, quant, T0, bias = WORKLOADS[args.workload]
+    T = args.tokens or T0
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, H, I, E, k, quant, T, bias, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
+        sys.exit(1)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from kernelswift_b200 import _lib
+    from kernelswift_b200 import fused_moe as fm
+
+    # ---- synthetic problem (weights N(0, 1/fan_in), tokens N(0, 1)) ----
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    hidden = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g, device=dev)
+    if bias:
+        logits = logits + torch.randn(E, generator=g, device=dev) * bias
+    model = fm.ModelNew(E, k, H, I).to(dev)
+    with torch.no_grad():
+        model.w1.normal_(0.0, 1.0 / math.sqrt(H), generator=g)
+        model.w2.normal_(0.0, 1.0 / math.sqrt(I), generator=g)
+    prep = model.prepared(torch.bfloat16, quant)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step(stage_arr=None):
+        tw, ti = fm.fused_topk(hidden, logits, k)
+        return fm.fused_experts(hidden, prep, None, tw.to(hidden.dtype), ti,
+                                use_fp8_w8a8=quant == "fp8", use_int8_w8a8=quant == "int8",
+                                stage_events=stage_arr)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    stage_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(_lib.STAGES) + 1)]
+                 for _ in range(K)]
+    for evs in stage_evs:
+        for ev in evs:
+            ev.record()  # create the events before the timed region
+    stage_arrs = [fm.stage_event_array(evs) for evs in stage_evs]
+    torch.cuda.synchronize()
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        wall0 = time.perf_counter()
+        for i in range(K):
+            flush.zero_()
+            starts[i].record()
+            step(stage_arrs[i])
+            ends[i].record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+    if world > 1:
+        dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    stage_ms = {name: sum(evs[j].elapsed_time(evs[j + 1]) for evs in stage_evs) / K
+                for j, name in enumerate(_lib.STAGES)}
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / K
+    tokens_per_s = T * world / (ms_per_step / 1e3)
+    tflops = flops_per_token(H, I, k) * T * world / (ms_per_step / 1e3) / 1e12
+
+    # ---- e2e through ModelNew.forward with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        h_host = hidden.cpu().pin_memory()
+        l_host = logits.cpu().pin_memory()
+        out_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+        h_dev = torch.empty_like(hidden)
+        l_dev = torch.empty_like(logits)
+        model_call = model
+        if quant != "none":
+            def model_call(hd, ld):
+                tw, ti = fm.fused_topk(hd, ld, k)
+                return fm.fused_experts(hd, prep, None, tw.to(hd.dtype), ti,
+                                        use_fp8_w8a8=quant == "fp8",
+                                        use_int8_w8a8=quant == "int8")
+
+        def e2e_step():
+            h_dev.copy_(h_host, non_blocking=True)
+            l_dev.copy_(l_host, non_blocking=True)
+            with torch.no_grad():
+                out = model_call(h_dev, l_dev)
+            out_host.copy_(out, non_blocking=True)
+
+        for _ in range(max(3, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / K
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s",
+               "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": hidden.numel() * hidden.element_size()
+               + logits.numel() * logits.element_size(),
+               "d2h_bytes_per_step": T * H * 2,
+               "path": "ModelNew.forward (drop-in module), pinned host buffers"}
+
+    # ---- roofline of the dominant kernel (gate-up GEMM) ----
+    peaks, peak_src = load_peaks()
+    gu_ms = stage_ms["gate_up"]
+    gu_flops = 4 * H * I * T * k
+    if quant == "none":
+        peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+        peak_note = f"bf16 dense, sustained, {peak_src}"
+    else:
+        peak = 2 * peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+        peak_note = f"2x bf16 dense sustained ({quant} rate), {peak_src}"
+    achieved = gu_flops / (gu_ms / 1e3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get(f"{args.workload}:{T}:gate_up")
+        except Exception:
+            traffic = None
+    roofline = {"kernel": "moe_grouped_gemm_kernel (gate-up, SiLU fused)", "bound": "tensor",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": peak_note, "traffic": traffic,
+                "algorithmic": f"4*H*I*T*k = {gu_flops:.4g} FLOP per launch"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample = cpu_sample_tokens(H, I, E)
+        rate, med, cores = cpu_reference_rate(H, I, E, k, quant, bias, sample, repeats=3)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{sample} tokens of the same layer, base.py forward restated in "
+                         f"torch-CPU bf16 (median of 3 calls, {med:.2f} s each)"}
+
+    # our kernels per step: align (1 launch up to 8192 routed rows, else 3),
+    # gather, gate-up, [activation quant], down, top-k sum
+    numel = T * k
+    launches_per_step = (1 if numel <= 8192 else 3) + 4 + (0 if quant == "none" else 1)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if quant == "none" else ("e4m3" if quant == "fp8" else "int8"),
+            "data": "synthetic",
+            "config": workload_config(args.workload, H, I, E, k, quant, T, world),
+            "tflops": tflops,
+            "stage_ms": stage_ms,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks.summary(),
+            "gpu_launches": launches_per_step * K,
+            "wall_s_timed": wall,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.path.insert(0, str(ROOT))
+    main()

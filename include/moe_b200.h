@@ -1,0 +1,297 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) fused Mixture-of-Experts operator.
+ *
+ * This is the drop-in boundary for the fused-MoE operator of the kernelswift
+ * track-1 suite. The reference operator is the pure-torch
+ * `Model.forward(hidden_states, router_logits)` of
+ * kernels/track1-triton/fused_moe/base.py:35-76; each entry point below names
+ * the lines of that file (or of the library pipeline in
+ * kernels/track1-triton/fused_moe/mlu/triton_fused_moe_006.py) whose work it
+ * replaces.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are raw device pointers to dense row-major arrays.
+ *   - Memory is owned by the caller. Entry points that need temporary device
+ *     memory take a `workspace` pointer and its size; the matching
+ *     *_workspace_size() query returns the required number of bytes.
+ *   - Work is enqueued on the caller's CUDA stream (`stream` is a
+ *     cudaStream_t passed as void*; NULL means the legacy default stream).
+ *     Nothing synchronises the host unless the entry point says so.
+ *   - Every entry point returns a moe_status_t. Arguments are validated on the
+ *     host before anything is launched; a failed validation launches nothing.
+ *     moe_last_error() returns a thread-local message for the last failure.
+ *   - Kernels that wait on on-chip barriers wait with a time limit. When a
+ *     wait runs out, the kernel stores MOE_ERR_TIMEOUT into the optional
+ *     device status word (`status`, may be NULL) and returns; the CUDA
+ *     context stays usable. moe_read_status() copies that word to the host.
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+typedef enum moe_status {
+  MOE_OK = 0,
+  MOE_ERR_INVALID_ARG = 1,  /* bad pointer, size, dtype or layout            */
+  MOE_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement   */
+  MOE_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed             */
+  MOE_ERR_TIMEOUT = 4,      /* a device-side bounded wait ran out            */
+  MOE_ERR_WORKSPACE = 5,    /* workspace missing or smaller than required    */
+  MOE_ERR_DEVICE = 6        /* current device is not an sm_100 part          */
+} moe_status_t;
+
+typedef enum moe_dtype {
+  MOE_DTYPE_F32 = 0,
+  MOE_DTYPE_F16 = 1,
+  MOE_DTYPE_BF16 = 2,
+  MOE_DTYPE_E4M3 = 3,       /* float8_e4m3fn                                  */
+  MOE_DTYPE_I8 = 4,
+  MOE_DTYPE_I32 = 5,
+  MOE_DTYPE_I64 = 6
+} moe_dtype_t;
+
+typedef enum moe_quant {
+  MOE_QUANT_NONE = 0,         /* bf16/fp16 weights and activations            */
+  MOE_QUANT_FP8_BLOCK = 1,    /* e4m3 W8A8: weight scales per 128x128 block,
+                                 activation scales per token per 128 columns  */
+  MOE_QUANT_INT8_CHANNEL = 2  /* int8 W8A8: weight scale per output channel,
+                                 activation scale per token                   */
+} moe_quant_t;
+
+/* ------------------------------------------------------------------------ */
+/* Status helpers                                                           */
+/* ------------------------------------------------------------------------ */
+
+/* Name of a status code ("MOE_OK", ...). Never returns NULL. */
+const char* moe_status_string(int status);
+
+/* Thread-local detail message of the last non-OK status returned on this
+ * host thread ("" when none). */
+const char* moe_last_error(void);
+
+/* ABI version of the loaded library (MOE_B200_ABI_VERSION). */
+int moe_abi_version(void);
+
+/* Synchronises `stream`, copies the device status word to *host_status and,
+ * when `reset` is non-zero, clears it. */
+int moe_read_status(int32_t* device_status, int32_t* host_status, int reset,
+                    void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Routing metadata: moe_align_block_size                                   */
+/* Replaces the per-expert grouping of base.py:64-68 (`mask = flat_ids == e`,
+ * `x_rep[mask]`) and tmo.moe_gen_idx of triton_fused_moe_006.py:38.         */
+/* ------------------------------------------------------------------------ */
+
+/* Number of int32 entries of `sorted_token_ids`:
+ * round_up(numel + num_experts * (block_m - 1), block_m).
+ * `expert_ids` has moe_align_buffer_len(...) / block_m entries. */
+int64_t moe_align_buffer_len(int64_t numel, int num_experts, int block_m);
+
+/* Bytes of workspace moe_align_block_size needs for this problem. */
+int moe_align_workspace_size(int64_t numel, int num_experts, int block_m,
+                             size_t* bytes);
+
+/*
+ * Groups the flat (token, slot) assignments `topk_ids[numel]` by expert.
+ *
+ * For flat index r (= token * top_k + slot, the row order of base.py:52-58):
+ *   cnt[e]    = #{r : topk_ids[r] == e}
+ *   padded[e] = ceil(cnt[e] / block_m) * block_m
+ *   off[e]    = sum of padded[e'] for e' < e
+ *   sorted_token_ids[off[e] + j] = j-th r (ascending) with topk_ids[r] == e
+ *   padding slots and the tail up to the buffer length hold `numel`
+ *   expert_ids[b] = e for every block b of expert e, -1 for unused blocks
+ *   *num_tokens_post_pad = sum of padded[e]
+ * Ids outside [0, num_experts) are dropped (used by expert parallelism).
+ * Bit-exact and deterministic: no atomics decide an element's position.
+ *
+ * ids_dtype: MOE_DTYPE_I32 or MOE_DTYPE_I64. Requires 1 <= num_experts <= 1024,
+ * block_m in {16, 32, 64, 128, 256}.
+ */
+int moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel,
+                         int num_experts, int block_m,
+                         int32_t* sorted_token_ids, int32_t* expert_ids,
+                         int32_t* num_tokens_post_pad, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Weight preparation (one-time per weight version)                         */
+/* Replaces the per-call casts `self.w1.to(dtype)` / `self.w2.to(dtype)` of
+ * base.py:60-61.                                                           */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * w1 [E, 2I, H] (gate rows [0, I), up rows [I, 2I), base.py:25-27,70) ->
+ * w13 [E, 2I, H] in the layout the gate/up GEMM reads: rows are regrouped in
+ * 16-row pairs, w13 row 32g + c = w1 row 16g + c (gate) and
+ * w13 row 32g + 16 + c = w1 row I + 16g + c (up), c in [0, 16).
+ *
+ * quant == MOE_QUANT_NONE:   src F32/F16/BF16 -> dst_dtype F16/BF16 (cast).
+ * quant == MOE_QUANT_FP8_BLOCK: src F32/F16/BF16 is quantised to e4m3 with one
+ *   scale per 128x128 block of the ORIGINAL layout, scale = absmax / 448;
+ *   `scale_out` receives [E, ceil(2I/128), ceil(H/128)] fp32.
+ *   src E4M3 is taken as already quantised: rows are regrouped and
+ *   `scale_in` ([E, ceil(2I/128), ceil(H/128)]) is copied to `scale_out`.
+ * quant == MOE_QUANT_INT8_CHANNEL: src F32/F16/BF16 is quantised to int8 with
+ *   one scale per output row, scale = absmax / 127; `scale_out` receives
+ *   [E, 2I] fp32 in the regrouped row order.
+ * Requires I % 16 == 0 and H % 16 == 0.
+ */
+int moe_prepare_w13(const void* w1, int src_dtype, const float* scale_in,
+                    int64_t num_experts, int64_t inter_size,
+                    int64_t hidden_size, int quant, void* w13_out,
+                    int dst_dtype, float* scale_out, void* stream);
+
+/*
+ * w2 [E, H, I] (base.py:29-31) -> the down-projection operand, same layout.
+ * quant NONE: cast. FP8_BLOCK: e4m3 + [E, ceil(H/128), ceil(I/128)] scales
+ * (or pass-through of an already-e4m3 source with `scale_in`). INT8_CHANNEL:
+ * int8 + [E, H] scales.
+ */
+int moe_prepare_w2(const void* w2, int src_dtype, const float* scale_in,
+                   int64_t num_experts, int64_t hidden_size,
+                   int64_t inter_size, int quant, void* w2_out, int dst_dtype,
+                   float* scale_out, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* The fused expert computation                                             */
+/* Replaces base.py:50-76: the replicate (52-58), the per-expert loop of
+ * gate/up GEMM, SiLU(gate)*up and down GEMM (64-72) and the weighted top-k
+ * reduction (75-76); equivalently group_gemm x2 + combine of
+ * triton_fused_moe_006.py:40-65.                                           */
+/* ------------------------------------------------------------------------ */
+
+typedef struct moe_problem {
+  int64_t num_tokens;       /* T                                             */
+  int64_t hidden_size;      /* H                                             */
+  int64_t inter_size;       /* I                                             */
+  int32_t num_experts;      /* E experts held by this process                */
+  int32_t top_k;            /* k                                             */
+  int32_t act_dtype;        /* hidden/out dtype: F32, F16 or BF16            */
+  int32_t quant;            /* moe_quant_t                                   */
+  int32_t ids_dtype;        /* I32 or I64                                    */
+  int32_t weights_dtype;    /* topk_weights dtype: F32, F16 or BF16          */
+  const void* hidden;       /* [T, H] act_dtype                              */
+  const void* w13;          /* moe_prepare_w13 output [E, 2I, H]             */
+  const void* w2;           /* moe_prepare_w2 output  [E, H, I]              */
+  const float* w13_scale;   /* per moe_prepare_w13 (NULL for QUANT_NONE)     */
+  const float* w2_scale;    /* per moe_prepare_w2  (NULL for QUANT_NONE)     */
+  const void* topk_weights; /* [T, k] weights_dtype                          */
+  const void* topk_ids;     /* [T, k] ids_dtype; ids outside [0,E) are dropped*/
+  void* out;                /* [T, H] act_dtype                              */
+  int32_t* status;          /* optional device status word (may be NULL)     */
+  void** stage_events;      /* optional cudaEvent_t[MOE_NUM_STAGES + 1]: event
+                               i is recorded on `stream` before stage i and
+                               event MOE_NUM_STAGES after the last one, for
+                               per-kernel timing (may be NULL)               */
+} moe_problem_t;
+
+/* Stages of moe_fused_experts, in launch order (for stage_events). */
+#define MOE_STAGE_ALIGN 0
+#define MOE_STAGE_GATHER 1
+#define MOE_STAGE_GATE_UP 2
+#define MOE_STAGE_QUANT 3
+#define MOE_STAGE_DOWN 4
+#define MOE_STAGE_SUM 5
+#define MOE_NUM_STAGES 6
+
+/* Bytes of workspace moe_fused_experts needs for `p` (pointers unused). */
+int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
+
+/*
+ * out[t] = sum_j topk_weights[t, j] *
+ *          W2[e] . (silu(W1g[e] . x_t) * (W1u[e] . x_t)),  e = topk_ids[t, j]
+ * Matmuls run on the tcgen05 tensor cores (bf16/fp16, e4m3 or int8 operands,
+ * fp32/int32 accumulation in tensor memory); SiLU, scaling and the top-k sum
+ * run in fp32. F32 activations are rounded to bf16 operands.
+ */
+int moe_fused_experts(const moe_problem_t* p, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* The stages of moe_fused_experts, one entry point each. Used by the expert-
+ * parallel path (which inserts the token exchange between them) and by tests.
+ * `buffer_len` is moe_align_buffer_len(numel, E, 128); the grouped GEMMs need
+ * routing metadata made with block_m = 128.                                */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * dst[m] = src[sorted_token_ids[m] / top_k] for m < *num_tokens_post_pad whose
+ * slot is not padding (base.py:52-58 replicate + base.py:68 gather); padding
+ * rows are left untouched. top_k == 0 copies row m itself (valid rows only).
+ * quant NONE: dst_dtype F16/BF16 (F32 sources are rounded).
+ * quant FP8_BLOCK: dst e4m3 + dst_scale [buffer_len, ceil(H/128)],
+ *   scale = absmax/448 per 128 columns. INT8_CHANNEL: dst int8 + dst_scale
+ *   [buffer_len], scale = absmax/127 per row.
+ */
+int moe_gather_rows(const void* src, int src_dtype, int64_t src_rows,
+                    int64_t hidden_size, int top_k,
+                    const int32_t* sorted_token_ids,
+                    const int32_t* num_tokens_post_pad, int64_t buffer_len,
+                    int64_t numel, int quant, void* dst, int dst_dtype,
+                    float* dst_scale, void* stream);
+
+/*
+ * act[m, :] = silu(gate) * up for every operand row m of a used block whose
+ * slot is not padding, gate/up = a[m] . w13[e]^T (base.py:69-71).
+ * act_out: [buffer_len, I] in compute_dtype (bf16 for INT8_CHANNEL).
+ * block_n: 0 picks the N tile, else 64, 128 or 256.
+ */
+int moe_gemm_gate_up(int quant, int compute_dtype, const void* a,
+                     const float* a_scale, const void* w13,
+                     const float* w13_scale, const int32_t* sorted_token_ids,
+                     const int32_t* expert_ids,
+                     const int32_t* num_tokens_post_pad, int64_t buffer_len,
+                     int64_t numel, int num_experts, int64_t hidden_size,
+                     int64_t inter_size, void* act_out, int block_n,
+                     int32_t* status, void* stream);
+
+/*
+ * partial[s, r, :] = row_weights[r] * (act[m] . w2[e]^T over K split s) for
+ * r = sorted_token_ids[m] (base.py:72 and the weight multiply of base.py:75).
+ * partial_out: [splits, numel, H] fp32; rows of dropped slots are not written.
+ * `splits` must leave no split empty: with kb = ceil(I * elem_bytes / 128)
+ * k-blocks, ceil(kb / ceil(kb / splits)) == splits.
+ */
+int moe_gemm_down(int quant, int compute_dtype, const void* act,
+                  const float* act_scale, const void* w2,
+                  const float* w2_scale, const int32_t* sorted_token_ids,
+                  const int32_t* expert_ids, const int32_t* num_tokens_post_pad,
+                  int64_t buffer_len, int64_t numel, int num_experts,
+                  int64_t hidden_size, int64_t inter_size,
+                  const void* row_weights, int weights_dtype, int splits,
+                  float* partial_out, int block_n, int32_t* status,
+                  void* stream);
+
+/*
+ * out[t, :] = sum_j sum_s partial[s, t*top_k + j, :] over slots whose id is in
+ * [0, num_experts) (all slots when topk_ids is NULL), in fixed order, fp32,
+ * then cast to out_dtype (base.py:75-76).
+ */
+int moe_sum_topk(const float* partial, int splits, int64_t num_tokens,
+                 int top_k, int64_t hidden_size, const void* topk_ids,
+                 int ids_dtype, int num_experts, void* out, int out_dtype,
+                 void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Self-test of the bounded device waits (failure detection without a GPU   */
+/* fault): launches one CTA whose mbarrier wait is never satisfied, with a   */
+/* limit of `limit_us` microseconds. The kernel stores MOE_ERR_TIMEOUT into  */
+/* `device_status` and returns.                                             */
+/* ------------------------------------------------------------------------ */
+int moe_selftest_wait_timeout(int32_t* device_status, int limit_us,
+                              void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* MOE_B200_H_ */

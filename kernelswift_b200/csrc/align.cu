@@ -1,0 +1,325 @@
+// moe_align_block_size: groups the flat (token, slot) -> expert assignments by
+// expert, pads each expert's group to a multiple of block_m and emits the
+// per-block expert id. Replaces the per-expert boolean masks of
+// kernels/track1-triton/fused_moe/base.py:64-68 with a stable counting sort.
+//
+// Determinism: an element's slot is its expert's offset + the number of
+// elements of the same expert before it in flat order. The rank inside a
+// warp comes from __match_any_sync + popc, the rank across warps from a
+// per-(warp, expert) count table in shared memory, the rank across chunks
+// from an exclusive scan of per-chunk histograms. No atomic decides an
+// element's position, so the output is bit-identical run to run.
+//
+// Paths:
+//   numel <= kSmallMax: one CTA does fill + histogram + scan + scatter.
+//   otherwise: three launches over chunks of kChunk ids:
+//     hist (per-chunk histogram, sentinel fill) -> scan (one CTA: offsets,
+//     expert_ids, num_tokens_post_pad, per-chunk bases) -> scatter.
+#include "common.cuh"
+
+namespace ksw {
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kChunk = 4096;          // ids per CTA on the multi-CTA path
+constexpr int64_t kSmallMax = 8192;   // single-CTA path up to this many ids
+constexpr int kMaxExperts = 1024;
+
+template <typename IdT>
+__device__ __forceinline__ int load_id(const IdT* ids, int64_t i, int E) {
+  const long long v = static_cast<long long>(ids[i]);
+  return (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+}
+
+// Exclusive prefix sum across a 1024-thread block. `tmp` holds >= 33 ints.
+__device__ __forceinline__ int block_excl_scan(int v, int* tmp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) tmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = tmp[lane];
+    int s = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    tmp[lane] = s - w;
+    if (lane == 31) tmp[32] = s;
+  }
+  __syncthreads();
+  const int excl = x - v + tmp[warp];
+  *total = tmp[32];
+  __syncthreads();
+  return excl;
+}
+
+// Places ids[base, min(base + 1024, end)) (one per thread) at their final
+// slots. running[e] is expert e's next free slot; warp_cnt[32][E] must be
+// all zero on entry and is all zero again on exit.
+template <typename IdT>
+__device__ __forceinline__ void scatter_subchunk(const IdT* ids, int64_t base,
+                                                 int64_t end, int E,
+                                                 int* running, int* warp_cnt,
+                                                 int32_t* sorted) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t i = base + tid;
+  const int e = (i < end) ? load_id(ids, i, E) : -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(peers & lanemask_lt());
+  if (e >= 0 && lane == __ffs(peers) - 1) warp_cnt[warp * E + e] = __popc(peers);
+  __syncthreads();
+  if (e >= 0) {
+    int prefix = 0;
+    for (int w = 0; w < warp; ++w) prefix += warp_cnt[w * E + e];
+    sorted[running[e] + prefix + rank] = static_cast<int32_t>(i);
+  }
+  __syncthreads();
+  for (int ee = tid; ee < E; ee += kThreads) {
+    int s = 0;
+#pragma unroll 8
+    for (int w = 0; w < 32; ++w) {
+      s += warp_cnt[w * E + ee];
+      warp_cnt[w * E + ee] = 0;
+    }
+    running[ee] += s;
+  }
+  __syncthreads();
+}
+
+// Writes expert_ids for the blocks of expert `e` (thread e) and -1 for the
+// blocks past the padded total.
+__device__ __forceinline__ void write_expert_ids(int e, int E, int off,
+                                                 int padded, int total, int BM,
+                                                 int64_t num_blocks,
+                                                 int32_t* expert_ids) {
+  if (e < E) {
+    for (int b = off / BM; b < (off + padded) / BM; ++b) expert_ids[b] = e;
+  }
+  for (int64_t b = total / BM + threadIdx.x; b < num_blocks; b += kThreads)
+    expert_ids[b] = -1;
+}
+
+template <typename IdT>
+__global__ void __launch_bounds__(kThreads)
+    align_small_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
+                       int BM, int64_t L, int32_t* __restrict__ sorted,
+                       int32_t* __restrict__ expert_ids,
+                       int32_t* __restrict__ num_post_pad) {
+  extern __shared__ int sm[];
+  int* counts = sm;                 // E
+  int* running = counts + E;        // E
+  int* scan_tmp = running + E;      // 64
+  int* warp_cnt = scan_tmp + 64;    // 32 * E
+  const int tid = threadIdx.x;
+
+  for (int64_t p = tid; p < L; p += kThreads) sorted[p] = static_cast<int32_t>(numel);
+  for (int e = tid; e < E; e += kThreads) counts[e] = 0;
+  for (int p = tid; p < 32 * E; p += kThreads) warp_cnt[p] = 0;
+  __syncthreads();
+
+  for (int64_t i = tid; i < numel; i += kThreads) {
+    const int e = load_id(ids, i, E);
+    if (e >= 0) atomicAdd(&counts[e], 1);
+  }
+  __syncthreads();
+
+  const int cnt = tid < E ? counts[tid] : 0;
+  const int padded = (cnt + BM - 1) / BM * BM;
+  int total = 0;
+  const int off = block_excl_scan(padded, scan_tmp, &total);
+  if (tid < E) running[tid] = off;
+  write_expert_ids(tid, E, off, padded, total, BM, L / BM, expert_ids);
+  if (tid == 0) *num_post_pad = total;
+  __syncthreads();
+
+  for (int64_t base = 0; base < numel; base += kThreads)
+    scatter_subchunk(ids, base, numel, E, running, warp_cnt, sorted);
+}
+
+template <typename IdT>
+__global__ void __launch_bounds__(kThreads)
+    align_hist_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
+                      int64_t L, int32_t* __restrict__ sorted,
+                      int32_t* __restrict__ chunk_counts) {
+  extern __shared__ int sm[];
+  int* counts = sm;  // E
+  const int tid = threadIdx.x;
+  for (int64_t p = int64_t(blockIdx.x) * kThreads + tid; p < L;
+       p += int64_t(gridDim.x) * kThreads)
+    sorted[p] = static_cast<int32_t>(numel);
+  for (int e = tid; e < E; e += kThreads) counts[e] = 0;
+  __syncthreads();
+  const int64_t begin = int64_t(blockIdx.x) * kChunk;
+  const int64_t end = min(numel, begin + kChunk);
+  for (int64_t i = begin + tid; i < end; i += kThreads) {
+    const int e = load_id(ids, i, E);
+    if (e >= 0) atomicAdd(&counts[e], 1);
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kThreads)
+    chunk_counts[int64_t(blockIdx.x) * E + e] = counts[e];
+}
+
+// One CTA. chunk_counts[c][e] is replaced by the first slot of chunk c's
+// elements of expert e.
+__global__ void __launch_bounds__(kThreads)
+    align_scan_kernel(int nchunks, int E, int BM, int64_t L,
+                      int32_t* __restrict__ chunk_counts,
+                      int32_t* __restrict__ expert_ids,
+                      int32_t* __restrict__ num_post_pad) {
+  __shared__ int scan_tmp[64];
+  const int tid = threadIdx.x;
+  int cnt = 0;
+  if (tid < E)
+    for (int c = 0; c < nchunks; ++c) cnt += chunk_counts[int64_t(c) * E + tid];
+  const int padded = (cnt + BM - 1) / BM * BM;
+  int total = 0;
+  const int off = block_excl_scan(padded, scan_tmp, &total);
+  if (tid < E) {
+    int run = off;
+    for (int c = 0; c < nchunks; ++c) {
+      const int v = chunk_counts[int64_t(c) * E + tid];
+      chunk_counts[int64_t(c) * E + tid] = run;
+      run += v;
+    }
+  }
+  write_expert_ids(tid, E, off, padded, total, BM, L / BM, expert_ids);
+  if (tid == 0) *num_post_pad = total;
+}
+
+template <typename IdT>
+__global__ void __launch_bounds__(kThreads)
+    align_scatter_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
+                         const int32_t* __restrict__ chunk_base,
+                         int32_t* __restrict__ sorted) {
+  extern __shared__ int sm[];
+  int* running = sm;           // E
+  int* warp_cnt = running + E; // 32 * E
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += kThreads)
+    running[e] = chunk_base[int64_t(blockIdx.x) * E + e];
+  for (int p = tid; p < 32 * E; p += kThreads) warp_cnt[p] = 0;
+  __syncthreads();
+  const int64_t begin = int64_t(blockIdx.x) * kChunk;
+  const int64_t end = min(numel, begin + kChunk);
+  for (int64_t base = begin; base < end; base += kThreads)
+    scatter_subchunk(ids, base, end, E, running, warp_cnt, sorted);
+}
+
+template <typename IdT>
+int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
+                 int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
+                 int32_t* ws, cudaStream_t s) {
+  if (numel <= kSmallMax) {
+    const size_t smem = size_t(2 * E + 64 + 32 * E) * sizeof(int);
+    auto k = align_small_kernel<IdT>;
+    if (smem > 48 * 1024)
+      KSW_CUDA(cudaFuncSetAttribute(
+          k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    k<<<1, kThreads, smem, s>>>(ids, numel, E, BM, L, sorted, expert_ids,
+                                num_post_pad);
+    KSW_CUDA(cudaGetLastError());
+    return MOE_OK;
+  }
+  const int nchunks = static_cast<int>(ceil_div(numel, kChunk));
+  align_hist_kernel<IdT><<<nchunks, kThreads, size_t(E) * sizeof(int), s>>>(
+      ids, numel, E, L, sorted, ws);
+  KSW_CUDA(cudaGetLastError());
+  align_scan_kernel<<<1, kThreads, 0, s>>>(nchunks, E, BM, L, ws, expert_ids,
+                                           num_post_pad);
+  KSW_CUDA(cudaGetLastError());
+  const size_t smem = size_t(E + 32 * E) * sizeof(int);
+  auto k = align_scatter_kernel<IdT>;
+  if (smem > 48 * 1024)
+    KSW_CUDA(cudaFuncSetAttribute(
+        k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  k<<<nchunks, kThreads, smem, s>>>(ids, numel, E, ws, sorted);
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+}  // namespace
+
+int64_t align_buffer_len(int64_t numel, int E, int BM) {
+  return round_up(numel + int64_t(E) * (BM - 1), BM);
+}
+
+size_t align_workspace_bytes(int64_t numel, int E) {
+  if (numel <= kSmallMax) return 0;
+  return align256(size_t(ceil_div(numel, kChunk)) * size_t(E) * sizeof(int32_t));
+}
+
+int align_validate(int64_t numel, int E, int BM) {
+  KSW_REQUIRE(numel >= 0, MOE_ERR_INVALID_ARG, "numel must be >= 0");
+  KSW_REQUIRE(E >= 1 && E <= kMaxExperts, MOE_ERR_UNSUPPORTED,
+              "num_experts must be in [1, 1024]");
+  KSW_REQUIRE(BM == 16 || BM == 32 || BM == 64 || BM == 128 || BM == 256,
+              MOE_ERR_UNSUPPORTED, "block_m must be one of 16/32/64/128/256");
+  KSW_REQUIRE(align_buffer_len(numel, E, BM) < (int64_t(1) << 31),
+              MOE_ERR_UNSUPPORTED, "numel too large for int32 indices");
+  return MOE_OK;
+}
+
+int align_launch(const void* ids, int ids_dtype, int64_t numel, int E, int BM,
+                 int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
+                 void* workspace, size_t ws_bytes, cudaStream_t s) {
+  int st = align_validate(numel, E, BM);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE(ids_dtype == MOE_DTYPE_I32 || ids_dtype == MOE_DTYPE_I64,
+              MOE_ERR_INVALID_ARG, "topk_ids dtype must be int32 or int64");
+  KSW_REQUIRE(sorted && expert_ids && num_post_pad, MOE_ERR_INVALID_ARG,
+              "null output pointer");
+  KSW_REQUIRE(numel == 0 || ids != nullptr, MOE_ERR_INVALID_ARG,
+              "null topk_ids");
+  const size_t need = align_workspace_bytes(numel, E);
+  KSW_REQUIRE(ws_bytes >= need && (need == 0 || workspace != nullptr),
+              MOE_ERR_WORKSPACE, "align workspace too small");
+  const int64_t L = align_buffer_len(numel, E, BM);
+  if (ids_dtype == MOE_DTYPE_I32)
+    return launch_align(static_cast<const int32_t*>(ids), numel, E, BM, L,
+                        sorted, expert_ids, num_post_pad,
+                        static_cast<int32_t*>(workspace), s);
+  return launch_align(static_cast<const int64_t*>(ids), numel, E, BM, L, sorted,
+                      expert_ids, num_post_pad,
+                      static_cast<int32_t*>(workspace), s);
+}
+
+}  // namespace ksw
+
+extern "C" {
+
+int64_t moe_align_buffer_len(int64_t numel, int num_experts, int block_m) {
+  if (numel < 0 || num_experts < 1 || block_m < 1) return -1;
+  return ksw::align_buffer_len(numel, num_experts, block_m);
+}
+
+int moe_align_workspace_size(int64_t numel, int num_experts, int block_m,
+                             size_t* bytes) {
+  KSW_REQUIRE(bytes != nullptr, MOE_ERR_INVALID_ARG, "null bytes pointer");
+  int st = ksw::align_validate(numel, num_experts, block_m);
+  if (st != MOE_OK) return st;
+  *bytes = ksw::align_workspace_bytes(numel, num_experts);
+  return MOE_OK;
+}
+
+int moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel,
+                         int num_experts, int block_m,
+                         int32_t* sorted_token_ids, int32_t* expert_ids,
+                         int32_t* num_tokens_post_pad, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  int st = ksw::check_device(nullptr);
+  if (st != MOE_OK) return st;
+  return ksw::align_launch(topk_ids, ids_dtype, numel, num_experts, block_m,
+                           sorted_token_ids, expert_ids, num_tokens_post_pad,
+                           workspace, workspace_bytes,
+                           static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

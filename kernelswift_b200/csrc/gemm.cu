@@ -1,0 +1,559 @@
+// Grouped expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM),
+// fed by TMA. One persistent kernel template serves both matmuls of the MoE
+// layer (kernels/track1-triton/fused_moe/base.py:69-72):
+//
+//   gate-up: act[m, :] = silu(A[m] . W13g[e]^T) * (A[m] . W13u[e]^T)
+//            (base.py:69-71; the SiLU(gate)*up epilogue is fused)
+//   down:    part[s, r, :] = w[r] * (act[m] . W2[e]^T)   restricted to K split s
+//            (base.py:72 and the topk-weight multiply of base.py:75)
+//
+// where m runs over the rows of the expert-sorted operand, r = sorted_ids[m]
+// is the flat (token, slot) index and e = expert_ids[m / 128].
+//
+// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A tile [128 x 128 B] + B tile [BN x 128 B] per
+//               k-block into a STAGES-deep shared-memory ring.
+//   warp 1      allocates 2*BN TMEM columns; lane 0 issues tcgen05.mma
+//               (M=128, N=BN, 4 MMAs per 128-byte k-block) into one of two
+//               accumulator buffers, so the epilogue of tile i overlaps the
+//               main loop of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 16 columns at a time, fused
+//               math, 16-byte stores to global memory.
+// Tiles are (m-block, n-tile, k-split) triples handed out round-robin; within
+// a group of 8 m-blocks the n-tile index varies slowest, so the CTAs running
+// at the same time share weight tiles through L2.
+//
+// Every barrier wait is bounded (one second): a role that runs out raises a
+// shared abort flag, every role leaves its loop, in-flight TMA loads and
+// MMAs are waited for, TMEM is freed and MOE_ERR_TIMEOUT is reported.
+#include "common.cuh"
+#include "internal.h"
+#include "runtime.h"
+
+namespace ksw {
+namespace {
+
+constexpr int BM = kBlockM;          // rows per tile (TMEM lanes)
+constexpr int kKBytes = 128;         // bytes of K per k-block (one swizzle row)
+constexpr int kABytes = BM * kKBytes;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 8;
+
+enum Epi : int { kEpiSwiGLU = 0, kEpiRows = 1 };
+
+struct KParams {
+  const int32_t* num_post_pad;
+  const int32_t* expert_ids;
+  const int32_t* sorted_ids;
+  const float* a_scale;     // INT8: [rows]
+  const float* b_scale;     // INT8: [E, n]
+  const void* row_weights;  // down: [numel]
+  void* out;
+  int32_t* status;
+  int64_t out_ld;           // elements between output rows
+  int32_t max_m_blocks;
+  int32_t n_total;
+  int32_t k_blocks;
+  int32_t splits;
+  int32_t kb_per_split;
+  int32_t numel;
+  int32_t num_experts;
+  int32_t row_weights_dtype;
+  uint64_t wait_limit_ns;
+};
+
+struct TileCoord {
+  int mb, nt, ks;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(int t, int num_mb, int n_tiles,
+                                                int splits) {
+  TileCoord c;
+  c.ks = t % splits;
+  const int u = t / splits;
+  const int per_group = kGroupM * n_tiles;
+  const int g = u / per_group;
+  const int v = u - g * per_group;
+  const int gm = min(kGroupM, num_mb - g * kGroupM);
+  c.nt = v / gm;
+  c.mb = g * kGroupM + (v - c.nt * gm);
+  return c;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return g / (1.0f + __expf(-g)) * u;
+}
+
+__device__ __forceinline__ float load_weight(const void* w, int dtype,
+                                             int64_t i) {
+  if (dtype == MOE_DTYPE_F32) return static_cast<const float*>(w)[i];
+  if (dtype == MOE_DTYPE_BF16)
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]);
+  return __half2float(static_cast<const __half*>(w)[i]);
+}
+
+template <int KIND>
+__device__ __forceinline__ float acc_to_f32(uint32_t v) {
+  if constexpr (KIND == kKindI8)
+    return static_cast<float>(static_cast<int32_t>(v));
+  else
+    return __uint_as_float(v);
+}
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kBBytes = BN * kKBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (192 * 1024) / kStageBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr size_t kSmemBytes =
+      1024 + size_t(kStages) * kStageBytes + 256;
+  static_assert(kStages >= 2, "pipeline needs at least two stages");
+  static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM columns");
+};
+
+// KIND: kKindF16 (AB_FMT 0 = f16, 1 = bf16) or kKindI8 (AB_FMT 1 = s8).
+// TOUT: element type of the gate-up output (f16/bf16).
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                            const __grid_constant__ CUtensorMap tmB,
+                            const KParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::kStages;
+  constexpr uint32_t D_FMT = (KIND == kKindI8) ? 2u : 1u;
+  constexpr uint32_t IDESC = make_idesc(D_FMT, AB_FMT, BM, BN);
+  constexpr bool kScaled = (KIND == kKindI8);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kBBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* final_bar = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_mb = min(__ldg(p.num_post_pad) / BM, p.max_m_blocks);
+  const int n_tiles = p.n_total / BN;
+  const int total_tiles = num_mb * n_tiles * p.splits;
+  const uint64_t limit = p.wait_limit_ns;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      const int kb0 = c.ks * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+      const int a_row = c.mb * BM;
+      const int b_row = e * p.n_total + c.nt * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+        const int kcol = kb * (kKBytes / (KIND == kKindF16 ? 2 : 1));
+        tma_load_2d(sA + stage * kABytes, &tmA, kcol, a_row, &full[stage]);
+        tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kcol, b_row, &full[stage]);
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // Drain: every load issued into a stage must have landed before the CTA
+    // may exit (on the normal path they have all been consumed already).
+    for (int s = 0; s < STAGES; ++s) {
+      const uint32_t n_s = issued / STAGES + (uint32_t(s) < issued % STAGES ? 1u : 0u);
+      if (n_s == 0) continue;
+      volatile int no_abort = 0;
+      mbar_wait_bounded(&full[s], (n_s - 1) & 1u, &no_abort, limit);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      const int kb0 = c.ks * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+      if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, limit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + stage * kABytes);
+        const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          tc_mma<KIND>(d_tmem, make_sw128_desc(a0 + kk * 32),
+                       make_sw128_desc(b0 + kk * 32), IDESC,
+                       (kb > kb0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      tc_commit(&tfull[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    // All MMAs issued by this thread must complete before TMEM is freed.
+    tc_commit(final_bar);
+    volatile int no_abort = 0;
+    mbar_wait_bounded(final_bar, 0, &no_abort, limit);
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, limit);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int m = c.mb * BM + row;
+      const int r = __ldg(p.sorted_ids + m);
+      const bool valid = r < p.numel;
+      const uint32_t tbase =
+          tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+      float a_s = 1.0f;
+      if constexpr (kScaled) a_s = valid ? __ldg(p.a_scale + m) : 0.0f;
+      const float* bsc =
+          kScaled ? p.b_scale + int64_t(e) * p.n_total + c.nt * BN : nullptr;
+
+      if constexpr (EPI == kEpiSwiGLU) {
+        TOUT* out_row = static_cast<TOUT*>(p.out) + int64_t(m) * p.out_ld +
+                        c.nt * (BN / 2);
+#pragma unroll 1
+        for (int g = 0; g < BN / 32; ++g) {
+          uint32_t gv[16], uv[16];
+          tmem_ld16(tbase + g * 32, gv);
+          tmem_ld16(tbase + g * 32 + 16, uv);
+          tmem_ld_wait();
+          if (valid) {
+            uint32_t packed[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float g0 = acc_to_f32<KIND>(gv[2 * j]);
+              float g1 = acc_to_f32<KIND>(gv[2 * j + 1]);
+              float u0 = acc_to_f32<KIND>(uv[2 * j]);
+              float u1 = acc_to_f32<KIND>(uv[2 * j + 1]);
+              if constexpr (kScaled) {
+                g0 *= a_s * __ldg(bsc + g * 32 + 2 * j);
+                g1 *= a_s * __ldg(bsc + g * 32 + 2 * j + 1);
+                u0 *= a_s * __ldg(bsc + g * 32 + 16 + 2 * j);
+                u1 *= a_s * __ldg(bsc + g * 32 + 16 + 2 * j + 1);
+              }
+              packed[j] = pack2<TOUT>(silu_mul(g0, u0), silu_mul(g1, u1));
+            }
+            uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
+            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+          }
+        }
+      } else {
+        const float w =
+            valid ? load_weight(p.row_weights, p.row_weights_dtype, r) : 0.0f;
+        float* out_row = static_cast<float*>(p.out) +
+                         (int64_t(c.ks) * p.numel + (valid ? r : 0)) * p.out_ld +
+                         c.nt * BN;
+#pragma unroll 1
+        for (int g = 0; g < BN / 16; ++g) {
+          uint32_t v[16];
+          tmem_ld16(tbase + g * 16, v);
+          tmem_ld_wait();
+          if (valid) {
+            float4* dst = reinterpret_cast<float4*>(out_row + g * 16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float x0 = acc_to_f32<KIND>(v[4 * j]);
+              float x1 = acc_to_f32<KIND>(v[4 * j + 1]);
+              float x2 = acc_to_f32<KIND>(v[4 * j + 2]);
+              float x3 = acc_to_f32<KIND>(v[4 * j + 3]);
+              if constexpr (kScaled) {
+                const float s = a_s * w;
+                x0 *= s * __ldg(bsc + g * 16 + 4 * j);
+                x1 *= s * __ldg(bsc + g * 16 + 4 * j + 1);
+                x2 *= s * __ldg(bsc + g * 16 + 4 * j + 2);
+                x3 *= s * __ldg(bsc + g * 16 + 4 * j + 3);
+              } else {
+                x0 *= w;
+                x1 *= w;
+                x2 *= w;
+                x3 *= w;
+              }
+              dst[j] = make_float4(x0, x1, x2, x3);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) report_status(p.status, MOE_ERR_TIMEOUT);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+int num_sms_or_fail(int* sms) { return check_device(sms); }
+
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
+                  const KParams& kp, int grid, cudaStream_t s) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT>;
+  KSW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(Cfg::kSmemBytes)));
+  kern<<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, kp);
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+template <int KIND, int AB_FMT, int EPI, typename TOUT>
+int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                const KParams& kp, int grid, cudaStream_t s) {
+  switch (bn) {
+    case 256: return launch_kernel<KIND, AB_FMT, 256, EPI, TOUT>(ta, tb, kp, grid, s);
+    case 128: return launch_kernel<KIND, AB_FMT, 128, EPI, TOUT>(ta, tb, kp, grid, s);
+    case 64: return launch_kernel<KIND, AB_FMT, 64, EPI, TOUT>(ta, tb, kp, grid, s);
+    default: return fail(MOE_ERR_UNSUPPORTED, "unsupported block_n");
+  }
+}
+
+// Picks the N tile: the largest of 256/128/64 dividing n that still gives
+// every SM about two tiles, given an upper bound on the m-blocks.
+int pick_block_n(int64_t n, int64_t est_m_blocks, int64_t splits, int sms) {
+  const int cands[3] = {256, 128, 64};
+  int best = 0;
+  for (int bn : cands) {
+    if (n % bn != 0) continue;
+    if (best == 0) best = bn;
+    if (est_m_blocks * (n / bn) * splits >= 2 * int64_t(sms)) return bn;
+    best = bn;
+  }
+  return best;
+}
+
+int common_checks(const GroupedGemmArgs& a) {
+  KSW_REQUIRE(a.a && a.b && a.sorted_ids && a.expert_ids && a.num_post_pad && a.out,
+              MOE_ERR_INVALID_ARG, "grouped GEMM: null pointer");
+  KSW_REQUIRE(a.rows > 0 && a.rows % BM == 0, MOE_ERR_INVALID_ARG,
+              "grouped GEMM: rows must be a positive multiple of 128");
+  KSW_REQUIRE(a.num_experts >= 1 && a.n > 0 && a.k > 0, MOE_ERR_INVALID_ARG,
+              "grouped GEMM: bad sizes");
+  KSW_REQUIRE(int64_t(a.num_experts) * a.n < (int64_t(1) << 31),
+              MOE_ERR_UNSUPPORTED, "grouped GEMM: E * N too large");
+  KSW_REQUIRE(a.rows < (int64_t(1) << 31) && a.numel < (int64_t(1) << 31),
+              MOE_ERR_UNSUPPORTED, "grouped GEMM: too many rows");
+  return MOE_OK;
+}
+
+struct OperandTypes {
+  CUtensorMapDataType tma_type;
+  int elem_bytes;
+};
+
+int operand_types(const GroupedGemmArgs& a, OperandTypes* ot) {
+  if (a.quant == MOE_QUANT_NONE) {
+    KSW_REQUIRE(a.compute_dtype == MOE_DTYPE_BF16 || a.compute_dtype == MOE_DTYPE_F16,
+                MOE_ERR_INVALID_ARG, "compute dtype must be bf16 or f16");
+    ot->tma_type = a.compute_dtype == MOE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    ot->elem_bytes = 2;
+    return MOE_OK;
+  }
+  if (a.quant == MOE_QUANT_INT8_CHANNEL) {
+    KSW_REQUIRE(a.a_scale && a.b_scale, MOE_ERR_INVALID_ARG,
+                "int8 GEMM needs activation and weight scales");
+    ot->tma_type = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    ot->elem_bytes = 1;
+    return MOE_OK;
+  }
+  return fail(MOE_ERR_UNSUPPORTED, "quant mode not handled by this GEMM");
+}
+
+int make_maps(const GroupedGemmArgs& a, const OperandTypes& ot, int bn,
+              CUtensorMap* ta, CUtensorMap* tb) {
+  const uint32_t box_k = uint32_t(kKBytes / ot.elem_bytes);
+  int st = encode_tma_2d(ta, ot.tma_type, ot.elem_bytes, a.a, uint64_t(a.k),
+                         uint64_t(a.rows), uint64_t(a.k), box_k, BM);
+  if (st != MOE_OK) return st;
+  return encode_tma_2d(tb, ot.tma_type, ot.elem_bytes, a.b, uint64_t(a.k),
+                       uint64_t(a.num_experts) * uint64_t(a.n), uint64_t(a.k),
+                       box_k, uint32_t(bn));
+}
+
+KParams base_params(const GroupedGemmArgs& a, int elem_bytes) {
+  KParams kp{};
+  kp.num_post_pad = a.num_post_pad;
+  kp.expert_ids = a.expert_ids;
+  kp.sorted_ids = a.sorted_ids;
+  kp.a_scale = a.a_scale;
+  kp.b_scale = a.b_scale;
+  kp.row_weights = a.row_weights;
+  kp.out = a.out;
+  kp.status = a.status;
+  kp.max_m_blocks = int32_t(a.rows / BM);
+  kp.n_total = int32_t(a.n);
+  kp.k_blocks = int32_t(ceil_div(a.k * elem_bytes, kKBytes));
+  kp.splits = 1;
+  kp.kb_per_split = kp.k_blocks;
+  kp.numel = int32_t(a.numel);
+  kp.num_experts = a.num_experts;
+  kp.row_weights_dtype = a.row_weights_dtype;
+  kp.wait_limit_ns = kWaitLimitNs;
+  return kp;
+}
+
+// Upper bound on the m-blocks actually used: every expert with rows adds at
+// most one partial block.
+int64_t est_m_blocks(const GroupedGemmArgs& a) {
+  return std::min<int64_t>(a.rows / BM,
+                           ceil_div(a.numel, BM) + std::min<int64_t>(a.num_experts, a.numel));
+}
+
+}  // namespace
+
+int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
+  int sms = 0;
+  int st = num_sms_or_fail(&sms);
+  if (st != MOE_OK) return st;
+  st = common_checks(a);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE(a.n % 32 == 0, MOE_ERR_UNSUPPORTED,
+              "gate-up GEMM: 2*I must be a multiple of 32");
+  OperandTypes ot;
+  st = operand_types(a, &ot);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE((a.k * ot.elem_bytes) % 16 == 0, MOE_ERR_UNSUPPORTED,
+              "gate-up GEMM: hidden size * element size must be a multiple of 16 B");
+  const int bn = a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), 1, sms);
+  KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED,
+              "gate-up GEMM: 2*I must be a multiple of 64");
+  CUtensorMap ta, tb;
+  st = make_maps(a, ot, bn, &ta, &tb);
+  if (st != MOE_OK) return st;
+  KParams kp = base_params(a, ot.elem_bytes);
+  kp.out_ld = a.n / 2;
+  const int grid = sms;
+  if (a.quant == MOE_QUANT_INT8_CHANNEL) {
+    // int8 products dequantise to bf16 activations
+    return dispatch_bn<kKindI8, 1, kEpiSwiGLU, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
+  }
+  if (a.compute_dtype == MOE_DTYPE_BF16)
+    return dispatch_bn<kKindF16, 1, kEpiSwiGLU, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
+  return dispatch_bn<kKindF16, 0, kEpiSwiGLU, __half>(bn, ta, tb, kp, grid, s);
+}
+
+int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
+  int sms = 0;
+  int st = num_sms_or_fail(&sms);
+  if (st != MOE_OK) return st;
+  st = common_checks(a);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE(a.row_weights != nullptr, MOE_ERR_INVALID_ARG,
+              "down GEMM: null row weights");
+  KSW_REQUIRE(a.row_weights_dtype == MOE_DTYPE_F32 || a.row_weights_dtype == MOE_DTYPE_F16 ||
+                  a.row_weights_dtype == MOE_DTYPE_BF16,
+              MOE_ERR_INVALID_ARG, "down GEMM: row weights must be f32/f16/bf16");
+  KSW_REQUIRE(a.splits >= 1, MOE_ERR_INVALID_ARG, "down GEMM: splits must be >= 1");
+  OperandTypes ot;
+  st = operand_types(a, &ot);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE((a.k * ot.elem_bytes) % 16 == 0, MOE_ERR_UNSUPPORTED,
+              "down GEMM: intermediate size * element size must be a multiple of 16 B");
+  KSW_REQUIRE(a.n % 64 == 0, MOE_ERR_UNSUPPORTED,
+              "down GEMM: hidden size must be a multiple of 64");
+  KParams kp = base_params(a, ot.elem_bytes);
+  // K splits: every split gets at least one k-block; the effective count is
+  // recomputed so that no split is empty.
+  const int kb_per = int(ceil_div(kp.k_blocks, a.splits));
+  kp.kb_per_split = kb_per;
+  kp.splits = int(ceil_div(kp.k_blocks, kb_per));
+  KSW_REQUIRE(kp.splits == a.splits, MOE_ERR_INVALID_ARG,
+              "down GEMM: splits leaves an empty K range; choose splits so that every split has k-blocks");
+  const int bn = a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms);
+  KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED, "down GEMM: bad block_n");
+  CUtensorMap ta, tb;
+  st = make_maps(a, ot, bn, &ta, &tb);
+  if (st != MOE_OK) return st;
+  kp.out_ld = a.n;
+  const int grid = sms;
+  if (a.quant == MOE_QUANT_INT8_CHANNEL)
+    return dispatch_bn<kKindI8, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s);
+  if (a.compute_dtype == MOE_DTYPE_BF16)
+    return dispatch_bn<kKindF16, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s);
+  return dispatch_bn<kKindF16, 0, kEpiRows, float>(bn, ta, tb, kp, grid, s);
+}
+
+}  // namespace ksw

@@ -1,0 +1,50 @@
+// Internal launchers shared between the translation units of the library.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace ksw {
+
+// ----- align.cu -----
+int64_t align_buffer_len(int64_t numel, int E, int BM);
+size_t align_workspace_bytes(int64_t numel, int E);
+int align_validate(int64_t numel, int E, int BM);
+int align_launch(const void* ids, int ids_dtype, int64_t numel, int E, int BM,
+                 int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
+                 void* workspace, size_t ws_bytes, cudaStream_t s);
+
+// ----- gemm.cu -----
+// Row-block height of the grouped GEMMs (and the align block size they need).
+constexpr int kBlockM = 128;
+
+struct GroupedGemmArgs {
+  int quant;                   // moe_quant_t
+  int compute_dtype;           // F16 or BF16 for QUANT_NONE
+  const void* a;               // [rows, K] operand rows in expert-sorted order
+  const float* a_scale;        // FP8: [rows, ceil(K/128)], INT8: [rows]
+  const void* b;               // [E, N, K] expert weights
+  const float* b_scale;        // FP8: [E, ceil(N/128), ceil(K/128)], INT8: [E, N]
+  const int32_t* sorted_ids;   // [rows]
+  const int32_t* expert_ids;   // [rows / kBlockM]
+  const int32_t* num_post_pad; // [1]
+  int64_t rows;                // buffer length (multiple of kBlockM)
+  int64_t numel;               // T * k: sorted_ids sentinel
+  int num_experts;
+  int64_t n;                   // output columns per expert (rows of B)
+  int64_t k;                   // reduction length
+  // epilogue
+  void* out;                   // gate-up: act [rows, n/2]; down: f32 [splits, numel, n]
+  const void* row_weights;     // down: [numel] weight of each flat row
+  int row_weights_dtype;
+  int splits;                  // down: K splits (partial sums summed later)
+  int32_t* status;
+  int block_n;                 // 0 = heuristic
+};
+
+int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s);
+int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s);
+
+}  // namespace ksw

@@ -1,0 +1,385 @@
+// moe_fused_experts: the whole expert computation of
+// kernels/track1-triton/fused_moe/base.py:50-76 as six launches on the
+// caller's stream, with no host synchronisation:
+//
+//   1. align      topk_ids -> sorted_token_ids, expert_ids, num_post_pad
+//   2. gather     hidden rows in expert-sorted order (+cast / quantise)
+//   3. gate-up    grouped tcgen05 GEMM, SiLU(gate)*up fused      [L, I]
+//   4. (quant)    per-row quantisation of the activation (W8A8 modes)
+//   5. down       grouped tcgen05 GEMM, topk weight fused, optional K split
+//   6. sum_topk   out[t] = sum over splits and slots, cast to act dtype
+//
+// Also exports the stages one by one (moe_gather_rows, moe_gemm_gate_up,
+// moe_gemm_down, moe_sum_topk) for callers that build their own pipeline
+// (expert parallelism) and for stage-level tests.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+#include "rows.h"
+
+namespace ksw {
+namespace {
+
+struct Plan {
+  int64_t T, H, I, numel, L;
+  int E, k;
+  int quant;
+  int compute_dtype;     // operand dtype for QUANT_NONE
+  int a_dtype;           // dtype of the gathered operand
+  int act_dtype;         // dtype of the gate-up output (bf16/f16)
+  int splits;
+  size_t align_ws;
+  size_t off_sorted, off_eids, off_npp, off_align, off_a, off_a_scale, off_act,
+      off_act_q, off_act_scale, off_part, total;
+};
+
+int elem_bytes(int dtype) {
+  switch (dtype) {
+    case MOE_DTYPE_F32: case MOE_DTYPE_I32: return 4;
+    case MOE_DTYPE_F16: case MOE_DTYPE_BF16: return 2;
+    case MOE_DTYPE_E4M3: case MOE_DTYPE_I8: return 1;
+    case MOE_DTYPE_I64: return 8;
+    default: return 0;
+  }
+}
+
+int choose_splits(int64_t numel, int64_t L, int E, int64_t H, int64_t K, int kbytes_per_elem,
+                  int sms) {
+  const int64_t est_mb = std::min<int64_t>(L / kBlockM, ceil_div(numel, kBlockM) +
+                                                            std::min<int64_t>(E, numel));
+  const int64_t tiles = std::max<int64_t>(1, est_mb * (H / 128));
+  const int64_t k_blocks = ceil_div(K * kbytes_per_elem, 128);
+  if (tiles >= sms) return 1;
+  int64_t splits = std::min<int64_t>(ceil_div(2 * sms, tiles), 16);
+  splits = std::min<int64_t>(splits, std::max<int64_t>(1, k_blocks / 4));
+  splits = std::max<int64_t>(splits, 1);
+  const int64_t per = ceil_div(k_blocks, splits);
+  return int(ceil_div(k_blocks, per));
+}
+
+int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
+  KSW_REQUIRE(p != nullptr, MOE_ERR_INVALID_ARG, "null problem");
+  KSW_REQUIRE(p->num_tokens >= 0 && p->hidden_size > 0 && p->inter_size > 0,
+              MOE_ERR_INVALID_ARG, "bad sizes");
+  KSW_REQUIRE(p->num_experts >= 1 && p->num_experts <= 1024, MOE_ERR_UNSUPPORTED,
+              "num_experts must be in [1, 1024]");
+  KSW_REQUIRE(p->top_k >= 1 && p->top_k <= 64, MOE_ERR_INVALID_ARG, "top_k must be in [1, 64]");
+  KSW_REQUIRE(p->hidden_size % 64 == 0, MOE_ERR_UNSUPPORTED,
+              "hidden_size must be a multiple of 64");
+  KSW_REQUIRE(p->inter_size % 16 == 0, MOE_ERR_UNSUPPORTED,
+              "intermediate_size must be a multiple of 16");
+  KSW_REQUIRE(p->act_dtype == MOE_DTYPE_F32 || p->act_dtype == MOE_DTYPE_F16 ||
+                  p->act_dtype == MOE_DTYPE_BF16,
+              MOE_ERR_INVALID_ARG, "act_dtype must be f32, f16 or bf16");
+  KSW_REQUIRE(p->ids_dtype == MOE_DTYPE_I32 || p->ids_dtype == MOE_DTYPE_I64,
+              MOE_ERR_INVALID_ARG, "ids_dtype must be int32 or int64");
+  KSW_REQUIRE(p->weights_dtype == MOE_DTYPE_F32 || p->weights_dtype == MOE_DTYPE_F16 ||
+                  p->weights_dtype == MOE_DTYPE_BF16,
+              MOE_ERR_INVALID_ARG, "weights_dtype must be f32, f16 or bf16");
+  Plan& P = *pl;
+  P.T = p->num_tokens;
+  P.H = p->hidden_size;
+  P.I = p->inter_size;
+  P.E = p->num_experts;
+  P.k = p->top_k;
+  P.quant = p->quant;
+  P.numel = P.T * P.k;
+  KSW_REQUIRE(P.numel < (int64_t(1) << 30), MOE_ERR_UNSUPPORTED, "too many tokens");
+  P.L = align_buffer_len(P.numel, P.E, kBlockM);
+  P.compute_dtype = p->act_dtype == MOE_DTYPE_F16 ? MOE_DTYPE_F16 : MOE_DTYPE_BF16;
+  int kbpe = 2;
+  if (P.quant == MOE_QUANT_NONE) {
+    P.a_dtype = P.compute_dtype;
+    P.act_dtype = P.compute_dtype;
+  } else if (P.quant == MOE_QUANT_INT8_CHANNEL) {
+    P.a_dtype = MOE_DTYPE_I8;
+    P.act_dtype = MOE_DTYPE_BF16;
+    kbpe = 1;
+  } else if (P.quant == MOE_QUANT_FP8_BLOCK) {
+    return fail(MOE_ERR_UNSUPPORTED, "fp8 block-scaled path not available in this build");
+  } else {
+    return fail(MOE_ERR_INVALID_ARG, "unknown quant mode");
+  }
+  P.splits = choose_splits(P.numel, P.L, P.E, P.H, P.I, kbpe, sms);
+  P.align_ws = align_workspace_bytes(P.numel, P.E);
+
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  P.off_sorted = take(size_t(P.L) * 4);
+  P.off_eids = take(size_t(P.L / kBlockM) * 4);
+  P.off_npp = take(4);
+  P.off_align = take(P.align_ws);
+  P.off_a = take(size_t(P.L) * P.H * elem_bytes(P.a_dtype));
+  P.off_a_scale = take(P.quant == MOE_QUANT_INT8_CHANNEL ? size_t(P.L) * 4 : 0);
+  P.off_act = take(size_t(P.L) * P.I * elem_bytes(P.act_dtype));
+  P.off_act_q = take(P.quant == MOE_QUANT_INT8_CHANNEL ? size_t(P.L) * P.I : 0);
+  P.off_act_scale = take(P.quant == MOE_QUANT_INT8_CHANNEL ? size_t(P.L) * 4 : 0);
+  P.off_part = take(size_t(P.splits) * P.numel * P.H * 4);
+  P.total = off;
+  return MOE_OK;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) {
+  return reinterpret_cast<T*>(static_cast<uint8_t*>(ws) + off);
+}
+
+}  // namespace
+}  // namespace ksw
+
+using namespace ksw;
+
+extern "C" {
+
+int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes) {
+  KSW_REQUIRE(bytes != nullptr, MOE_ERR_INVALID_ARG, "null bytes pointer");
+  int sms = 148;
+  int st = check_device(&sms);
+  if (st != MOE_OK) sms = 148;  // size queries work without a B200 present
+  Plan pl;
+  st = make_plan(p, sms, &pl);
+  if (st != MOE_OK) return st;
+  *bytes = pl.total;
+  return MOE_OK;
+}
+
+int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  int sms = 0;
+  int st = check_device(&sms);
+  if (st != MOE_OK) return st;
+  Plan P;
+  st = make_plan(p, sms, &P);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE(workspace != nullptr && workspace_bytes >= P.total, MOE_ERR_WORKSPACE,
+              "moe_fused_experts: workspace smaller than moe_fused_experts_workspace_size");
+  KSW_REQUIRE(p->out != nullptr, MOE_ERR_INVALID_ARG, "null out");
+  if (P.T == 0) return MOE_OK;
+  KSW_REQUIRE(p->hidden && p->w13 && p->w2 && p->topk_weights && p->topk_ids,
+              MOE_ERR_INVALID_ARG, "null input pointer");
+  if (P.quant != MOE_QUANT_NONE)
+    KSW_REQUIRE(p->w13_scale && p->w2_scale, MOE_ERR_INVALID_ARG, "null weight scales");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto mark = [&](int stage) -> int {
+    if (p->stage_events == nullptr) return MOE_OK;
+    return check_cuda(cudaEventRecord(static_cast<cudaEvent_t>(p->stage_events[stage]), s),
+                      "cudaEventRecord(stage event)");
+  };
+#define KSW_MARK(stage)           \
+  do {                            \
+    st = mark(stage);             \
+    if (st != MOE_OK) return st;  \
+  } while (0)
+  int32_t* sorted = at<int32_t>(workspace, P.off_sorted);
+  int32_t* eids = at<int32_t>(workspace, P.off_eids);
+  int32_t* npp = at<int32_t>(workspace, P.off_npp);
+
+  KSW_MARK(MOE_STAGE_ALIGN);
+  st = align_launch(p->topk_ids, p->ids_dtype, P.numel, P.E, kBlockM, sorted, eids, npp,
+                    at<void>(workspace, P.off_align), P.align_ws, s);
+  if (st != MOE_OK) return st;
+
+  GatherArgs g{};
+  g.src = p->hidden;
+  g.src_dtype = p->act_dtype;
+  g.src_rows = P.T;
+  g.H = P.H;
+  g.top_k = P.k;
+  g.sorted = sorted;
+  g.num_post_pad = npp;
+  g.max_rows = P.L;
+  g.numel = P.numel;
+  g.quant = P.quant;
+  g.dst = at<void>(workspace, P.off_a);
+  g.dst_dtype = P.a_dtype;
+  g.scale = P.quant == MOE_QUANT_NONE ? nullptr : at<float>(workspace, P.off_a_scale);
+  KSW_MARK(MOE_STAGE_GATHER);
+  st = gather_launch(g, s);
+  if (st != MOE_OK) return st;
+
+  KSW_MARK(MOE_STAGE_GATE_UP);
+  GroupedGemmArgs ga{};
+  ga.quant = P.quant;
+  ga.compute_dtype = P.compute_dtype;
+  ga.a = g.dst;
+  ga.a_scale = g.scale;
+  ga.b = p->w13;
+  ga.b_scale = p->w13_scale;
+  ga.sorted_ids = sorted;
+  ga.expert_ids = eids;
+  ga.num_post_pad = npp;
+  ga.rows = P.L;
+  ga.numel = P.numel;
+  ga.num_experts = P.E;
+  ga.n = 2 * P.I;
+  ga.k = P.H;
+  ga.out = at<void>(workspace, P.off_act);
+  ga.splits = 1;
+  ga.status = p->status;
+  st = gemm_gate_up_launch(ga, s);
+  if (st != MOE_OK) return st;
+
+  const void* down_a = ga.out;
+  const float* down_a_scale = nullptr;
+  KSW_MARK(MOE_STAGE_QUANT);
+  if (P.quant != MOE_QUANT_NONE) {
+    GatherArgs q{};
+    q.src = ga.out;
+    q.src_dtype = P.act_dtype;
+    q.src_rows = P.L;
+    q.H = P.I;
+    q.top_k = 0;
+    q.sorted = sorted;
+    q.num_post_pad = npp;
+    q.max_rows = P.L;
+    q.numel = P.numel;
+    q.quant = P.quant;
+    q.dst = at<void>(workspace, P.off_act_q);
+    q.dst_dtype = P.a_dtype;
+    q.scale = at<float>(workspace, P.off_act_scale);
+    st = gather_launch(q, s);
+    if (st != MOE_OK) return st;
+    down_a = q.dst;
+    down_a_scale = q.scale;
+  }
+
+  KSW_MARK(MOE_STAGE_DOWN);
+  GroupedGemmArgs gd = ga;
+  gd.a = down_a;
+  gd.a_scale = down_a_scale;
+  gd.b = p->w2;
+  gd.b_scale = p->w2_scale;
+  gd.n = P.H;
+  gd.k = P.I;
+  gd.out = at<void>(workspace, P.off_part);
+  gd.row_weights = p->topk_weights;
+  gd.row_weights_dtype = p->weights_dtype;
+  gd.splits = P.splits;
+  st = gemm_down_launch(gd, s);
+  if (st != MOE_OK) return st;
+
+  SumArgs sa{};
+  sa.part = at<float>(workspace, P.off_part);
+  sa.splits = P.splits;
+  sa.T = P.T;
+  sa.top_k = P.k;
+  sa.H = P.H;
+  sa.ids = p->topk_ids;
+  sa.ids_dtype = p->ids_dtype;
+  sa.E = P.E;
+  sa.out = p->out;
+  sa.out_dtype = p->act_dtype;
+  KSW_MARK(MOE_STAGE_SUM);
+  st = sum_topk_launch(sa, s);
+  if (st != MOE_OK) return st;
+  KSW_MARK(MOE_NUM_STAGES);
+  return MOE_OK;
+#undef KSW_MARK
+}
+
+int moe_gather_rows(const void* src, int src_dtype, int64_t src_rows, int64_t hidden_size,
+                    int top_k, const int32_t* sorted_token_ids,
+                    const int32_t* num_tokens_post_pad, int64_t buffer_len, int64_t numel,
+                    int quant, void* dst, int dst_dtype, float* dst_scale, void* stream) {
+  int st = check_device(nullptr);
+  if (st != MOE_OK) return st;
+  GatherArgs g{};
+  g.src = src;
+  g.src_dtype = src_dtype;
+  g.src_rows = src_rows;
+  g.H = hidden_size;
+  g.top_k = top_k;
+  g.sorted = sorted_token_ids;
+  g.num_post_pad = num_tokens_post_pad;
+  g.max_rows = buffer_len;
+  g.numel = numel;
+  g.quant = quant;
+  g.dst = dst;
+  g.dst_dtype = dst_dtype;
+  g.scale = dst_scale;
+  return gather_launch(g, static_cast<cudaStream_t>(stream));
+}
+
+int moe_gemm_gate_up(int quant, int compute_dtype, const void* a, const float* a_scale,
+                     const void* w13, const float* w13_scale,
+                     const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                     const int32_t* num_tokens_post_pad, int64_t buffer_len, int64_t numel,
+                     int num_experts, int64_t hidden_size, int64_t inter_size,
+                     void* act_out, int block_n, int32_t* status, void* stream) {
+  GroupedGemmArgs ga{};
+  ga.quant = quant;
+  ga.compute_dtype = compute_dtype;
+  ga.a = a;
+  ga.a_scale = a_scale;
+  ga.b = w13;
+  ga.b_scale = w13_scale;
+  ga.sorted_ids = sorted_token_ids;
+  ga.expert_ids = expert_ids;
+  ga.num_post_pad = num_tokens_post_pad;
+  ga.rows = buffer_len;
+  ga.numel = numel;
+  ga.num_experts = num_experts;
+  ga.n = 2 * inter_size;
+  ga.k = hidden_size;
+  ga.out = act_out;
+  ga.splits = 1;
+  ga.status = status;
+  ga.block_n = block_n;
+  return gemm_gate_up_launch(ga, static_cast<cudaStream_t>(stream));
+}
+
+int moe_gemm_down(int quant, int compute_dtype, const void* act, const float* act_scale,
+                  const void* w2, const float* w2_scale, const int32_t* sorted_token_ids,
+                  const int32_t* expert_ids, const int32_t* num_tokens_post_pad,
+                  int64_t buffer_len, int64_t numel, int num_experts, int64_t hidden_size,
+                  int64_t inter_size, const void* row_weights, int weights_dtype, int splits,
+                  float* partial_out, int block_n, int32_t* status, void* stream) {
+  GroupedGemmArgs gd{};
+  gd.quant = quant;
+  gd.compute_dtype = compute_dtype;
+  gd.a = act;
+  gd.a_scale = act_scale;
+  gd.b = w2;
+  gd.b_scale = w2_scale;
+  gd.sorted_ids = sorted_token_ids;
+  gd.expert_ids = expert_ids;
+  gd.num_post_pad = num_tokens_post_pad;
+  gd.rows = buffer_len;
+  gd.numel = numel;
+  gd.num_experts = num_experts;
+  gd.n = hidden_size;
+  gd.k = inter_size;
+  gd.out = partial_out;
+  gd.row_weights = row_weights;
+  gd.row_weights_dtype = weights_dtype;
+  gd.splits = splits;
+  gd.status = status;
+  gd.block_n = block_n;
+  return gemm_down_launch(gd, static_cast<cudaStream_t>(stream));
+}
+
+int moe_sum_topk(const float* partial, int splits, int64_t num_tokens, int top_k,
+                 int64_t hidden_size, const void* topk_ids, int ids_dtype, int num_experts,
+                 void* out, int out_dtype, void* stream) {
+  int st = check_device(nullptr);
+  if (st != MOE_OK) return st;
+  SumArgs sa{};
+  sa.part = partial;
+  sa.splits = splits;
+  sa.T = num_tokens;
+  sa.top_k = top_k;
+  sa.H = hidden_size;
+  sa.ids = topk_ids;
+  sa.ids_dtype = ids_dtype;
+  sa.E = num_experts;
+  sa.out = out;
+  sa.out_dtype = out_dtype;
+  return sum_topk_launch(sa, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

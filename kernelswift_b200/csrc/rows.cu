@@ -1,0 +1,343 @@
+// Row-wise kernels around the grouped GEMMs (all HBM-bound, one warp per row):
+//   gather_rows: A[m] = hidden[sorted_ids[m] / top_k] in expert-sorted order
+//                (the replicate + boolean gather of base.py:52-58,68), with
+//                an optional cast (f32 -> bf16) or quantisation (e4m3 per
+//                128-column group, int8 per row).
+//   quant_rows:  the same quantisations for the gate-up output (the second
+//                GEMM's operand).
+//   sum_topk:    out[t] = sum_s sum_j part[s, t*k + j] (the top-k reduction of
+//                base.py:75-76), in fixed order, fp32, then cast.
+#include "common.cuh"
+#include "rows.h"
+
+namespace ksw {
+namespace {
+
+constexpr int kWarps = 8;  // rows per CTA
+constexpr float kFp8Max = 448.0f;
+constexpr float kInt8Max = 127.0f;
+
+// Loads 8 consecutive elements as floats (16-byte aligned source).
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p,
+                                                     float (&v)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p,
+                                                      const float (&v)[8]) {
+  uint4 o;
+  o.x = pack2<__nv_bfloat16>(v[0], v[1]);
+  o.y = pack2<__nv_bfloat16>(v[2], v[3]);
+  o.z = pack2<__nv_bfloat16>(v[4], v[5]);
+  o.w = pack2<__nv_bfloat16>(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = o;
+}
+template <>
+__device__ __forceinline__ void store8<__half>(__half* p, const float (&v)[8]) {
+  uint4 o;
+  o.x = pack2<__half>(v[0], v[1]);
+  o.y = pack2<__half>(v[2], v[3]);
+  o.z = pack2<__half>(v[4], v[5]);
+  o.w = pack2<__half>(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = o;
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Quantisation arithmetic shared with the oracle: scale = absmax / qmax
+// (1 when the group is all zero), q = clamp(x / scale, -qmax, qmax) rounded
+// to nearest-even in the target format.
+__device__ __forceinline__ float quant_scale(float absmax, float qmax) {
+  const float s = absmax / qmax;
+  return s > 0.0f ? s : 1.0f;
+}
+
+__device__ __forceinline__ uint8_t to_e4m3(float x, float scale) {
+  const float q = fminf(fmaxf(x / scale, -kFp8Max), kFp8Max);
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3));
+}
+
+__device__ __forceinline__ int8_t to_i8(float x, float scale) {
+  const float q = fminf(fmaxf(x / scale, -kInt8Max), kInt8Max);
+  return static_cast<int8_t>(__float2int_rn(q));
+}
+
+// Source row of operand row m, or -1 for a padding slot. top_k == 0 maps a
+// valid row to itself (quantising an operand that is already in sorted order).
+__device__ __forceinline__ int64_t source_row(const int32_t* sorted, int64_t m,
+                                              int64_t numel, int top_k) {
+  const int r = __ldg(sorted + m);
+  if (r >= numel) return -1;
+  return top_k > 0 ? int64_t(r / top_k) : m;
+}
+
+// ---------------- plain gather (+ cast) ----------------
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(kWarps * 32)
+    gather_cast_kernel(const Tin* __restrict__ src, int64_t H, int top_k,
+                       const int32_t* __restrict__ sorted,
+                       const int32_t* __restrict__ num_post_pad, int64_t max_rows,
+                       int64_t numel, int64_t src_rows, Tout* __restrict__ dst) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
+  for (int64_t m = int64_t(blockIdx.x) * kWarps + warp; m < rows;
+       m += int64_t(gridDim.x) * kWarps) {
+    const int64_t sr = source_row(sorted, m, numel, top_k);
+    if (sr < 0 || sr >= src_rows) continue;
+    const Tin* s = src + sr * H;
+    Tout* d = dst + m * H;
+    for (int64_t h = int64_t(lane) * 8; h < H; h += 32 * 8) {
+      float v[8];
+      load8(s + h, v);
+      store8(d + h, v);
+    }
+  }
+}
+
+// ---------------- gather + e4m3 per (row, 128 columns) ----------------
+template <typename Tin>
+__global__ void __launch_bounds__(kWarps * 32)
+    gather_fp8_kernel(const Tin* __restrict__ src, int64_t H, int top_k,
+                      const int32_t* __restrict__ sorted,
+                      const int32_t* __restrict__ num_post_pad, int64_t max_rows,
+                      int64_t numel, int64_t src_rows, uint8_t* __restrict__ dst,
+                      float* __restrict__ scale) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
+  const int64_t groups = (H + 127) / 128;
+  for (int64_t m = int64_t(blockIdx.x) * kWarps + warp; m < rows;
+       m += int64_t(gridDim.x) * kWarps) {
+    const int64_t sr = sorted ? source_row(sorted, m, numel, top_k) : m;
+    if (sr < 0 || sr >= src_rows) continue;
+    const Tin* s = src + sr * H;
+    for (int64_t g = 0; g < groups; ++g) {
+      const int64_t h0 = g * 128 + lane * 4;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (h0 + i < H) v[i] = to_f32(s[h0 + i]);
+      float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+      amax = warp_max(amax);
+      const float sc = quant_scale(amax, kFp8Max);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (h0 + i < H) dst[m * H + h0 + i] = to_e4m3(v[i], sc);
+      if (lane == 0) scale[m * groups + g] = sc;
+    }
+  }
+}
+
+// ---------------- gather + int8 per row ----------------
+template <typename Tin>
+__global__ void __launch_bounds__(kWarps * 32)
+    gather_i8_kernel(const Tin* __restrict__ src, int64_t H, int top_k,
+                     const int32_t* __restrict__ sorted,
+                     const int32_t* __restrict__ num_post_pad, int64_t max_rows,
+                     int64_t numel, int64_t src_rows, int8_t* __restrict__ dst,
+                     float* __restrict__ scale) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
+  for (int64_t m = int64_t(blockIdx.x) * kWarps + warp; m < rows;
+       m += int64_t(gridDim.x) * kWarps) {
+    const int64_t sr = sorted ? source_row(sorted, m, numel, top_k) : m;
+    if (sr < 0 || sr >= src_rows) continue;
+    const Tin* s = src + sr * H;
+    float amax = 0.0f;
+    for (int64_t h = int64_t(lane) * 8; h < H; h += 32 * 8) {
+      float v[8];
+      load8(s + h, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+    amax = warp_max(amax);
+    const float sc = quant_scale(amax, kInt8Max);
+    for (int64_t h = int64_t(lane) * 8; h < H; h += 32 * 8) {
+      float v[8];
+      load8(s + h, v);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        lo |= uint32_t(uint8_t(to_i8(v[i], sc))) << (8 * i);
+        hi |= uint32_t(uint8_t(to_i8(v[4 + i], sc))) << (8 * i);
+      }
+      *reinterpret_cast<uint2*>(dst + m * H + h) = make_uint2(lo, hi);
+    }
+    if (lane == 0) scale[m] = sc;
+  }
+}
+
+// ---------------- top-k (and K-split) reduction ----------------
+template <typename Tout, typename IdT>
+__global__ void __launch_bounds__(256)
+    sum_topk_kernel(const float* __restrict__ part, int splits, int64_t T,
+                    int top_k, int64_t H, int64_t numel, const IdT* __restrict__ ids,
+                    int E, Tout* __restrict__ out) {
+  const int64_t vec_per_row = H / 8;
+  const int64_t total = T * vec_per_row;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec_per_row;
+    const int64_t h = (i - t * vec_per_row) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < top_k; ++j) {
+      const int64_t r = t * top_k + j;
+      if (ids != nullptr) {
+        const long long e = static_cast<long long>(ids[r]);
+        if (e < 0 || e >= E) continue;
+      }
+      for (int s = 0; s < splits; ++s) {
+        float v[8];
+        load8(part + (int64_t(s) * numel + r) * H + h, v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += v[q];
+      }
+    }
+    store8(out + t * H + h, acc);
+  }
+}
+
+int grid_for_rows(int64_t rows) {
+  return int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, kWarps), 148 * 16)));
+}
+
+}  // namespace
+
+int gather_launch(const GatherArgs& a, cudaStream_t s) {
+  KSW_REQUIRE(a.src && a.dst && a.num_post_pad, MOE_ERR_INVALID_ARG, "gather: null pointer");
+  KSW_REQUIRE(a.sorted || a.quant != MOE_QUANT_NONE, MOE_ERR_INVALID_ARG,
+              "gather: null sorted ids");
+  KSW_REQUIRE(a.sorted || a.top_k == 0, MOE_ERR_INVALID_ARG,
+              "gather: sorted ids needed when top_k > 0");
+  KSW_REQUIRE(a.H % 16 == 0 && a.H > 0, MOE_ERR_UNSUPPORTED, "gather: H % 16 != 0");
+  KSW_REQUIRE(a.top_k >= 0, MOE_ERR_INVALID_ARG, "gather: top_k < 0");
+  const int grid = grid_for_rows(a.max_rows);
+  const int block = kWarps * 32;
+  if (a.quant == MOE_QUANT_NONE) {
+    if (a.src_dtype == MOE_DTYPE_F32 && a.dst_dtype == MOE_DTYPE_BF16)
+      gather_cast_kernel<float, __nv_bfloat16><<<grid, block, 0, s>>>(
+          static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<__nv_bfloat16*>(a.dst));
+    else if (a.src_dtype == MOE_DTYPE_F32 && a.dst_dtype == MOE_DTYPE_F16)
+      gather_cast_kernel<float, __half><<<grid, block, 0, s>>>(
+          static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<__half*>(a.dst));
+    else if (a.src_dtype == MOE_DTYPE_BF16 && a.dst_dtype == MOE_DTYPE_BF16)
+      gather_cast_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, block, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(a.src), a.H, a.top_k, a.sorted,
+          a.num_post_pad, a.max_rows, a.numel, a.src_rows,
+          static_cast<__nv_bfloat16*>(a.dst));
+    else if (a.src_dtype == MOE_DTYPE_F16 && a.dst_dtype == MOE_DTYPE_F16)
+      gather_cast_kernel<__half, __half><<<grid, block, 0, s>>>(
+          static_cast<const __half*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<__half*>(a.dst));
+    else
+      return fail(MOE_ERR_UNSUPPORTED, "gather: unsupported dtype pair");
+  } else if (a.quant == MOE_QUANT_FP8_BLOCK) {
+    KSW_REQUIRE(a.scale != nullptr, MOE_ERR_INVALID_ARG, "gather: null scale");
+    if (a.src_dtype == MOE_DTYPE_F32)
+      gather_fp8_kernel<float><<<grid, block, 0, s>>>(
+          static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<uint8_t*>(a.dst), a.scale);
+    else if (a.src_dtype == MOE_DTYPE_BF16)
+      gather_fp8_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(a.src), a.H, a.top_k, a.sorted,
+          a.num_post_pad, a.max_rows, a.numel, a.src_rows,
+          static_cast<uint8_t*>(a.dst), a.scale);
+    else if (a.src_dtype == MOE_DTYPE_F16)
+      gather_fp8_kernel<__half><<<grid, block, 0, s>>>(
+          static_cast<const __half*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<uint8_t*>(a.dst), a.scale);
+    else
+      return fail(MOE_ERR_UNSUPPORTED, "gather: unsupported source dtype");
+  } else if (a.quant == MOE_QUANT_INT8_CHANNEL) {
+    KSW_REQUIRE(a.scale != nullptr, MOE_ERR_INVALID_ARG, "gather: null scale");
+    if (a.src_dtype == MOE_DTYPE_F32)
+      gather_i8_kernel<float><<<grid, block, 0, s>>>(
+          static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<int8_t*>(a.dst), a.scale);
+    else if (a.src_dtype == MOE_DTYPE_BF16)
+      gather_i8_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(a.src), a.H, a.top_k, a.sorted,
+          a.num_post_pad, a.max_rows, a.numel, a.src_rows,
+          static_cast<int8_t*>(a.dst), a.scale);
+    else if (a.src_dtype == MOE_DTYPE_F16)
+      gather_i8_kernel<__half><<<grid, block, 0, s>>>(
+          static_cast<const __half*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<int8_t*>(a.dst), a.scale);
+    else
+      return fail(MOE_ERR_UNSUPPORTED, "gather: unsupported source dtype");
+  } else {
+    return fail(MOE_ERR_UNSUPPORTED, "gather: unknown quant mode");
+  }
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+int sum_topk_launch(const SumArgs& a, cudaStream_t s) {
+  KSW_REQUIRE(a.part && a.out, MOE_ERR_INVALID_ARG, "sum_topk: null pointer");
+  KSW_REQUIRE(a.H % 8 == 0, MOE_ERR_UNSUPPORTED, "sum_topk: H % 8 != 0");
+  KSW_REQUIRE(a.splits >= 1 && a.top_k >= 1, MOE_ERR_INVALID_ARG, "sum_topk: bad sizes");
+  if (a.T == 0) return MOE_OK;
+  const int64_t total = a.T * (a.H / 8);
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 148 * 32)));
+  const int64_t numel = a.T * a.top_k;
+#define KSW_SUM(TOUT, IDT)                                                             \
+  sum_topk_kernel<TOUT, IDT><<<grid, 256, 0, s>>>(a.part, a.splits, a.T, a.top_k, a.H, \
+                                                   numel, static_cast<const IDT*>(a.ids), \
+                                                   a.E, static_cast<TOUT*>(a.out))
+  const bool i64 = a.ids_dtype == MOE_DTYPE_I64;
+  if (a.out_dtype == MOE_DTYPE_BF16) {
+    if (i64) KSW_SUM(__nv_bfloat16, int64_t); else KSW_SUM(__nv_bfloat16, int32_t);
+  } else if (a.out_dtype == MOE_DTYPE_F16) {
+    if (i64) KSW_SUM(__half, int64_t); else KSW_SUM(__half, int32_t);
+  } else if (a.out_dtype == MOE_DTYPE_F32) {
+    if (i64) KSW_SUM(float, int64_t); else KSW_SUM(float, int32_t);
+  } else {
+    return fail(MOE_ERR_UNSUPPORTED, "sum_topk: unsupported output dtype");
+  }
+#undef KSW_SUM
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+}  // namespace ksw

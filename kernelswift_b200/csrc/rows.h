@@ -1,0 +1,43 @@
+// Launchers of the row-wise kernels (rows.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace ksw {
+
+struct GatherArgs {
+  const void* src;              // [src_rows, H]
+  int src_dtype;                // F32 / F16 / BF16
+  int64_t src_rows;
+  int64_t H;
+  int top_k;                    // source row of operand row m = sorted[m] / top_k;
+                                // 0: source row m itself (valid rows only)
+  const int32_t* sorted;        // [max_rows]; NULL: row m reads source row m (quant only)
+  const int32_t* num_post_pad;  // rows to process (device)
+  int64_t max_rows;
+  int64_t numel;                // sentinel of padding slots
+  int quant;                    // moe_quant_t
+  void* dst;                    // [max_rows, H] dst_dtype / e4m3 / int8
+  int dst_dtype;                // for QUANT_NONE: F16 or BF16
+  float* scale;                 // FP8: [max_rows, ceil(H/128)], INT8: [max_rows]
+};
+
+struct SumArgs {
+  const float* part;            // [splits, T*top_k, H]
+  int splits;
+  int64_t T;
+  int top_k;
+  int64_t H;
+  const void* ids;              // [T*top_k] or NULL (all rows valid)
+  int ids_dtype;
+  int E;
+  void* out;                    // [T, H]
+  int out_dtype;
+};
+
+int gather_launch(const GatherArgs& a, cudaStream_t s);
+int sum_topk_launch(const SumArgs& a, cudaStream_t s);
+
+}  // namespace ksw

@@ -1,0 +1,399 @@
+"""Fused-MoE operator for B200: the host side above the C ABI.
+
+Mirrors the reference operator kernels/track1-triton/fused_moe/base.py:
+  - `ModelNew(num_experts, top_k, hidden_size, intermediate_size, renormalize)`
+    with parameters `w1` [E, 2I, H] and `w2` [E, H, I] (base.py:9-33) and
+    `forward(hidden_states, router_logits)` (base.py:35-76), so that
+    auto_bench.py's v0/v1 comparison loads it unchanged;
+  - the functional pieces of that forward: `fused_topk` (routing,
+    base.py:44-48), `moe_align_block_size` (the per-expert grouping of
+    base.py:64-68) and `fused_experts` (base.py:50-76), which also accepts
+    fp8 block-scaled and int8 per-channel W8A8 weights.
+
+Device memory, streams and routing ops come from PyTorch; every expert
+computation runs in libmoe_b200.so (sm_100a). There is no CPU fallback:
+CPU tensors or a missing library raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+BLOCK_M = 128
+
+_DTYPE_CODE = {
+    torch.float32: _lib.DT_F32,
+    torch.float16: _lib.DT_F16,
+    torch.bfloat16: _lib.DT_BF16,
+    torch.float8_e4m3fn: _lib.DT_E4M3,
+    torch.int8: _lib.DT_I8,
+    torch.int32: _lib.DT_I32,
+    torch.int64: _lib.DT_I64,
+}
+
+_QUANT = {"none": _lib.QUANT_NONE, "fp8": _lib.QUANT_FP8_BLOCK, "int8": _lib.QUANT_INT8_CHANNEL}
+
+
+def _code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _check_cuda(name: str, t: torch.Tensor) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this operator has no CPU path)")
+
+
+def _contig(t: torch.Tensor) -> torch.Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------------------
+# Workspace: one grow-only buffer per (device, stream) so that calls never
+# allocate once warm.
+# ---------------------------------------------------------------------------
+_ws_lock = threading.Lock()
+_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(),
+           torch.cuda.current_stream(device).cuda_stream)
+    with _ws_lock:
+        buf = _ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _ws[key] = buf
+        return buf
+
+
+# ---------------------------------------------------------------------------
+# Routing (base.py:44-48)
+# ---------------------------------------------------------------------------
+
+def fused_topk(hidden_states: torch.Tensor, gating_output: torch.Tensor, topk: int,
+               renormalize: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """softmax(fp32) -> top-k (sorted) -> optional renormalisation.
+
+    Returns (topk_weights fp32 [T, k], topk_ids int64 [T, k]); the same torch
+    ops as base.py:44-47 on the same device, so the ids are bit-identical.
+    """
+    if gating_output.shape[0] != hidden_states.shape[0]:
+        raise ValueError("gating_output and hidden_states disagree on the token count")
+    scores = torch.softmax(gating_output.float(), dim=-1)
+    topk_weights, topk_ids = torch.topk(scores, topk, dim=-1)
+    if renormalize:
+        topk_weights = topk_weights / topk_weights.sum(-1, keepdim=True)
+    return topk_weights, topk_ids
+
+
+# ---------------------------------------------------------------------------
+# moe_align_block_size
+# ---------------------------------------------------------------------------
+
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int
+                         ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Groups flat (token, slot) indices by expert, padded to `block_size`.
+
+    Returns (sorted_token_ids int32 [L], expert_ids int32 [L / block_size],
+    num_tokens_post_pad int32 [1]) with L = moe_align_buffer_len. Within an
+    expert the flat indices ascend (the row order of base.py's
+    `x_rep[flat_ids == e]`); padding slots hold topk_ids.numel(); ids outside
+    [0, num_experts) are dropped.
+    """
+    _check_cuda("topk_ids", topk_ids)
+    ids = _contig(topk_ids)
+    if ids.dtype not in (torch.int32, torch.int64):
+        raise TypeError("topk_ids must be int32 or int64")
+    lib = _lib.load()
+    numel = ids.numel()
+    L = lib.moe_align_buffer_len(numel, num_experts, block_size)
+    if L < 0:
+        raise ValueError("invalid align arguments")
+    ws_bytes = ctypes.c_size_t(0)
+    _lib.check(lib.moe_align_workspace_size(numel, num_experts, block_size,
+                                            ctypes.byref(ws_bytes)), "moe_align_workspace_size")
+    dev = ids.device
+    sorted_ids = torch.empty(L, dtype=torch.int32, device=dev)
+    expert_ids = torch.empty(L // block_size, dtype=torch.int32, device=dev)
+    npp = torch.empty(1, dtype=torch.int32, device=dev)
+    ws = _workspace(dev, ws_bytes.value) if ws_bytes.value else None
+    _lib.call("moe_align_block_size", _ptr(ids), _code(ids), numel, num_experts, block_size,
+              _ptr(sorted_ids), _ptr(expert_ids), _ptr(npp), _ptr(ws), ws_bytes.value,
+              _stream(dev))
+    return sorted_ids, expert_ids, npp
+
+
+# ---------------------------------------------------------------------------
+# Weight preparation (replaces the per-call casts of base.py:60-61)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class PreparedWeights:
+    """Expert weights in the layout and format the grouped GEMMs read."""
+
+    w13: torch.Tensor               # [E, 2I, H], gate/up rows regrouped by 16
+    w2: torch.Tensor                # [E, H, I]
+    w13_scale: torch.Tensor | None  # fp8: [E, 2I/128, H/128]; int8: [E, 2I]
+    w2_scale: torch.Tensor | None   # fp8: [E, H/128, I/128];  int8: [E, H]
+    quant: str                      # "none" | "fp8" | "int8"
+    num_experts: int
+    inter_size: int
+    hidden_size: int
+
+    @property
+    def compute_dtype(self) -> torch.dtype:
+        return self.w13.dtype
+
+
+def prepare_weights(w1: torch.Tensor, w2: torch.Tensor, quant: str = "none",
+                    compute_dtype: torch.dtype = torch.bfloat16,
+                    w1_scale: torch.Tensor | None = None,
+                    w2_scale: torch.Tensor | None = None) -> PreparedWeights:
+    """Casts or quantises w1 [E, 2I, H] and w2 [E, H, I] once.
+
+    quant "none": cast to `compute_dtype` (bf16 or f16). quant "fp8": e4m3
+    with one fp32 scale per 128x128 block (absmax / 448), or pass-through of
+    already-e4m3 weights with `w1_scale`/`w2_scale`. quant "int8": int8 with
+    one scale per output row (absmax / 127).
+    """
+    _check_cuda("w1", w1)
+    _check_cuda("w2", w2)
+    if quant not in _QUANT:
+        raise ValueError(f"quant must be one of {sorted(_QUANT)}")
+    if w1.dim() != 3 or w2.dim() != 3:
+        raise ValueError("w1 must be [E, 2I, H] and w2 [E, H, I]")
+    E, two_i, H = w1.shape
+    if two_i % 2 or w2.shape != (E, H, two_i // 2):
+        raise ValueError(f"w2 shape {tuple(w2.shape)} does not match w1 {tuple(w1.shape)}")
+    inter = two_i // 2
+    w1c, w2c = _contig(w1.detach()), _contig(w2.detach())
+    dev = w1.device
+    q = _QUANT[quant]
+    if quant == "none":
+        if compute_dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("compute_dtype must be bf16 or f16")
+        dst_dtype = compute_dtype
+        s13 = s2 = None
+    elif quant == "fp8":
+        dst_dtype = torch.float8_e4m3fn
+        s13 = torch.empty(E, -(-two_i // 128), -(-H // 128), dtype=torch.float32, device=dev)
+        s2 = torch.empty(E, -(-H // 128), -(-inter // 128), dtype=torch.float32, device=dev)
+    else:
+        dst_dtype = torch.int8
+        s13 = torch.empty(E, two_i, dtype=torch.float32, device=dev)
+        s2 = torch.empty(E, H, dtype=torch.float32, device=dev)
+    if w1c.dtype == torch.float8_e4m3fn and (w1_scale is None or w2_scale is None):
+        raise ValueError("e4m3 weights need w1_scale and w2_scale")
+    o13 = torch.empty(E, two_i, H, dtype=dst_dtype, device=dev)
+    o2 = torch.empty(E, H, inter, dtype=dst_dtype, device=dev)
+    st = _stream(dev)
+    sc1 = _contig(w1_scale.float()) if w1_scale is not None else None
+    sc2 = _contig(w2_scale.float()) if w2_scale is not None else None
+    _lib.call("moe_prepare_w13", _ptr(w1c), _code(w1c), _ptr(sc1), E, inter, H, q, _ptr(o13),
+              _DTYPE_CODE[dst_dtype], _ptr(s13), st)
+    _lib.call("moe_prepare_w2", _ptr(w2c), _code(w2c), _ptr(sc2), E, H, inter, q, _ptr(o2),
+              _DTYPE_CODE[dst_dtype], _ptr(s2), st)
+    return PreparedWeights(o13, o2, s13, s2, quant, E, inter, H)
+
+
+_prep_lock = threading.Lock()
+_prep_cache: dict = {}
+
+
+def _cached_prepare(w1, w2, quant, compute_dtype, w1_scale, w2_scale) -> PreparedWeights:
+    """prepare_weights memoised on the identity and version of the inputs."""
+    key = (w1.data_ptr(), w1._version, tuple(w1.shape), w1.dtype,
+           w2.data_ptr(), w2._version, tuple(w2.shape), w2.dtype, quant, compute_dtype,
+           None if w1_scale is None else (w1_scale.data_ptr(), w1_scale._version),
+           None if w2_scale is None else (w2_scale.data_ptr(), w2_scale._version))
+    with _prep_lock:
+        hit = _prep_cache.get(key)
+    if hit is not None:
+        return hit
+    prep = prepare_weights(w1, w2, quant, compute_dtype, w1_scale, w2_scale)
+    with _prep_lock:
+        if len(_prep_cache) > 8:
+            _prep_cache.clear()
+        _prep_cache[key] = prep
+    return prep
+
+
+# ---------------------------------------------------------------------------
+# fused_experts (base.py:50-76)
+# ---------------------------------------------------------------------------
+
+def _problem(hidden, prep: PreparedWeights, topk_weights, topk_ids, out, status,
+             events_array=None):
+    p = _lib.MoeProblem()
+    p.num_tokens = hidden.shape[0]
+    p.hidden_size = prep.hidden_size
+    p.inter_size = prep.inter_size
+    p.num_experts = prep.num_experts
+    p.top_k = topk_ids.shape[1]
+    p.act_dtype = _code(hidden)
+    p.quant = _QUANT[prep.quant]
+    p.ids_dtype = _code(topk_ids)
+    p.weights_dtype = _code(topk_weights)
+    p.hidden = hidden.data_ptr()
+    p.w13 = prep.w13.data_ptr()
+    p.w2 = prep.w2.data_ptr()
+    p.w13_scale = prep.w13_scale.data_ptr() if prep.w13_scale is not None else None
+    p.w2_scale = prep.w2_scale.data_ptr() if prep.w2_scale is not None else None
+    p.topk_weights = topk_weights.data_ptr()
+    p.topk_ids = topk_ids.data_ptr()
+    p.out = out.data_ptr()
+    p.status = status.data_ptr() if status is not None else None
+    p.stage_events = ctypes.cast(events_array, ctypes.c_void_p) if events_array is not None \
+        else None
+    return p
+
+
+def stage_event_array(events) -> ctypes.Array:
+    """cudaEvent_t[7] for moe_problem_t.stage_events from torch.cuda.Event
+    objects (each must have been recorded once so that it exists)."""
+    if len(events) != len(_lib.STAGES) + 1:
+        raise ValueError(f"need {len(_lib.STAGES) + 1} events")
+    handles = [ev.cuda_event for ev in events]
+    if any(h == 0 for h in handles):
+        raise ValueError("record each event once before passing it")
+    return (ctypes.c_void_p * len(handles))(*handles)
+
+
+def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
+                  topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                  activation: str = "silu", use_fp8_w8a8: bool = False,
+                  use_int8_w8a8: bool = False, w1_scale: torch.Tensor | None = None,
+                  w2_scale: torch.Tensor | None = None, a1_scale: torch.Tensor | None = None,
+                  a2_scale: torch.Tensor | None = None, block_shape: list[int] | None = None,
+                  out: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                  stage_events: ctypes.Array | None = None) -> torch.Tensor:
+    """out[t] = sum_j w[t,j] * W2[e] (silu(W1g[e] x_t) * W1u[e] x_t), e = ids[t,j].
+
+    hidden_states [T, H] (f32/f16/bf16); w1 [E, 2I, H] and w2 [E, H, I] raw
+    (cast or quantised once and cached) or `w1` a PreparedWeights and `w2`
+    None; topk_weights [T, k] (f32/f16/bf16); topk_ids [T, k] (int32/int64).
+    Activations are quantised dynamically in the W8A8 modes (fp8: per token
+    per 128 columns; int8: per token). Returns [T, H] in hidden_states.dtype.
+    """
+    if activation != "silu":
+        raise ValueError(f"unsupported activation {activation!r}; the operator is SiLU-gated")
+    if a1_scale is not None or a2_scale is not None:
+        raise NotImplementedError("static activation scales are not supported; "
+                                  "activations are quantised per token")
+    if use_fp8_w8a8 and use_int8_w8a8:
+        raise ValueError("choose one of use_fp8_w8a8 / use_int8_w8a8")
+    if use_fp8_w8a8 and block_shape is not None and list(block_shape) != [128, 128]:
+        raise ValueError("fp8 W8A8 supports block_shape [128, 128] only")
+    _check_cuda("hidden_states", hidden_states)
+    _check_cuda("topk_weights", topk_weights)
+    _check_cuda("topk_ids", topk_ids)
+    if hidden_states.dim() != 2 or topk_ids.dim() != 2 or topk_weights.shape != topk_ids.shape:
+        raise ValueError("expected hidden_states [T, H], topk_weights/topk_ids [T, k]")
+    if topk_ids.shape[0] != hidden_states.shape[0]:
+        raise ValueError("topk_ids and hidden_states disagree on the token count")
+    quant = "fp8" if use_fp8_w8a8 else ("int8" if use_int8_w8a8 else "none")
+    compute = torch.float16 if hidden_states.dtype == torch.float16 else torch.bfloat16
+    if isinstance(w1, PreparedWeights):
+        prep = w1
+        if prep.quant != quant:
+            raise ValueError(f"prepared weights are {prep.quant!r}, call asked for {quant!r}")
+        if quant == "none" and prep.compute_dtype != compute:
+            raise ValueError("prepared weights dtype does not match the activation dtype")
+    else:
+        _check_cuda("w1", w1)
+        _check_cuda("w2", w2)
+        prep = _cached_prepare(w1, w2, quant, compute, w1_scale, w2_scale)
+    T, H = hidden_states.shape
+    if H != prep.hidden_size:
+        raise ValueError(f"hidden size {H} does not match the weights ({prep.hidden_size})")
+    hidden = _contig(hidden_states)
+    tw = _contig(topk_weights)
+    ti = _contig(topk_ids)
+    if out is None:
+        out = torch.empty_like(hidden)
+    elif out.shape != hidden.shape or out.dtype != hidden.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor like hidden_states")
+    p = _problem(hidden, prep, tw, ti, out, status, stage_events)
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.moe_fused_experts_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)),
+               "moe_fused_experts_workspace_size")
+    ws = _workspace(hidden.device, nbytes.value)
+    _lib.check(lib.moe_fused_experts(ctypes.byref(p), _ptr(ws), ws.numel(),
+                                     _stream(hidden.device)), "moe_fused_experts")
+    return out
+
+
+def fused_moe(hidden_states: torch.Tensor, w1, w2, gating_output: torch.Tensor, topk: int,
+              renormalize: bool = True, **kwargs) -> torch.Tensor:
+    """Routing + experts: the whole of base.py:35-76 as one call."""
+    topk_weights, topk_ids = fused_topk(hidden_states, gating_output, topk, renormalize)
+    return fused_experts(hidden_states, w1, w2, topk_weights.to(hidden_states.dtype), topk_ids,
+                         **kwargs)
+
+
+# ---------------------------------------------------------------------------
+# Drop-in module (base.py:8-76)
+# ---------------------------------------------------------------------------
+
+class ModelNew(nn.Module):
+    """Same constructor, parameters and forward contract as base.py's Model."""
+
+    def __init__(self, num_experts: int, top_k: int, hidden_size: int,
+                 intermediate_size: int, renormalize: bool = True):
+        super().__init__()
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.renormalize = renormalize
+        self.w1 = nn.Parameter(torch.empty(num_experts, 2 * intermediate_size, hidden_size))
+        self.w2 = nn.Parameter(torch.empty(num_experts, hidden_size, intermediate_size))
+        nn.init.normal_(self.w1, std=0.02)
+        nn.init.normal_(self.w2, std=0.02)
+        # not a buffer: load_state_dict(strict=True) must see only w1/w2
+        self._prepared: dict = {}
+
+    def prepared(self, act_dtype: torch.dtype, quant: str = "none") -> PreparedWeights:
+        compute = torch.float16 if act_dtype == torch.float16 else torch.bfloat16
+        key = (quant, compute, self.w1.data_ptr(), self.w1._version, self.w2.data_ptr(),
+               self.w2._version)
+        prep = self._prepared.get(key)
+        if prep is None:
+            self._prepared.clear()
+            prep = prepare_weights(self.w1, self.w2, quant, compute)
+            self._prepared[key] = prep
+        return prep
+
+    def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        self._last_hidden = hidden_states  # for run_out (auto_bench kernel profiling)
+        topk_weights, topk_ids = fused_topk(hidden_states, router_logits, self.top_k,
+                                            self.renormalize)
+        topk_weights = topk_weights.to(hidden_states.dtype)  # base.py:48
+        return fused_experts(hidden_states, self.prepared(hidden_states.dtype), None,
+                             topk_weights, topk_ids)
+
+    def run_out(self, router_logits: torch.Tensor, out: torch.Tensor,
+                hidden_states: torch.Tensor | None = None) -> torch.Tensor:
+        """auto_bench `--profile-mode kernel` hook: forward into `out`."""
+        hidden = hidden_states if hidden_states is not None else self._last_hidden
+        topk_weights, topk_ids = fused_topk(hidden, router_logits, self.top_k, self.renormalize)
+        return fused_experts(hidden, self.prepared(hidden.dtype), None,
+                             topk_weights.to(hidden.dtype), topk_ids, out=out)

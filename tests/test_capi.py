@@ -1,0 +1,89 @@
+"""CPU tests of the C ABI: the library loads, exports every function that
+include/*.h declares, and answers size queries without a GPU."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from kernelswift_b200 import _lib
+from oracle import moe_oracle as orc
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def header_functions():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"^\s*[A-Za-z_][\w\s\*]*?\b(moe_\w+)\s*\(", text, flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_parsed():
+    names = header_functions()
+    assert {"moe_align_block_size", "moe_fused_experts", "moe_gemm_gate_up"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    missing = [n for n in sorted(header_functions()) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    assert header_functions() == set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.moe_abi_version() == 1
+    assert _lib.status_name(_lib.MOE_OK) == "MOE_OK"
+    assert _lib.status_name(_lib.MOE_ERR_TIMEOUT) == "MOE_ERR_TIMEOUT"
+    assert _lib.status_name(12345) == "MOE_ERR_UNKNOWN"
+
+
+@pytest.mark.parametrize("numel,E,bm", [(0, 8, 16), (1, 8, 128), (166, 8, 128),
+                                        (65536, 256, 128), (512, 256, 64)])
+def test_align_buffer_len_matches_oracle(numel, E, bm):
+    assert _lib.load().moe_align_buffer_len(numel, E, bm) == orc.align_buffer_len(numel, E, bm)
+
+
+def test_align_workspace_query_rejects_bad_args():
+    lib = _lib.load()
+    n = ctypes.c_size_t(0)
+    assert lib.moe_align_workspace_size(100, 8, 128, ctypes.byref(n)) == _lib.MOE_OK
+    assert lib.moe_align_workspace_size(100, 0, 128, ctypes.byref(n)) == _lib.MOE_ERR_UNSUPPORTED
+    assert lib.moe_align_workspace_size(100, 8, 100, ctypes.byref(n)) == _lib.MOE_ERR_UNSUPPORTED
+    assert lib.moe_align_workspace_size(10 ** 6, 256, 128, ctypes.byref(n)) == _lib.MOE_OK
+    assert n.value > 0  # the multi-CTA path needs per-chunk histograms
+
+
+def test_fused_workspace_query_without_gpu():
+    lib = _lib.load()
+    p = _lib.MoeProblem()
+    p.num_tokens, p.hidden_size, p.inter_size = 4096, 4096, 14336
+    p.num_experts, p.top_k = 8, 2
+    p.act_dtype, p.quant = _lib.DT_BF16, _lib.QUANT_NONE
+    p.ids_dtype, p.weights_dtype = _lib.DT_I64, _lib.DT_BF16
+    n = ctypes.c_size_t(0)
+    assert lib.moe_fused_experts_workspace_size(ctypes.byref(p), ctypes.byref(n)) == _lib.MOE_OK
+    L = orc.align_buffer_len(4096 * 2, 8, 128)
+    assert n.value >= L * 4096 * 2 + L * 14336 * 2
+    p.hidden_size = 100  # not a multiple of 64
+    assert lib.moe_fused_experts_workspace_size(ctypes.byref(p), ctypes.byref(n)) \
+        == _lib.MOE_ERR_UNSUPPORTED
+    assert "hidden_size" in lib.moe_last_error().decode()
+
+
+def test_compute_entry_points_fail_cleanly_without_gpu():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    lib = _lib.load()
+    st = lib.moe_align_block_size(None, _lib.DT_I32, 0, 8, 128, None, None, None, None, 0, None)
+    assert st in (_lib.MOE_ERR_CUDA, _lib.MOE_ERR_DEVICE)
+    with pytest.raises(_lib.MoeError):
+        _lib.call("moe_selftest_wait_timeout", None, 10, None)
