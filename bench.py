@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (0 = workload default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--heat-seconds", type=float, default=1.0,
+                    help="untimed busy period before timing, so clock samples see a loaded GPU")
     return ap.parse_args()
 
 
@@ -90,7 +92,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -162,9 +164,9 @@ def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1
 
 
 def cpu_sample_tokens(H, I, E):
-    # keep one CPU call around a second or two: bigger layers get fewer tokens
+    # about 3 s per CPU call on a 16-core host: bigger layers get fewer tokens
     per_token = 6 * H * I * 2
-    return int(max(16, min(512, 2e10 / per_token)))
+    return int(max(32, min(4096, 5e11 / per_token)))
 
 
 def run_reference(args, H, I, E, k, quant, T, bias, rank):
@@ -255,6 +257,13 @@ def main():
     torch.cuda.synchronize()
 
     K = args.steps
+    clocks = ClockSampler(local_rank).__enter__()
+    # keep the GPU busy for a second before timing so that the clock samples
+    # cover a loaded GPU (these steps are untimed warm-up)
+    t_heat = time.perf_counter()
+    while time.perf_counter() - t_heat < args.heat_seconds:
+        step()
+        torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     stage_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(_lib.STAGES) + 1)]
@@ -268,15 +277,15 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clocks:
-        wall0 = time.perf_counter()
-        for i in range(K):
-            flush.zero_()
-            starts[i].record()
-            step(stage_arrs[i])
-            ends[i].record()
-        torch.cuda.synchronize()
-        wall = time.perf_counter() - wall0
+    wall0 = time.perf_counter()
+    for i in range(K):
+        flush.zero_()
+        starts[i].record()
+        step(stage_arrs[i])
+        ends[i].record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    clocks.__exit__(None, None, None)
     if world > 1:
         dist.barrier()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]

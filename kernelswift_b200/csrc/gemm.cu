@@ -59,6 +59,11 @@ struct KParams {
   int32_t numel;
   int32_t num_experts;
   int32_t row_weights_dtype;
+  // FP8 block scales: a_scale [rows, sa_ld], b_scale [E, sb_rb, sb_kb]
+  int32_t sa_ld;
+  int32_t sb_rb;
+  int32_t sb_kb;
+  int32_t up_offset;        // gate-up: original row of the first up row (= I)
   uint64_t wait_limit_ns;
 };
 
@@ -361,6 +366,254 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && *abort_flag) report_status(p.status, MOE_ERR_TIMEOUT);
 }
 
+
+// ---------------------------------------------------------------------------
+// FP8 (e4m3) block-scaled variant.
+//
+// The scales change every 128 elements of K (per token for A, per 128x128
+// block for B), so the products of one k-block cannot be summed in TMEM
+// across k-blocks. Each k-block is accumulated into a fresh TMEM buffer
+// (two buffers, so the MMAs of k-block kb+1 overlap the promotion of kb) and
+// eight epilogue warps promote it into fp32 registers:
+//   acc[m, n] += a_scale[m, kb] * b_scale[e, n / 128, kb] * P_kb[m, n]
+// Warp w (2..9) owns TMEM lane quarter w % 4 and column half (w - 2) / 4.
+// After the last k-block the gate-up epilogue applies SiLU(gate)*up and
+// writes bf16 activations; the down epilogue scales by the top-k weight and
+// writes fp32 rows.
+// ---------------------------------------------------------------------------
+constexpr int kThreadsF8 = 320;
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreadsF8, 1)
+    moe_grouped_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA,
+                                const __grid_constant__ CUtensorMap tmB,
+                                const KParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::kStages;
+  constexpr uint32_t IDESC = make_idesc(1u, 0u, BM, BN);  // f32 <- e4m3 x e4m3
+  constexpr int HALF = BN / 2;
+  constexpr int CH = 32;  // columns per TMEM read chunk
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kBBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* final_bar = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 256);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_mb = min(__ldg(p.num_post_pad) / BM, p.max_m_blocks);
+  const int n_tiles = p.n_total / BN;
+  const int total_tiles = num_mb * n_tiles * p.splits;
+  const uint64_t limit = p.wait_limit_ns;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      const int kb0 = c.ks * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+      const int a_row = c.mb * BM;
+      const int b_row = e * p.n_total + c.nt * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+        tma_load_2d(sA + stage * kABytes, &tmA, kb * kKBytes, a_row, &full[stage]);
+        tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kb * kKBytes, b_row, &full[stage]);
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    for (int s = 0; s < STAGES; ++s) {
+      const uint32_t n_s = issued / STAGES + (uint32_t(s) < issued % STAGES ? 1u : 0u);
+      if (n_s == 0) continue;
+      volatile int no_abort = 0;
+      mbar_wait_bounded(&full[s], (n_s - 1) & 1u, &no_abort, limit);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer: one TMEM buffer per k-block ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int pb = 0;
+    uint32_t pphase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      const int kb0 = c.ks * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(&tempty[pb], pphase ^ 1u, abort_flag, limit) ||
+            !mbar_wait_bounded(&full[stage], phase, abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(pb * BN);
+        const uint32_t a0 = smem_u32(sA + stage * kABytes);
+        const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma<kKindF8>(d_tmem, make_sw128_desc(a0 + kk * 32), make_sw128_desc(b0 + kk * 32),
+                          IDESC, kk > 0 ? 1u : 0u);
+        tc_commit(&empty[stage]);
+        tc_commit(&tfull[pb]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        pb ^= 1;
+        if (pb == 0) pphase ^= 1u;
+      }
+    }
+    tc_commit(final_bar);
+    volatile int no_abort = 0;
+    mbar_wait_bounded(final_bar, 0, &no_abort, limit);
+  } else if (warp >= 2) {
+    // ---------------- promotion + epilogue (8 warps) ----------------
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const int col0 = h * HALF;
+    int pb = 0;
+    uint32_t pphase = 0;
+    bool aborted = false;
+    for (int t = blockIdx.x; !aborted && t < total_tiles; t += gridDim.x) {
+      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      const int kb0 = c.ks * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+      const int m = c.mb * BM + row;
+      const int r = __ldg(p.sorted_ids + m);
+      const bool valid = r < p.numel;
+      const int n0 = c.nt * BN + col0;  // first output column of this half
+      int rb0, rb1;
+      if constexpr (EPI == kEpiSwiGLU) {
+        rb0 = (16 * (n0 / 32)) / 128;                 // gate rows' block
+        rb1 = (p.up_offset + 16 * (n0 / 32)) / 128;   // up rows' block
+      } else {
+        rb0 = n0 / 128;
+        rb1 = rb0;
+      }
+      const float* sb0 = p.b_scale + (int64_t(e) * p.sb_rb + rb0) * p.sb_kb;
+      const float* sb1 = p.b_scale + (int64_t(e) * p.sb_rb + rb1) * p.sb_kb;
+      const float* sap = p.a_scale + int64_t(m) * p.sa_ld;
+      float acc[HALF];
+#pragma unroll
+      for (int j = 0; j < HALF; ++j) acc[j] = 0.0f;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const bool ok = mbar_wait_bounded(&tfull[pb], pphase, abort_flag, limit);
+        if (!__all_sync(0xffffffffu, ok)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        const float sa = valid ? __ldg(sap + kb) : 0.0f;
+        const float s0 = sa * __ldg(sb0 + kb);
+        const float s1 = sa * __ldg(sb1 + kb);
+        const uint32_t tbase =
+            tmem_base + (uint32_t(q * 32) << 16) + uint32_t(pb * BN + col0);
+#pragma unroll
+        for (int ch = 0; ch < HALF / CH; ++ch) {
+          uint32_t v[CH];
+          tmem_ld16(tbase + ch * CH, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+          tmem_ld16(tbase + ch * CH + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            // a 32-column group holds 16 gate columns then 16 up columns
+            const float sc = (EPI == kEpiSwiGLU && j >= 16) ? s1 : s0;
+            acc[ch * CH + j] = fmaf(sc, __uint_as_float(v[j]), acc[ch * CH + j]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[pb]);
+        pb ^= 1;
+        if (pb == 0) pphase ^= 1u;
+      }
+      if (aborted || !valid) continue;
+      if constexpr (EPI == kEpiSwiGLU) {
+        __nv_bfloat16* out_row =
+            static_cast<__nv_bfloat16*>(p.out) + int64_t(m) * p.out_ld + n0 / 2;
+#pragma unroll
+        for (int gi = 0; gi < HALF / 32; ++gi) {
+          uint32_t packed[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            packed[j] = pack2<__nv_bfloat16>(
+                silu_mul(acc[gi * 32 + 2 * j], acc[gi * 32 + 16 + 2 * j]),
+                silu_mul(acc[gi * 32 + 2 * j + 1], acc[gi * 32 + 16 + 2 * j + 1]));
+          uint4* dst = reinterpret_cast<uint4*>(out_row + gi * 16);
+          dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        }
+      } else {
+        const float w = load_weight(p.row_weights, p.row_weights_dtype, r);
+        float* out_row =
+            static_cast<float*>(p.out) + (int64_t(c.ks) * p.numel + r) * p.out_ld + n0;
+#pragma unroll
+        for (int j = 0; j < HALF; j += 4)
+          *reinterpret_cast<float4*>(out_row + j) =
+              make_float4(w * acc[j], w * acc[j + 1], w * acc[j + 2], w * acc[j + 3]);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) report_status(p.status, MOE_ERR_TIMEOUT);
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -379,6 +632,28 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
   return MOE_OK;
 }
 
+template <int BN, int EPI>
+int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+               cudaStream_t s) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = moe_grouped_gemm_fp8_kernel<BN, EPI>;
+  KSW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(Cfg::kSmemBytes)));
+  kern<<<grid, kThreadsF8, Cfg::kSmemBytes, s>>>(ta, tb, kp);
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+template <int EPI>
+int dispatch_fp8(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
+                 int grid, cudaStream_t s) {
+  switch (bn) {
+    case 256: return launch_fp8<256, EPI>(ta, tb, kp, grid, s);
+    case 128: return launch_fp8<128, EPI>(ta, tb, kp, grid, s);
+    default: return fail(MOE_ERR_UNSUPPORTED, "fp8 GEMM: block_n must be 128 or 256");
+  }
+}
+
 template <int KIND, int AB_FMT, int EPI, typename TOUT>
 int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
                 const KParams& kp, int grid, cudaStream_t s) {
@@ -392,10 +667,12 @@ int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
 
 // Picks the N tile: the largest of 256/128/64 dividing n that still gives
 // every SM about two tiles, given an upper bound on the m-blocks.
-int pick_block_n(int64_t n, int64_t est_m_blocks, int64_t splits, int sms) {
+int pick_block_n(int64_t n, int64_t est_m_blocks, int64_t splits, int sms,
+                 bool allow64 = true) {
   const int cands[3] = {256, 128, 64};
   int best = 0;
   for (int bn : cands) {
+    if (bn == 64 && !allow64) break;
     if (n % bn != 0) continue;
     if (best == 0) best = bn;
     if (est_m_blocks * (n / bn) * splits >= 2 * int64_t(sms)) return bn;
@@ -432,9 +709,9 @@ int operand_types(const GroupedGemmArgs& a, OperandTypes* ot) {
     ot->elem_bytes = 2;
     return MOE_OK;
   }
-  if (a.quant == MOE_QUANT_INT8_CHANNEL) {
+  if (a.quant == MOE_QUANT_INT8_CHANNEL || a.quant == MOE_QUANT_FP8_BLOCK) {
     KSW_REQUIRE(a.a_scale && a.b_scale, MOE_ERR_INVALID_ARG,
-                "int8 GEMM needs activation and weight scales");
+                "W8A8 GEMM needs activation and weight scales");
     ot->tma_type = CU_TENSOR_MAP_DATA_TYPE_UINT8;
     ot->elem_bytes = 1;
     return MOE_OK;
@@ -471,6 +748,10 @@ KParams base_params(const GroupedGemmArgs& a, int elem_bytes) {
   kp.numel = int32_t(a.numel);
   kp.num_experts = a.num_experts;
   kp.row_weights_dtype = a.row_weights_dtype;
+  kp.sa_ld = int32_t(ceil_div(a.k, 128));
+  kp.sb_rb = int32_t(ceil_div(a.n, 128));
+  kp.sb_kb = int32_t(ceil_div(a.k, 128));
+  kp.up_offset = int32_t(a.n / 2);
   kp.wait_limit_ns = kWaitLimitNs;
   return kp;
 }
@@ -497,7 +778,11 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   if (st != MOE_OK) return st;
   KSW_REQUIRE((a.k * ot.elem_bytes) % 16 == 0, MOE_ERR_UNSUPPORTED,
               "gate-up GEMM: hidden size * element size must be a multiple of 16 B");
-  const int bn = a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), 1, sms);
+  const bool fp8 = a.quant == MOE_QUANT_FP8_BLOCK;
+  if (fp8)
+    KSW_REQUIRE(a.n % 256 == 0, MOE_ERR_UNSUPPORTED,
+                "fp8 gate-up GEMM: I must be a multiple of 128");
+  const int bn = a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), 1, sms, !fp8);
   KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED,
               "gate-up GEMM: 2*I must be a multiple of 64");
   CUtensorMap ta, tb;
@@ -506,6 +791,7 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   KParams kp = base_params(a, ot.elem_bytes);
   kp.out_ld = a.n / 2;
   const int grid = sms;
+  if (fp8) return dispatch_fp8<kEpiSwiGLU>(bn, ta, tb, kp, grid, s);
   if (a.quant == MOE_QUANT_INT8_CHANNEL) {
     // int8 products dequantise to bf16 activations
     return dispatch_bn<kKindI8, 1, kEpiSwiGLU, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
@@ -542,13 +828,19 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   kp.splits = int(ceil_div(kp.k_blocks, kb_per));
   KSW_REQUIRE(kp.splits == a.splits, MOE_ERR_INVALID_ARG,
               "down GEMM: splits leaves an empty K range; choose splits so that every split has k-blocks");
-  const int bn = a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms);
+  const bool fp8 = a.quant == MOE_QUANT_FP8_BLOCK;
+  if (fp8)
+    KSW_REQUIRE(a.n % 128 == 0, MOE_ERR_UNSUPPORTED,
+                "fp8 down GEMM: hidden size must be a multiple of 128");
+  const int bn =
+      a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms, !fp8);
   KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED, "down GEMM: bad block_n");
   CUtensorMap ta, tb;
   st = make_maps(a, ot, bn, &ta, &tb);
   if (st != MOE_OK) return st;
   kp.out_ld = a.n;
   const int grid = sms;
+  if (fp8) return dispatch_fp8<kEpiRows>(bn, ta, tb, kp, grid, s);
   if (a.quant == MOE_QUANT_INT8_CHANNEL)
     return dispatch_bn<kKindI8, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s);
   if (a.compute_dtype == MOE_DTYPE_BF16)

@@ -97,7 +97,11 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
     P.act_dtype = MOE_DTYPE_BF16;
     kbpe = 1;
   } else if (P.quant == MOE_QUANT_FP8_BLOCK) {
-    return fail(MOE_ERR_UNSUPPORTED, "fp8 block-scaled path not available in this build");
+    KSW_REQUIRE(P.I % 128 == 0 && P.H % 128 == 0, MOE_ERR_UNSUPPORTED,
+                "fp8 block-scaled path needs hidden and intermediate sizes divisible by 128");
+    P.a_dtype = MOE_DTYPE_E4M3;
+    P.act_dtype = MOE_DTYPE_BF16;
+    kbpe = 1;
   } else {
     return fail(MOE_ERR_INVALID_ARG, "unknown quant mode");
   }
@@ -115,10 +119,16 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.off_npp = take(4);
   P.off_align = take(P.align_ws);
   P.off_a = take(size_t(P.L) * P.H * elem_bytes(P.a_dtype));
-  P.off_a_scale = take(P.quant == MOE_QUANT_INT8_CHANNEL ? size_t(P.L) * 4 : 0);
+  // per-row scales: int8 one per row, fp8 one per row per 128 columns
+  auto scale_bytes = [&](int64_t cols) -> size_t {
+    if (P.quant == MOE_QUANT_INT8_CHANNEL) return size_t(P.L) * 4;
+    if (P.quant == MOE_QUANT_FP8_BLOCK) return size_t(P.L) * size_t(ceil_div(cols, 128)) * 4;
+    return 0;
+  };
+  P.off_a_scale = take(scale_bytes(P.H));
   P.off_act = take(size_t(P.L) * P.I * elem_bytes(P.act_dtype));
-  P.off_act_q = take(P.quant == MOE_QUANT_INT8_CHANNEL ? size_t(P.L) * P.I : 0);
-  P.off_act_scale = take(P.quant == MOE_QUANT_INT8_CHANNEL ? size_t(P.L) * 4 : 0);
+  P.off_act_q = take(P.quant != MOE_QUANT_NONE ? size_t(P.L) * P.I : 0);
+  P.off_act_scale = take(scale_bytes(P.I));
   P.off_part = take(size_t(P.splits) * P.numel * P.H * 4);
   P.total = off;
   return MOE_OK;
@@ -158,8 +168,8 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   if (st != MOE_OK) return st;
   KSW_REQUIRE(workspace != nullptr && workspace_bytes >= P.total, MOE_ERR_WORKSPACE,
               "moe_fused_experts: workspace smaller than moe_fused_experts_workspace_size");
-  KSW_REQUIRE(p->out != nullptr, MOE_ERR_INVALID_ARG, "null out");
   if (P.T == 0) return MOE_OK;
+  KSW_REQUIRE(p->out != nullptr, MOE_ERR_INVALID_ARG, "null out");
   KSW_REQUIRE(p->hidden && p->w13 && p->w2 && p->topk_weights && p->topk_ids,
               MOE_ERR_INVALID_ARG, "null input pointer");
   if (P.quant != MOE_QUANT_NONE)

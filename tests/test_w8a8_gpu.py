@@ -1,0 +1,86 @@
+"""GPU: fp8 block-scaled and int8 per-channel W8A8 paths against the fp32
+dequantised oracle (relative L2 <= 5e-2)."""
+import pytest
+import torch
+
+from kernelswift_b200 import fused_moe as fm
+from oracle import moe_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 5e-2
+
+
+def problem(T, H, I, E, k, seed, bias=0.0, device="cuda"):
+    g = torch.Generator().manual_seed(seed)
+    hidden = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g)
+    if bias:
+        logits = logits + torch.randn(E, generator=g) * bias
+    w, ids = orc.route(logits, k)
+    gd = torch.Generator(device=device).manual_seed(seed)
+    w1 = torch.randn(E, 2 * I, H, generator=gd, device=device) / H ** 0.5
+    w2 = torch.randn(E, H, I, generator=gd, device=device) / I ** 0.5
+    return hidden.to(device), w1, w2, w, ids
+
+
+def oracle_quant(kind, hidden, w1, w2, w, ids, tokens):
+    sub = ids[tokens]
+    hit = torch.unique(sub)
+    remap = torch.full((w1.shape[0],), -1, dtype=torch.int64)
+    remap[hit] = torch.arange(hit.numel())
+    f = orc.fused_experts_fp8 if kind == "fp8" else orc.fused_experts_int8
+    return f(hidden[tokens].cpu(), w1[hit.to(w1.device)].cpu(), w2[hit.to(w2.device)].cpu(),
+             w[tokens], remap[sub])
+
+
+FP8_SHAPES = [
+    # name, T, H, I, E, k, tokens checked
+    ("small", 50, 256, 256, 16, 4, 50),
+    ("tail_blocks", 129, 384, 128, 8, 2, 129),
+    ("dsv3_T64", 64, 7168, 2048, 256, 8, 4),
+    ("dsv3_T4096", 4096, 7168, 2048, 256, 8, 4),
+]
+
+
+@pytest.mark.parametrize("name,T,H,I,E,k,n_check", FP8_SHAPES, ids=[s[0] for s in FP8_SHAPES])
+def test_fp8_block_w8a8(cuda_device, name, T, H, I, E, k, n_check):
+    hidden, w1, w2, w, ids = problem(T, H, I, E, k, seed=T + H)
+    out = fm.fused_experts(hidden, w1, w2, w.to(cuda_device), ids.to(cuda_device),
+                           use_fp8_w8a8=True, block_shape=[128, 128])
+    torch.cuda.synchronize()
+    tokens = torch.randperm(T, generator=torch.Generator().manual_seed(0))[:n_check]
+    ref = oracle_quant("fp8", hidden, w1, w2, w, ids, tokens)
+    assert orc.rel_l2(out.cpu()[tokens], ref) <= REL_L2
+
+
+INT8_SHAPES = [
+    ("small", 50, 256, 256, 16, 4, 50),
+    ("qwen3_T64", 64, 2048, 768, 128, 8, 16),
+    ("qwen3_T1024", 1024, 2048, 768, 128, 8, 16),
+]
+
+
+@pytest.mark.parametrize("name,T,H,I,E,k,n_check", INT8_SHAPES, ids=[s[0] for s in INT8_SHAPES])
+def test_int8_channel_w8a8(cuda_device, name, T, H, I, E, k, n_check):
+    hidden, w1, w2, w, ids = problem(T, H, I, E, k, seed=T + 7, bias=0.5)
+    out = fm.fused_experts(hidden, w1, w2, w.to(cuda_device), ids.to(cuda_device),
+                           use_int8_w8a8=True)
+    torch.cuda.synchronize()
+    tokens = torch.randperm(T, generator=torch.Generator().manual_seed(0))[:n_check]
+    ref = oracle_quant("int8", hidden, w1, w2, w, ids, tokens)
+    assert orc.rel_l2(out.cpu()[tokens], ref) <= REL_L2
+
+
+def test_fp8_prequantised_weights_pass_through(cuda_device):
+    """Already-e4m3 weights with their block scales give the same result as
+    quantising the fp32 weights inside prepare_weights."""
+    hidden, w1, w2, w, ids = problem(40, 256, 256, 8, 2, seed=3)
+    q1, s1 = orc.quant_fp8_block(w1.cpu())
+    q2, s2 = orc.quant_fp8_block(w2.cpu())
+    a = fm.fused_experts(hidden, w1, w2, w.to(cuda_device), ids.to(cuda_device),
+                         use_fp8_w8a8=True).clone()
+    b = fm.fused_experts(hidden, q1.to(cuda_device), q2.to(cuda_device), w.to(cuda_device),
+                         ids.to(cuda_device), use_fp8_w8a8=True, w1_scale=s1.to(cuda_device),
+                         w2_scale=s2.to(cuda_device))
+    assert torch.equal(a, b)
