@@ -163,17 +163,19 @@ def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1
     return sample_tokens / med, med, torch.get_num_threads()
 
 
-def cpu_sample_tokens(H, I, E):
-    # about 3 s per CPU call on a 16-core host: bigger layers get fewer tokens
-    per_token = 6 * H * I * 2
-    return int(max(32, min(4096, 5e11 / per_token)))
+def cpu_sample_tokens(H, I, E, k, T, bias, target_s=3.0):
+    """Tokens per CPU call so that one call of the reference path takes about
+    `target_s` seconds on this host (at most the GPU batch T)."""
+    probe = min(T, 256)
+    rate, _, _ = cpu_reference_rate(H, I, E, k, "none", bias, probe, repeats=1, warmup=0)
+    return int(max(16, min(T, rate * target_s)))
 
 
 def run_reference(args, H, I, E, k, quant, T, bias, rank):
     """--impl reference: the reference's CPU torch path, rank 0 only."""
     if rank != 0:
         return
-    sample = cpu_sample_tokens(H, I, E)
+    sample = cpu_sample_tokens(H, I, E, k, T, bias)
     rate, med, cores = cpu_reference_rate(H, I, E, k, quant, bias, sample,
                                           repeats=max(1, args.steps), warmup=max(0, args.warmup))
     line = {
@@ -197,7 +199,8 @@ def workload_config(name, H, I, E, k, quant, T, n):
                         f"{'bf16' if quant == 'none' else quant + ' W8A8'}, {T} tokens/GPU",
             "hidden": H, "intermediate": I, "experts": E, "top_k": k, "quant": quant,
             "tokens_per_gpu": T, "global_tokens": T * n,
-            "parallelism": "replicas" if n > 1 else "single",
+            "parallelism": f"ep{n} (E/{n} experts per GPU, NCCL all_to_all)" if n > 1
+            else "single",
             "l2": f"flushed between steps ({L2_FLUSH_BYTES >> 20} MB write) outside the "
                   "timed windows; weights also exceed L2"}
 
@@ -239,18 +242,38 @@ def main():
     logits = torch.randn(T, E, generator=g, device=dev)
     if bias:
         logits = logits + torch.randn(E, generator=g, device=dev) * bias
-    model = fm.ModelNew(E, k, H, I).to(dev)
-    with torch.no_grad():
-        model.w1.normal_(0.0, 1.0 / math.sqrt(H), generator=g)
-        model.w2.normal_(0.0, 1.0 / math.sqrt(I), generator=g)
-    prep = model.prepared(torch.bfloat16, quant)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    rows_per_launch = [T * k]  # routed rows the local gate-up GEMM saw (last step)
+    if world == 1:
+        # the drop-in module: fp32 master weights as in base.py, prepared once
+        model = fm.ModelNew(E, k, H, I).to(dev)
+        with torch.no_grad():
+            model.w1.normal_(0.0, 1.0 / math.sqrt(H), generator=g)
+            model.w2.normal_(0.0, 1.0 / math.sqrt(I), generator=g)
+        prep = model.prepared(torch.bfloat16, quant)
 
-    def step(stage_arr=None):
-        tw, ti = fm.fused_topk(hidden, logits, k)
-        return fm.fused_experts(hidden, prep, None, tw.to(hidden.dtype), ti,
-                                use_fp8_w8a8=quant == "fp8", use_int8_w8a8=quant == "int8",
-                                stage_events=stage_arr)
+        def step(stage_arr=None):
+            tw, ti = fm.fused_topk(hidden, logits, k)
+            return fm.fused_experts(hidden, prep, None, tw.to(hidden.dtype), ti,
+                                    use_fp8_w8a8=quant == "fp8", use_int8_w8a8=quant == "int8",
+                                    stage_events=stage_arr)
+    else:
+        # expert parallel: this rank holds E/world experts, routes its own T
+        # tokens over all E, exchanges rows with NCCL all_to_all
+        from kernelswift_b200.ep import ExpertParallelMoE
+
+        if E % world:
+            raise SystemExit(f"{E} experts do not shard over {world} GPUs")
+        el = E // world
+        w1 = torch.randn(el, 2 * I, H, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(H)
+        w2 = torch.randn(el, H, I, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(I)
+        ep = ExpertParallelMoE(w1, w2, E, k, quant=quant)
+        del w1, w2
+
+        def step(stage_arr=None):
+            tw, ti = fm.fused_topk(hidden, logits, k)
+            out = ep(hidden, tw.to(hidden.dtype), ti, stage_events=stage_arr)
+            rows_per_launch[0] = ep.last_rows_received
+            return out
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -308,10 +331,13 @@ def main():
         out_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
         h_dev = torch.empty_like(hidden)
         l_dev = torch.empty_like(logits)
-        model_call = model
-        if quant != "none":
+        if world == 1 and quant == "none":
+            model_call = model
+        else:
             def model_call(hd, ld):
                 tw, ti = fm.fused_topk(hd, ld, k)
+                if world > 1:
+                    return ep(hd, tw.to(hd.dtype), ti)
                 return fm.fused_experts(hd, prep, None, tw.to(hd.dtype), ti,
                                         use_fp8_w8a8=quant == "fp8",
                                         use_int8_w8a8=quant == "int8")
@@ -345,12 +371,15 @@ def main():
                "h2d_bytes_per_step": hidden.numel() * hidden.element_size()
                + logits.numel() * logits.element_size(),
                "d2h_bytes_per_step": T * H * 2,
-               "path": "ModelNew.forward (drop-in module), pinned host buffers"}
+               "path": ("ModelNew.forward (drop-in module)" if world == 1 and quant == "none"
+                        else "fused_topk + " + ("ExpertParallelMoE.forward" if world > 1
+                                                else "fused_experts"))
+               + ", pinned host buffers"}
 
     # ---- roofline of the dominant kernel (gate-up GEMM) ----
     peaks, peak_src = load_peaks()
     gu_ms = stage_ms["gate_up"]
-    gu_flops = 4 * H * I * T * k
+    gu_flops = 4 * H * I * rows_per_launch[0]
     if quant == "none":
         peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
         peak_note = f"bf16 dense, sustained, {peak_src}"
@@ -362,17 +391,19 @@ def main():
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
         try:
-            traffic = json.loads(tfile.read_text()).get(f"{args.workload}:{T}:gate_up")
+            entry = json.loads(tfile.read_text()).get(f"{args.workload}:{T}:gate_up")
+            traffic = entry["bytes"] if entry and world == 1 else None
         except Exception:
             traffic = None
     roofline = {"kernel": "moe_grouped_gemm_kernel (gate-up, SiLU fused)", "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": peak_note, "traffic": traffic,
+                "traffic_unit": "DRAM bytes per launch (ncu capture, profiles/)",
                 "algorithmic": f"4*H*I*T*k = {gu_flops:.4g} FLOP per launch"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sample = cpu_sample_tokens(H, I, E)
+        sample = cpu_sample_tokens(H, I, E, k, T, bias)
         rate, med, cores = cpu_reference_rate(H, I, E, k, quant, bias, sample, repeats=3)
         cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{sample} tokens of the same layer, base.py forward restated in "
@@ -380,8 +411,10 @@ def main():
 
     # our kernels per step: align (1 launch up to 8192 routed rows, else 3),
     # gather, gate-up, [activation quant], down, top-k sum
-    numel = T * k
+    numel = rows_per_launch[0]
     launches_per_step = (1 if numel <= 8192 else 3) + 4 + (0 if quant == "none" else 1)
+    if world > 1:
+        launches_per_step += 2  # pack rows by destination, weighted combine
     if rank == 0:
         line = {
             "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,

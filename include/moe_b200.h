@@ -281,6 +281,20 @@ int moe_sum_topk(const float* partial, int splits, int64_t num_tokens,
                  int ids_dtype, int num_experts, void* out, int out_dtype,
                  void* stream);
 
+/*
+ * Expert-parallel combine on the token's own rank: rows[inv_index[r]] is the
+ * expert output for flat slot r = t*top_k + j (computed on whichever rank
+ * holds that expert and sent back);
+ *   out[t, :] = sum_j weights[r] * rows[inv_index[r], :]   (j ascending, fp32)
+ * Slots with inv_index < 0 contribute nothing. rows and out share a dtype
+ * (F32/F16/BF16). The weighted top-k reduction of base.py:75-76 for rows
+ * that were not computed locally.
+ */
+int moe_combine_rows(const void* rows, int rows_dtype, const int32_t* inv_index,
+                     const void* weights, int weights_dtype, int64_t num_tokens,
+                     int top_k, int64_t hidden_size, void* out, int out_dtype,
+                     void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Self-test of the bounded device waits (failure detection without a GPU   */
 /* fault): launches one CTA whose mbarrier wait is never satisfied, with a   */

@@ -392,4 +392,23 @@ int moe_sum_topk(const float* partial, int splits, int64_t num_tokens, int top_k
   return sum_topk_launch(sa, static_cast<cudaStream_t>(stream));
 }
 
+int moe_combine_rows(const void* rows, int rows_dtype, const int32_t* inv_index,
+                     const void* weights, int weights_dtype, int64_t num_tokens, int top_k,
+                     int64_t hidden_size, void* out, int out_dtype, void* stream) {
+  int st = check_device(nullptr);
+  if (st != MOE_OK) return st;
+  CombineArgs c{};
+  c.rows = rows;
+  c.rows_dtype = rows_dtype;
+  c.inv = inv_index;
+  c.weights = weights;
+  c.weights_dtype = weights_dtype;
+  c.T = num_tokens;
+  c.top_k = top_k;
+  c.H = hidden_size;
+  c.out = out;
+  c.out_dtype = out_dtype;
+  return combine_launch(c, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -236,6 +236,33 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ---------------- combine rows computed elsewhere ----------------
+template <typename Tin, typename Tw, typename Tout>
+__global__ void __launch_bounds__(256)
+    combine_rows_kernel(const Tin* __restrict__ rows, const int32_t* __restrict__ inv,
+                        const Tw* __restrict__ w, int64_t T, int top_k, int64_t H,
+                        Tout* __restrict__ out) {
+  const int64_t vec_per_row = H / 8;
+  const int64_t total = T * vec_per_row;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec_per_row;
+    const int64_t h = (i - t * vec_per_row) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < top_k; ++j) {
+      const int64_t r = t * top_k + j;
+      const int src = __ldg(inv + r);
+      if (src < 0) continue;
+      const float wj = to_f32(w[r]);
+      float v[8];
+      load8(rows + int64_t(src) * H + h, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = fmaf(wj, v[q], acc[q]);
+    }
+    store8(out + t * H + h, acc);
+  }
+}
+
 int grid_for_rows(int64_t rows) {
   return int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, kWarps), 148 * 16)));
 }
@@ -336,6 +363,39 @@ int sum_topk_launch(const SumArgs& a, cudaStream_t s) {
     return fail(MOE_ERR_UNSUPPORTED, "sum_topk: unsupported output dtype");
   }
 #undef KSW_SUM
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+int combine_launch(const CombineArgs& a, cudaStream_t s) {
+  KSW_REQUIRE(a.inv && a.weights && a.out && (a.rows || a.T == 0), MOE_ERR_INVALID_ARG,
+              "combine: null pointer");
+  KSW_REQUIRE(a.H % 8 == 0 && a.top_k >= 1, MOE_ERR_UNSUPPORTED, "combine: bad sizes");
+  if (a.T == 0) return MOE_OK;
+  const int64_t total = a.T * (a.H / 8);
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 148 * 32)));
+#define KSW_COMB(TIN, TW, TOUT)                                                         \
+  combine_rows_kernel<TIN, TW, TOUT><<<grid, 256, 0, s>>>(                              \
+      static_cast<const TIN*>(a.rows), a.inv, static_cast<const TW*>(a.weights), a.T,   \
+      a.top_k, a.H, static_cast<TOUT*>(a.out))
+#define KSW_COMB_W(TIN, TOUT)                                                           \
+  if (a.weights_dtype == MOE_DTYPE_F32) KSW_COMB(TIN, float, TOUT);                     \
+  else if (a.weights_dtype == MOE_DTYPE_BF16) KSW_COMB(TIN, __nv_bfloat16, TOUT);       \
+  else if (a.weights_dtype == MOE_DTYPE_F16) KSW_COMB(TIN, __half, TOUT);               \
+  else return fail(MOE_ERR_INVALID_ARG, "combine: bad weights dtype")
+  if (a.rows_dtype != a.out_dtype)
+    return fail(MOE_ERR_UNSUPPORTED, "combine: rows and out must share a dtype");
+  if (a.out_dtype == MOE_DTYPE_BF16) {
+    KSW_COMB_W(__nv_bfloat16, __nv_bfloat16);
+  } else if (a.out_dtype == MOE_DTYPE_F16) {
+    KSW_COMB_W(__half, __half);
+  } else if (a.out_dtype == MOE_DTYPE_F32) {
+    KSW_COMB_W(float, float);
+  } else {
+    return fail(MOE_ERR_UNSUPPORTED, "combine: unsupported dtype");
+  }
+#undef KSW_COMB_W
+#undef KSW_COMB
   KSW_CUDA(cudaGetLastError());
   return MOE_OK;
 }

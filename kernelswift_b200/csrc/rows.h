@@ -37,7 +37,21 @@ struct SumArgs {
   int out_dtype;
 };
 
+struct CombineArgs {
+  const void* rows;             // [R, H] rows computed for the flat slots
+  int rows_dtype;
+  const int32_t* inv;           // [T*top_k] row of each flat slot, -1 = none
+  const void* weights;          // [T*top_k]
+  int weights_dtype;
+  int64_t T;
+  int top_k;
+  int64_t H;
+  void* out;                    // [T, H]
+  int out_dtype;
+};
+
 int gather_launch(const GatherArgs& a, cudaStream_t s);
+int combine_launch(const CombineArgs& a, cudaStream_t s);
 int sum_topk_launch(const SumArgs& a, cudaStream_t s);
 
 }  // namespace ksw
