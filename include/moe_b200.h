@@ -122,6 +122,31 @@ int moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel,
                          int32_t* num_tokens_post_pad, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/*
+ * Same result as moe_align_block_size, but allocates nothing and takes no
+ * workspace. No counterpart in the reference: this entry point exists for
+ * callers that cannot allocate device memory -- e.g. a serving runtime that
+ * has given all free HBM to its own pool and offers operators no workspace,
+ * or a latency-critical path that must not call cudaMalloc because it can
+ * synchronise the device.
+ *
+ * Its scratch is one static device array of MOE_ALIGN_NOALLOC_SCRATCH_BYTES
+ * (1 MiB) that every GPU loading the library holds until the process exits.
+ * Problems needing more (more than MOE_ALIGN_NOALLOC_SCRATCH_BYTES / 4 ints of
+ * per-chunk histograms: ceil(numel / 4096) * num_experts) are rejected with
+ * MOE_ERR_UNSUPPORTED and a message; up to 8192 ids need no scratch at all.
+ * The first call on each device looks up the array's device address with
+ * cudaGetSymbolAddress (that device must be current) and should come before
+ * any stream capture. All calls share the array: calls whose work overlaps
+ * on the GPU race on it, so order them on one stream or with events. Nothing
+ * in the array has to start at zero.
+ */
+#define MOE_ALIGN_NOALLOC_SCRATCH_BYTES (1u << 20)
+int moe_align_block_size_noalloc(const void* topk_ids, int ids_dtype,
+                                 int64_t numel, int num_experts, int block_m,
+                                 int32_t* sorted_token_ids, int32_t* expert_ids,
+                                 int32_t* num_tokens_post_pad, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Weight preparation (one-time per weight version)                         */
 /* Replaces the per-call casts `self.w1.to(dtype)` / `self.w2.to(dtype)` of

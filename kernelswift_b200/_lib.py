@@ -74,6 +74,7 @@ SIGNATURES = {
     "moe_align_buffer_len": (_i64, [_i64, _int, _int]),
     "moe_align_workspace_size": (_int, [_i64, _int, _int, ctypes.POINTER(_sz)]),
     "moe_align_block_size": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "moe_align_block_size_noalloc": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp]),
     "moe_prepare_w13": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _int, _vp, _int, _vp, _vp]),
     "moe_prepare_w2": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _int, _vp, _int, _vp, _vp]),
     "moe_fused_experts_workspace_size": (_int, [ctypes.POINTER(MoeProblem), ctypes.POINTER(_sz)]),

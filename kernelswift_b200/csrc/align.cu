@@ -15,6 +15,8 @@
 //   otherwise: three launches over chunks of kChunk ids:
 //     hist (per-chunk histogram, sentinel fill) -> scan (one CTA: offsets,
 //     expert_ids, num_tokens_post_pad, per-chunk bases) -> scatter.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace ksw {
@@ -323,3 +325,83 @@ int moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: moe_align_block_size_noalloc
+//
+// For callers that cannot allocate device memory: a serving runtime that has
+// handed all free HBM to its own pool (KV cache, activations) and gives an
+// operator no workspace hook, or a latency-critical path that must not call
+// cudaMalloc because it can synchronise the device. The per-chunk histograms
+// of the multi-CTA path live in one static device array instead of a caller
+// workspace.
+//
+//   - The array has a fixed size (kNoAllocScratchBytes, 1 MiB) and exists once
+//     on every GPU that loads this library, until the process exits.
+//   - Host code cannot pass the array's name to a kernel: in host code that
+//     name is only a stand-in for the symbol. Its device address is looked up
+//     with cudaGetSymbolAddress the first time the entry point runs on a
+//     device (with that device current) and cached per device. That first
+//     call on each device therefore does the look-up and should come before
+//     any stream capture.
+//   - Every call on a device shares the array and it keeps the previous
+//     call's contents. Nothing in it needs to start at zero: every entry the
+//     kernels read is written earlier in the same call. Calls whose work
+//     overlaps on the GPU (different streams, no ordering between them) race
+//     on the array; order them on one stream or with events.
+//   - No cudaMalloc, cudaFree or other allocating call is made.
+// ---------------------------------------------------------------------------
+namespace ksw {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) int32_t g_align_noalloc_scratch[kNoAllocScratchBytes / 4];
+
+std::mutex g_noalloc_mu;
+int32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the static scratch on the current device.
+int noalloc_scratch_address(int32_t** out) {
+  int dev = 0;
+  KSW_CUDA(cudaGetDevice(&dev));
+  KSW_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, MOE_ERR_DEVICE,
+              "moe_align_block_size_noalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    int32_t* ptr = nullptr;
+    KSW_CUDA(cudaGetSymbolAddress((void**)&ptr, g_align_noalloc_scratch));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return MOE_OK;
+}
+
+}  // namespace
+}  // namespace ksw
+
+extern "C" int moe_align_block_size_noalloc(const void* topk_ids, int ids_dtype,
+                                            int64_t numel, int num_experts, int block_m,
+                                            int32_t* sorted_token_ids, int32_t* expert_ids,
+                                            int32_t* num_tokens_post_pad, void* stream) {
+  using namespace ksw;
+  int st = check_device(nullptr);
+  if (st != MOE_OK) return st;
+  st = align_validate(numel, num_experts, block_m);
+  if (st != MOE_OK) return st;
+  const size_t need = align_workspace_bytes(numel, num_experts);
+  if (need > kNoAllocScratchBytes)
+    return fail(MOE_ERR_UNSUPPORTED,
+                "moe_align_block_size_noalloc: this problem needs " + std::to_string(need) +
+                    " bytes of scratch but the static scratch holds " +
+                    std::to_string(kNoAllocScratchBytes) +
+                    " (numel * num_experts too large); use moe_align_block_size with a "
+                    "workspace");
+  int32_t* scratch = nullptr;
+  st = noalloc_scratch_address(&scratch);
+  if (st != MOE_OK) return st;
+  return align_launch(topk_ids, ids_dtype, numel, num_experts, block_m, sorted_token_ids,
+                      expert_ids, num_tokens_post_pad, scratch, kNoAllocScratchBytes,
+                      static_cast<cudaStream_t>(stream));
+}
