@@ -138,8 +138,13 @@ class ClockSampler:
 # CPU side: the reference's torch path on the host cores
 # ---------------------------------------------------------------------------
 
-def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1):
-    """tokens/s of base.py's forward (oracle restatement) on the host CPU."""
+_CPU_WEIGHTS: dict = {}
+
+
+def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1,
+                       min_seconds=0.0):
+    """tokens/s of base.py's forward (oracle restatement) on the host CPU:
+    median over `repeats` calls, more calls until `min_seconds` of timed work."""
     import torch
     from oracle import moe_oracle as orc
 
@@ -150,24 +155,29 @@ def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1
     if bias:
         logits = logits + torch.randn(E, generator=g) * bias
     # base.py keeps fp32 master weights and casts them on every call
-    w1 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
-    w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
+    key = (E, I, H)
+    if key not in _CPU_WEIGHTS:
+        _CPU_WEIGHTS.clear()
+        gw = torch.Generator().manual_seed(1)
+        _CPU_WEIGHTS[key] = (torch.randn(E, 2 * I, H, generator=gw) / H ** 0.5,
+                             torch.randn(E, H, I, generator=gw) / I ** 0.5)
+    w1, w2 = _CPU_WEIGHTS[key]
+    for _ in range(warmup):
+        orc.model_forward_native(hidden, logits, w1, w2, k)
     times = []
-    for i in range(warmup + repeats):
+    while len(times) < repeats or (sum(times) < min_seconds and len(times) < 50):
         t0 = time.perf_counter()
         orc.model_forward_native(hidden, logits, w1, w2, k)
-        dt = time.perf_counter() - t0
-        if i >= warmup:
-            times.append(dt)
+        times.append(time.perf_counter() - t0)
     med = statistics.median(times)
-    return sample_tokens / med, med, torch.get_num_threads()
+    return sample_tokens / med, med, torch.get_num_threads(), len(times)
 
 
 def cpu_sample_tokens(H, I, E, k, T, bias, target_s=3.0):
     """Tokens per CPU call so that one call of the reference path takes about
     `target_s` seconds on this host (at most the GPU batch T)."""
     probe = min(T, 256)
-    rate, _, _ = cpu_reference_rate(H, I, E, k, "none", bias, probe, repeats=1, warmup=0)
+    rate, _, _, _ = cpu_reference_rate(H, I, E, k, "none", bias, probe, repeats=1, warmup=1)
     return int(max(16, min(T, rate * target_s)))
 
 
@@ -176,8 +186,8 @@ def run_reference(args, H, I, E, k, quant, T, bias, rank):
     if rank != 0:
         return
     sample = cpu_sample_tokens(H, I, E, k, T, bias)
-    rate, med, cores = cpu_reference_rate(H, I, E, k, quant, bias, sample,
-                                          repeats=max(1, args.steps), warmup=max(0, args.warmup))
+    rate, med, cores, n = cpu_reference_rate(H, I, E, k, quant, bias, sample,
+                                             repeats=max(1, args.steps), warmup=max(0, args.warmup))
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -242,7 +252,9 @@ def main():
     logits = torch.randn(T, E, generator=g, device=dev)
     if bias:
         logits = logits + torch.randn(E, generator=g, device=dev) * bias
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     rows_per_launch = [T * k]  # routed rows the local gate-up GEMM saw (last step)
+    experts_hit = [0]          # distinct local experts with rows (for the byte count)
     if world == 1:
         # the drop-in module: fp32 master weights as in base.py, prepared once
         model = fm.ModelNew(E, k, H, I).to(dev)
@@ -278,15 +290,32 @@ def main():
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
+    _, ti0 = fm.fused_topk(hidden, logits, k)
+    if world == 1:
+        experts_hit[0] = int(torch.unique(ti0).numel())
+    else:
+        el = E // world
+        got = torch.zeros(E, dtype=torch.int32, device=dev)
+        got[torch.unique(ti0)] = 1
+        dist.all_reduce(got)
+        experts_hit[0] = int((got[rank * el:(rank + 1) * el] > 0).sum())
 
     K = args.steps
     clocks = ClockSampler(local_rank).__enter__()
     # keep the GPU busy for a second before timing so that the clock samples
     # cover a loaded GPU (these steps are untimed warm-up)
-    t_heat = time.perf_counter()
-    while time.perf_counter() - t_heat < args.heat_seconds:
+    # The number of heat steps is agreed across ranks (every rank must issue
+    # the same collectives): time one step, take the max over ranks.
+    t_one = time.perf_counter()
+    step()
+    torch.cuda.synchronize()
+    t_one = torch.tensor([time.perf_counter() - t_one], device=dev)
+    if world > 1:
+        dist.all_reduce(t_one, op=dist.ReduceOp.MAX)
+    n_heat = int(args.heat_seconds / max(float(t_one.item()), 1e-4))
+    for _ in range(min(n_heat, 100000)):
         step()
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     stage_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(_lib.STAGES) + 1)]
@@ -377,16 +406,34 @@ def main():
                + ", pinned host buffers"}
 
     # ---- roofline of the dominant kernel (gate-up GEMM) ----
+    # Algorithmic work of one launch: 4*H*I*rows FLOPs; bytes = the w13 slices
+    # of the experts hit + the gathered rows read + the activations written.
+    # The binding resource is whichever of (FLOPs / tensor peak) and
+    # (bytes / HBM peak) takes longer.
     peaks, peak_src = load_peaks()
     gu_ms = stage_ms["gate_up"]
-    gu_flops = 4 * H * I * rows_per_launch[0]
-    if quant == "none":
-        peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
-        peak_note = f"bf16 dense, sustained, {peak_src}"
+    rows = rows_per_launch[0]
+    gu_flops = 4 * H * I * rows
+    w_bytes = 2 if quant == "none" else 1
+    e_local = E if world == 1 else E // world
+    hit = experts_hit[0] if experts_hit[0] else e_local
+    gu_bytes = hit * 2 * I * H * w_bytes + rows * H * w_bytes + rows * I * 2
+    tensor_peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    tensor_note = f"bf16 dense, sustained, {peak_src}"
+    if quant != "none":
+        tensor_peak *= 2
+        tensor_note = f"2x bf16 dense sustained ({quant} operand rate), {peak_src}"
+    hbm_peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    t_tensor = gu_flops / (tensor_peak * 1e12)
+    t_hbm = gu_bytes / (hbm_peak * 1e9)
+    if t_tensor >= t_hbm:
+        achieved = gu_flops / (gu_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tensor_peak,
+                "unit": "TFLOP/s", "frac": achieved / tensor_peak, "peak_source": tensor_note}
     else:
-        peak = 2 * peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
-        peak_note = f"2x bf16 dense sustained ({quant} rate), {peak_src}"
-    achieved = gu_flops / (gu_ms / 1e3) / 1e12
+        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_source": f"copy bandwidth, {peak_src}"}
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
@@ -395,19 +442,23 @@ def main():
             traffic = entry["bytes"] if entry and world == 1 else None
         except Exception:
             traffic = None
-    roofline = {"kernel": "moe_grouped_gemm_kernel (gate-up, SiLU fused)", "bound": "tensor",
-                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_source": peak_note, "traffic": traffic,
+    roofline = {"kernel": "moe_grouped_gemm_kernel (gate-up, SiLU fused)", **roof,
+                "traffic": traffic,
                 "traffic_unit": "DRAM bytes per launch (ncu capture, profiles/)",
-                "algorithmic": f"4*H*I*T*k = {gu_flops:.4g} FLOP per launch"}
+                "algorithmic": f"{gu_flops:.4g} FLOP (4*H*I*rows, rows={rows}) and "
+                               f"{gu_bytes / 1e9:.4g} GB ({hit} experts' w13 + rows in + act out) "
+                               "per launch",
+                "launch_ms": gu_ms}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sample = cpu_sample_tokens(H, I, E, k, T, bias)
-        rate, med, cores = cpu_reference_rate(H, I, E, k, quant, bias, sample, repeats=3)
+        rate, med, cores, n = cpu_reference_rate(H, I, E, k, quant, bias, sample, repeats=3,
+                                                 min_seconds=10.0)
         cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{sample} tokens of the same layer, base.py forward restated in "
-                         f"torch-CPU bf16 (median of 3 calls, {med:.2f} s each)"}
+               "sample": f"{sample} tokens of the same layer per call, base.py forward "
+                         f"restated in torch-CPU bf16 with its per-call weight casts "
+                         f"(median of {n} calls, {med:.2f} s each)"}
 
     # our kernels per step: align (1 launch up to 8192 routed rows, else 3),
     # gather, gate-up, [activation quant], down, top-k sum

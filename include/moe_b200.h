@@ -85,6 +85,27 @@ int moe_read_status(int32_t* device_status, int32_t* host_status, int reset,
                     void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Routing: softmax -> top-k -> renormalise -> cast                          */
+/* Replaces base.py:44-48 (torch.softmax, torch.topk, the renormalising      */
+/* division and the cast of the weights to the activation dtype).           */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * For every token t: w_e = exp(l_e - max) / sum_e' exp(l_e' - max) over the
+ * router logits l = router_logits[t, :] (fp32 arithmetic); the top_k experts
+ * by logit, largest first, ties broken by the lower expert index (softmax is
+ * strictly increasing, so this is the top-k of the probabilities); with
+ * renormalize != 0 each selected weight is divided by the sum of the
+ * selected weights. Writes topk_weights [T, top_k] (F32/F16/BF16) and
+ * topk_ids [T, top_k] (I32/I64). logits dtype F32/F16/BF16;
+ * 1 <= num_experts <= 1024, 1 <= top_k <= min(32, num_experts).
+ */
+int moe_topk_softmax(const void* router_logits, int logits_dtype,
+                     int64_t num_tokens, int num_experts, int top_k,
+                     int renormalize, void* topk_weights, int weights_dtype,
+                     void* topk_ids, int ids_dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Routing metadata: moe_align_block_size                                   */
 /* Replaces the per-expert grouping of base.py:64-68 (`mask = flat_ids == e`,
  * `x_rep[mask]`) and tmo.moe_gen_idx of triton_fused_moe_006.py:38.         */

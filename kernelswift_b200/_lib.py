@@ -71,6 +71,7 @@ SIGNATURES = {
     "moe_last_error": (ctypes.c_char_p, []),
     "moe_abi_version": (_int, []),
     "moe_read_status": (_int, [_vp, _vp, _int, _vp]),
+    "moe_topk_softmax": (_int, [_vp, _int, _i64, _int, _int, _int, _vp, _int, _vp, _int, _vp]),
     "moe_align_buffer_len": (_i64, [_i64, _int, _int]),
     "moe_align_workspace_size": (_int, [_i64, _int, _int, ctypes.POINTER(_sz)]),
     "moe_align_block_size": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _sz, _vp]),

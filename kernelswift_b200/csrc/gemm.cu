@@ -26,6 +26,8 @@
 // Every barrier wait is bounded (one second): a role that runs out raises a
 // shared abort flag, every role leaves its loop, in-flight TMA loads and
 // MMAs are waited for, TMEM is freed and MOE_ERR_TIMEOUT is reported.
+#include <atomic>
+
 #include "common.cuh"
 #include "internal.h"
 #include "runtime.h"
@@ -89,8 +91,11 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return g / (1.0f + __expf(-g)) * u;
 }
 
+// Weight of flat row i; a null weight array means unit weights (the
+// unweighted partial rows of the split-K gate-up GEMM).
 __device__ __forceinline__ float load_weight(const void* w, int dtype,
                                              int64_t i) {
+  if (w == nullptr) return 1.0f;
   if (dtype == MOE_DTYPE_F32) return static_cast<const float*>(w)[i];
   if (dtype == MOE_DTYPE_BF16)
     return __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]);
@@ -294,6 +299,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld16(tbase + g * 32 + 16, uv);
           tmem_ld_wait();
           if (valid) {
+            float gs[16], us[16];
+            if constexpr (kScaled) {
+              // per-column weight scales of this 32-column group, times the row scale
+              const float4* sg = reinterpret_cast<const float4*>(bsc + g * 32);
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const float4 a4 = __ldg(sg + q4), b4 = __ldg(sg + 4 + q4);
+                gs[4 * q4] = a_s * a4.x; gs[4 * q4 + 1] = a_s * a4.y;
+                gs[4 * q4 + 2] = a_s * a4.z; gs[4 * q4 + 3] = a_s * a4.w;
+                us[4 * q4] = a_s * b4.x; us[4 * q4 + 1] = a_s * b4.y;
+                us[4 * q4 + 2] = a_s * b4.z; us[4 * q4 + 3] = a_s * b4.w;
+              }
+            }
             uint32_t packed[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -302,10 +320,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               float u0 = acc_to_f32<KIND>(uv[2 * j]);
               float u1 = acc_to_f32<KIND>(uv[2 * j + 1]);
               if constexpr (kScaled) {
-                g0 *= a_s * __ldg(bsc + g * 32 + 2 * j);
-                g1 *= a_s * __ldg(bsc + g * 32 + 2 * j + 1);
-                u0 *= a_s * __ldg(bsc + g * 32 + 16 + 2 * j);
-                u1 *= a_s * __ldg(bsc + g * 32 + 16 + 2 * j + 1);
+                g0 *= gs[2 * j];
+                g1 *= gs[2 * j + 1];
+                u0 *= us[2 * j];
+                u1 *= us[2 * j + 1];
               }
               packed[j] = pack2<TOUT>(silu_mul(g0, u0), silu_mul(g1, u1));
             }
@@ -335,10 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               float x3 = acc_to_f32<KIND>(v[4 * j + 3]);
               if constexpr (kScaled) {
                 const float s = a_s * w;
-                x0 *= s * __ldg(bsc + g * 16 + 4 * j);
-                x1 *= s * __ldg(bsc + g * 16 + 4 * j + 1);
-                x2 *= s * __ldg(bsc + g * 16 + 4 * j + 2);
-                x3 *= s * __ldg(bsc + g * 16 + 4 * j + 3);
+                const float4 b4 = __ldg(reinterpret_cast<const float4*>(bsc + g * 16) + j);
+                x0 *= s * b4.x;
+                x1 *= s * b4.y;
+                x2 *= s * b4.z;
+                x3 *= s * b4.w;
               } else {
                 x0 *= w;
                 x1 *= w;
@@ -620,13 +639,28 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
 
 int num_sms_or_fail(int* sms) { return check_device(sms); }
 
+// Raises a kernel's dynamic shared-memory limit once per device (the
+// attribute is per function and device; setting it on every launch costs
+// host time on the decode path).
+template <typename Kern>
+int set_smem_once(Kern kern, size_t bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  KSW_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return MOE_OK;
+  KSW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)));
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return MOE_OK;
+}
+
 template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
                   const KParams& kp, int grid, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
   auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT>;
-  KSW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(Cfg::kSmemBytes)));
+  static std::atomic<uint64_t> smem_set{0};
+  int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
+  if (st != MOE_OK) return st;
   kern<<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, kp);
   KSW_CUDA(cudaGetLastError());
   return MOE_OK;
@@ -637,8 +671,9 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, 
                cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
   auto kern = moe_grouped_gemm_fp8_kernel<BN, EPI>;
-  KSW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(Cfg::kSmemBytes)));
+  static std::atomic<uint64_t> smem_set{0};
+  int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
+  if (st != MOE_OK) return st;
   kern<<<grid, kThreadsF8, Cfg::kSmemBytes, s>>>(ta, tb, kp);
   KSW_CUDA(cudaGetLastError());
   return MOE_OK;
@@ -801,14 +836,23 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   return dispatch_bn<kKindF16, 0, kEpiSwiGLU, __half>(bn, ta, tb, kp, grid, s);
 }
 
+// Gate-up GEMM split along K: writes unweighted fp32 partial rows
+// part[s, r, :] (2I columns, regrouped order) for the flat row r of every
+// valid operand row; swiglu_reduce then sums the splits and applies SiLU*up.
+// Used when there are too few output tiles to fill the GPU (decode).
+int gemm_gate_up_split_launch(const GroupedGemmArgs& a, cudaStream_t s) {
+  GroupedGemmArgs d = a;
+  d.row_weights = nullptr;
+  d.row_weights_dtype = MOE_DTYPE_F32;
+  return gemm_down_launch(d, s);
+}
+
 int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   int sms = 0;
   int st = num_sms_or_fail(&sms);
   if (st != MOE_OK) return st;
   st = common_checks(a);
   if (st != MOE_OK) return st;
-  KSW_REQUIRE(a.row_weights != nullptr, MOE_ERR_INVALID_ARG,
-              "down GEMM: null row weights");
   KSW_REQUIRE(a.row_weights_dtype == MOE_DTYPE_F32 || a.row_weights_dtype == MOE_DTYPE_F16 ||
                   a.row_weights_dtype == MOE_DTYPE_BF16,
               MOE_ERR_INVALID_ARG, "down GEMM: row weights must be f32/f16/bf16");

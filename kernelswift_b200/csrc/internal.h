@@ -46,5 +46,6 @@ struct GroupedGemmArgs {
 
 int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s);
 int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s);
+int gemm_gate_up_split_launch(const GroupedGemmArgs& a, cudaStream_t s);
 
 }  // namespace ksw

@@ -28,10 +28,12 @@ struct Plan {
   int compute_dtype;     // operand dtype for QUANT_NONE
   int a_dtype;           // dtype of the gathered operand
   int act_dtype;         // dtype of the gate-up output (bf16/f16)
-  int splits;
+  int splits;            // down GEMM K splits
+  int gu_splits;         // gate-up GEMM K splits (1: fused SiLU*up epilogue)
+  int dn_bn, gu_bn;      // N tile widths
   size_t align_ws;
   size_t off_sorted, off_eids, off_npp, off_align, off_a, off_a_scale, off_act,
-      off_act_q, off_act_scale, off_part, total;
+      off_act_q, off_act_scale, off_part, off_gu_part, total;
 };
 
 int elem_bytes(int dtype) {
@@ -44,18 +46,46 @@ int elem_bytes(int dtype) {
   }
 }
 
-int choose_splits(int64_t numel, int64_t L, int E, int64_t H, int64_t K, int kbytes_per_elem,
-                  int sms) {
-  const int64_t est_mb = std::min<int64_t>(L / kBlockM, ceil_div(numel, kBlockM) +
-                                                            std::min<int64_t>(E, numel));
-  const int64_t tiles = std::max<int64_t>(1, est_mb * (H / 128));
-  const int64_t k_blocks = ceil_div(K * kbytes_per_elem, 128);
-  if (tiles >= sms) return 1;
-  int64_t splits = std::min<int64_t>(ceil_div(2 * sms, tiles), 16);
-  splits = std::min<int64_t>(splits, std::max<int64_t>(1, k_blocks / 4));
-  splits = std::max<int64_t>(splits, 1);
-  const int64_t per = ceil_div(k_blocks, splits);
-  return int(ceil_div(k_blocks, per));
+// Upper bound on the m-blocks a routing can use: an expert with c rows needs
+// ceil(c / 128) <= c / 128 + 1 blocks and at most min(E, numel) experts
+// have rows.
+int64_t est_m_blocks(int64_t numel, int64_t L, int E) {
+  return std::min<int64_t>(L / kBlockM, numel / kBlockM + std::min<int64_t>(E, numel));
+}
+
+// Tile width and K split of one grouped GEMM with `n` output columns and
+// `k_blocks` 128-byte k-blocks over `mb` m-blocks. Model: a CTA's time per
+// tile is proportional to the bytes it streams, (BN + 32) / S (the +32
+// stands for the A tile, read from L2), and the kernel takes
+// ceil(tiles / SMs) such waves; each extra split costs 2 % for its partial
+// sums. Wide tiles win ties (less A traffic, fewer partials).
+struct Tiling {
+  int bn;
+  int splits;
+};
+
+Tiling choose_tiling(int64_t mb, int64_t n, int64_t k_blocks, int sms, bool allow_split,
+                     bool allow64) {
+  Tiling best{0, 1};
+  double best_cost = 1e300;
+  mb = std::max<int64_t>(mb, 1);
+  for (int bn : {256, 128, 64}) {
+    if (n % bn != 0 || (bn == 64 && !allow64)) continue;
+    const int64_t tiles = mb * (n / bn);
+    const int64_t max_s =
+        allow_split ? std::min<int64_t>(16, std::max<int64_t>(1, k_blocks / 4)) : 1;
+    for (int64_t s = 1; s <= max_s; ++s) {
+      const int64_t per = ceil_div(k_blocks, s);
+      if (ceil_div(k_blocks, per) != s) continue;  // a split would be empty
+      const double waves = double(ceil_div(tiles * s, sms));
+      const double cost = waves * double(bn + 32) / double(s) * (1.0 + 0.02 * double(s - 1));
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = Tiling{bn, int(s)};
+      }
+    }
+  }
+  return best;
 }
 
 int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
@@ -105,7 +135,18 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   } else {
     return fail(MOE_ERR_INVALID_ARG, "unknown quant mode");
   }
-  P.splits = choose_splits(P.numel, P.L, P.E, P.H, P.I, kbpe, sms);
+  const int64_t est_mb = est_m_blocks(P.numel, P.L, P.E);
+  const bool fp8 = P.quant == MOE_QUANT_FP8_BLOCK;
+  const Tiling dn = choose_tiling(est_mb, P.H, ceil_div(P.I * kbpe, 128), sms, true, !fp8);
+  // the split gate-up path has no fp8 epilogue (its block scales follow the
+  // regrouped gate/up rows); fp8 keeps the fused SiLU*up epilogue
+  const Tiling gu = choose_tiling(est_mb, 2 * P.I, ceil_div(P.H * kbpe, 128), sms, !fp8, !fp8);
+  KSW_REQUIRE(dn.bn > 0 && gu.bn > 0, MOE_ERR_UNSUPPORTED,
+              "hidden size and 2*intermediate size must be multiples of 64 (128 for fp8)");
+  P.splits = dn.splits;
+  P.dn_bn = dn.bn;
+  P.gu_splits = gu.splits;
+  P.gu_bn = gu.bn;
   P.align_ws = align_workspace_bytes(P.numel, P.E);
 
   size_t off = 0;
@@ -130,6 +171,7 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.off_act_q = take(P.quant != MOE_QUANT_NONE ? size_t(P.L) * P.I : 0);
   P.off_act_scale = take(scale_bytes(P.I));
   P.off_part = take(size_t(P.splits) * P.numel * P.H * 4);
+  P.off_gu_part = take(P.gu_splits > 1 ? size_t(P.gu_splits) * P.numel * 2 * P.I * 4 : 0);
   P.total = off;
   return MOE_OK;
 }
@@ -231,7 +273,20 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   ga.out = at<void>(workspace, P.off_act);
   ga.splits = 1;
   ga.status = p->status;
-  st = gemm_gate_up_launch(ga, s);
+  if (P.gu_splits > 1) {
+    // decode-sized: split K, unweighted fp32 partial rows, then SiLU*up
+    GroupedGemmArgs gs = ga;
+    gs.out = at<void>(workspace, P.off_gu_part);
+    gs.splits = P.gu_splits;
+    gs.block_n = P.gu_bn;
+    st = gemm_gate_up_split_launch(gs, s);
+    if (st != MOE_OK) return st;
+    st = swiglu_reduce_launch(at<float>(workspace, P.off_gu_part), P.gu_splits, P.numel, P.I,
+                              sorted, npp, P.L, ga.out, P.act_dtype, s);
+  } else {
+    ga.block_n = P.gu_bn;
+    st = gemm_gate_up_launch(ga, s);
+  }
   if (st != MOE_OK) return st;
 
   const void* down_a = ga.out;
@@ -270,6 +325,7 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   gd.row_weights = p->topk_weights;
   gd.row_weights_dtype = p->weights_dtype;
   gd.splits = P.splits;
+  gd.block_n = P.dn_bn;
   st = gemm_down_launch(gd, s);
   if (st != MOE_OK) return st;
 

@@ -135,6 +135,20 @@ __global__ void __launch_bounds__(kWarps * 32)
 }
 
 // ---------------- gather + e4m3 per (row, 128 columns) ----------------
+// Each lane handles 8 consecutive columns (one 16-byte load for 16-bit
+// sources); 16 lanes cover one 128-column group, so the group's absmax is a
+// 16-lane shuffle reduction. Requires H % 8 == 0 (checked on the host); a
+// partial last group is handled by masking lanes past H.
+__device__ __forceinline__ uint2 pack_e4m3x8(const float (&v)[8], float sc) {
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    lo |= uint32_t(to_e4m3(v[i], sc)) << (8 * i);
+    hi |= uint32_t(to_e4m3(v[4 + i], sc)) << (8 * i);
+  }
+  return make_uint2(lo, hi);
+}
+
 template <typename Tin>
 __global__ void __launch_bounds__(kWarps * 32)
     gather_fp8_kernel(const Tin* __restrict__ src, int64_t H, int top_k,
@@ -150,19 +164,21 @@ __global__ void __launch_bounds__(kWarps * 32)
     const int64_t sr = sorted ? source_row(sorted, m, numel, top_k) : m;
     if (sr < 0 || sr >= src_rows) continue;
     const Tin* s = src + sr * H;
-    for (int64_t g = 0; g < groups; ++g) {
-      const int64_t h0 = g * 128 + lane * 4;
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
+    // two groups per warp iteration: lanes 0-15 group g, lanes 16-31 group g+1
+    for (int64_t g0 = 0; g0 < groups; g0 += 2) {
+      const int64_t g = g0 + (lane >> 4);
+      const int64_t h = g * 128 + (lane & 15) * 8;
+      const bool in = g < groups && h < H;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (in) load8(s + h, v);
+      float amax = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (h0 + i < H) v[i] = to_f32(s[h0 + i]);
-      float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-      amax = warp_max(amax);
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float sc = quant_scale(amax, kFp8Max);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (h0 + i < H) dst[m * H + h0 + i] = to_e4m3(v[i], sc);
-      if (lane == 0) scale[m * groups + g] = sc;
+      if (in) *reinterpret_cast<uint2*>(dst + m * H + h) = pack_e4m3x8(v, sc);
+      if (in && (lane & 15) == 0) scale[m * groups + g] = sc;
     }
   }
 }
@@ -233,6 +249,47 @@ __global__ void __launch_bounds__(256)
       }
     }
     store8(out + t * H + h, acc);
+  }
+}
+
+// ---------------- split-K gate-up: sum the splits, SiLU(gate) * up ----------------
+// part [S, numel, 2I] in the regrouped column order (32-column groups: 16
+// gate, then the 16 matching up columns); act[m, 16g + c] for operand row m
+// whose flat row r = sorted[m] is valid.
+template <typename Tout>
+__global__ void __launch_bounds__(256)
+    swiglu_reduce_kernel(const float* __restrict__ part, int splits, int64_t numel, int64_t I,
+                         const int32_t* __restrict__ sorted,
+                         const int32_t* __restrict__ num_post_pad, int64_t max_rows,
+                         Tout* __restrict__ act) {
+  const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
+  const int64_t vec_per_row = I / 8;
+  const int64_t total = rows * vec_per_row;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = i / vec_per_row;
+    const int r = __ldg(sorted + m);
+    if (r >= numel) continue;
+    const int64_t a0 = (i - m * vec_per_row) * 8;     // first act column
+    const int64_t g = a0 / 16, c0 = a0 % 16;          // 8 columns stay in one group
+    const int64_t gate_col = 32 * g + c0, up_col = gate_col + 16;
+    float gsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float usum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < splits; ++s) {
+      const float* row = part + (int64_t(s) * numel + r) * (2 * I);
+      float gv[8], uv[8];
+      load8(row + gate_col, gv);
+      load8(row + up_col, uv);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        gsum[q] += gv[q];
+        usum[q] += uv[q];
+      }
+    }
+    float out[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) out[q] = gsum[q] / (1.0f + __expf(-gsum[q])) * usum[q];
+    store8(act + m * I + a0, out);
   }
 }
 
@@ -363,6 +420,26 @@ int sum_topk_launch(const SumArgs& a, cudaStream_t s) {
     return fail(MOE_ERR_UNSUPPORTED, "sum_topk: unsupported output dtype");
   }
 #undef KSW_SUM
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+int swiglu_reduce_launch(const float* part, int splits, int64_t numel, int64_t I,
+                         const int32_t* sorted, const int32_t* num_post_pad, int64_t max_rows,
+                         void* act, int act_dtype, cudaStream_t s) {
+  KSW_REQUIRE(part && sorted && num_post_pad && act, MOE_ERR_INVALID_ARG,
+              "swiglu_reduce: null pointer");
+  KSW_REQUIRE(I % 16 == 0 && splits >= 1, MOE_ERR_UNSUPPORTED, "swiglu_reduce: bad sizes");
+  const int64_t total = max_rows * (I / 8);
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 148 * 16)));
+  if (act_dtype == MOE_DTYPE_BF16)
+    swiglu_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        part, splits, numel, I, sorted, num_post_pad, max_rows, static_cast<__nv_bfloat16*>(act));
+  else if (act_dtype == MOE_DTYPE_F16)
+    swiglu_reduce_kernel<__half><<<grid, 256, 0, s>>>(
+        part, splits, numel, I, sorted, num_post_pad, max_rows, static_cast<__half*>(act));
+  else
+    return fail(MOE_ERR_UNSUPPORTED, "swiglu_reduce: act dtype must be bf16/f16");
   KSW_CUDA(cudaGetLastError());
   return MOE_OK;
 }

@@ -52,6 +52,9 @@ struct CombineArgs {
 
 int gather_launch(const GatherArgs& a, cudaStream_t s);
 int combine_launch(const CombineArgs& a, cudaStream_t s);
+int swiglu_reduce_launch(const float* part, int splits, int64_t numel, int64_t I,
+                         const int32_t* sorted, const int32_t* num_post_pad, int64_t max_rows,
+                         void* act, int act_dtype, cudaStream_t s);
 int sum_topk_launch(const SumArgs& a, cudaStream_t s);
 
 }  // namespace ksw

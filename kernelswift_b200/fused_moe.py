@@ -88,19 +88,27 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 
 def fused_topk(hidden_states: torch.Tensor, gating_output: torch.Tensor, topk: int,
-               renormalize: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
-    """softmax(fp32) -> top-k (sorted) -> optional renormalisation.
+               renormalize: bool = True, weights_dtype: torch.dtype = torch.float32,
+               ids_dtype: torch.dtype = torch.int32) -> tuple[torch.Tensor, torch.Tensor]:
+    """softmax(fp32) -> top-k -> optional renormalisation, in one kernel.
 
-    Returns (topk_weights fp32 [T, k], topk_ids int64 [T, k]); the same torch
-    ops as base.py:44-47 on the same device, so the ids are bit-identical.
+    The routing of base.py:44-48 (moe_topk_softmax): experts are selected by
+    logit, largest first, ties to the lower index; the weights are the fp32
+    softmax probabilities of the selected experts, renormalised to sum to 1
+    when `renormalize`, returned in `weights_dtype` (base.py:48 casts them to
+    the activation dtype). Returns (topk_weights [T, k], topk_ids [T, k]).
     """
-    if gating_output.shape[0] != hidden_states.shape[0]:
-        raise ValueError("gating_output and hidden_states disagree on the token count")
-    scores = torch.softmax(gating_output.float(), dim=-1)
-    topk_weights, topk_ids = torch.topk(scores, topk, dim=-1)
-    if renormalize:
-        topk_weights = topk_weights / topk_weights.sum(-1, keepdim=True)
-    return topk_weights, topk_ids
+    _check_cuda("gating_output", gating_output)
+    if gating_output.dim() != 2 or gating_output.shape[0] != hidden_states.shape[0]:
+        raise ValueError("gating_output must be [T, E] with T = hidden_states.shape[0]")
+    logits = _contig(gating_output)
+    T, E = logits.shape
+    dev = logits.device
+    w = torch.empty(T, topk, dtype=weights_dtype, device=dev)
+    ids = torch.empty(T, topk, dtype=ids_dtype, device=dev)
+    _lib.call("moe_topk_softmax", _ptr(logits), _code(logits), T, E, topk, int(renormalize),
+              _ptr(w), _code(w), _ptr(ids), _code(ids), _stream(dev))
+    return w, ids
 
 
 # ---------------------------------------------------------------------------
@@ -344,9 +352,9 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
 def fused_moe(hidden_states: torch.Tensor, w1, w2, gating_output: torch.Tensor, topk: int,
               renormalize: bool = True, **kwargs) -> torch.Tensor:
     """Routing + experts: the whole of base.py:35-76 as one call."""
-    topk_weights, topk_ids = fused_topk(hidden_states, gating_output, topk, renormalize)
-    return fused_experts(hidden_states, w1, w2, topk_weights.to(hidden_states.dtype), topk_ids,
-                         **kwargs)
+    topk_weights, topk_ids = fused_topk(hidden_states, gating_output, topk, renormalize,
+                                        weights_dtype=hidden_states.dtype)
+    return fused_experts(hidden_states, w1, w2, topk_weights, topk_ids, **kwargs)
 
 
 # ---------------------------------------------------------------------------
@@ -384,9 +392,9 @@ class ModelNew(nn.Module):
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         self._last_hidden = hidden_states  # for run_out (auto_bench kernel profiling)
+        # weights in the activation dtype, as base.py:48 casts them
         topk_weights, topk_ids = fused_topk(hidden_states, router_logits, self.top_k,
-                                            self.renormalize)
-        topk_weights = topk_weights.to(hidden_states.dtype)  # base.py:48
+                                            self.renormalize, weights_dtype=hidden_states.dtype)
         return fused_experts(hidden_states, self.prepared(hidden_states.dtype), None,
                              topk_weights, topk_ids)
 
@@ -394,6 +402,7 @@ class ModelNew(nn.Module):
                 hidden_states: torch.Tensor | None = None) -> torch.Tensor:
         """auto_bench `--profile-mode kernel` hook: forward into `out`."""
         hidden = hidden_states if hidden_states is not None else self._last_hidden
-        topk_weights, topk_ids = fused_topk(hidden, router_logits, self.top_k, self.renormalize)
-        return fused_experts(hidden, self.prepared(hidden.dtype), None,
-                             topk_weights.to(hidden.dtype), topk_ids, out=out)
+        topk_weights, topk_ids = fused_topk(hidden, router_logits, self.top_k, self.renormalize,
+                                            weights_dtype=hidden.dtype)
+        return fused_experts(hidden, self.prepared(hidden.dtype), None, topk_weights, topk_ids,
+                             out=out)

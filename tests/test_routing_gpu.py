@@ -1,0 +1,69 @@
+"""GPU: the fused routing kernel (moe_topk_softmax) against base.py's torch
+routing (softmax -> topk -> renormalise, base.py:44-48)."""
+import numpy as np
+import pytest
+import torch
+
+from cases import CASES, make_inputs
+from kernelswift_b200 import fused_moe as fm
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden"
+
+
+def torch_route(logits, k, renorm):
+    scores = torch.softmax(logits.float(), dim=-1)
+    w, ids = torch.topk(scores, k, dim=-1)
+    if renorm:
+        w = w / w.sum(-1, keepdim=True)
+    return w, ids
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: c.name)
+def test_ids_match_reference_golden(cuda_device, case):
+    hidden, logits, _, _ = make_inputs(case)
+    w, ids = fm.fused_topk(hidden.to(cuda_device), logits.to(cuda_device), case.k,
+                           case.renormalize)
+    want = torch.from_numpy(np.load(GOLDEN / f"{case.name}.npz")["topk_ids"])
+    assert torch.equal(ids.cpu(), want)
+
+
+@pytest.mark.parametrize("T,E,k,bias,renorm,dtype", [
+    (4096, 8, 2, 0.0, True, torch.float32),
+    (8192, 128, 8, 0.5, True, torch.float32),
+    (4096, 256, 8, 0.0, True, torch.float32),
+    (1000, 64, 6, 1.0, False, torch.float32),
+    (333, 1024, 8, 0.0, True, torch.float32),
+    (2048, 128, 8, 0.5, True, torch.bfloat16),
+    (1, 8, 2, 0.0, True, torch.float32),
+    (77, 40, 32, 0.0, True, torch.float32),
+])
+def test_matches_torch_routing(cuda_device, T, E, k, bias, renorm, dtype):
+    g = torch.Generator().manual_seed(T + E)
+    logits = torch.randn(T, E, generator=g) + torch.randn(E, generator=g) * bias
+    logits = logits.to(dtype).to(cuda_device)
+    hidden = torch.empty(T, 8, device=cuda_device)
+    w, ids = fm.fused_topk(hidden, logits, k, renorm)
+    rw, rids = torch_route(logits, k, renorm)
+    assert torch.equal(ids.long(), rids)
+    torch.testing.assert_close(w, rw, rtol=1e-5, atol=1e-6)
+
+
+def test_weights_in_activation_dtype_and_int64_ids(cuda_device):
+    logits = torch.randn(50, 16, device=cuda_device)
+    hidden = torch.empty(50, 8, device=cuda_device)
+    w, ids = fm.fused_topk(hidden, logits, 4, True, weights_dtype=torch.bfloat16,
+                           ids_dtype=torch.int64)
+    rw, rids = torch_route(logits, 4, True)
+    assert w.dtype == torch.bfloat16 and ids.dtype == torch.int64
+    assert torch.equal(ids, rids)
+    torch.testing.assert_close(w, rw.to(torch.bfloat16), rtol=8e-3, atol=1e-6)
+
+
+def test_ties_go_to_the_lower_expert(cuda_device):
+    logits = torch.zeros(3, 8, device=cuda_device)
+    logits[1, 5] = 1.0
+    hidden = torch.empty(3, 8, device=cuda_device)
+    _, ids = fm.fused_topk(hidden, logits, 3, True)
+    assert ids.cpu().tolist() == [[0, 1, 2], [5, 0, 1], [0, 1, 2]]
