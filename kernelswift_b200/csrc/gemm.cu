@@ -27,6 +27,7 @@
 // shared abort flag, every role leaves its loop, in-flight TMA loads and
 // MMAs are waited for, TMEM is freed and MOE_ERR_TIMEOUT is reported.
 #include <atomic>
+#include <type_traits>
 
 #include "common.cuh"
 #include "internal.h"
@@ -335,36 +336,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const float w =
             valid ? load_weight(p.row_weights, p.row_weights_dtype, r) : 0.0f;
-        float* out_row = static_cast<float*>(p.out) +
-                         (int64_t(c.ks) * p.numel + (valid ? r : 0)) * p.out_ld +
-                         c.nt * BN;
+        // weighted rows in fp32 (K-split partial sums) or the activation dtype
+        TOUT* out_row = static_cast<TOUT*>(p.out) +
+                        (int64_t(c.ks) * p.numel + (valid ? r : 0)) * p.out_ld + c.nt * BN;
 #pragma unroll 1
         for (int g = 0; g < BN / 16; ++g) {
           uint32_t v[16];
           tmem_ld16(tbase + g * 16, v);
           tmem_ld_wait();
           if (valid) {
-            float4* dst = reinterpret_cast<float4*>(out_row + g * 16);
+            float x[16];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              float x0 = acc_to_f32<KIND>(v[4 * j]);
-              float x1 = acc_to_f32<KIND>(v[4 * j + 1]);
-              float x2 = acc_to_f32<KIND>(v[4 * j + 2]);
-              float x3 = acc_to_f32<KIND>(v[4 * j + 3]);
+              float s4[4] = {w, w, w, w};
               if constexpr (kScaled) {
                 const float s = a_s * w;
                 const float4 b4 = __ldg(reinterpret_cast<const float4*>(bsc + g * 16) + j);
-                x0 *= s * b4.x;
-                x1 *= s * b4.y;
-                x2 *= s * b4.z;
-                x3 *= s * b4.w;
-              } else {
-                x0 *= w;
-                x1 *= w;
-                x2 *= w;
-                x3 *= w;
+                s4[0] = s * b4.x;
+                s4[1] = s * b4.y;
+                s4[2] = s * b4.z;
+                s4[3] = s * b4.w;
               }
-              dst[j] = make_float4(x0, x1, x2, x3);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) x[4 * j + q] = acc_to_f32<KIND>(v[4 * j + q]) * s4[q];
+            }
+            if constexpr (std::is_same<TOUT, float>::value) {
+              float4* dst = reinterpret_cast<float4*>(out_row + g * 16);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                dst[j] = make_uint4(pack2<TOUT>(x[8 * j], x[8 * j + 1]),
+                                    pack2<TOUT>(x[8 * j + 2], x[8 * j + 3]),
+                                    pack2<TOUT>(x[8 * j + 4], x[8 * j + 5]),
+                                    pack2<TOUT>(x[8 * j + 6], x[8 * j + 7]));
             }
           }
         }
@@ -884,7 +892,24 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   if (st != MOE_OK) return st;
   kp.out_ld = a.n;
   const int grid = sms;
+  KSW_REQUIRE(a.out_dtype == MOE_DTYPE_F32 || ((a.out_dtype == MOE_DTYPE_BF16 ||
+                                                  a.out_dtype == MOE_DTYPE_F16) &&
+                                                 kp.splits == 1 && !fp8),
+              MOE_ERR_UNSUPPORTED,
+              "down GEMM: 16-bit rows only without K split and without fp8");
   if (fp8) return dispatch_fp8<kEpiRows>(bn, ta, tb, kp, grid, s);
+  if (a.out_dtype == MOE_DTYPE_BF16) {
+    if (a.quant == MOE_QUANT_INT8_CHANNEL)
+      return dispatch_bn<kKindI8, 1, kEpiRows, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
+    if (a.compute_dtype == MOE_DTYPE_BF16)
+      return dispatch_bn<kKindF16, 1, kEpiRows, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
+    return fail(MOE_ERR_UNSUPPORTED, "down GEMM: bf16 rows need bf16 operands");
+  }
+  if (a.out_dtype == MOE_DTYPE_F16) {
+    if (a.quant == MOE_QUANT_NONE && a.compute_dtype == MOE_DTYPE_F16)
+      return dispatch_bn<kKindF16, 0, kEpiRows, __half>(bn, ta, tb, kp, grid, s);
+    return fail(MOE_ERR_UNSUPPORTED, "down GEMM: f16 rows need f16 operands");
+  }
   if (a.quant == MOE_QUANT_INT8_CHANNEL)
     return dispatch_bn<kKindI8, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s);
   if (a.compute_dtype == MOE_DTYPE_BF16)

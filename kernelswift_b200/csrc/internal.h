@@ -40,6 +40,7 @@ struct GroupedGemmArgs {
   const void* row_weights;     // down: [numel] weight of each flat row
   int row_weights_dtype;
   int splits;                  // down: K splits (partial sums summed later)
+  int out_dtype;               // down: rows dtype, F32 (0, default) or the 16-bit act dtype
   int32_t* status;
   int block_n;                 // 0 = heuristic
 };

@@ -31,6 +31,7 @@ struct Plan {
   int splits;            // down GEMM K splits
   int gu_splits;         // gate-up GEMM K splits (1: fused SiLU*up epilogue)
   int dn_bn, gu_bn;      // N tile widths
+  int part_dtype;        // dtype of the down GEMM's weighted rows
   size_t align_ws;
   size_t off_sorted, off_eids, off_npp, off_align, off_a, off_a_scale, off_act,
       off_act_q, off_act_scale, off_part, off_gu_part, total;
@@ -147,6 +148,13 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.dn_bn = dn.bn;
   P.gu_splits = gu.splits;
   P.gu_bn = gu.bn;
+  // Without a K split each weighted row is final: keep it in the 16-bit
+  // activation dtype (as base.py:72,75 does) and halve the row traffic;
+  // K-split partial sums and fp32 activations stay fp32.
+  P.part_dtype = MOE_DTYPE_F32;
+  if (P.splits == 1 && !fp8 && p->act_dtype == P.compute_dtype &&
+      (P.quant == MOE_QUANT_NONE || P.compute_dtype == MOE_DTYPE_BF16))
+    P.part_dtype = P.compute_dtype;
   P.align_ws = align_workspace_bytes(P.numel, P.E);
 
   size_t off = 0;
@@ -170,7 +178,7 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.off_act = take(size_t(P.L) * P.I * elem_bytes(P.act_dtype));
   P.off_act_q = take(P.quant != MOE_QUANT_NONE ? size_t(P.L) * P.I : 0);
   P.off_act_scale = take(scale_bytes(P.I));
-  P.off_part = take(size_t(P.splits) * P.numel * P.H * 4);
+  P.off_part = take(size_t(P.splits) * P.numel * P.H * elem_bytes(P.part_dtype));
   P.off_gu_part = take(P.gu_splits > 1 ? size_t(P.gu_splits) * P.numel * 2 * P.I * 4 : 0);
   P.total = off;
   return MOE_OK;
@@ -326,11 +334,13 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   gd.row_weights_dtype = p->weights_dtype;
   gd.splits = P.splits;
   gd.block_n = P.dn_bn;
+  gd.out_dtype = P.part_dtype;
   st = gemm_down_launch(gd, s);
   if (st != MOE_OK) return st;
 
   SumArgs sa{};
-  sa.part = at<float>(workspace, P.off_part);
+  sa.part = at<void>(workspace, P.off_part);
+  sa.part_dtype = P.part_dtype;
   sa.splits = P.splits;
   sa.T = P.T;
   sa.top_k = P.k;
@@ -436,6 +446,7 @@ int moe_sum_topk(const float* partial, int splits, int64_t num_tokens, int top_k
   if (st != MOE_OK) return st;
   SumArgs sa{};
   sa.part = partial;
+  sa.part_dtype = MOE_DTYPE_F32;
   sa.splits = splits;
   sa.T = num_tokens;
   sa.top_k = top_k;

@@ -223,9 +223,9 @@ __global__ void __launch_bounds__(kWarps * 32)
 }
 
 // ---------------- top-k (and K-split) reduction ----------------
-template <typename Tout, typename IdT>
+template <typename Tout, typename IdT, typename Tp>
 __global__ void __launch_bounds__(256)
-    sum_topk_kernel(const float* __restrict__ part, int splits, int64_t T,
+    sum_topk_kernel(const Tp* __restrict__ part, int splits, int64_t T,
                     int top_k, int64_t H, int64_t numel, const IdT* __restrict__ ids,
                     int E, Tout* __restrict__ out) {
   const int64_t vec_per_row = H / 8;
@@ -401,21 +401,28 @@ int sum_topk_launch(const SumArgs& a, cudaStream_t s) {
   KSW_REQUIRE(a.part && a.out, MOE_ERR_INVALID_ARG, "sum_topk: null pointer");
   KSW_REQUIRE(a.H % 8 == 0, MOE_ERR_UNSUPPORTED, "sum_topk: H % 8 != 0");
   KSW_REQUIRE(a.splits >= 1 && a.top_k >= 1, MOE_ERR_INVALID_ARG, "sum_topk: bad sizes");
+  KSW_REQUIRE(a.part_dtype == MOE_DTYPE_F32 || a.part_dtype == a.out_dtype, MOE_ERR_UNSUPPORTED,
+              "sum_topk: partial rows must be f32 or the output dtype");
   if (a.T == 0) return MOE_OK;
   const int64_t total = a.T * (a.H / 8);
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 148 * 32)));
   const int64_t numel = a.T * a.top_k;
-#define KSW_SUM(TOUT, IDT)                                                             \
-  sum_topk_kernel<TOUT, IDT><<<grid, 256, 0, s>>>(a.part, a.splits, a.T, a.top_k, a.H, \
-                                                   numel, static_cast<const IDT*>(a.ids), \
-                                                   a.E, static_cast<TOUT*>(a.out))
+#define KSW_SUM(TOUT, IDT)                                                                   \
+  if (a.part_dtype == MOE_DTYPE_F32)                                                         \
+    sum_topk_kernel<TOUT, IDT, float><<<grid, 256, 0, s>>>(                                  \
+        static_cast<const float*>(a.part), a.splits, a.T, a.top_k, a.H, numel,               \
+        static_cast<const IDT*>(a.ids), a.E, static_cast<TOUT*>(a.out));                     \
+  else                                                                                       \
+    sum_topk_kernel<TOUT, IDT, TOUT><<<grid, 256, 0, s>>>(                                   \
+        static_cast<const TOUT*>(a.part), a.splits, a.T, a.top_k, a.H, numel,                \
+        static_cast<const IDT*>(a.ids), a.E, static_cast<TOUT*>(a.out))
   const bool i64 = a.ids_dtype == MOE_DTYPE_I64;
   if (a.out_dtype == MOE_DTYPE_BF16) {
-    if (i64) KSW_SUM(__nv_bfloat16, int64_t); else KSW_SUM(__nv_bfloat16, int32_t);
+    if (i64) { KSW_SUM(__nv_bfloat16, int64_t); } else { KSW_SUM(__nv_bfloat16, int32_t); }
   } else if (a.out_dtype == MOE_DTYPE_F16) {
-    if (i64) KSW_SUM(__half, int64_t); else KSW_SUM(__half, int32_t);
+    if (i64) { KSW_SUM(__half, int64_t); } else { KSW_SUM(__half, int32_t); }
   } else if (a.out_dtype == MOE_DTYPE_F32) {
-    if (i64) KSW_SUM(float, int64_t); else KSW_SUM(float, int32_t);
+    if (i64) { KSW_SUM(float, int64_t); } else { KSW_SUM(float, int32_t); }
   } else {
     return fail(MOE_ERR_UNSUPPORTED, "sum_topk: unsupported output dtype");
   }

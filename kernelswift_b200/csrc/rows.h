@@ -25,7 +25,8 @@ struct GatherArgs {
 };
 
 struct SumArgs {
-  const float* part;            // [splits, T*top_k, H]
+  const void* part;             // [splits, T*top_k, H] in part_dtype
+  int part_dtype;               // F32, or the output dtype
   int splits;
   int64_t T;
   int top_k;

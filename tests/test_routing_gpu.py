@@ -29,25 +29,52 @@ def test_ids_match_reference_golden(cuda_device, case):
     assert torch.equal(ids.cpu(), want)
 
 
-@pytest.mark.parametrize("T,E,k,bias,renorm,dtype", [
-    (4096, 8, 2, 0.0, True, torch.float32),
-    (8192, 128, 8, 0.5, True, torch.float32),
-    (4096, 256, 8, 0.0, True, torch.float32),
-    (1000, 64, 6, 1.0, False, torch.float32),
-    (333, 1024, 8, 0.0, True, torch.float32),
-    (2048, 128, 8, 0.5, True, torch.bfloat16),
-    (1, 8, 2, 0.0, True, torch.float32),
-    (77, 40, 32, 0.0, True, torch.float32),
+@pytest.mark.parametrize("T,E,k,bias,renorm", [
+    (4096, 8, 2, 0.0, True),
+    (8192, 128, 8, 0.5, True),
+    (4096, 256, 8, 0.0, True),
+    (1000, 64, 6, 1.0, False),
+    (333, 1024, 8, 0.0, True),
+    (1, 8, 2, 0.0, True),
+    (77, 40, 32, 0.0, True),
 ])
-def test_matches_torch_routing(cuda_device, T, E, k, bias, renorm, dtype):
+def test_matches_torch_routing_fp32_logits(cuda_device, T, E, k, bias, renorm):
+    """fp32 logits (no exact ties): ids bit-identical to torch.topk."""
     g = torch.Generator().manual_seed(T + E)
-    logits = torch.randn(T, E, generator=g) + torch.randn(E, generator=g) * bias
-    logits = logits.to(dtype).to(cuda_device)
+    logits = (torch.randn(T, E, generator=g) + torch.randn(E, generator=g) * bias).to(cuda_device)
     hidden = torch.empty(T, 8, device=cuda_device)
     w, ids = fm.fused_topk(hidden, logits, k, renorm)
     rw, rids = torch_route(logits, k, renorm)
     assert torch.equal(ids.long(), rids)
     torch.testing.assert_close(w, rw, rtol=1e-5, atol=1e-6)
+
+
+def test_bf16_logits_with_exact_ties(cuda_device):
+    """bf16 logits tie exactly and often; torch.topk leaves the order of tied
+    values unspecified. Ours must be a valid top-k (every selected logit >=
+    every unselected one), in descending order with ties to the lower index,
+    and its weights equal torch's position by position (tied experts have
+    equal weights)."""
+    T, E, k = 2048, 128, 8
+    g = torch.Generator().manual_seed(5)
+    logits = (torch.randn(T, E, generator=g) + torch.randn(E, generator=g) * 0.5)
+    logits = logits.to(torch.bfloat16).to(cuda_device)
+    hidden = torch.empty(T, 8, device=cuda_device)
+    w, ids = fm.fused_topk(hidden, logits, k, True)
+    rw, rids = torch_route(logits, k, True)
+    lf = logits.float()
+    sel = torch.gather(lf, 1, ids.long())
+    mask = torch.ones_like(lf, dtype=torch.bool)
+    mask.scatter_(1, ids.long(), False)
+    unsel_max = torch.where(mask, lf, torch.full_like(lf, -float("inf"))).amax(1)
+    assert bool((sel.min(1).values >= unsel_max).all())
+    assert bool((sel[:, :-1] >= sel[:, 1:]).all())
+    tie = sel[:, :-1] == sel[:, 1:]
+    assert bool((ids[:, :-1][tie] < ids[:, 1:][tie]).all())
+    torch.testing.assert_close(w, rw, rtol=1e-5, atol=1e-6)
+    # the tie-free rows agree with torch exactly
+    no_tie = ~(sel[:, :-1] == sel[:, 1:]).any(1) & (sel[:, -1] > unsel_max)
+    assert torch.equal(ids.long()[no_tie], rids[no_tie])
 
 
 def test_weights_in_activation_dtype_and_int64_ids(cuda_device):
