@@ -54,6 +54,9 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (0 = workload default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="time CUDA-graph replays of the whole forward (1 GPU; the per-kernel "
+                         "breakdown still comes from an instrumented non-graph pass)")
     ap.add_argument("--heat-seconds", type=float, default=1.0,
                     help="untimed busy period before timing, so clock samples see a loaded GPU")
     return ap.parse_args()
@@ -264,8 +267,8 @@ def main():
         prep = model.prepared(torch.bfloat16, quant)
 
         def step(stage_arr=None):
-            tw, ti = fm.fused_topk(hidden, logits, k)
-            return fm.fused_experts(hidden, prep, None, tw.to(hidden.dtype), ti,
+            tw, ti = fm.fused_topk(hidden, logits, k, weights_dtype=hidden.dtype)
+            return fm.fused_experts(hidden, prep, None, tw, ti,
                                     use_fp8_w8a8=quant == "fp8", use_int8_w8a8=quant == "int8",
                                     stage_events=stage_arr)
     else:
@@ -282,8 +285,8 @@ def main():
         del w1, w2
 
         def step(stage_arr=None):
-            tw, ti = fm.fused_topk(hidden, logits, k)
-            out = ep(hidden, tw.to(hidden.dtype), ti, stage_events=stage_arr)
+            tw, ti = fm.fused_topk(hidden, logits, k, weights_dtype=hidden.dtype)
+            out = ep(hidden, tw, ti, stage_events=stage_arr)
             rows_per_launch[0] = ep.last_rows_received
             return out
 
@@ -344,6 +347,27 @@ def main():
     total_ms = sum(step_ms)
     stage_ms = {name: sum(evs[j].elapsed_time(evs[j + 1]) for evs in stage_evs) / K
                 for j, name in enumerate(_lib.STAGES)}
+    use_graph = args.graph and world == 1
+    graph = None
+    if use_graph:
+        def graph_fn(hd, ld):
+            tw, ti = fm.fused_topk(hd, ld, k, weights_dtype=hd.dtype)
+            return fm.fused_experts(hd, prep, None, tw, ti, use_fp8_w8a8=quant == "fp8",
+                                    use_int8_w8a8=quant == "int8")
+
+        graph = fm.CapturedMoE(graph_fn, T, H, E, dtype=torch.bfloat16, device=dev)
+        graph.hidden.copy_(hidden)
+        graph.logits.copy_(logits)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        for i in range(K):
+            flush.zero_()
+            starts[i].record()
+            graph.replay()
+            ends[i].record()
+        torch.cuda.synchronize()
+        total_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -360,14 +384,17 @@ def main():
         out_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
         h_dev = torch.empty_like(hidden)
         l_dev = torch.empty_like(logits)
-        if world == 1 and quant == "none":
+        if use_graph:
+            def model_call(hd, ld):
+                return graph(hd, ld)
+        elif world == 1 and quant == "none":
             model_call = model
         else:
             def model_call(hd, ld):
-                tw, ti = fm.fused_topk(hd, ld, k)
+                tw, ti = fm.fused_topk(hd, ld, k, weights_dtype=hd.dtype)
                 if world > 1:
-                    return ep(hd, tw.to(hd.dtype), ti)
-                return fm.fused_experts(hd, prep, None, tw.to(hd.dtype), ti,
+                    return ep(hd, tw, ti)
+                return fm.fused_experts(hd, prep, None, tw, ti,
                                         use_fp8_w8a8=quant == "fp8",
                                         use_int8_w8a8=quant == "int8")
 
@@ -400,7 +427,8 @@ def main():
                "h2d_bytes_per_step": hidden.numel() * hidden.element_size()
                + logits.numel() * logits.element_size(),
                "d2h_bytes_per_step": T * H * 2,
-               "path": ("ModelNew.forward (drop-in module)" if world == 1 and quant == "none"
+               "path": ("CapturedMoE (CUDA graph of fused_topk + fused_experts)" if use_graph
+                        else "ModelNew.forward (drop-in module)" if world == 1 and quant == "none"
                         else "fused_topk + " + ("ExpertParallelMoE.forward" if world > 1
                                                 else "fused_experts"))
                + ", pinned host buffers"}
@@ -460,10 +488,11 @@ def main():
                          f"restated in torch-CPU bf16 with its per-call weight casts "
                          f"(median of {n} calls, {med:.2f} s each)"}
 
-    # our kernels per step: align (1 launch up to 8192 routed rows, else 3),
-    # gather, gate-up, [activation quant], down, top-k sum
+    # our kernels per step: routing, align (1 launch up to 8192 routed rows,
+    # else 3), gather, gate-up (+ swiglu_reduce when K-split), [activation
+    # quant], down, top-k sum
     numel = rows_per_launch[0]
-    launches_per_step = (1 if numel <= 8192 else 3) + 4 + (0 if quant == "none" else 1)
+    launches_per_step = 1 + (1 if numel <= 8192 else 3) + 4 + (0 if quant == "none" else 1)
     if world > 1:
         launches_per_step += 2  # pack rows by destination, weighted combine
     if rank == 0:
@@ -481,6 +510,7 @@ def main():
             "e2e": e2e,
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * K,
+            "cuda_graph": use_graph,
             "wall_s_timed": wall,
         }
         print(json.dumps(line), flush=True)

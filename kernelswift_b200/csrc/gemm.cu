@@ -10,15 +10,16 @@
 // where m runs over the rows of the expert-sorted operand, r = sorted_ids[m]
 // is the flat (token, slot) index and e = expert_ids[m / 128].
 //
-// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+// CTA layout (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A tile [128 x 128 B] + B tile [BN x 128 B] per
 //               k-block into a STAGES-deep shared-memory ring.
 //   warp 1      allocates 2*BN TMEM columns; lane 0 issues tcgen05.mma
 //               (M=128, N=BN, 4 MMAs per 128-byte k-block) into one of two
 //               accumulator buffers, so the epilogue of tile i overlaps the
 //               main loop of tile i+1.
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 16 columns at a time, fused
-//               math, 16-byte stores to global memory.
+//   warps 2..9  epilogue: warp w reads TMEM lane quarter w % 4 and column
+//               half (w - 2) / 4, several 32-lane x 16-column tcgen05.ld per
+//               wait, fused math, 16-byte stores to global memory.
 // Tiles are (m-block, n-tile, k-split) triples handed out round-robin; within
 // a group of 8 m-blocks the n-tile index varies slowest, so the CTAs running
 // at the same time share weight tiles through L2.
@@ -39,7 +40,7 @@ namespace {
 constexpr int BM = kBlockM;          // rows per tile (TMEM lanes)
 constexpr int kKBytes = 128;         // bytes of K per k-block (one swizzle row)
 constexpr int kABytes = BM * kKBytes;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 constexpr int kGroupM = 8;
 
 enum Epi : int { kEpiSwiGLU = 0, kEpiRows = 1 };
@@ -159,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 256);
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
@@ -268,8 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int no_abort = 0;
     mbar_wait_bounded(final_bar, 0, &no_abort, limit);
   } else if (warp >= 2) {
-    // ---------------- epilogue ----------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // ---------------- epilogue (8 warps) ----------------
+    // warp w (2..9) reads TMEM lane quarter w % 4 and column half (w - 2) / 4
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -291,88 +294,106 @@ __global__ void __launch_bounds__(kThreads, 1)
           kScaled ? p.b_scale + int64_t(e) * p.n_total + c.nt * BN : nullptr;
 
       if constexpr (EPI == kEpiSwiGLU) {
+        constexpr int G_HALF = BN / 64;              // 32-column groups per half
+        constexpr int GPI = G_HALF >= 2 ? 2 : 1;     // groups per TMEM wait
         TOUT* out_row = static_cast<TOUT*>(p.out) + int64_t(m) * p.out_ld +
                         c.nt * (BN / 2);
 #pragma unroll 1
-        for (int g = 0; g < BN / 32; ++g) {
-          uint32_t gv[16], uv[16];
-          tmem_ld16(tbase + g * 32, gv);
-          tmem_ld16(tbase + g * 32 + 16, uv);
+        for (int gg = 0; gg < G_HALF; gg += GPI) {
+          uint32_t gv[GPI][16], uv[GPI][16];
+#pragma unroll
+          for (int u = 0; u < GPI; ++u) {
+            const int g = h * G_HALF + gg + u;
+            tmem_ld16(tbase + g * 32, gv[u]);
+            tmem_ld16(tbase + g * 32 + 16, uv[u]);
+          }
           tmem_ld_wait();
           if (valid) {
-            float gs[16], us[16];
-            if constexpr (kScaled) {
-              // per-column weight scales of this 32-column group, times the row scale
-              const float4* sg = reinterpret_cast<const float4*>(bsc + g * 32);
 #pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) {
-                const float4 a4 = __ldg(sg + q4), b4 = __ldg(sg + 4 + q4);
-                gs[4 * q4] = a_s * a4.x; gs[4 * q4 + 1] = a_s * a4.y;
-                gs[4 * q4 + 2] = a_s * a4.z; gs[4 * q4 + 3] = a_s * a4.w;
-                us[4 * q4] = a_s * b4.x; us[4 * q4 + 1] = a_s * b4.y;
-                us[4 * q4 + 2] = a_s * b4.z; us[4 * q4 + 3] = a_s * b4.w;
-              }
-            }
-            uint32_t packed[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float g0 = acc_to_f32<KIND>(gv[2 * j]);
-              float g1 = acc_to_f32<KIND>(gv[2 * j + 1]);
-              float u0 = acc_to_f32<KIND>(uv[2 * j]);
-              float u1 = acc_to_f32<KIND>(uv[2 * j + 1]);
+            for (int u = 0; u < GPI; ++u) {
+              const int g = h * G_HALF + gg + u;
+              float gs[16], us[16];
               if constexpr (kScaled) {
-                g0 *= gs[2 * j];
-                g1 *= gs[2 * j + 1];
-                u0 *= us[2 * j];
-                u1 *= us[2 * j + 1];
+                // per-column weight scales of this 32-column group, times the row scale
+                const float4* sg = reinterpret_cast<const float4*>(bsc + g * 32);
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                  const float4 a4 = __ldg(sg + q4), b4 = __ldg(sg + 4 + q4);
+                  gs[4 * q4] = a_s * a4.x; gs[4 * q4 + 1] = a_s * a4.y;
+                  gs[4 * q4 + 2] = a_s * a4.z; gs[4 * q4 + 3] = a_s * a4.w;
+                  us[4 * q4] = a_s * b4.x; us[4 * q4 + 1] = a_s * b4.y;
+                  us[4 * q4 + 2] = a_s * b4.z; us[4 * q4 + 3] = a_s * b4.w;
+                }
               }
-              packed[j] = pack2<TOUT>(silu_mul(g0, u0), silu_mul(g1, u1));
+              uint32_t packed[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float g0 = acc_to_f32<KIND>(gv[u][2 * j]);
+                float g1 = acc_to_f32<KIND>(gv[u][2 * j + 1]);
+                float u0 = acc_to_f32<KIND>(uv[u][2 * j]);
+                float u1 = acc_to_f32<KIND>(uv[u][2 * j + 1]);
+                if constexpr (kScaled) {
+                  g0 *= gs[2 * j];
+                  g1 *= gs[2 * j + 1];
+                  u0 *= us[2 * j];
+                  u1 *= us[2 * j + 1];
+                }
+                packed[j] = pack2<TOUT>(silu_mul(g0, u0), silu_mul(g1, u1));
+              }
+              uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
+              dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+              dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
             }
-            uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
-            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
           }
         }
       } else {
+        constexpr int C_HALF = BN / 32;              // 16-column chunks per half
+        constexpr int CPI = C_HALF >= 4 ? 4 : C_HALF;  // chunks per TMEM wait
         const float w =
             valid ? load_weight(p.row_weights, p.row_weights_dtype, r) : 0.0f;
         // weighted rows in fp32 (K-split partial sums) or the activation dtype
         TOUT* out_row = static_cast<TOUT*>(p.out) +
                         (int64_t(c.ks) * p.numel + (valid ? r : 0)) * p.out_ld + c.nt * BN;
 #pragma unroll 1
-        for (int g = 0; g < BN / 16; ++g) {
-          uint32_t v[16];
-          tmem_ld16(tbase + g * 16, v);
+        for (int cc = 0; cc < C_HALF; cc += CPI) {
+          uint32_t v[CPI][16];
+#pragma unroll
+          for (int u = 0; u < CPI; ++u) tmem_ld16(tbase + (h * C_HALF + cc + u) * 16, v[u]);
           tmem_ld_wait();
           if (valid) {
-            float x[16];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float s4[4] = {w, w, w, w};
-              if constexpr (kScaled) {
-                const float s = a_s * w;
-                const float4 b4 = __ldg(reinterpret_cast<const float4*>(bsc + g * 16) + j);
-                s4[0] = s * b4.x;
-                s4[1] = s * b4.y;
-                s4[2] = s * b4.z;
-                s4[3] = s * b4.w;
+            for (int u = 0; u < CPI; ++u) {
+              const int g = h * C_HALF + cc + u;
+              float x[16];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float s4[4] = {w, w, w, w};
+                if constexpr (kScaled) {
+                  const float s = a_s * w;
+                  const float4 b4 = __ldg(reinterpret_cast<const float4*>(bsc + g * 16) + j);
+                  s4[0] = s * b4.x;
+                  s4[1] = s * b4.y;
+                  s4[2] = s * b4.z;
+                  s4[3] = s * b4.w;
+                }
+#pragma unroll
+                for (int q2 = 0; q2 < 4; ++q2)
+                  x[4 * j + q2] = acc_to_f32<KIND>(v[u][4 * j + q2]) * s4[q2];
               }
+              if constexpr (std::is_same<TOUT, float>::value) {
+                float4* dst = reinterpret_cast<float4*>(out_row + g * 16);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) x[4 * j + q] = acc_to_f32<KIND>(v[4 * j + q]) * s4[q];
-            }
-            if constexpr (std::is_same<TOUT, float>::value) {
-              float4* dst = reinterpret_cast<float4*>(out_row + g * 16);
+                for (int j = 0; j < 4; ++j)
+                  dst[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+              } else {
+                uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                dst[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
-            } else {
-              uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
-#pragma unroll
-              for (int j = 0; j < 2; ++j)
-                dst[j] = make_uint4(pack2<TOUT>(x[8 * j], x[8 * j + 1]),
-                                    pack2<TOUT>(x[8 * j + 2], x[8 * j + 3]),
-                                    pack2<TOUT>(x[8 * j + 4], x[8 * j + 5]),
-                                    pack2<TOUT>(x[8 * j + 6], x[8 * j + 7]));
+                for (int j = 0; j < 2; ++j)
+                  dst[j] = make_uint4(pack2<TOUT>(x[8 * j], x[8 * j + 1]),
+                                      pack2<TOUT>(x[8 * j + 2], x[8 * j + 3]),
+                                      pack2<TOUT>(x[8 * j + 4], x[8 * j + 5]),
+                                      pack2<TOUT>(x[8 * j + 6], x[8 * j + 7]));
+              }
             }
           }
         }

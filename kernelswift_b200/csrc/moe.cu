@@ -54,22 +54,27 @@ int64_t est_m_blocks(int64_t numel, int64_t L, int E) {
   return std::min<int64_t>(L / kBlockM, numel / kBlockM + std::min<int64_t>(E, numel));
 }
 
-// Tile width and K split of one grouped GEMM with `n` output columns and
-// `k_blocks` 128-byte k-blocks over `mb` m-blocks. Model: a CTA's time per
-// tile is proportional to the bytes it streams, (BN + 32) / S (the +32
-// stands for the A tile, read from L2), and the kernel takes
-// ceil(tiles / SMs) such waves; each extra split costs 2 % for its partial
-// sums. Wide tiles win ties (less A traffic, fewer partials).
+// Tile width and K split of one grouped GEMM with `n` output columns, a
+// reduction of `k_bytes` bytes per row and `rows` routed rows over `mb`
+// m-blocks. Cost model in bytes moved at the whole-GPU rate:
+//   waves * per-tile bytes * sms, per-tile bytes = (BN + 32) * k_bytes / S
+// (a CTA streams its B tile, BN rows, plus the A tile, counted as 32 rows
+// since it mostly hits L2, over its 1/S share of K; the kernel takes
+// ceil(tiles * S / sms) such waves, each with a fixed start-up cost of about
+// a microsecond of streaming, 48 KB), plus the split's extra traffic: S fp32
+// partial rows written and read back instead of one 16-bit row
+// ((8*S - 4) * rows * n bytes; S = 1 costs nothing extra).
 struct Tiling {
   int bn;
   int splits;
 };
 
-Tiling choose_tiling(int64_t mb, int64_t n, int64_t k_blocks, int sms, bool allow_split,
-                     bool allow64) {
+Tiling choose_tiling(int64_t mb, int64_t rows, int64_t n, int64_t k_bytes, int sms,
+                     bool allow_split, bool allow64) {
   Tiling best{0, 1};
   double best_cost = 1e300;
   mb = std::max<int64_t>(mb, 1);
+  const int64_t k_blocks = ceil_div(k_bytes, 128);
   for (int bn : {256, 128, 64}) {
     if (n % bn != 0 || (bn == 64 && !allow64)) continue;
     const int64_t tiles = mb * (n / bn);
@@ -79,7 +84,9 @@ Tiling choose_tiling(int64_t mb, int64_t n, int64_t k_blocks, int sms, bool allo
       const int64_t per = ceil_div(k_blocks, s);
       if (ceil_div(k_blocks, per) != s) continue;  // a split would be empty
       const double waves = double(ceil_div(tiles * s, sms));
-      const double cost = waves * double(bn + 32) / double(s) * (1.0 + 0.02 * double(s - 1));
+      double cost =
+          waves * (double(bn + 32) * double(k_bytes) / double(s) + 48.0 * 1024.0) * double(sms);
+      if (s > 1) cost += double(8 * s - 4) * double(rows) * double(n);
       if (cost < best_cost * 0.999) {
         best_cost = cost;
         best = Tiling{bn, int(s)};
@@ -138,10 +145,10 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   }
   const int64_t est_mb = est_m_blocks(P.numel, P.L, P.E);
   const bool fp8 = P.quant == MOE_QUANT_FP8_BLOCK;
-  const Tiling dn = choose_tiling(est_mb, P.H, ceil_div(P.I * kbpe, 128), sms, true, !fp8);
+  const Tiling dn = choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !fp8);
   // the split gate-up path has no fp8 epilogue (its block scales follow the
   // regrouped gate/up rows); fp8 keeps the fused SiLU*up epilogue
-  const Tiling gu = choose_tiling(est_mb, 2 * P.I, ceil_div(P.H * kbpe, 128), sms, !fp8, !fp8);
+  const Tiling gu = choose_tiling(est_mb, P.numel, 2 * P.I, P.H * kbpe, sms, !fp8, !fp8);
   KSW_REQUIRE(dn.bn > 0 && gu.bn > 0, MOE_ERR_UNSUPPORTED,
               "hidden size and 2*intermediate size must be multiples of 64 (128 for fp8)");
   P.splits = dn.splits;

@@ -84,21 +84,26 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Quantisation arithmetic shared with the oracle: scale = absmax / qmax
-// (1 when the group is all zero), q = clamp(x / scale, -qmax, qmax) rounded
-// to nearest-even in the target format.
+// Activation quantisation arithmetic (the oracle's quant_fp8_group /
+// quant_int8_rows restate it): scale = absmax / qmax (1 when the group is all
+// zero), inv = 1 / scale (one IEEE division per group),
+// q = clamp(x * inv, -qmax, qmax) rounded to nearest-even in the target
+// format. Multiplying by the reciprocal keeps the per-element work to a
+// multiply, a clamp and a conversion, which these HBM-bound kernels need.
 __device__ __forceinline__ float quant_scale(float absmax, float qmax) {
   const float s = absmax / qmax;
   return s > 0.0f ? s : 1.0f;
 }
 
-__device__ __forceinline__ uint8_t to_e4m3(float x, float scale) {
-  const float q = fminf(fmaxf(x / scale, -kFp8Max), kFp8Max);
-  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3));
+// Two values -> two e4m3 bytes (low byte = first value).
+__device__ __forceinline__ uint32_t to_e4m3x2(float x0, float x1, float inv) {
+  const float q0 = fminf(fmaxf(x0 * inv, -kFp8Max), kFp8Max);
+  const float q1 = fminf(fmaxf(x1 * inv, -kFp8Max), kFp8Max);
+  return uint32_t(__nv_cvt_float2_to_fp8x2(make_float2(q0, q1), __NV_SATFINITE, __NV_E4M3));
 }
 
-__device__ __forceinline__ int8_t to_i8(float x, float scale) {
-  const float q = fminf(fmaxf(x / scale, -kInt8Max), kInt8Max);
+__device__ __forceinline__ int8_t to_i8(float x, float inv) {
+  const float q = fminf(fmaxf(x * inv, -kInt8Max), kInt8Max);
   return static_cast<int8_t>(__float2int_rn(q));
 }
 
@@ -139,13 +144,9 @@ __global__ void __launch_bounds__(kWarps * 32)
 // sources); 16 lanes cover one 128-column group, so the group's absmax is a
 // 16-lane shuffle reduction. Requires H % 8 == 0 (checked on the host); a
 // partial last group is handled by masking lanes past H.
-__device__ __forceinline__ uint2 pack_e4m3x8(const float (&v)[8], float sc) {
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    lo |= uint32_t(to_e4m3(v[i], sc)) << (8 * i);
-    hi |= uint32_t(to_e4m3(v[4 + i], sc)) << (8 * i);
-  }
+__device__ __forceinline__ uint2 pack_e4m3x8(const float (&v)[8], float inv) {
+  const uint32_t lo = to_e4m3x2(v[0], v[1], inv) | (to_e4m3x2(v[2], v[3], inv) << 16);
+  const uint32_t hi = to_e4m3x2(v[4], v[5], inv) | (to_e4m3x2(v[6], v[7], inv) << 16);
   return make_uint2(lo, hi);
 }
 
@@ -177,7 +178,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float sc = quant_scale(amax, kFp8Max);
-      if (in) *reinterpret_cast<uint2*>(dst + m * H + h) = pack_e4m3x8(v, sc);
+      const float inv = 1.0f / sc;
+      if (in) *reinterpret_cast<uint2*>(dst + m * H + h) = pack_e4m3x8(v, inv);
       if (in && (lane & 15) == 0) scale[m * groups + g] = sc;
     }
   }
@@ -207,14 +209,15 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
     amax = warp_max(amax);
     const float sc = quant_scale(amax, kInt8Max);
+    const float inv = 1.0f / sc;
     for (int64_t h = int64_t(lane) * 8; h < H; h += 32 * 8) {
       float v[8];
       load8(s + h, v);
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        lo |= uint32_t(uint8_t(to_i8(v[i], sc))) << (8 * i);
-        hi |= uint32_t(uint8_t(to_i8(v[4 + i], sc))) << (8 * i);
+        lo |= uint32_t(uint8_t(to_i8(v[i], inv))) << (8 * i);
+        hi |= uint32_t(uint8_t(to_i8(v[4 + i], inv))) << (8 * i);
       }
       *reinterpret_cast<uint2*>(dst + m * H + h) = make_uint2(lo, hi);
     }

@@ -70,16 +70,25 @@ def _contig(t: torch.Tensor) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 _ws_lock = threading.Lock()
 _ws: dict[tuple[int, int], torch.Tensor] = {}
+# buffers replaced after a CUDA graph captured them: a graph keeps using the
+# addresses it recorded, so these stay allocated for the life of the process
+_ws_captured: list[torch.Tensor] = []
+_ws_in_graph: set[int] = set()
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     key = (device.index if device.index is not None else torch.cuda.current_device(),
            torch.cuda.current_stream(device).cuda_stream)
+    capturing = torch.cuda.is_current_stream_capturing()
     with _ws_lock:
         buf = _ws.get(key)
         if buf is None or buf.numel() < nbytes:
+            if buf is not None and buf.data_ptr() in _ws_in_graph:
+                _ws_captured.append(buf)
             buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
             _ws[key] = buf
+        if capturing:
+            _ws_in_graph.add(buf.data_ptr())
         return buf
 
 
@@ -406,3 +415,46 @@ class ModelNew(nn.Module):
                                             weights_dtype=hidden.dtype)
         return fused_experts(hidden, self.prepared(hidden.dtype), None, topk_weights, topk_ids,
                              out=out)
+
+
+# ---------------------------------------------------------------------------
+# CUDA-graph capture for a fixed token count (decode loops)
+# ---------------------------------------------------------------------------
+
+class CapturedMoE:
+    """Routing + fused experts for a fixed token count, captured once in a CUDA
+    graph and replayed: one graph launch instead of 6-8 kernel launches, which
+    is what bounds decode-sized batches.
+
+    `fn(hidden, logits) -> out` is the forward to capture (e.g. a ModelNew);
+    it must not synchronise the host. Inputs are copied into static buffers
+    (`hidden`, `logits` attributes; write them directly to skip the copies);
+    the returned tensor is the static output buffer, overwritten by the next
+    replay.
+    """
+
+    def __init__(self, fn, num_tokens: int, hidden_size: int, num_experts: int,
+                 dtype: torch.dtype = torch.bfloat16, device=None, warmup: int = 2):
+        dev = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.fn = fn
+        self.hidden = torch.zeros(num_tokens, hidden_size, dtype=dtype, device=dev)
+        self.logits = torch.zeros(num_tokens, num_experts, dtype=torch.float32, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.no_grad():
+            for _ in range(warmup):  # one-time setup (weights, attributes) off the capture
+                fn(self.hidden, self.logits)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.no_grad():
+            self.out = fn(self.hidden, self.logits)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
+
+    def __call__(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        self.hidden.copy_(hidden_states, non_blocking=True)
+        self.logits.copy_(router_logits, non_blocking=True)
+        return self.replay()

@@ -27,8 +27,11 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixtral")
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--experts", type=int, default=0,
+                    help="override the expert count (a smaller capture of the same kernel)")
     args = ap.parse_args()
     H, I, E, k, quant, bias = WORKLOADS[args.workload]
+    E = args.experts or E
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     hidden = torch.randn(args.tokens, H, generator=g, device=dev).to(torch.bfloat16)

@@ -173,3 +173,38 @@ def test_bounded_wait_reports_timeout(cuda_device):
     assert int(status.item()) == 0  # reset
     x = torch.ones(16, device=cuda_device)
     assert float((x * 2).sum()) == 32.0
+
+
+@pytest.mark.parametrize("quant", ["fp8", "int8"])
+@pytest.mark.parametrize("H", [256, 7168, 320])
+def test_gather_quantisers_bit_exact(cuda_device, quant, H):
+    """The gather's per-token quantisation equals the oracle's activation
+    quantiser bit for bit (fp8: per 128 columns, int8: per row)."""
+    T, E, k = 37, 8, 2
+    hidden, _, _, _, ids = setup(T, H, 64, E, k, seed=H)
+    sorted_ids, expert_ids, npp = fm.moe_align_block_size(ids, 128, E)
+    L = sorted_ids.numel()
+    numel = ids.numel()
+    if quant == "fp8":
+        dst = torch.zeros(L, H, dtype=torch.uint8, device=cuda_device)
+        scale = torch.zeros(L, -(-H // 128), device=cuda_device)
+        code = _lib.QUANT_FP8_BLOCK
+    else:
+        dst = torch.zeros(L, H, dtype=torch.int8, device=cuda_device)
+        scale = torch.zeros(L, device=cuda_device)
+        code = _lib.QUANT_INT8_CHANNEL
+    _lib.call("moe_gather_rows", p(hidden), _lib.DT_BF16, T, H, k, p(sorted_ids), p(npp), L,
+              numel, code, p(dst), _lib.DT_E4M3 if quant == "fp8" else _lib.DT_I8, p(scale),
+              stream())
+    torch.cuda.synchronize()
+    s = sorted_ids.cpu()
+    n = int(npp.item())
+    valid = (s[:n] < numel).nonzero().view(-1)
+    rows = hidden.cpu()[s[valid] // k]
+    if quant == "fp8":
+        q, sc = orc.quant_fp8_group(rows)
+        assert torch.equal(dst.cpu()[valid], q.view(torch.uint8))
+    else:
+        q, sc = orc.quant_int8_rows(rows, reciprocal=True)
+        assert torch.equal(dst.cpu()[valid], q)
+    assert torch.equal(scale.cpu()[valid], sc)
