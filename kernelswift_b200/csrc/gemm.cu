@@ -420,16 +420,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 //
 // The scales change every 128 elements of K (per token for A, per 128x128
 // block for B), so the products of one k-block cannot be summed in TMEM
-// across k-blocks. Each k-block is accumulated into a fresh TMEM buffer
-// (two buffers, so the MMAs of k-block kb+1 overlap the promotion of kb) and
+// across k-blocks. Each k-block is accumulated into a fresh TMEM buffer and
 // eight epilogue warps promote it into fp32 registers:
 //   acc[m, n] += a_scale[m, kb] * b_scale[e, n / 128, kb] * P_kb[m, n]
-// Warp w (2..9) owns TMEM lane quarter w % 4 and column half (w - 2) / 4.
+// TMEM holds 512 / BN such buffers (4 at BN = 128), so the MMAs of the next
+// k-blocks run while one is promoted; each epilogue warp copies its columns
+// out with one wait per 64 columns and releases the buffer before doing the
+// arithmetic, which keeps the buffer hand-off shorter than an MMA.
+// Warp w (2..9) owns TMEM lane quarter w % 4 and column half (w - 2) / 4;
+// warps whose 32 rows are all padding skip the arithmetic.
 // After the last k-block the gate-up epilogue applies SiLU(gate)*up and
 // writes bf16 activations; the down epilogue scales by the top-k weight and
 // writes fp32 rows.
 // ---------------------------------------------------------------------------
 constexpr int kThreadsF8 = 320;
+
+template <int BN>
+struct Fp8Cfg {
+  static constexpr int kBufs = 512 / BN;                  // TMEM partial buffers
+  static constexpr int kHalf = BN / 2;                    // columns per epilogue warp
+  static constexpr int kBatch = kHalf > 64 ? 64 : kHalf;  // columns per TMEM wait
+};
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreadsF8, 1)
@@ -437,10 +448,13 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
                                 const __grid_constant__ CUtensorMap tmB,
                                 const KParams p) {
   using Cfg = GemmCfg<BN>;
+  using F = Fp8Cfg<BN>;
   constexpr int STAGES = Cfg::kStages;
+  constexpr int NBUF = F::kBufs;
+  constexpr int HALF = F::kHalf;
+  constexpr int BATCH = F::kBatch;
   constexpr uint32_t IDESC = make_idesc(1u, 0u, BM, BN);  // f32 <- e4m3 x e4m3
-  constexpr int HALF = BN / 2;
-  constexpr int CH = 32;  // columns per TMEM read chunk
+  static_assert(NBUF * BN == 512 && HALF % BATCH == 0 && BATCH % 16 == 0, "fp8 tiling");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -450,8 +464,8 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kBBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* final_bar = tempty + 2;
+  uint64_t* tempty = tfull + NBUF;
+  uint64_t* final_bar = tempty + NBUF;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -463,7 +477,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 256);
     }
@@ -472,7 +486,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -555,8 +569,10 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
           stage = 0;
           phase ^= 1u;
         }
-        pb ^= 1;
-        if (pb == 0) pphase ^= 1u;
+        if (++pb == NBUF) {
+          pb = 0;
+          pphase ^= 1u;
+        }
       }
     }
     tc_commit(final_bar);
@@ -580,6 +596,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
       const int m = c.mb * BM + row;
       const int r = __ldg(p.sorted_ids + m);
       const bool valid = r < p.numel;
+      const bool warp_live = __any_sync(0xffffffffu, valid);
       const int n0 = c.nt * BN + col0;  // first output column of this half
       int rb0, rb1;
       if constexpr (EPI == kEpiSwiGLU) {
@@ -608,22 +625,30 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
         const uint32_t tbase =
             tmem_base + (uint32_t(q * 32) << 16) + uint32_t(pb * BN + col0);
 #pragma unroll
-        for (int ch = 0; ch < HALF / CH; ++ch) {
-          uint32_t v[CH];
-          tmem_ld16(tbase + ch * CH, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-          tmem_ld16(tbase + ch * CH + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-          tmem_ld_wait();
+        for (int b0 = 0; b0 < HALF; b0 += BATCH) {
+          uint32_t v[BATCH];
 #pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            // a 32-column group holds 16 gate columns then 16 up columns
-            const float sc = (EPI == kEpiSwiGLU && j >= 16) ? s1 : s0;
-            acc[ch * CH + j] = fmaf(sc, __uint_as_float(v[j]), acc[ch * CH + j]);
+          for (int u = 0; u < BATCH / 16; ++u)
+            tmem_ld16(tbase + b0 + 16 * u, *reinterpret_cast<uint32_t(*)[16]>(&v[16 * u]));
+          tmem_ld_wait();
+          if (b0 + BATCH >= HALF) {
+            // every column of this buffer is in registers: hand it back
+            tc_fence_before();
+            mbar_arrive(&tempty[pb]);
+          }
+          if (warp_live) {
+#pragma unroll
+            for (int j = 0; j < BATCH; ++j) {
+              // a 32-column group holds 16 gate columns then 16 up columns
+              const float sc = (EPI == kEpiSwiGLU && ((b0 + j) & 31) >= 16) ? s1 : s0;
+              acc[b0 + j] = fmaf(sc, __uint_as_float(v[j]), acc[b0 + j]);
+            }
           }
         }
-        tc_fence_before();
-        mbar_arrive(&tempty[pb]);
-        pb ^= 1;
-        if (pb == 0) pphase ^= 1u;
+        if (++pb == NBUF) {
+          pb = 0;
+          pphase ^= 1u;
+        }
       }
       if (aborted || !valid) continue;
       if constexpr (EPI == kEpiSwiGLU) {
@@ -657,7 +682,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    tmem_dealloc(tmem_base, 512);
   }
   if (threadIdx.x == 0 && *abort_flag) report_status(p.status, MOE_ERR_TIMEOUT);
 }
@@ -711,11 +736,10 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, 
 template <int EPI>
 int dispatch_fp8(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
                  int grid, cudaStream_t s) {
-  switch (bn) {
-    case 256: return launch_fp8<256, EPI>(ta, tb, kp, grid, s);
-    case 128: return launch_fp8<128, EPI>(ta, tb, kp, grid, s);
-    default: return fail(MOE_ERR_UNSUPPORTED, "fp8 GEMM: block_n must be 128 or 256");
-  }
+  // 128-wide tiles only: 4 TMEM partial buffers and 64 promoted columns per
+  // epilogue thread (256-wide tiles would leave 2 buffers and spill)
+  if (bn != 128) return fail(MOE_ERR_UNSUPPORTED, "fp8 GEMM: block_n must be 128");
+  return launch_fp8<128, EPI>(ta, tb, kp, grid, s);
 }
 
 template <int KIND, int AB_FMT, int EPI, typename TOUT>
@@ -846,7 +870,7 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   if (fp8)
     KSW_REQUIRE(a.n % 256 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 gate-up GEMM: I must be a multiple of 128");
-  const int bn = a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), 1, sms, !fp8);
+  const int bn = fp8 ? 128 : (a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), 1, sms));
   KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED,
               "gate-up GEMM: 2*I must be a multiple of 64");
   CUtensorMap ta, tb;
@@ -906,7 +930,7 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
     KSW_REQUIRE(a.n % 128 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 down GEMM: hidden size must be a multiple of 128");
   const int bn =
-      a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms, !fp8);
+      fp8 ? 128 : (a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms));
   KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED, "down GEMM: bad block_n");
   CUtensorMap ta, tb;
   st = make_maps(a, ot, bn, &ta, &tb);

@@ -70,13 +70,13 @@ struct Tiling {
 };
 
 Tiling choose_tiling(int64_t mb, int64_t rows, int64_t n, int64_t k_bytes, int sms,
-                     bool allow_split, bool allow64) {
+                     bool allow_split, bool allow64, int max_bn = 256) {
   Tiling best{0, 1};
   double best_cost = 1e300;
   mb = std::max<int64_t>(mb, 1);
   const int64_t k_blocks = ceil_div(k_bytes, 128);
   for (int bn : {256, 128, 64}) {
-    if (n % bn != 0 || (bn == 64 && !allow64)) continue;
+    if (n % bn != 0 || (bn == 64 && !allow64) || bn > max_bn) continue;
     const int64_t tiles = mb * (n / bn);
     const int64_t max_s =
         allow_split ? std::min<int64_t>(16, std::max<int64_t>(1, k_blocks / 4)) : 1;
@@ -145,10 +145,13 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   }
   const int64_t est_mb = est_m_blocks(P.numel, P.L, P.E);
   const bool fp8 = P.quant == MOE_QUANT_FP8_BLOCK;
-  const Tiling dn = choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !fp8);
+  // fp8 runs 128-wide tiles only (see the fp8 kernel's TMEM buffering)
+  const int max_bn = fp8 ? 128 : 256;
+  const Tiling dn = choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !fp8, max_bn);
   // the split gate-up path has no fp8 epilogue (its block scales follow the
   // regrouped gate/up rows); fp8 keeps the fused SiLU*up epilogue
-  const Tiling gu = choose_tiling(est_mb, P.numel, 2 * P.I, P.H * kbpe, sms, !fp8, !fp8);
+  const Tiling gu =
+      choose_tiling(est_mb, P.numel, 2 * P.I, P.H * kbpe, sms, !fp8, !fp8, max_bn);
   KSW_REQUIRE(dn.bn > 0 && gu.bn > 0, MOE_ERR_UNSUPPORTED,
               "hidden size and 2*intermediate size must be multiples of 64 (128 for fp8)");
   P.splits = dn.splits;
