@@ -12,9 +12,13 @@ weights, N(0,1) router logits).
                     [--workload mixtral|qwen3|dsv3-fp8|qwen3-int8] [--tokens T]
 
 `value` is device time (CUDA events, inputs resident in HBM, L2 flushed
-between steps outside the timed windows, max over ranks); `e2e` is the same
-metric through ModelNew.forward with pinned host inputs, including the H2D
-copies of hidden states and router logits and the D2H copy of the output.
+between steps outside the timed windows, max over ranks). On one GPU a step
+is a replay of a CUDA graph that holds the whole forward (fused_moe.CapturedMoE;
+`--no-graph` launches every kernel eagerly instead); expert parallelism
+(N > 1) launches eagerly, since it syncs the host for the all_to_all split
+sizes. `e2e` is the same metric through the public API with pinned host
+inputs, including the H2D copies of hidden states and router logits and the
+D2H copy of the output.
 `--impl reference` times the reference's CPU torch path (base.py:35-76,
 restated in the oracle) on the host cores instead.
 """
@@ -54,9 +58,9 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (0 = workload default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--graph", action="store_true",
-                    help="time CUDA-graph replays of the whole forward (1 GPU; the per-kernel "
-                         "breakdown still comes from an instrumented non-graph pass)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="launch every step eagerly instead of replaying a CUDA graph of the "
+                         "whole forward (1 GPU runs use the graph by default)")
     ap.add_argument("--heat-seconds", type=float, default=1.0,
                     help="untimed busy period before timing, so clock samples see a loaded GPU")
     return ap.parse_args()
@@ -350,14 +354,30 @@ def main():
     use_graph = args.graph and world == 1
     graph = None
     if use_graph:
-        def graph_fn(hd, ld):
+        # The whole forward (routing + all kernels) captured once and replayed:
+        # no host launch gaps. A second capture carries stage events (event
+        # record nodes) for the per-kernel breakdown.
+        def graph_fn(hd, ld, stage_arr=None):
             tw, ti = fm.fused_topk(hd, ld, k, weights_dtype=hd.dtype)
             return fm.fused_experts(hd, prep, None, tw, ti, use_fp8_w8a8=quant == "fp8",
-                                    use_int8_w8a8=quant == "int8")
+                                    use_int8_w8a8=quant == "int8", stage_events=stage_arr)
 
         graph = fm.CapturedMoE(graph_fn, T, H, E, dtype=torch.bfloat16, device=dev)
         graph.hidden.copy_(hidden)
         graph.logits.copy_(logits)
+        gevs = stage_evs[0]
+        gi = fm.CapturedMoE(lambda hd, ld: graph_fn(hd, ld, stage_arrs[0]), T, H, E,
+                            dtype=torch.bfloat16, device=dev)
+        gi.hidden.copy_(hidden)
+        gi.logits.copy_(logits)
+        acc = [0.0] * len(_lib.STAGES)
+        for i in range(K):
+            flush.zero_()
+            gi.replay()
+            torch.cuda.synchronize()
+            for j in range(len(_lib.STAGES)):
+                acc[j] += gevs[j].elapsed_time(gevs[j + 1])
+        stage_ms = {name: acc[j] / K for j, name in enumerate(_lib.STAGES)}
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize()

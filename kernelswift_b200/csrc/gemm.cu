@@ -612,16 +612,25 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
       float acc[HALF];
 #pragma unroll
       for (int j = 0; j < HALF; ++j) acc[j] = 0.0f;
+      // scales of the next k-block are loaded one step ahead, so their
+      // latency hides behind the barrier wait and the TMEM copy
+      float sa_n = valid ? __ldg(sap + kb0) : 0.0f;
+      float sb0_n = __ldg(sb0 + kb0);
+      float sb1_n = __ldg(sb1 + kb0);
       for (int kb = kb0; kb < kb1; ++kb) {
+        const float s0 = sa_n * sb0_n;
+        const float s1 = sa_n * sb1_n;
+        if (kb + 1 < kb1) {
+          sa_n = valid ? __ldg(sap + kb + 1) : 0.0f;
+          sb0_n = __ldg(sb0 + kb + 1);
+          sb1_n = __ldg(sb1 + kb + 1);
+        }
         const bool ok = mbar_wait_bounded(&tfull[pb], pphase, abort_flag, limit);
         if (!__all_sync(0xffffffffu, ok)) {
           aborted = true;
           break;
         }
         tc_fence_after();
-        const float sa = valid ? __ldg(sap + kb) : 0.0f;
-        const float s0 = sa * __ldg(sb0 + kb);
-        const float s1 = sa * __ldg(sb1 + kb);
         const uint32_t tbase =
             tmem_base + (uint32_t(q * 32) << 16) + uint32_t(pb * BN + col0);
 #pragma unroll

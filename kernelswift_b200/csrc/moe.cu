@@ -235,10 +235,18 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   if (P.quant != MOE_QUANT_NONE)
     KSW_REQUIRE(p->w13_scale && p->w2_scale, MOE_ERR_INVALID_ARG, "null weight scales");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Stage events: inside a stream capture they become event-record nodes of
+  // the graph (external records), so a replayed graph can be timed per stage.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (p->stage_events != nullptr)
+    KSW_CUDA(cudaStreamIsCapturing(s, &cap));
   auto mark = [&](int stage) -> int {
     if (p->stage_events == nullptr) return MOE_OK;
-    return check_cuda(cudaEventRecord(static_cast<cudaEvent_t>(p->stage_events[stage]), s),
-                      "cudaEventRecord(stage event)");
+    cudaEvent_t ev = static_cast<cudaEvent_t>(p->stage_events[stage]);
+    if (cap == cudaStreamCaptureStatusActive)
+      return check_cuda(cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal),
+                        "cudaEventRecordWithFlags(stage event)");
+    return check_cuda(cudaEventRecord(ev, s), "cudaEventRecord(stage event)");
   };
 #define KSW_MARK(stage)           \
   do {                            \

@@ -166,3 +166,24 @@ def test_rejects_other_activation(cuda_device):
         fm.fused_experts(torch.zeros(2, 128, device=cuda_device), None, None,
                          torch.zeros(2, 1), torch.zeros(2, 1, dtype=torch.int64),
                          activation="gelu")
+
+
+def test_captured_graph_matches_eager(cuda_device):
+    """CapturedMoE replays the same kernels: bit-identical to eager calls,
+    also after new inputs are copied into the static buffers."""
+    T, H, I, E, k = 16, 512, 256, 8, 2
+    m = fm.ModelNew(E, k, H, I).to(cuda_device)
+    g = torch.Generator(device=cuda_device).manual_seed(0)
+    with torch.no_grad():
+        m.w1.normal_(0, H ** -0.5, generator=g)
+        m.w2.normal_(0, I ** -0.5, generator=g)
+    cap = fm.CapturedMoE(m, T, H, E, dtype=torch.bfloat16, device=cuda_device)
+    for seed in (1, 2):
+        gi = torch.Generator(device=cuda_device).manual_seed(seed)
+        hidden = torch.randn(T, H, generator=gi, device=cuda_device).to(torch.bfloat16)
+        logits = torch.randn(T, E, generator=gi, device=cuda_device)
+        with torch.no_grad():
+            eager = m(hidden, logits).clone()
+        out = cap(hidden, logits)
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
