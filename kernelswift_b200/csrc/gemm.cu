@@ -437,13 +437,17 @@ constexpr int kThreadsF8 = 320;
 
 template <int BN>
 struct Fp8Cfg {
-  static constexpr int kBufs = 512 / BN;                  // TMEM partial buffers
-  static constexpr int kHalf = BN / 2;                    // columns per epilogue warp
-  static constexpr int kBatch = kHalf > 64 ? 64 : kHalf;  // columns per TMEM wait
+  static constexpr int kBufs = 512 / BN;  // TMEM partial buffers
+  static constexpr int kHalf = BN / 2;    // columns per epilogue warp
+  // columns per TMEM wait: 64 while the registers allow (BN = 128), 32 at
+  // BN = 256, where 128 accumulators per thread leave no room for more
+  static constexpr int kBatch = kHalf > 64 ? 32 : kHalf;
 };
 
+// 10 warps x 200 registers fit the 64K-register file; the default cap for a
+// 320-thread block (168) would spill the 128 fp32 accumulators at BN = 256.
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreadsF8, 1)
+__global__ void __maxnreg__(200)
     moe_grouped_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA,
                                 const __grid_constant__ CUtensorMap tmB,
                                 const KParams p) {
@@ -745,10 +749,11 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, 
 template <int EPI>
 int dispatch_fp8(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
                  int grid, cudaStream_t s) {
-  // 128-wide tiles only: 4 TMEM partial buffers and 64 promoted columns per
-  // epilogue thread (256-wide tiles would leave 2 buffers and spill)
-  if (bn != 128) return fail(MOE_ERR_UNSUPPORTED, "fp8 GEMM: block_n must be 128");
-  return launch_fp8<128, EPI>(ta, tb, kp, grid, s);
+  switch (bn) {
+    case 256: return launch_fp8<256, EPI>(ta, tb, kp, grid, s);
+    case 128: return launch_fp8<128, EPI>(ta, tb, kp, grid, s);
+    default: return fail(MOE_ERR_UNSUPPORTED, "fp8 GEMM: block_n must be 128 or 256");
+  }
 }
 
 template <int KIND, int AB_FMT, int EPI, typename TOUT>
@@ -879,7 +884,7 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   if (fp8)
     KSW_REQUIRE(a.n % 256 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 gate-up GEMM: I must be a multiple of 128");
-  const int bn = fp8 ? 128 : (a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), 1, sms));
+  const int bn = a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), 1, sms, !fp8);
   KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED,
               "gate-up GEMM: 2*I must be a multiple of 64");
   CUtensorMap ta, tb;
@@ -939,7 +944,7 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
     KSW_REQUIRE(a.n % 128 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 down GEMM: hidden size must be a multiple of 128");
   const int bn =
-      fp8 ? 128 : (a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms));
+      a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms, !fp8);
   KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED, "down GEMM: bad block_n");
   CUtensorMap ta, tb;
   st = make_maps(a, ot, bn, &ta, &tb);

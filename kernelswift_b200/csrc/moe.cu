@@ -145,8 +145,7 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   }
   const int64_t est_mb = est_m_blocks(P.numel, P.L, P.E);
   const bool fp8 = P.quant == MOE_QUANT_FP8_BLOCK;
-  // fp8 runs 128-wide tiles only (see the fp8 kernel's TMEM buffering)
-  const int max_bn = fp8 ? 128 : 256;
+  const int max_bn = 256;
   const Tiling dn = choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !fp8, max_bn);
   // the split gate-up path has no fp8 epilogue (its block scales follow the
   // regrouped gate/up rows); fp8 keeps the fused SiLU*up epilogue
