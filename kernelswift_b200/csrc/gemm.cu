@@ -439,15 +439,16 @@ template <int BN>
 struct Fp8Cfg {
   static constexpr int kBufs = 512 / BN;  // TMEM partial buffers
   static constexpr int kHalf = BN / 2;    // columns per epilogue warp
-  // columns per TMEM wait: 64 while the registers allow (BN = 128), 32 at
+  // columns per TMEM wait: 64 while the registers allow (BN = 128), 16 at
   // BN = 256, where 128 accumulators per thread leave no room for more
-  static constexpr int kBatch = kHalf > 64 ? 32 : kHalf;
+  static constexpr int kBatch = kHalf > 64 ? 16 : kHalf;
 };
 
-// 10 warps x 200 registers fit the 64K-register file; the default cap for a
-// 320-thread block (168) would spill the 128 fp32 accumulators at BN = 256.
+// 10 warps x 192 registers fit one SM's register file; the compiler's default
+// cap for a 320-thread block (168) would spill the 128 fp32 accumulators of
+// a 256-wide tile.
 template <int BN, int EPI>
-__global__ void __maxnreg__(200)
+__global__ void __maxnreg__(192)
     moe_grouped_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA,
                                 const __grid_constant__ CUtensorMap tmB,
                                 const KParams p) {
