@@ -444,11 +444,11 @@ struct Fp8Cfg {
   static constexpr int kBatch = kHalf > 64 ? 16 : kHalf;
 };
 
-// 10 warps x 192 registers fit one SM's register file; the compiler's default
-// cap for a 320-thread block (168) would spill the 128 fp32 accumulators of
-// a 256-wide tile.
+// A 10-warp block is provisioned as 12 warps, so 168 registers per thread is
+// the most it can launch with; 16-column TMEM batches keep the 128 fp32
+// accumulators of a 256-wide tile within that.
 template <int BN, int EPI>
-__global__ void __maxnreg__(192)
+__global__ void __launch_bounds__(kThreadsF8, 1)
     moe_grouped_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA,
                                 const __grid_constant__ CUtensorMap tmB,
                                 const KParams p) {
