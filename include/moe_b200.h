@@ -341,6 +341,26 @@ int moe_combine_rows(const void* rows, int rows_dtype, const int32_t* inv_index,
                      int top_k, int64_t hidden_size, void* out, int out_dtype,
                      void* stream);
 
+/*
+ * Expert-parallel dispatch plan for this rank's routing (experts sharded in
+ * contiguous blocks of num_experts / world per rank). For flat slot r with
+ * expert id e = topk_ids[r] and destination rank d = e / (num_experts/world):
+ *   order[p]     slot at send position p: slots grouped by d (ascending),
+ *                ascending r within a rank; send positions run over
+ *                [0, counts[0] + ... + counts[world-1])
+ *   send_eid[p]  e - d * (num_experts / world), the id on the receiving rank
+ *   inv_index[r] send position of slot r (-1 for ids outside [0, num_experts))
+ *   counts[d]    slots for rank d (int64, d < world); counts[world] = slots
+ *                with ids outside [0, num_experts)
+ * order/send_eid/inv_index hold numel int32 each; counts world + 1 int64.
+ * Deterministic (stable counting sort, no atomics decide positions).
+ * Replaces the per-expert grouping of base.py:64-68 across ranks.
+ * 1 <= world <= 128.
+ */
+int moe_ep_plan(const void* topk_ids, int ids_dtype, int64_t numel,
+                int num_experts, int world, int32_t* order, int32_t* send_eid,
+                int32_t* inv_index, int64_t* counts, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Self-test of the bounded device waits (failure detection without a GPU   */
 /* fault): launches one CTA whose mbarrier wait is never satisfied, with a   */

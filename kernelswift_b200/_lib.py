@@ -87,6 +87,7 @@ SIGNATURES = {
     "moe_gemm_down": (_int, [_int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int,
                              _i64, _i64, _vp, _int, _int, _vp, _int, _vp, _vp]),
     "moe_sum_topk": (_int, [_vp, _int, _i64, _int, _i64, _vp, _int, _int, _vp, _int, _vp]),
+    "moe_ep_plan": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp]),
     "moe_combine_rows": (_int, [_vp, _int, _vp, _vp, _int, _i64, _int, _i64, _vp, _int, _vp]),
     "moe_selftest_wait_timeout": (_int, [_vp, _int, _vp]),
 }

@@ -1,0 +1,126 @@
+// Expert-parallel dispatch plan: one launch that turns this rank's routing
+// into everything the token exchange needs (replacing a sort, a bincount, two
+// gathers and an inverse-permutation scatter of torch ops).
+//
+// Experts are sharded in contiguous blocks of e_local per rank, so slot r
+// (= token * top_k + j) goes to rank dest[r] = topk_ids[r] / e_local; ids
+// outside [0, num_experts) go to an extra bucket `world` that is never sent.
+// The send order is a stable counting sort of the slots by destination:
+//   order[p]      = the slot at send position p (slots ascending within a rank)
+//   send_eid[p]   = topk_ids[order[p]] - dest * e_local (id local to the rank)
+//   inv[r]        = the send position of slot r (-1 for the extra bucket)
+//   counts[d]     = slots for rank d, d <= world (counts[world] = invalid ids)
+// Positions come from the same warp-match / per-warp-count / running-offset
+// scheme as moe_align_block_size, so the plan is deterministic.
+#include "common.cuh"
+
+namespace ksw {
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kMaxBuckets = 129;  // world <= 128 ranks, plus the invalid bucket
+
+template <typename IdT>
+__global__ void __launch_bounds__(kThreads)
+    ep_plan_kernel(const IdT* __restrict__ ids, int64_t numel, int num_experts, int e_local,
+                   int world, int32_t* __restrict__ order, int32_t* __restrict__ send_eid,
+                   int32_t* __restrict__ inv, int64_t* __restrict__ counts) {
+  __shared__ int cnt[kMaxBuckets];
+  __shared__ int running[kMaxBuckets];
+  __shared__ int warp_cnt[32 * kMaxBuckets];
+  __shared__ int scan_tmp[64];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int B = world + 1;
+  for (int b = tid; b < B; b += kThreads) cnt[b] = 0;
+  for (int i = tid; i < 32 * B; i += kThreads) warp_cnt[i] = 0;
+  __syncthreads();
+  auto bucket_of = [&](int64_t i, int* local) -> int {
+    const long long v = static_cast<long long>(ids[i]);
+    if (v < 0 || v >= num_experts) {
+      *local = -1;
+      return world;
+    }
+    const int d = static_cast<int>(v / e_local);
+    *local = static_cast<int>(v - int64_t(d) * e_local);
+    return d;
+  };
+  for (int64_t i = tid; i < numel; i += kThreads) {
+    int loc;
+    atomicAdd(&cnt[bucket_of(i, &loc)], 1);
+  }
+  __syncthreads();
+  // exclusive scan over the (<= 129) buckets by warp 0..4
+  if (tid == 0) {
+    int run = 0;
+    for (int b = 0; b < B; ++b) {
+      running[b] = run;
+      run += cnt[b];
+    }
+  }
+  for (int b = tid; b < B; b += kThreads) counts[b] = cnt[b];
+  __syncthreads();
+  for (int64_t base = 0; base < numel; base += kThreads) {
+    const int64_t i = base + tid;
+    int loc = -1;
+    const int d = i < numel ? bucket_of(i, &loc) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    const int rank = __popc(peers & lanemask_lt());
+    if (d >= 0 && lane == __ffs(peers) - 1) warp_cnt[warp * B + d] = __popc(peers);
+    __syncthreads();
+    if (d >= 0) {
+      int prefix = 0;
+      for (int w = 0; w < warp; ++w) prefix += warp_cnt[w * B + d];
+      const int pos = running[d] + prefix + rank;
+      if (d < world) {
+        order[pos] = static_cast<int32_t>(i);
+        send_eid[pos] = loc;
+        inv[i] = pos;
+      } else {
+        inv[i] = -1;
+      }
+    }
+    __syncthreads();
+    for (int b = tid; b < B; b += kThreads) {
+      int s = 0;
+      for (int w = 0; w < 32; ++w) {
+        s += warp_cnt[w * B + b];
+        warp_cnt[w * B + b] = 0;
+      }
+      running[b] += s;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+}  // namespace ksw
+
+extern "C" int moe_ep_plan(const void* topk_ids, int ids_dtype, int64_t numel, int num_experts,
+                           int world, int32_t* order, int32_t* send_eid, int32_t* inv_index,
+                           int64_t* counts, void* stream) {
+  using namespace ksw;
+  int st = check_device(nullptr);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE(world >= 1 && world + 1 <= kMaxBuckets, MOE_ERR_UNSUPPORTED,
+              "ep_plan: world must be in [1, 128]");
+  KSW_REQUIRE(num_experts >= world && num_experts % world == 0, MOE_ERR_INVALID_ARG,
+              "ep_plan: num_experts must be a positive multiple of world");
+  KSW_REQUIRE(numel >= 0 && numel < (int64_t(1) << 31), MOE_ERR_UNSUPPORTED,
+              "ep_plan: numel out of range");
+  KSW_REQUIRE(ids_dtype == MOE_DTYPE_I32 || ids_dtype == MOE_DTYPE_I64, MOE_ERR_INVALID_ARG,
+              "ep_plan: ids dtype must be int32 or int64");
+  KSW_REQUIRE(counts && (numel == 0 || (topk_ids && order && send_eid && inv_index)),
+              MOE_ERR_INVALID_ARG, "ep_plan: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int e_local = num_experts / world;
+  if (ids_dtype == MOE_DTYPE_I32)
+    ep_plan_kernel<int32_t><<<1, kThreads, 0, s>>>(static_cast<const int32_t*>(topk_ids), numel,
+                                                   num_experts, e_local, world, order, send_eid,
+                                                   inv_index, counts);
+  else
+    ep_plan_kernel<int64_t><<<1, kThreads, 0, s>>>(static_cast<const int64_t*>(topk_ids), numel,
+                                                   num_experts, e_local, world, order, send_eid,
+                                                   inv_index, counts);
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}

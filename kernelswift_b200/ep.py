@@ -4,8 +4,10 @@ Experts are sharded in contiguous blocks: with E experts over `world` ranks,
 rank r holds experts [r*E/world, (r+1)*E/world). Tokens stay data-parallel:
 every rank routes its own tokens. One forward is
 
-  1. dest[r] = topk_ids[r] // E_local for every flat slot r = t*k + j;
-     `order` = the slots sorted by destination rank (stable)
+  1. plan (moe_ep_plan, one launch): dest[r] = topk_ids[r] // E_local for
+     every flat slot r = t*k + j; `order` = the slots sorted by destination
+     rank (stable), the destination-local expert ids in that order, the
+     inverse permutation and the per-destination counts
   2. all_to_all of the per-destination counts (the only host sync: NCCL's
      variable-size all_to_all needs the split sizes on the host)
   3. pack: send_rows[i] = hidden[order[i] // k]       (moe_gather_rows)
@@ -21,7 +23,8 @@ torch.distributed (NCCL over NVLink/NVSwitch on B200); every rank issues the
 same collectives in the same order, so a rank that fails makes the others'
 next collective end with the process group's timeout instead of hanging.
 
-The device work (pack, local experts, combine) goes through a backend object;
+The device work (plan, pack, local experts, combine) goes through a backend
+object;
 `CudaBackend` runs the library's kernels and is the only backend this package
 provides.
 """
@@ -42,6 +45,20 @@ class CudaBackend:
     def __init__(self, prepared: fm.PreparedWeights, quant: str = "none"):
         self.prep = prepared
         self.quant = quant
+
+    def plan(self, topk_ids: torch.Tensor, num_experts: int, world: int):
+        """(order, send_eid, inv, counts) of moe_ep_plan for this rank's ids."""
+        ids = topk_ids.reshape(-1).contiguous()
+        n = ids.numel()
+        dev = ids.device
+        order = torch.empty(n, dtype=torch.int32, device=dev)
+        send_eid = torch.empty(n, dtype=torch.int32, device=dev)
+        inv = torch.empty(n, dtype=torch.int32, device=dev)
+        counts = torch.empty(world + 1, dtype=torch.int64, device=dev)
+        _lib.call("moe_ep_plan", fm._ptr(ids), fm._code(ids), n, num_experts, world,
+                  fm._ptr(order), fm._ptr(send_eid), fm._ptr(inv), fm._ptr(counts),
+                  fm._stream(dev))
+        return order, send_eid, inv, counts
 
     def pack(self, hidden: torch.Tensor, order: torch.Tensor, top_k: int) -> torch.Tensor:
         n = order.numel()
@@ -111,26 +128,21 @@ class ExpertParallelMoE:
         T, H = hidden.shape
         k = topk_ids.shape[1]
         dev = hidden.device
-        flat = topk_ids.reshape(-1).to(torch.int64)
-        # ids outside [0, E) are counted in an extra bin that no rank
-        # receives; the check after the count exchange rejects them
-        valid = (flat >= 0) & (flat < self.num_experts)
-        dest = torch.where(valid, torch.div(flat, self.e_local, rounding_mode="floor"),
-                           torch.full_like(flat, self.world))
-        order = torch.sort(dest, stable=True).indices
-        send_counts = torch.bincount(dest, minlength=self.world + 1)
-        recv_counts = torch.empty(self.world, dtype=send_counts.dtype, device=dev)
-        dist.all_to_all_single(recv_counts, send_counts[:self.world].contiguous(),
-                               group=self.group)
-        counts = torch.cat([send_counts, recv_counts]).cpu()  # the one host sync
-        send_split = counts[:self.world].tolist()
-        recv_split = counts[self.world + 1:].tolist()
+        numel = topk_ids.numel()
+        order, send_eid, inv, counts = self.backend.plan(topk_ids, self.num_experts, self.world)
+        recv_counts = torch.empty(self.world, dtype=counts.dtype, device=dev)
+        dist.all_to_all_single(recv_counts, counts[:self.world].contiguous(), group=self.group)
+        both = torch.cat([counts, recv_counts]).cpu()  # the one host sync
+        send_split = both[:self.world].tolist()
+        recv_split = both[self.world + 1:].tolist()
         n_recv = sum(recv_split)
-        if sum(send_split) != flat.numel():
+        if int(both[self.world]) != 0:
             raise ValueError("expert ids out of range")
+        n_send = numel
+        order = order[:n_send]
+        send_eid = send_eid[:n_send]
 
         send_rows = self.backend.pack(hidden, order, k)
-        send_eid = (flat[order] - dest[order] * self.e_local).to(torch.int32)
         recv_rows = torch.empty(n_recv, H, dtype=hidden.dtype, device=dev)
         recv_eid = torch.empty(n_recv, dtype=torch.int32, device=dev)
         dist.all_to_all_single(recv_rows, send_rows, recv_split, send_split, group=self.group)
@@ -141,11 +153,8 @@ class ExpertParallelMoE:
             out_rows = self.backend.experts(recv_rows, recv_eid, stage_events=stage_events)
         else:
             out_rows = self.backend.experts(recv_rows, recv_eid)
-        back = torch.empty(flat.numel(), H, dtype=out_rows.dtype, device=dev)
+        back = torch.empty(n_send, H, dtype=out_rows.dtype, device=dev)
         dist.all_to_all_single(back, out_rows, send_split, recv_split, group=self.group)
-
-        inv = torch.empty_like(order)
-        inv[order] = torch.arange(order.numel(), device=dev)
         return self.backend.combine(back, inv, topk_weights, T, k)
 
     __call__ = forward

@@ -24,8 +24,22 @@ class CpuBackend:
     def __init__(self, w1_local, w2_local):
         self.w1, self.w2 = w1_local, w2_local
 
+    def plan(self, topk_ids, num_experts, world):
+        """moe_ep_plan restated with torch ops."""
+        flat = topk_ids.reshape(-1).long()
+        el = num_experts // world
+        valid = (flat >= 0) & (flat < num_experts)
+        dest = torch.where(valid, flat // el, torch.full_like(flat, world))
+        order = torch.sort(dest, stable=True).indices
+        counts = torch.bincount(dest, minlength=world + 1)
+        n_send = int(counts[:world].sum())
+        send_eid = (flat[order] - dest[order] * el).to(torch.int32)
+        inv = torch.full_like(flat, -1)
+        inv[order[:n_send]] = torch.arange(n_send)
+        return order.to(torch.int32), send_eid, inv.to(torch.int32), counts
+
     def pack(self, hidden, order, top_k):
-        return hidden[torch.div(order, top_k, rounding_mode="floor")]
+        return hidden[torch.div(order.long(), top_k, rounding_mode="floor")]
 
     def experts(self, rows, local_ids):
         ones = torch.ones(rows.shape[0], 1)
@@ -34,7 +48,7 @@ class CpuBackend:
 
     def combine(self, rows, inv, weights, num_tokens, top_k):
         w = weights.reshape(-1, 1).float()
-        return (rows.float()[inv] * w).view(num_tokens, top_k, -1).sum(1).to(rows.dtype)
+        return (rows.float()[inv.long()] * w).view(num_tokens, top_k, -1).sum(1).to(rows.dtype)
 
 
 def free_port():

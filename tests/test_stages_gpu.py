@@ -208,3 +208,30 @@ def test_gather_quantisers_bit_exact(cuda_device, quant, H):
         q, sc = orc.quant_int8_rows(rows, reciprocal=True)
         assert torch.equal(dst.cpu()[valid], q)
     assert torch.equal(scale.cpu()[valid], sc)
+
+
+@pytest.mark.parametrize("T,k,E,world,invalid", [(4096, 2, 8, 2, False), (8192, 8, 256, 8, False),
+                                                 (333, 4, 16, 4, True), (1, 8, 128, 8, False)])
+def test_ep_plan_bit_exact(cuda_device, T, k, E, world, invalid):
+    """moe_ep_plan equals the stable sort by destination rank (torch ops)."""
+    from kernelswift_b200.ep import CudaBackend
+
+    g = torch.Generator().manual_seed(T + E)
+    ids = torch.topk(torch.randn(T, E, generator=g), k, dim=-1).indices
+    if invalid:
+        ids[::5, 0] = -1
+        ids[1::7, -1] = E + 3
+    order, send_eid, inv, counts = CudaBackend(None).plan(ids.to(cuda_device), E, world)
+    flat = ids.reshape(-1)
+    el = E // world
+    valid = (flat >= 0) & (flat < E)
+    dest = torch.where(valid, flat // el, torch.full_like(flat, world))
+    want_order = torch.sort(dest, stable=True).indices
+    want_counts = torch.bincount(dest, minlength=world + 1)
+    n = int(want_counts[:world].sum())
+    want_inv = torch.full_like(flat, -1)
+    want_inv[want_order[:n]] = torch.arange(n)
+    assert torch.equal(counts.cpu(), want_counts)
+    assert torch.equal(order.cpu()[:n].long(), want_order[:n])
+    assert torch.equal(send_eid.cpu()[:n].long(), (flat - dest * el)[want_order[:n]])
+    assert torch.equal(inv.cpu().long(), want_inv)
