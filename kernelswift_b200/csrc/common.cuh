@@ -302,6 +302,17 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// Register re-allocation between warpgroups (all four warps of a warpgroup
+// execute it together).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Packs two floats into one 32-bit word of two 16-bit elements (lo first).
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi);

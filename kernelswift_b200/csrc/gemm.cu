@@ -421,32 +421,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 // The scales change every 128 elements of K (per token for A, per 128x128
 // block for B), so the products of one k-block cannot be summed in TMEM
 // across k-blocks. Each k-block is accumulated into a fresh TMEM buffer and
-// eight epilogue warps promote it into fp32 registers:
+// sixteen epilogue warps promote it into fp32 registers:
 //   acc[m, n] += a_scale[m, kb] * b_scale[e, n / 128, kb] * P_kb[m, n]
 // TMEM holds 512 / BN such buffers (4 at BN = 128), so the MMAs of the next
 // k-blocks run while one is promoted; each epilogue warp copies its columns
 // out with one wait per 64 columns and releases the buffer before doing the
 // arithmetic, which keeps the buffer hand-off shorter than an MMA.
-// Warp w (2..9) owns TMEM lane quarter w % 4 and column half (w - 2) / 4;
+// Warp w (4..19) owns TMEM lane quarter w % 4 and column quarter (w - 4) / 4
+// (four warps per SM sub-partition hide the TMEM load latency);
 // warps whose 32 rows are all padding skip the arithmetic.
 // After the last k-block the gate-up epilogue applies SiLU(gate)*up and
 // writes bf16 activations; the down epilogue scales by the top-k weight and
 // writes fp32 rows.
 // ---------------------------------------------------------------------------
-constexpr int kThreadsF8 = 320;
+// Warps 0-3 form the control warpgroup (TMA producer, MMA issuer, two idle
+// warps); warps 4-19 are the epilogue. The block launches at kLaunchRegsF8
+// registers per thread; the control warpgroup then gives registers back and
+// the epilogue warpgroups take them (setmaxnreg), so the split must add up to
+// the launch total exactly, which the host checks before the first launch.
+constexpr int kEpiWarpsF8 = 16;
+constexpr int kThreadsF8 = 128 + 32 * kEpiWarpsF8;
+constexpr int kLaunchRegsF8 = 96;
+constexpr int kCtrlRegsF8 = 32;
+constexpr int kEpiRegsF8 = 112;
+static_assert(128 * kCtrlRegsF8 + 32 * kEpiWarpsF8 * kEpiRegsF8 == kThreadsF8 * kLaunchRegsF8,
+              "setmaxnreg split must equal the launch allocation");
 
 template <int BN>
 struct Fp8Cfg {
   static constexpr int kBufs = 512 / BN;  // TMEM partial buffers
-  static constexpr int kHalf = BN / 2;    // columns per epilogue warp
-  // columns per TMEM wait: 64 while the registers allow (BN = 128), 16 at
-  // BN = 256, where 128 accumulators per thread leave no room for more
-  static constexpr int kBatch = kHalf > 64 ? 16 : kHalf;
+  static constexpr int kHalf = BN / 4;    // columns per epilogue warp
+  // columns per TMEM wait
+  static constexpr int kBatch = kHalf > 32 ? 16 : kHalf;
 };
 
-// A 10-warp block is provisioned as 12 warps, so 168 registers per thread is
-// the most it can launch with; 16-column TMEM batches keep the 128 fp32
-// accumulators of a 256-wide tile within that.
+// Each epilogue warp holds BN / 4 fp32 accumulators per thread (64 at
+// BN = 256) plus one 16-column TMEM batch, within its 112 registers.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreadsF8, 1)
     moe_grouped_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -484,7 +494,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
     }
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 256);
+      mbar_init(&tempty[b], 32 * kEpiWarpsF8);
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
@@ -504,6 +514,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
   const int total_tiles = num_mb * n_tiles * p.splits;
   const uint64_t limit = p.wait_limit_ns;
 
+  if (warp < 4) setmaxnreg_dec<kCtrlRegsF8>();
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
     tma_prefetch_desc(&tmA);
@@ -583,10 +594,11 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
     tc_commit(final_bar);
     volatile int no_abort = 0;
     mbar_wait_bounded(final_bar, 0, &no_abort, limit);
-  } else if (warp >= 2) {
-    // ---------------- promotion + epilogue (8 warps) ----------------
+  } else if (warp >= 4) {
+    // ---------------- promotion + epilogue (16 warps) ----------------
+    setmaxnreg_inc<kEpiRegsF8>();
     const int q = warp & 3;
-    const int h = (warp - 2) >> 2;
+    const int h = (warp - 4) >> 2;
     const int row = q * 32 + lane;
     const int col0 = h * HALF;
     int pb = 0;
@@ -742,6 +754,16 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, 
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
+  // The setmaxnreg split inside the kernel assumes this launch allocation;
+  // with any other, the epilogue's register request could never be met.
+  static std::atomic<int> regs_ok{0};
+  if (!regs_ok.load(std::memory_order_acquire)) {
+    cudaFuncAttributes attr{};
+    KSW_CUDA(cudaFuncGetAttributes(&attr, kern));
+    KSW_REQUIRE(attr.numRegs == kLaunchRegsF8, MOE_ERR_DEVICE,
+                "fp8 GEMM: kernel built with an unexpected register count");
+    regs_ok.store(1, std::memory_order_release);
+  }
   kern<<<grid, kThreadsF8, Cfg::kSmemBytes, s>>>(ta, tb, kp);
   KSW_CUDA(cudaGetLastError());
   return MOE_OK;
