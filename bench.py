@@ -48,6 +48,25 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 L2_FLUSH_BYTES = 256 << 20
 
 
+class L2Flush:
+    """Empties L2 between timed steps: writes a buffer twice the size of L2,
+    then (unless MOE_BENCH_WRITE_FLUSH_ONLY=1) reads a second one, so the
+    dirty lines of the write are written back before the timed window opens
+    instead of inside it."""
+
+    evict = os.environ.get("MOE_BENCH_WRITE_FLUSH_ONLY", "0") in ("", "0")
+
+    def __init__(self, dev):
+        import torch
+        self.buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.rd = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev) if self.evict else None
+
+    def __call__(self):
+        self.buf.zero_()
+        if self.rd is not None:
+            self.rd.max()
+
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -218,8 +237,9 @@ def workload_config(name, H, I, E, k, quant, T, n):
             "tokens_per_gpu": T, "global_tokens": T * n,
             "parallelism": f"ep{n} (E/{n} experts per GPU, NCCL all_to_all)" if n > 1
             else "single",
-            "l2": f"flushed between steps ({L2_FLUSH_BYTES >> 20} MB write) outside the "
-                  "timed windows; weights also exceed L2"}
+            "l2": f"flushed between steps outside the timed windows ({L2_FLUSH_BYTES >> 20} MB "
+                  f"write{', then a read of another ' + str(L2_FLUSH_BYTES >> 20) + ' MB that evicts the dirty lines' if L2Flush.evict else ''}); "
+                  "weights also exceed L2"}
 
 
 # ---------------------------------------------------------------------------
@@ -259,7 +279,7 @@ def main():
     logits = torch.randn(T, E, generator=g, device=dev)
     if bias:
         logits = logits + torch.randn(E, generator=g, device=dev) * bias
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     rows_per_launch = [T * k]  # routed rows the local gate-up GEMM saw (last step)
     experts_hit = [0]          # distinct local experts with rows (for the byte count)
     if world == 1:
@@ -338,7 +358,7 @@ def main():
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
     for i in range(K):
-        flush.zero_()
+        flush()
         starts[i].record()
         step(stage_arrs[i])
         ends[i].record()
@@ -372,7 +392,7 @@ def main():
         gi.logits.copy_(logits)
         acc = [0.0] * len(_lib.STAGES)
         for i in range(K):
-            flush.zero_()
+            flush()
             gi.replay()
             torch.cuda.synchronize()
             for j in range(len(_lib.STAGES)):
@@ -382,7 +402,7 @@ def main():
             graph.replay()
         torch.cuda.synchronize()
         for i in range(K):
-            flush.zero_()
+            flush()
             starts[i].record()
             graph.replay()
             ends[i].record()

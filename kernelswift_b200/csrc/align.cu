@@ -114,6 +114,8 @@ __global__ void __launch_bounds__(kThreads)
                        int BM, int64_t L, int32_t* __restrict__ sorted,
                        int32_t* __restrict__ expert_ids,
                        int32_t* __restrict__ num_post_pad) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sm[];
   int* counts = sm;                 // E
   int* running = counts + E;        // E
@@ -150,6 +152,8 @@ __global__ void __launch_bounds__(kThreads)
     align_hist_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
                       int64_t L, int32_t* __restrict__ sorted,
                       int32_t* __restrict__ chunk_counts) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sm[];
   int* counts = sm;  // E
   const int tid = threadIdx.x;
@@ -176,6 +180,8 @@ __global__ void __launch_bounds__(kThreads)
                       int32_t* __restrict__ chunk_counts,
                       int32_t* __restrict__ expert_ids,
                       int32_t* __restrict__ num_post_pad) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int scan_tmp[64];
   const int tid = threadIdx.x;
   int cnt = 0;
@@ -201,6 +207,8 @@ __global__ void __launch_bounds__(kThreads)
     align_scatter_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
                          const int32_t* __restrict__ chunk_base,
                          int32_t* __restrict__ sorted) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sm[];
   int* running = sm;           // E
   int* warp_cnt = running + E; // 32 * E
@@ -225,25 +233,22 @@ int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
     if (smem > 48 * 1024)
       KSW_CUDA(cudaFuncSetAttribute(
           k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    k<<<1, kThreads, smem, s>>>(ids, numel, E, BM, L, sorted, expert_ids,
-                                num_post_pad);
-    KSW_CUDA(cudaGetLastError());
+    KSW_LAUNCH(k, dim3(1), dim3(kThreads), smem, s, ids, numel, E, BM, L, sorted,
+               expert_ids, num_post_pad);
     return MOE_OK;
   }
   const int nchunks = static_cast<int>(ceil_div(numel, kChunk));
-  align_hist_kernel<IdT><<<nchunks, kThreads, size_t(E) * sizeof(int), s>>>(
-      ids, numel, E, L, sorted, ws);
-  KSW_CUDA(cudaGetLastError());
-  align_scan_kernel<<<1, kThreads, 0, s>>>(nchunks, E, BM, L, ws, expert_ids,
-                                           num_post_pad);
-  KSW_CUDA(cudaGetLastError());
+  KSW_LAUNCH(align_hist_kernel<IdT>, dim3(nchunks), dim3(kThreads),
+             size_t(E) * sizeof(int), s, ids, numel, E, L, sorted, ws);
+  KSW_LAUNCH(align_scan_kernel, dim3(1), dim3(kThreads), 0, s, nchunks, E, BM, L, ws,
+             expert_ids, num_post_pad);
   const size_t smem = size_t(E + 32 * E) * sizeof(int);
   auto k = align_scatter_kernel<IdT>;
   if (smem > 48 * 1024)
     KSW_CUDA(cudaFuncSetAttribute(
         k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  k<<<nchunks, kThreads, smem, s>>>(ids, numel, E, ws, sorted);
-  KSW_CUDA(cudaGetLastError());
+  KSW_LAUNCH(k, dim3(nchunks), dim3(kThreads), smem, s, ids, numel, E,
+             static_cast<const int32_t*>(ws), sorted);
   return MOE_OK;
 }
 

@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -45,6 +46,56 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Default wait limit for on-chip barrier waits: one second.
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch
+//
+// Every kernel of the forward is launched with programmatic stream
+// serialisation, so it may start while the previous kernel in the stream is
+// still running. Each kernel therefore
+//   * calls pdl_wait() before it reads anything the previous kernel writes or
+//     writes anything the previous kernel reads or writes, and
+//   * calls pdl_trigger() only after its own pdl_wait().
+// The second rule makes the ordering transitive: when kernel n starts,
+// kernel n-1 has passed its wait, so kernel n-2 and everything before it
+// have completed. Kernel n may therefore read the outputs of kernel n-2 and
+// earlier (the align metadata, the weights) before its own wait.
+// MOE_NO_PDL=1 in the environment launches everything plainly.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+bool pdl_enabled();
+
+#define KSW_LAUNCH(...)                                       \
+  do {                                                        \
+    int _st = ::ksw::launch(__VA_ARGS__);                     \
+    if (_st != MOE_OK) return _st;                            \
+  } while (0)
+
+// Launches `kern` on `s`, with programmatic stream serialisation unless
+// disabled.
+template <typename... KArgs, typename... Args>
+int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...),
+                    "cudaLaunchKernelEx");
+}
 
 // ---------------------------------------------------------------------------
 // Generic device helpers

@@ -25,10 +25,11 @@ __global__ void __launch_bounds__(kThreads)
     ep_plan_kernel(const IdT* __restrict__ ids, int64_t numel, int num_experts, int e_local,
                    int world, int32_t* __restrict__ order, int32_t* __restrict__ send_eid,
                    int32_t* __restrict__ inv, int64_t* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int cnt[kMaxBuckets];
   __shared__ int running[kMaxBuckets];
   __shared__ int warp_cnt[32 * kMaxBuckets];
-  __shared__ int scan_tmp[64];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int B = world + 1;
   for (int b = tid; b < B; b += kThreads) cnt[b] = 0;
@@ -114,13 +115,12 @@ extern "C" int moe_ep_plan(const void* topk_ids, int ids_dtype, int64_t numel, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int e_local = num_experts / world;
   if (ids_dtype == MOE_DTYPE_I32)
-    ep_plan_kernel<int32_t><<<1, kThreads, 0, s>>>(static_cast<const int32_t*>(topk_ids), numel,
-                                                   num_experts, e_local, world, order, send_eid,
-                                                   inv_index, counts);
+    KSW_LAUNCH(ep_plan_kernel<int32_t>, dim3(1), dim3(kThreads), 0, s,
+               static_cast<const int32_t*>(topk_ids), numel, num_experts, e_local, world,
+               order, send_eid, inv_index, counts);
   else
-    ep_plan_kernel<int64_t><<<1, kThreads, 0, s>>>(static_cast<const int64_t*>(topk_ids), numel,
-                                                   num_experts, e_local, world, order, send_eid,
-                                                   inv_index, counts);
-  KSW_CUDA(cudaGetLastError());
+    KSW_LAUNCH(ep_plan_kernel<int64_t>, dim3(1), dim3(kThreads), 0, s,
+               static_cast<const int64_t*>(topk_ids), numel, num_experts, e_local, world,
+               order, send_eid, inv_index, counts);
   return MOE_OK;
 }

@@ -68,6 +68,7 @@ struct KParams {
   int32_t sb_rb;
   int32_t sb_kb;
   int32_t up_offset;        // gate-up: original row of the first up row (= I)
+  int32_t early_meta;       // see GroupedGemmArgs::early_meta
   uint64_t wait_limit_ns;
 };
 
@@ -175,15 +176,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Programmatic dependent launch: without early metadata every thread
+  // waits for the previous kernel here; with it, only the A loads (and so
+  // everything downstream of them) wait, after the first weight tiles have
+  // been requested.
+  const bool producer = warp == 0 && lane == 0;
+  if (!p.early_meta || !producer) {
+    pdl_wait();
+    pdl_trigger();
+  }
   const int num_mb = min(__ldg(p.num_post_pad) / BM, p.max_m_blocks);
   const int n_tiles = p.n_total / BN;
   const int total_tiles = num_mb * n_tiles * p.splits;
   const uint64_t limit = p.wait_limit_ns;
 
-  if (warp == 0 && lane == 0) {
+  if (producer) {
     // ---------------- TMA producer ----------------
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    constexpr int kColsPerKb = kKBytes / (KIND == kKindF16 ? 2 : 1);
+    // With early metadata the weight tiles of the first STAGES k-blocks (in
+    // the order the main loop visits them) are requested before the wait
+    // for the A operand's producer; those stages later get only their A tile.
+    uint32_t pre = 0;
+    if (p.early_meta) {
+      for (int t = blockIdx.x; pre < uint32_t(STAGES) && t < total_tiles; t += gridDim.x) {
+        const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+        const int e = __ldg(p.expert_ids + c.mb);
+        if (e < 0 || e >= p.num_experts) continue;
+        const int kb0 = c.ks * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        const int b_row = e * p.n_total + c.nt * BN;
+        for (int kb = kb0; kb < kb1 && pre < uint32_t(STAGES); ++kb, ++pre) {
+          mbar_arrive_expect_tx(&full[pre], Cfg::kStageBytes);
+          tma_load_2d(sB + pre * Cfg::kBBytes, &tmB, kb * kColsPerKb, b_row, &full[pre]);
+        }
+      }
+      pdl_wait();
+      pdl_trigger();
+    }
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued = 0;
@@ -197,14 +228,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int a_row = c.mb * BM;
       const int b_row = e * p.n_total + c.nt * BN;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit)) {
-          ok = false;
-          break;
+        const int kcol = kb * kColsPerKb;
+        if (issued < pre) {
+          // first pass over the ring (stage == issued): B is on its way
+          tma_load_2d(sA + stage * kABytes, &tmA, kcol, a_row, &full[stage]);
+        } else {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sA + stage * kABytes, &tmA, kcol, a_row, &full[stage]);
+          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kcol, b_row, &full[stage]);
         }
-        mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-        const int kcol = kb * (kKBytes / (KIND == kKindF16 ? 2 : 1));
-        tma_load_2d(sA + stage * kABytes, &tmA, kcol, a_row, &full[stage]);
-        tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kcol, b_row, &full[stage]);
         ++issued;
         if (++stage == STAGES) {
           stage = 0;
@@ -509,16 +545,43 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Programmatic dependent launch: without early metadata every thread
+  // waits for the previous kernel here; with it, only the A loads (and so
+  // everything downstream of them) wait, after the first weight tiles have
+  // been requested.
+  const bool producer = warp == 0 && lane == 0;
+  if (!p.early_meta || !producer) {
+    pdl_wait();
+    pdl_trigger();
+  }
   const int num_mb = min(__ldg(p.num_post_pad) / BM, p.max_m_blocks);
   const int n_tiles = p.n_total / BN;
   const int total_tiles = num_mb * n_tiles * p.splits;
   const uint64_t limit = p.wait_limit_ns;
 
   if (warp < 4) setmaxnreg_dec<kCtrlRegsF8>();
-  if (warp == 0 && lane == 0) {
+  if (producer) {
     // ---------------- TMA producer ----------------
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    // early weight tiles, as in the bf16/int8 kernel
+    uint32_t pre = 0;
+    if (p.early_meta) {
+      for (int t = blockIdx.x; pre < uint32_t(STAGES) && t < total_tiles; t += gridDim.x) {
+        const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+        const int e = __ldg(p.expert_ids + c.mb);
+        if (e < 0 || e >= p.num_experts) continue;
+        const int kb0 = c.ks * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        const int b_row = e * p.n_total + c.nt * BN;
+        for (int kb = kb0; kb < kb1 && pre < uint32_t(STAGES); ++kb, ++pre) {
+          mbar_arrive_expect_tx(&full[pre], Cfg::kStageBytes);
+          tma_load_2d(sB + pre * Cfg::kBBytes, &tmB, kb * kKBytes, b_row, &full[pre]);
+        }
+      }
+      pdl_wait();
+      pdl_trigger();
+    }
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued = 0;
@@ -532,13 +595,17 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
       const int a_row = c.mb * BM;
       const int b_row = e * p.n_total + c.nt * BN;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit)) {
-          ok = false;
-          break;
+        if (issued < pre) {
+          tma_load_2d(sA + stage * kABytes, &tmA, kb * kKBytes, a_row, &full[stage]);
+        } else {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sA + stage * kABytes, &tmA, kb * kKBytes, a_row, &full[stage]);
+          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kb * kKBytes, b_row, &full[stage]);
         }
-        mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-        tma_load_2d(sA + stage * kABytes, &tmA, kb * kKBytes, a_row, &full[stage]);
-        tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kb * kKBytes, b_row, &full[stage]);
         ++issued;
         if (++stage == STAGES) {
           stage = 0;
@@ -741,8 +808,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
-  kern<<<grid, kThreads, Cfg::kSmemBytes, s>>>(ta, tb, kp);
-  KSW_CUDA(cudaGetLastError());
+  KSW_LAUNCH(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, s, ta, tb, kp);
   return MOE_OK;
 }
 
@@ -764,8 +830,7 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, 
                 "fp8 GEMM: kernel built with an unexpected register count");
     regs_ok.store(1, std::memory_order_release);
   }
-  kern<<<grid, kThreadsF8, Cfg::kSmemBytes, s>>>(ta, tb, kp);
-  KSW_CUDA(cudaGetLastError());
+  KSW_LAUNCH(kern, dim3(grid), dim3(kThreadsF8), Cfg::kSmemBytes, s, ta, tb, kp);
   return MOE_OK;
 }
 
@@ -877,6 +942,7 @@ KParams base_params(const GroupedGemmArgs& a, int elem_bytes) {
   kp.sb_rb = int32_t(ceil_div(a.n, 128));
   kp.sb_kb = int32_t(ceil_div(a.k, 128));
   kp.up_offset = int32_t(a.n / 2);
+  kp.early_meta = a.early_meta;
   kp.wait_limit_ns = kWaitLimitNs;
   return kp;
 }

@@ -43,6 +43,11 @@ struct GroupedGemmArgs {
   int out_dtype;               // down: rows dtype, F32 (0, default) or the 16-bit act dtype
   int32_t* status;
   int block_n;                 // 0 = heuristic
+  // 1 when the align outputs (sorted_ids, expert_ids, num_post_pad) were
+  // written at least two kernels earlier in the stream, so the GEMM may read
+  // them, and request its first weight tiles, before waiting on the kernel
+  // that produced its A operand (programmatic dependent launch).
+  int early_meta;
 };
 
 int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s);

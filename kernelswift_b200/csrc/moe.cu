@@ -298,6 +298,7 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   ga.out = at<void>(workspace, P.off_act);
   ga.splits = 1;
   ga.status = p->status;
+  ga.early_meta = 1;  // align ran two launches earlier (the gather is between)
   if (P.gu_splits > 1) {
     // decode-sized: split K, unweighted fp32 partial rows, then SiLU*up
     GroupedGemmArgs gs = ga;

@@ -37,6 +37,8 @@ template <int PER_LANE, typename Tin, typename Tw, typename Tid>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     topk_softmax_kernel(const Tin* __restrict__ logits, int64_t T, int E, int k, int renorm,
                         Tw* __restrict__ weights, Tid* __restrict__ ids) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int64_t t = int64_t(blockIdx.x) * kWarpsPerBlock + warp; t < T;
        t += int64_t(gridDim.x) * kWarpsPerBlock) {
@@ -96,12 +98,13 @@ int launch_ids(const Tin* logits, int64_t T, int E, int k, int renorm, Tw* w, vo
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(T, kWarpsPerBlock),
                                                                148 * 16)));
   if (ids_dtype == MOE_DTYPE_I32)
-    topk_softmax_kernel<PER_LANE, Tin, Tw, int32_t><<<grid, kWarpsPerBlock * 32, 0, s>>>(
-        logits, T, E, k, renorm, w, static_cast<int32_t*>(ids));
+    KSW_LAUNCH(topk_softmax_kernel<PER_LANE, Tin, Tw, int32_t>, dim3(grid),
+               dim3(kWarpsPerBlock * 32), 0, s, logits, T, E, k, renorm, w,
+               static_cast<int32_t*>(ids));
   else
-    topk_softmax_kernel<PER_LANE, Tin, Tw, int64_t><<<grid, kWarpsPerBlock * 32, 0, s>>>(
-        logits, T, E, k, renorm, w, static_cast<int64_t*>(ids));
-  KSW_CUDA(cudaGetLastError());
+    KSW_LAUNCH(topk_softmax_kernel<PER_LANE, Tin, Tw, int64_t>, dim3(grid),
+               dim3(kWarpsPerBlock * 32), 0, s, logits, T, E, k, renorm, w,
+               static_cast<int64_t*>(ids));
   return MOE_OK;
 }
 

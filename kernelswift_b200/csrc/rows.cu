@@ -123,6 +123,8 @@ __global__ void __launch_bounds__(kWarps * 32)
                        const int32_t* __restrict__ sorted,
                        const int32_t* __restrict__ num_post_pad, int64_t max_rows,
                        int64_t numel, int64_t src_rows, Tout* __restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
   for (int64_t m = int64_t(blockIdx.x) * kWarps + warp; m < rows;
@@ -157,6 +159,8 @@ __global__ void __launch_bounds__(kWarps * 32)
                       const int32_t* __restrict__ num_post_pad, int64_t max_rows,
                       int64_t numel, int64_t src_rows, uint8_t* __restrict__ dst,
                       float* __restrict__ scale) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
   const int64_t groups = (H + 127) / 128;
@@ -193,6 +197,8 @@ __global__ void __launch_bounds__(kWarps * 32)
                      const int32_t* __restrict__ num_post_pad, int64_t max_rows,
                      int64_t numel, int64_t src_rows, int8_t* __restrict__ dst,
                      float* __restrict__ scale) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
   for (int64_t m = int64_t(blockIdx.x) * kWarps + warp; m < rows;
@@ -231,6 +237,8 @@ __global__ void __launch_bounds__(256)
     sum_topk_kernel(const Tp* __restrict__ part, int splits, int64_t T,
                     int top_k, int64_t H, int64_t numel, const IdT* __restrict__ ids,
                     int E, Tout* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t vec_per_row = H / 8;
   const int64_t total = T * vec_per_row;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -265,6 +273,8 @@ __global__ void __launch_bounds__(256)
                          const int32_t* __restrict__ sorted,
                          const int32_t* __restrict__ num_post_pad, int64_t max_rows,
                          Tout* __restrict__ act) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
   const int64_t vec_per_row = I / 8;
   const int64_t total = rows * vec_per_row;
@@ -302,6 +312,8 @@ __global__ void __launch_bounds__(256)
     combine_rows_kernel(const Tin* __restrict__ rows, const int32_t* __restrict__ inv,
                         const Tw* __restrict__ w, int64_t T, int top_k, int64_t H,
                         Tout* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t vec_per_row = H / 8;
   const int64_t total = T * vec_per_row;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -341,20 +353,20 @@ int gather_launch(const GatherArgs& a, cudaStream_t s) {
   const int block = kWarps * 32;
   if (a.quant == MOE_QUANT_NONE) {
     if (a.src_dtype == MOE_DTYPE_F32 && a.dst_dtype == MOE_DTYPE_BF16)
-      gather_cast_kernel<float, __nv_bfloat16><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_cast_kernel<float, __nv_bfloat16>, dim3(grid), dim3(block), 0, s,
           static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<__nv_bfloat16*>(a.dst));
     else if (a.src_dtype == MOE_DTYPE_F32 && a.dst_dtype == MOE_DTYPE_F16)
-      gather_cast_kernel<float, __half><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_cast_kernel<float, __half>, dim3(grid), dim3(block), 0, s,
           static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<__half*>(a.dst));
     else if (a.src_dtype == MOE_DTYPE_BF16 && a.dst_dtype == MOE_DTYPE_BF16)
-      gather_cast_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_cast_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(grid), dim3(block), 0, s,
           static_cast<const __nv_bfloat16*>(a.src), a.H, a.top_k, a.sorted,
           a.num_post_pad, a.max_rows, a.numel, a.src_rows,
           static_cast<__nv_bfloat16*>(a.dst));
     else if (a.src_dtype == MOE_DTYPE_F16 && a.dst_dtype == MOE_DTYPE_F16)
-      gather_cast_kernel<__half, __half><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_cast_kernel<__half, __half>, dim3(grid), dim3(block), 0, s,
           static_cast<const __half*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<__half*>(a.dst));
     else
@@ -362,16 +374,16 @@ int gather_launch(const GatherArgs& a, cudaStream_t s) {
   } else if (a.quant == MOE_QUANT_FP8_BLOCK) {
     KSW_REQUIRE(a.scale != nullptr, MOE_ERR_INVALID_ARG, "gather: null scale");
     if (a.src_dtype == MOE_DTYPE_F32)
-      gather_fp8_kernel<float><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_fp8_kernel<float>, dim3(grid), dim3(block), 0, s,
           static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<uint8_t*>(a.dst), a.scale);
     else if (a.src_dtype == MOE_DTYPE_BF16)
-      gather_fp8_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_fp8_kernel<__nv_bfloat16>, dim3(grid), dim3(block), 0, s,
           static_cast<const __nv_bfloat16*>(a.src), a.H, a.top_k, a.sorted,
           a.num_post_pad, a.max_rows, a.numel, a.src_rows,
           static_cast<uint8_t*>(a.dst), a.scale);
     else if (a.src_dtype == MOE_DTYPE_F16)
-      gather_fp8_kernel<__half><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_fp8_kernel<__half>, dim3(grid), dim3(block), 0, s,
           static_cast<const __half*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<uint8_t*>(a.dst), a.scale);
     else
@@ -379,16 +391,16 @@ int gather_launch(const GatherArgs& a, cudaStream_t s) {
   } else if (a.quant == MOE_QUANT_INT8_CHANNEL) {
     KSW_REQUIRE(a.scale != nullptr, MOE_ERR_INVALID_ARG, "gather: null scale");
     if (a.src_dtype == MOE_DTYPE_F32)
-      gather_i8_kernel<float><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_i8_kernel<float>, dim3(grid), dim3(block), 0, s,
           static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<int8_t*>(a.dst), a.scale);
     else if (a.src_dtype == MOE_DTYPE_BF16)
-      gather_i8_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_i8_kernel<__nv_bfloat16>, dim3(grid), dim3(block), 0, s,
           static_cast<const __nv_bfloat16*>(a.src), a.H, a.top_k, a.sorted,
           a.num_post_pad, a.max_rows, a.numel, a.src_rows,
           static_cast<int8_t*>(a.dst), a.scale);
     else if (a.src_dtype == MOE_DTYPE_F16)
-      gather_i8_kernel<__half><<<grid, block, 0, s>>>(
+      KSW_LAUNCH(gather_i8_kernel<__half>, dim3(grid), dim3(block), 0, s,
           static_cast<const __half*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<int8_t*>(a.dst), a.scale);
     else
@@ -412,11 +424,11 @@ int sum_topk_launch(const SumArgs& a, cudaStream_t s) {
   const int64_t numel = a.T * a.top_k;
 #define KSW_SUM(TOUT, IDT)                                                                   \
   if (a.part_dtype == MOE_DTYPE_F32)                                                         \
-    sum_topk_kernel<TOUT, IDT, float><<<grid, 256, 0, s>>>(                                  \
+    KSW_LAUNCH(sum_topk_kernel<TOUT, IDT, float>, dim3(grid), dim3(256), 0, s,                                   \
         static_cast<const float*>(a.part), a.splits, a.T, a.top_k, a.H, numel,               \
         static_cast<const IDT*>(a.ids), a.E, static_cast<TOUT*>(a.out));                     \
   else                                                                                       \
-    sum_topk_kernel<TOUT, IDT, TOUT><<<grid, 256, 0, s>>>(                                   \
+    KSW_LAUNCH(sum_topk_kernel<TOUT, IDT, TOUT>, dim3(grid), dim3(256), 0, s,                                    \
         static_cast<const TOUT*>(a.part), a.splits, a.T, a.top_k, a.H, numel,                \
         static_cast<const IDT*>(a.ids), a.E, static_cast<TOUT*>(a.out))
   const bool i64 = a.ids_dtype == MOE_DTYPE_I64;
@@ -443,10 +455,10 @@ int swiglu_reduce_launch(const float* part, int splits, int64_t numel, int64_t I
   const int64_t total = max_rows * (I / 8);
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 148 * 16)));
   if (act_dtype == MOE_DTYPE_BF16)
-    swiglu_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+    KSW_LAUNCH(swiglu_reduce_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s,
         part, splits, numel, I, sorted, num_post_pad, max_rows, static_cast<__nv_bfloat16*>(act));
   else if (act_dtype == MOE_DTYPE_F16)
-    swiglu_reduce_kernel<__half><<<grid, 256, 0, s>>>(
+    KSW_LAUNCH(swiglu_reduce_kernel<__half>, dim3(grid), dim3(256), 0, s,
         part, splits, numel, I, sorted, num_post_pad, max_rows, static_cast<__half*>(act));
   else
     return fail(MOE_ERR_UNSUPPORTED, "swiglu_reduce: act dtype must be bf16/f16");
@@ -462,7 +474,7 @@ int combine_launch(const CombineArgs& a, cudaStream_t s) {
   const int64_t total = a.T * (a.H / 8);
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 148 * 32)));
 #define KSW_COMB(TIN, TW, TOUT)                                                         \
-  combine_rows_kernel<TIN, TW, TOUT><<<grid, 256, 0, s>>>(                              \
+  KSW_LAUNCH(combine_rows_kernel<TIN, TW, TOUT>, dim3(grid), dim3(256), 0, s,                               \
       static_cast<const TIN*>(a.rows), a.inv, static_cast<const TW*>(a.weights), a.T,   \
       a.top_k, a.H, static_cast<TOUT*>(a.out))
 #define KSW_COMB_W(TIN, TOUT)                                                           \

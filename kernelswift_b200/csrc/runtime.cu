@@ -1,6 +1,7 @@
 // Host runtime of the C ABI: status strings, the thread-local error message,
 // device checks, the device status word, TMA tensor-map encoding and the
 // bounded-wait self-test kernel.
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -61,6 +62,14 @@ int check_device(int* num_sms) {
                 "not a compute capability 10.0 GPU");
   if (num_sms) *num_sms = g_dev_sms[dev];
   return MOE_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_NO_PDL");
+    return !(v && v[0] && v[0] != '0');
+  }();
+  return on;
 }
 
 int encode_tma_2d(CUtensorMap* tm, CUtensorMapDataType dtype, int elem_bytes,
