@@ -14,6 +14,7 @@ namespace ksw {
 namespace {
 
 constexpr int kWarps = 8;  // rows per CTA
+constexpr int kBatch = 4;  // loads in flight per lane in the row loops
 constexpr float kFp8Max = 448.0f;
 constexpr float kInt8Max = 127.0f;
 
@@ -133,10 +134,15 @@ __global__ void __launch_bounds__(kWarps * 32)
     if (sr < 0 || sr >= src_rows) continue;
     const Tin* s = src + sr * H;
     Tout* d = dst + m * H;
-    for (int64_t h = int64_t(lane) * 8; h < H; h += 32 * 8) {
-      float v[8];
-      load8(s + h, v);
-      store8(d + h, v);
+    // kBatch 16-byte loads in flight per lane before the stores
+    for (int64_t h0 = int64_t(lane) * 8; h0 < H; h0 += kBatch * 256) {
+      float v[kBatch][8];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (h0 + u * 256 < H) load8(s + h0 + u * 256, v[u]);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (h0 + u * 256 < H) store8(d + h0 + u * 256, v[u]);
     }
   }
 }
@@ -169,22 +175,34 @@ __global__ void __launch_bounds__(kWarps * 32)
     const int64_t sr = sorted ? source_row(sorted, m, numel, top_k) : m;
     if (sr < 0 || sr >= src_rows) continue;
     const Tin* s = src + sr * H;
-    // two groups per warp iteration: lanes 0-15 group g, lanes 16-31 group g+1
-    for (int64_t g0 = 0; g0 < groups; g0 += 2) {
-      const int64_t g = g0 + (lane >> 4);
-      const int64_t h = g * 128 + (lane & 15) * 8;
-      const bool in = g < groups && h < H;
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (in) load8(s + h, v);
-      float amax = 0.0f;
+    // two groups per warp step: lanes 0-15 group g, lanes 16-31 group g+1;
+    // kBatch steps' loads are issued before any of them is quantised
+    for (int64_t gb = 0; gb < groups; gb += 2 * kBatch) {
+      float v[kBatch][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t g = gb + 2 * u + (lane >> 4);
+        const int64_t h = g * 128 + (lane & 15) * 8;
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float sc = quant_scale(amax, kFp8Max);
-      const float inv = 1.0f / sc;
-      if (in) *reinterpret_cast<uint2*>(dst + m * H + h) = pack_e4m3x8(v, inv);
-      if (in && (lane & 15) == 0) scale[m * groups + g] = sc;
+        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+        if (g < groups && h < H) load8(s + h, v[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t g = gb + 2 * u + (lane >> 4);
+        const int64_t h = g * 128 + (lane & 15) * 8;
+        const bool in = g < groups && h < H;
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1)
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float sc = quant_scale(amax, kFp8Max);
+        const float inv = 1.0f / sc;
+        if (in) *reinterpret_cast<uint2*>(dst + m * H + h) = pack_e4m3x8(v[u], inv);
+        if (in && (lane & 15) == 0) scale[m * groups + g] = sc;
+      }
     }
   }
 }
@@ -207,25 +225,39 @@ __global__ void __launch_bounds__(kWarps * 32)
     if (sr < 0 || sr >= src_rows) continue;
     const Tin* s = src + sr * H;
     float amax = 0.0f;
-    for (int64_t h = int64_t(lane) * 8; h < H; h += 32 * 8) {
-      float v[8];
-      load8(s + h, v);
+    for (int64_t h0 = int64_t(lane) * 8; h0 < H; h0 += kBatch * 256) {
+      float v[kBatch][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      for (int u = 0; u < kBatch; ++u) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+        if (h0 + u * 256 < H) load8(s + h0 + u * 256, v[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
     }
     amax = warp_max(amax);
     const float sc = quant_scale(amax, kInt8Max);
     const float inv = 1.0f / sc;
-    for (int64_t h = int64_t(lane) * 8; h < H; h += 32 * 8) {
-      float v[8];
-      load8(s + h, v);
-      uint32_t lo = 0, hi = 0;
+    for (int64_t h0 = int64_t(lane) * 8; h0 < H; h0 += kBatch * 256) {
+      float v[kBatch][8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        lo |= uint32_t(uint8_t(to_i8(v[i], inv))) << (8 * i);
-        hi |= uint32_t(uint8_t(to_i8(v[4 + i], inv))) << (8 * i);
+      for (int u = 0; u < kBatch; ++u)
+        if (h0 + u * 256 < H) load8(s + h0 + u * 256, v[u]);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t h = h0 + u * 256;
+        if (h >= H) continue;
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          lo |= uint32_t(uint8_t(to_i8(v[u][i], inv))) << (8 * i);
+          hi |= uint32_t(uint8_t(to_i8(v[u][4 + i], inv))) << (8 * i);
+        }
+        *reinterpret_cast<uint2*>(dst + m * H + h) = make_uint2(lo, hi);
       }
-      *reinterpret_cast<uint2*>(dst + m * H + h) = make_uint2(lo, hi);
     }
     if (lane == 0) scale[m] = sc;
   }
@@ -246,18 +278,34 @@ __global__ void __launch_bounds__(256)
     const int64_t t = i / vec_per_row;
     const int64_t h = (i - t * vec_per_row) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < top_k; ++j) {
-      const int64_t r = t * top_k + j;
-      if (ids != nullptr) {
-        const long long e = static_cast<long long>(ids[r]);
-        if (e < 0 || e >= E) continue;
-      }
-      for (int s = 0; s < splits; ++s) {
-        float v[8];
-        load8(part + (int64_t(s) * numel + r) * H + h, v);
+    // (slot j, split s) pairs in j-major order, eight at a time: all eight
+    // loads are in flight before the adds (at decode sizes each thread has
+    // few rows and the reduction is load-latency bound); the additions keep
+    // the j-major, s-minor order. Dropped slots add exact zeros.
+    const int pairs = top_k * splits;
+    for (int c0 = 0; c0 < pairs; c0 += 8) {
+      float v[8][8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] += v[q];
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u;
+        const int j = c / splits;
+        const int64_t r = t * top_k + j;
+        bool ok = c < pairs;
+        if (ok && ids != nullptr) {
+          const long long e = static_cast<long long>(ids[r]);
+          ok = e >= 0 && e < E;
+        }
+        if (ok) {
+          load8(part + (int64_t(c - j * splits) * numel + r) * H + h, v[u]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[u][q] = 0.f;
+        }
       }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += v[u][q];
     }
     store8(out + t * H + h, acc);
   }
@@ -288,16 +336,27 @@ __global__ void __launch_bounds__(256)
     const int64_t gate_col = 32 * g + c0, up_col = gate_col + 16;
     float gsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float usum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < splits; ++s) {
-      const float* row = part + (int64_t(s) * numel + r) * (2 * I);
-      float gv[8], uv[8];
-      load8(row + gate_col, gv);
-      load8(row + up_col, uv);
+    // four splits' loads in flight at a time; sums in split order
+    for (int s0 = 0; s0 < splits; s0 += 4) {
+      float gv[4][8], uv[4][8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        gsum[q] += gv[q];
-        usum[q] += uv[q];
+      for (int u = 0; u < 4; ++u) {
+        if (s0 + u < splits) {
+          const float* row = part + (int64_t(s0 + u) * numel + r) * (2 * I);
+          load8(row + gate_col, gv[u]);
+          load8(row + up_col, uv[u]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) gv[u][q] = uv[u][q] = 0.f;
+        }
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          gsum[q] += gv[u][q];
+          usum[q] += uv[u][q];
+        }
     }
     float out[8];
 #pragma unroll
@@ -321,15 +380,27 @@ __global__ void __launch_bounds__(256)
     const int64_t t = i / vec_per_row;
     const int64_t h = (i - t * vec_per_row) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < top_k; ++j) {
-      const int64_t r = t * top_k + j;
-      const int src = __ldg(inv + r);
-      if (src < 0) continue;
-      const float wj = to_f32(w[r]);
-      float v[8];
-      load8(rows + int64_t(src) * H + h, v);
+    // four slots at a time, loads first (as in sum_topk_kernel); slots that
+    // were not sent contribute 0 * 0
+    for (int j0 = 0; j0 < top_k; j0 += 4) {
+      float v[4][8], wj[4];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] = fmaf(wj, v[q], acc[q]);
+      for (int u = 0; u < 4; ++u) {
+        const int64_t r = t * top_k + j0 + u;
+        const int src = j0 + u < top_k ? __ldg(inv + r) : -1;
+        if (src >= 0) {
+          wj[u] = to_f32(w[r]);
+          load8(rows + int64_t(src) * H + h, v[u]);
+        } else {
+          wj[u] = 0.f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[u][q] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = fmaf(wj[u], v[u][q], acc[q]);
     }
     store8(out + t * H + h, acc);
   }
