@@ -278,34 +278,38 @@ __global__ void __launch_bounds__(256)
     const int64_t t = i / vec_per_row;
     const int64_t h = (i - t * vec_per_row) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    // (slot j, split s) pairs in j-major order, eight at a time: all eight
-    // loads are in flight before the adds (at decode sizes each thread has
-    // few rows and the reduction is load-latency bound); the additions keep
-    // the j-major, s-minor order. Dropped slots add exact zeros.
-    const int pairs = top_k * splits;
-    for (int c0 = 0; c0 < pairs; c0 += 8) {
-      float v[8][8];
+    // Four top-k slots at a time: their ids first, then for each K split
+    // the four partial rows, all in flight before the adds (at decode sizes
+    // each thread has few rows to visit and the reduction is bound by load
+    // latency). Dropped slots add exact zeros.
+    for (int j0 = 0; j0 < top_k; j0 += 4) {
+      int64_t rr[4];
+      bool ok[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int c = c0 + u;
-        const int j = c / splits;
-        const int64_t r = t * top_k + j;
-        bool ok = c < pairs;
-        if (ok && ids != nullptr) {
-          const long long e = static_cast<long long>(ids[r]);
-          ok = e >= 0 && e < E;
-        }
-        if (ok) {
-          load8(part + (int64_t(c - j * splits) * numel + r) * H + h, v[u]);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) v[u][q] = 0.f;
+      for (int u = 0; u < 4; ++u) {
+        rr[u] = t * top_k + j0 + u;
+        ok[u] = j0 + u < top_k;
+        if (ok[u] && ids != nullptr) {
+          const long long e = static_cast<long long>(ids[rr[u]]);
+          ok[u] = e >= 0 && e < E;
         }
       }
+      for (int sp = 0; sp < splits; ++sp) {
+        float v[4][8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < 4; ++u) {
+          if (ok[u]) {
+            load8(part + (int64_t(sp) * numel + rr[u]) * H + h, v[u]);
+          } else {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] += v[u][q];
+            for (int q = 0; q < 8; ++q) v[u][q] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] += v[u][q];
+      }
     }
     store8(out + t * H + h, acc);
   }
