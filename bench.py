@@ -219,7 +219,8 @@ def run_reference(args, H, I, E, k, quant, T, bias, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": workload_config(args.workload, H, I, E, k, quant, T, args.gpus),
+        "config": dict(workload_config(args.workload, H, I, E, k, quant, T, args.gpus),
+                       l2="not applicable: host CPU run", parallelism="single host process"),
         "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{sample} tokens per step of the {args.workload} layer, "
                                    "base.py forward restated in torch-CPU bf16 with the "
