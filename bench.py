@@ -77,6 +77,9 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (0 = workload default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ep-exchange", choices=("auto", "nccl", "peer"), default="auto",
+                    help="expert-parallel row exchange for --gpus > 1 (auto: NVLink peer "
+                         "memory)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every step eagerly instead of replaying a CUDA graph of the "
                          "whole forward (1 GPU runs use the graph by default)")
@@ -231,13 +234,14 @@ def run_reference(args, H, I, E, k, quant, T, bias, rank):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(name, H, I, E, k, quant, T, n):
+def workload_config(name, H, I, E, k, quant, T, n, exchange=None):
     return {"workload": f"{name} MoE layer H={H} I={I} E={E} top-{k} "
                         f"{'bf16' if quant == 'none' else quant + ' W8A8'}, {T} tokens/GPU",
             "hidden": H, "intermediate": I, "experts": E, "top_k": k, "quant": quant,
             "tokens_per_gpu": T, "global_tokens": T * n,
-            "parallelism": f"ep{n} (E/{n} experts per GPU, NCCL all_to_all)" if n > 1
-            else "single",
+            "parallelism": (f"ep{n} (E/{n} experts per GPU, " + (
+                "token rows exchanged by dispatch/combine kernels over NVLink peer memory)"
+                if exchange == "peer" else "NCCL all_to_all)")) if n > 1 else "single",
             "l2": f"flushed between steps outside the timed windows ({L2_FLUSH_BYTES >> 20} MB "
                   f"write{', then a read of another ' + str(L2_FLUSH_BYTES >> 20) + ' MB that evicts the dirty lines' if L2Flush.evict else ''}); "
                   "weights also exceed L2"}
@@ -298,7 +302,8 @@ def main():
                                     stage_events=stage_arr)
     else:
         # expert parallel: this rank holds E/world experts, routes its own T
-        # tokens over all E, exchanges rows with NCCL all_to_all
+        # tokens over all E; rows move through the peer-memory dispatch and
+        # combine kernels (--ep-exchange nccl: NCCL all_to_all)
         from kernelswift_b200.ep import ExpertParallelMoE
 
         if E % world:
@@ -306,18 +311,21 @@ def main():
         el = E // world
         w1 = torch.randn(el, 2 * I, H, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(H)
         w2 = torch.randn(el, H, I, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(I)
-        ep = ExpertParallelMoE(w1, w2, E, k, quant=quant)
+        ep = ExpertParallelMoE(w1, w2, E, k, quant=quant, exchange=args.ep_exchange,
+                               max_tokens=T, dtype=hidden.dtype)
         del w1, w2
 
         def step(stage_arr=None):
             tw, ti = fm.fused_topk(hidden, logits, k, weights_dtype=hidden.dtype)
-            out = ep(hidden, tw, ti, stage_events=stage_arr)
-            rows_per_launch[0] = ep.last_rows_received
-            return out
+            return ep(hidden, tw, ti, stage_events=stage_arr)
 
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
+    if world > 1:
+        rows_per_launch[0] = ep.rows_received()  # the same routing every step
+        if ep.peer is not None:
+            ep.peer.check()
     _, ti0 = fm.fused_topk(hidden, logits, k)
     if world == 1:
         experts_hit[0] = int(torch.unique(ti0).numel())
@@ -533,9 +541,12 @@ def main():
     # else 3), gather, gate-up (+ swiglu_reduce when K-split), [activation
     # quant], down, top-k sum
     numel = rows_per_launch[0]
+    if world > 1 and ep.peer is not None:
+        numel = ep.peer.capacity  # align runs over the whole receive buffer
     launches_per_step = 1 + (1 if numel <= 8192 else 3) + 4 + (0 if quant == "none" else 1)
     if world > 1:
-        launches_per_step += 2  # pack rows by destination, weighted combine
+        # plan, pack, combine (nccl) | plan, dispatch, signal, combine, step end (peer)
+        launches_per_step += 3 if ep.peer is None else 5
     if rank == 0:
         line = {
             "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
@@ -543,7 +554,8 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16" if quant == "none" else ("e4m3" if quant == "fp8" else "int8"),
             "data": "synthetic",
-            "config": workload_config(args.workload, H, I, E, k, quant, T, world),
+            "config": workload_config(args.workload, H, I, E, k, quant, T, world,
+                                      None if world == 1 else ep.exchange),
             "tflops": tflops,
             "stage_ms": stage_ms,
             "roofline": roofline,
@@ -556,6 +568,9 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        if ep.peer is not None:
+            ep.peer.check()
+        ep.close()
         dist.destroy_process_group()
 
 

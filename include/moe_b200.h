@@ -362,6 +362,75 @@ int moe_ep_plan(const void* topk_ids, int ids_dtype, int64_t numel,
                 int32_t* inv_index, int64_t* counts, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Expert parallelism over NVLink peer memory. No reference counterpart (the */
+/* reference has no expert parallelism): it replaces, across the ranks of    */
+/* one node, the per-expert loop and weighted sum of                         */
+/* kernels/track1-triton/fused_moe/base.py:64-76, with token rows moved by   */
+/* the dispatch and combine kernels themselves (stores into and loads from   */
+/* the other GPUs' buffers) and no host synchronisation.                     */
+/*                                                                          */
+/* Each rank owns one device buffer (created here, shared with the others   */
+/* through CUDA IPC handles): a control block, `capacity` received expert    */
+/* ids, `capacity` received rows and `capacity` result rows of hidden_size   */
+/* act_dtype (F16/BF16) elements. One step, all on the caller's stream:      */
+/*   moe_ep_plan -> moe_ep_peer_dispatch -> moe_fused_experts over the      */
+/*   received rows (num_tokens = capacity, top_k = 1, unit weights, ids from */
+/*   the buffer; unused slots hold id -1 and are dropped) writing the result */
+/*   rows -> moe_ep_peer_combine.                                           */
+/* Every rank must take every step. Waits on other ranks are bounded;       */
+/* on expiry, or when a rank would receive more than `capacity` rows, the    */
+/* kernels store an error code (MOE_ERR_TIMEOUT / MOE_ERR_WORKSPACE) in the  */
+/* optional device status word and skip their work.                         */
+/* ------------------------------------------------------------------------ */
+#define MOE_EP_MAX_RANKS 8
+#define MOE_EP_HANDLE_BYTES 64
+
+typedef struct moe_ep_peer moe_ep_peer_t;
+
+/* Allocates this rank's buffer; writes its IPC handle (MOE_EP_HANDLE_BYTES)
+ * to handle_out. 2 <= world <= MOE_EP_MAX_RANKS. wait_limit_ms bounds every
+ * wait on another rank (0: 5000 ms). After a timeout the object is unusable
+ * (ranks may disagree on the step) and must be destroyed. */
+int moe_ep_peer_create(int world, int rank, int64_t capacity, int64_t hidden_size,
+                       int act_dtype, int wait_limit_ms, moe_ep_peer_t** out,
+                       void* handle_out);
+
+/* Opens the other ranks' buffers: `handles` holds world handles, rank order. */
+int moe_ep_peer_connect(moe_ep_peer_t* ep, const void* handles);
+
+/* This rank's received rows [capacity, hidden_size], received expert ids
+ * [capacity] (int32, destination-local) and result rows [capacity,
+ * hidden_size]. */
+int moe_ep_peer_buffers(const moe_ep_peer_t* ep, void** recv_rows, int32_t** recv_ids,
+                        void** result_rows);
+
+/* Sends this rank's rows: for send position p (moe_ep_plan's order,
+ * send_eid and counts), row hidden[order[p] / top_k] and id send_eid[p] go
+ * to the destination rank's buffer; returns (on the stream) once every rank's
+ * rows for this rank have arrived. hidden is [num_tokens, hidden_size] in the
+ * buffer's act dtype. */
+int moe_ep_peer_dispatch(moe_ep_peer_t* ep, const void* hidden, int64_t num_tokens, int top_k,
+                         const int32_t* order, const int32_t* send_eid, const int64_t* counts,
+                         int32_t* status, void* stream);
+
+/* Signals that this rank's result rows are complete, waits for the other
+ * ranks' signals and computes out[t] = sum_j w[t,j] * result row of slot
+ * t*top_k + j (read from the rank that computed it; slots with
+ * inv_index < 0 contribute nothing). out is [num_tokens, hidden_size] in
+ * the act dtype; weights F32/F16/BF16. Ends the step. */
+int moe_ep_peer_combine(moe_ep_peer_t* ep, const int32_t* inv_index, const void* weights,
+                        int weights_dtype, int64_t num_tokens, int top_k, void* out,
+                        int32_t* status, void* stream);
+
+/* Closes the mappings of the other ranks' buffers. */
+int moe_ep_peer_disconnect(moe_ep_peer_t* ep);
+
+/* Frees this rank's buffer (closing any mappings still open). Call it after
+ * the stream has drained and every rank has disconnected: other ranks must
+ * not hold a mapping of a buffer that is freed. */
+int moe_ep_peer_destroy(moe_ep_peer_t* ep);
+
+/* ------------------------------------------------------------------------ */
 /* Self-test of the bounded device waits (failure detection without a GPU   */
 /* fault): launches one CTA whose mbarrier wait is never satisfied, with a   */
 /* limit of `limit_us` microseconds. The kernel stores MOE_ERR_TIMEOUT into  */

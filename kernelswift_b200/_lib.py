@@ -90,7 +90,17 @@ SIGNATURES = {
     "moe_ep_plan": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp]),
     "moe_combine_rows": (_int, [_vp, _int, _vp, _vp, _int, _i64, _int, _i64, _vp, _int, _vp]),
     "moe_selftest_wait_timeout": (_int, [_vp, _int, _vp]),
+    "moe_ep_peer_create": (_int, [_int, _int, _i64, _i64, _int, _int, _vp, _vp]),
+    "moe_ep_peer_connect": (_int, [_vp, _vp]),
+    "moe_ep_peer_buffers": (_int, [_vp, _vp, _vp, _vp]),
+    "moe_ep_peer_dispatch": (_int, [_vp, _vp, _i64, _int, _vp, _vp, _vp, _vp, _vp]),
+    "moe_ep_peer_combine": (_int, [_vp, _vp, _vp, _int, _i64, _int, _vp, _vp, _vp]),
+    "moe_ep_peer_disconnect": (_int, [_vp]),
+    "moe_ep_peer_destroy": (_int, [_vp]),
 }
+
+EP_MAX_RANKS = 8
+EP_HANDLE_BYTES = 64
 
 
 class MoeError(RuntimeError):

@@ -27,6 +27,17 @@ The device work (plan, pack, local experts, combine) goes through a backend
 object;
 `CudaBackend` runs the library's kernels and is the only backend this package
 provides.
+
+With exchange="peer" (ranks on one node, 2-8 GPUs) steps 2-4 and 6 are
+replaced by two kernels that move the rows themselves over NVLink
+(`PeerExchange`, the moe_ep_peer_* entry points): dispatch stores each row
+into the destination GPU's receive buffer (mapped with CUDA IPC) at an
+offset every rank derives from a counts matrix the ranks write into each
+other's memory, and combine loads each result row from the GPU that computed
+it. The ranks hand off through flags in each other's memory, so a step needs
+no host synchronisation and no NCCL call. The local expert pass then runs
+over the whole receive buffer (`capacity` rows; unused slots carry id -1 and
+are dropped by align).
 """
 from __future__ import annotations
 
@@ -94,6 +105,79 @@ class CudaBackend:
         return out
 
 
+class _DeviceArray:
+    """__cuda_array_interface__ of device memory the library owns."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3,
+                                         "strides": None}
+
+
+class PeerExchange:
+    """This rank's moe_ep_peer buffer, connected to every rank's buffer.
+
+    Collective: every rank of `group` constructs it with the same capacity,
+    hidden size and dtype (the IPC handles are exchanged with
+    all_gather_object). `close()` is collective too.
+    """
+
+    def __init__(self, group, world: int, rank: int, capacity: int, hidden_size: int,
+                 dtype: torch.dtype, device: torch.device, wait_limit_ms: int = 0):
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("the peer exchange moves f16/bf16 rows")
+        self.group = group
+        self.device = device
+        self.capacity = capacity
+        self.dtype = dtype
+        handle = ctypes.c_void_p()
+        raw = (ctypes.c_uint8 * _lib.EP_HANDLE_BYTES)()
+        _lib.call("moe_ep_peer_create", world, rank, capacity, hidden_size,
+                  fm._code(torch.empty(0, dtype=dtype)), wait_limit_ms, ctypes.byref(handle),
+                  raw)
+        self.handle = handle
+        try:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(raw), group=group)
+            _lib.call("moe_ep_peer_connect", handle, b"".join(handles))
+            dist.barrier(group=group)
+        except Exception:
+            _lib.load().moe_ep_peer_destroy(handle)
+            self.handle = None
+            raise
+        rows, ids, res = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.call("moe_ep_peer_buffers", handle, ctypes.byref(rows), ctypes.byref(ids),
+                  ctypes.byref(res))
+        shape = (capacity, hidden_size)
+        self.recv_rows = torch.as_tensor(_DeviceArray(rows.value, shape, "<i2"),
+                                         device=device).view(dtype)
+        self.recv_ids = torch.as_tensor(_DeviceArray(ids.value, (capacity,), "<i4"),
+                                        device=device)
+        self.result_rows = torch.as_tensor(_DeviceArray(res.value, shape, "<i2"),
+                                           device=device).view(dtype)
+        self.ones = torch.ones(capacity, 1, dtype=torch.float32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def check(self) -> None:
+        """Raises if a kernel of the exchange recorded an error (synchronises)."""
+        code = int(self.status.item())
+        if code:
+            raise _lib.MoeError(code, "expert-parallel peer exchange",
+                                "a rank did not arrive in time or a receive buffer overflowed")
+
+    def close(self) -> None:
+        """Collective: unmaps the other ranks' buffers, then frees this one."""
+        if self.handle is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        _lib.load().moe_ep_peer_disconnect(self.handle)
+        dist.barrier(group=self.group)
+        self.recv_rows = self.recv_ids = self.result_rows = None
+        _lib.call("moe_ep_peer_destroy", self.handle)
+        self.handle = None
+
+
 class ExpertParallelMoE:
     """Fused MoE with experts sharded over the ranks of `group`.
 
@@ -105,7 +189,13 @@ class ExpertParallelMoE:
 
     def __init__(self, w1_local: torch.Tensor | None, w2_local: torch.Tensor | None,
                  num_experts: int, top_k: int, group=None, quant: str = "none",
-                 backend=None):
+                 backend=None, exchange: str = "auto", max_tokens: int | None = None,
+                 dtype: torch.dtype = torch.bfloat16, wait_limit_ms: int = 0):
+        """exchange: "nccl" (all_to_all), "peer" (NVLink peer memory, needs
+        max_tokens: the most tokens a rank passes to one forward) or "auto"
+        (peer when max_tokens is given, the CUDA backend is used and the group
+        has 2-8 ranks on GPUs, else nccl). `dtype` is the row dtype of the
+        peer exchange (the hidden states' dtype)."""
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -120,11 +210,30 @@ class ExpertParallelMoE:
             compute = torch.bfloat16 if w1_local.dtype != torch.float16 else torch.float16
             backend = CudaBackend(fm.prepare_weights(w1_local, w2_local, quant, compute), quant)
         self.backend = backend
+        self.quant = quant
+        if exchange == "auto":
+            exchange = ("peer" if max_tokens is not None and isinstance(backend, CudaBackend)
+                        and 2 <= self.world <= _lib.EP_MAX_RANKS else "nccl")
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        self.exchange = exchange
+        self.peer = None
+        self.max_tokens = max_tokens
+        self.last_rows_received = 0
+        if exchange == "peer":
+            if max_tokens is None or not isinstance(backend, CudaBackend):
+                raise ValueError("the peer exchange needs max_tokens and the CUDA backend")
+            dev = backend.prep.w13.device
+            # worst case: every token of every rank routed to this rank's experts
+            self.peer = PeerExchange(group, self.world, self.rank, max_tokens * top_k * self.world,
+                                     backend.prep.hidden_size, dtype, dev, wait_limit_ms)
 
     def forward(self, hidden: torch.Tensor, topk_weights: torch.Tensor,
                 topk_ids: torch.Tensor, stage_events=None) -> torch.Tensor:
         """`stage_events` (fused_moe.stage_event_array) times the launches of
         the local expert computation."""
+        if self.peer is not None:
+            return self._forward_peer(hidden, topk_weights, topk_ids, stage_events)
         T, H = hidden.shape
         k = topk_ids.shape[1]
         dev = hidden.device
@@ -156,5 +265,41 @@ class ExpertParallelMoE:
         back = torch.empty(n_send, H, dtype=out_rows.dtype, device=dev)
         dist.all_to_all_single(back, out_rows, send_split, recv_split, group=self.group)
         return self.backend.combine(back, inv, topk_weights, T, k)
+
+    def _forward_peer(self, hidden, topk_weights, topk_ids, stage_events=None):
+        px = self.peer
+        T, H = hidden.shape
+        k = topk_ids.shape[1]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens}")
+        if hidden.dtype != px.dtype:
+            raise ValueError(f"hidden states are {hidden.dtype}, the exchange moves {px.dtype}")
+        dev = hidden.device
+        stream = fm._stream(dev)
+        hidden = hidden.contiguous()
+        order, send_eid, inv, counts = self.backend.plan(topk_ids, self.num_experts, self.world)
+        _lib.call("moe_ep_peer_dispatch", px.handle, fm._ptr(hidden), T, k, fm._ptr(order),
+                  fm._ptr(send_eid), fm._ptr(counts), fm._ptr(px.status), stream)
+        fm.fused_experts(px.recv_rows, self.backend.prep, None, px.ones, px.recv_ids.view(-1, 1),
+                         use_fp8_w8a8=self.quant == "fp8", use_int8_w8a8=self.quant == "int8",
+                         out=px.result_rows, status=px.status, stage_events=stage_events)
+        out = torch.empty(T, H, dtype=hidden.dtype, device=dev)
+        w = topk_weights.contiguous()
+        _lib.call("moe_ep_peer_combine", px.handle, fm._ptr(inv), fm._ptr(w), fm._code(w), T, k,
+                  fm._ptr(out), fm._ptr(px.status), stream)
+        return out
+
+    def rows_received(self) -> int:
+        """Rows this rank's experts processed in the last forward (synchronises
+        in the peer exchange)."""
+        if self.peer is not None:
+            return int((self.peer.recv_ids >= 0).sum())
+        return self.last_rows_received
+
+    def close(self) -> None:
+        """Collective: releases the peer exchange buffers (no-op for nccl)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     __call__ = forward

@@ -1,5 +1,7 @@
-"""GPU: expert parallelism over NCCL, one process per GPU (never more ranks
-than GPUs), checked against the fp32 oracle on each rank's tokens."""
+"""GPU: expert parallelism, one process per GPU (never more ranks than GPUs),
+checked against the fp32 oracle on each rank's tokens: the NCCL all_to_all
+exchange and the NVLink peer-memory dispatch/combine kernels (including a
+rank that never takes a step: the others' bounded waits report a timeout)."""
 import datetime
 import os
 import socket
@@ -34,7 +36,8 @@ def worker(rank, world, port, cfg, q):
         w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
         el = E // world
         ep = ExpertParallelMoE(w1[rank * el:(rank + 1) * el].to(dev),
-                               w2[rank * el:(rank + 1) * el].to(dev), E, k, quant=quant)
+                               w2[rank * el:(rank + 1) * el].to(dev), E, k, quant=quant,
+                               exchange="nccl")
         gt = torch.Generator().manual_seed(10 + rank)
         hidden = torch.randn(T, H, generator=gt).to(torch.bfloat16)
         w, ids = orc.route(torch.randn(T, E, generator=gt), k)
@@ -73,3 +76,140 @@ def test_ep_matches_oracle(cuda_device, quant):
             assert rel <= 5e-2, (rank, rel)  # relative L2 vs the dequantised oracle
         else:
             assert close, (rank, rel)  # rtol 2e-2 / atol 2e-2 vs the fp32 oracle
+
+
+def peer_worker(rank, world, port, cfg, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from kernelswift_b200.ep import ExpertParallelMoE
+    from oracle import moe_oracle as orc
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    ep = None
+    try:
+        E, k, T, H, I, quant, steps = cfg
+        g = torch.Generator().manual_seed(0)
+        w1 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
+        w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
+        el = E // world
+        ep = ExpertParallelMoE(w1[rank * el:(rank + 1) * el].to(dev),
+                               w2[rank * el:(rank + 1) * el].to(dev), E, k, quant=quant,
+                               exchange="peer", max_tokens=T + world, wait_limit_ms=5000)
+        worst = 0.0
+        for step in range(steps):
+            # different token counts per rank and per step, skewed routing
+            gt = torch.Generator().manual_seed(100 * step + rank)
+            Tr = T + rank - (step % 2) * 3
+            hidden = torch.randn(Tr, H, generator=gt).to(torch.bfloat16)
+            logits = torch.randn(Tr, E, generator=gt) + torch.linspace(0, 2, E)
+            w, ids = orc.route(logits, k)
+            out = ep(hidden.to(dev), w.to(dev), ids.to(dev))
+            torch.cuda.synchronize()
+            ep.peer.check()
+            if quant == "fp8":
+                ref = orc.fused_experts_fp8(hidden, w1, w2, w, ids)
+            else:
+                ref = orc.fused_experts(hidden, w1, w2, w, ids)
+            if quant == "none" and not torch.allclose(out.cpu().float(), ref, rtol=2e-2,
+                                                      atol=2e-2):
+                raise AssertionError(f"step {step}: rel {orc.rel_l2(out.cpu(), ref)}")
+            worst = max(worst, orc.rel_l2(out.cpu(), ref))
+        q.put((rank, "ok", worst))
+    except Exception as exc:
+        q.put((rank, "error", repr(exc)[:300]))
+    finally:
+        if ep is not None:
+            ep.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("quant", ["none", "fp8"])
+def test_ep_peer_exchange_matches_oracle(cuda_device, quant):
+    """Dispatch/combine over NVLink peer memory: several steps (the epoch
+    flags advance), uneven token counts per rank, checked on every rank."""
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two GPUs")
+    cfg = (16, 4, 120, 256, 256, quant, 3)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=peer_worker, args=(r, world, port, cfg, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert r[1] == "ok", r
+        assert r[2] <= 5e-2, r
+
+
+def absent_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from kernelswift_b200.ep import ExpertParallelMoE
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    ep = None
+    try:
+        E, k, T, H, I = 8, 2, 16, 128, 128
+        g = torch.Generator().manual_seed(0)
+        el = E // world
+        w1 = (torch.randn(el, 2 * I, H, generator=g) / H ** 0.5).to(dev)
+        w2 = (torch.randn(el, H, I, generator=g) / I ** 0.5).to(dev)
+        ep = ExpertParallelMoE(w1, w2, E, k, exchange="peer", max_tokens=T, wait_limit_ms=1000)
+        if rank == 0:
+            # rank 0 takes a step that no other rank takes: its waits run out
+            hidden = torch.randn(T, H, device=dev).to(torch.bfloat16)
+            w = torch.full((T, k), 0.5, device=dev)
+            ids = torch.randint(0, E, (T, k), device=dev)
+            ep(hidden, w, ids)
+            torch.cuda.synchronize()
+            code = int(ep.peer.status.item())
+            # the context is still usable after the timeout
+            x = torch.ones(4, device=dev).sum().item()
+            q.put((rank, "ok", code, x))
+        else:
+            q.put((rank, "ok", 0, 4.0))
+        dist.barrier()
+    except Exception as exc:
+        q.put((rank, "error", repr(exc)[:300], 0))
+    finally:
+        if ep is not None:
+            ep.close()
+        dist.destroy_process_group()
+
+
+def test_ep_peer_absent_rank_times_out(cuda_device):
+    """A rank that never takes the step: the others' bounded waits end with
+    MOE_ERR_TIMEOUT in the status word instead of hanging (no GPU fault)."""
+    import torch.multiprocessing as mp
+
+    from kernelswift_b200 import _lib
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=absent_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] == "ok" for r in res), res
+    assert res[0][2] == _lib.MOE_ERR_TIMEOUT, res
+    assert res[0][3] == 4.0
