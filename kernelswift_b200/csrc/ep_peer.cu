@@ -56,7 +56,7 @@ struct EpCtrl {
   uint32_t epoch;     // finished steps (local)
   uint32_t cta_done;  // dispatch CTAs finished this step (local)
   int32_t n_recv;     // rows received this step (local)
-  int32_t pad;
+  uint32_t dispatched;  // last step whose dispatch offsets are valid (local)
   uint32_t arrive[kMaxRanks];  // [s]: last step rank s started (written by s)
   uint32_t sent[kMaxRanks];    // [s]: last step whose rows s delivered here
   uint32_t done[kMaxRanks];    // [s]: last step whose result rows s finished
@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(kThreadsEp)
       my->n_recv = n_recv;
       for (int d = 0; d <= v.world; ++d) my->send_start[d] = s_start[d];
       for (int d = 0; d < v.world; ++d) my->dst_off[d] = s_dst_off[d];
+      my->dispatched = e;  // combine reads the offsets only for this step
     }
   }
   __syncthreads();
@@ -249,7 +250,9 @@ __global__ void __launch_bounds__(kThreadsEp)
   EpCtrl* my = ctrl_of(v, v.me);
   const uint32_t e = my->epoch + 1;
   if (threadIdx.x == 0) {
-    const bool ok = wait_flags(my->done, v.world, e, v.wait_limit_ns);
+    // this rank's dispatch of the step must have completed its offsets
+    bool ok = my->dispatched == e;
+    if (ok) ok = wait_flags(my->done, v.world, e, v.wait_limit_ns);
     if (!ok) report_status(status, MOE_ERR_TIMEOUT);
     s_ok = ok;
     for (int d = 0; d < v.world; ++d) s_dst_off[d] = my->dst_off[d];
@@ -270,9 +273,9 @@ __global__ void __launch_bounds__(kThreadsEp)
       for (int u = 0; u < 4; ++u) {
         const int64_t r = t * top_k + j0 + u;
         const int p = j0 + u < top_k ? __ldg(inv + r) : -1;
-        if (p >= 0) {
-          const int d = bucket_of(s_start, v.world, p);
-          const int64_t row = int64_t(s_dst_off[d]) + (p - s_start[d]);
+        const int d = p >= 0 ? bucket_of(s_start, v.world, p) : 0;
+        const int64_t row = int64_t(s_dst_off[d]) + (p - s_start[d]);
+        if (p >= 0 && p < s_start[v.world] && row >= 0 && row < v.capacity) {
           const T* src = reinterpret_cast<const T*>(v.base[d] + v.off_res) + row * v.hidden + h;
           const uint4 raw = *reinterpret_cast<const uint4*>(src);
           const T* x = reinterpret_cast<const T*>(&raw);
