@@ -311,9 +311,17 @@ def main():
         el = E // world
         w1 = torch.randn(el, 2 * I, H, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(H)
         w2 = torch.randn(el, H, I, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(I)
-        ep = ExpertParallelMoE(w1, w2, E, k, quant=quant, exchange=args.ep_exchange,
-                               max_tokens=T, dtype=hidden.dtype)
-        del w1, w2
+        def make_ep(exchange):
+            return ExpertParallelMoE(w1, w2, E, k, quant=quant, exchange=exchange,
+                                     max_tokens=T, dtype=hidden.dtype)
+
+        try:
+            ep = make_ep(args.ep_exchange)
+        except RuntimeError as exc:  # raised on every rank alike
+            if args.ep_exchange != "auto":
+                raise
+            print(f"peer exchange unavailable, using NCCL: {exc}", file=sys.stderr)
+            ep = make_ep("nccl")
 
         def step(stage_arr=None):
             tw, ti = fm.fused_topk(hidden, logits, k, weights_dtype=hidden.dtype)
@@ -323,6 +331,14 @@ def main():
         step()
     torch.cuda.synchronize()
     if world > 1:
+        if ep.peer is not None and not ep.peer.all_ok() and args.ep_exchange == "auto":
+            # a peer-exchange wait ran out on some rank: every rank switches
+            print("peer exchange reported an error, using NCCL", file=sys.stderr)
+            ep.close()
+            ep = make_ep("nccl")
+            for _ in range(max(3, args.warmup)):
+                step()
+            torch.cuda.synchronize()
         rows_per_launch[0] = ep.rows_received()  # the same routing every step
         if ep.peer is not None:
             ep.peer.check()

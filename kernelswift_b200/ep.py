@@ -130,21 +130,31 @@ class PeerExchange:
         self.device = device
         self.capacity = capacity
         self.dtype = dtype
+        self.handle = None
         handle = ctypes.c_void_p()
         raw = (ctypes.c_uint8 * _lib.EP_HANDLE_BYTES)()
-        _lib.call("moe_ep_peer_create", world, rank, capacity, hidden_size,
-                  fm._code(torch.empty(0, dtype=dtype)), wait_limit_ms, ctypes.byref(handle),
-                  raw)
-        self.handle = handle
-        try:
-            handles = [None] * world
-            dist.all_gather_object(handles, bytes(raw), group=group)
-            _lib.call("moe_ep_peer_connect", handle, b"".join(handles))
+        lib = _lib.load()
+        # every step below is agreed on by all ranks, so that a failure on one
+        # rank raises on all of them instead of leaving the others in a
+        # collective
+        st = lib.moe_ep_peer_create(world, rank, capacity, hidden_size,
+                                    fm._code(torch.empty(0, dtype=dtype)), wait_limit_ms,
+                                    ctypes.byref(handle), raw)
+        detail = lib.moe_last_error().decode() if st else ""
+        if not self._all_ok(st == 0):
+            if st == 0:
+                lib.moe_ep_peer_destroy(handle)
+            raise RuntimeError(f"peer exchange unavailable (rank {rank}: {detail or 'ok'})")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(raw), group=group)
+        st = lib.moe_ep_peer_connect(handle, b"".join(handles))
+        detail = lib.moe_last_error().decode() if st else ""
+        if not self._all_ok(st == 0):
+            lib.moe_ep_peer_disconnect(handle)
             dist.barrier(group=group)
-        except Exception:
-            _lib.load().moe_ep_peer_destroy(handle)
-            self.handle = None
-            raise
+            lib.moe_ep_peer_destroy(handle)
+            raise RuntimeError(f"peer exchange unavailable (rank {rank}: {detail or 'ok'})")
+        self.handle = handle
         rows, ids, res = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
         _lib.call("moe_ep_peer_buffers", handle, ctypes.byref(rows), ctypes.byref(ids),
                   ctypes.byref(res))
@@ -157,6 +167,18 @@ class PeerExchange:
                                            device=device).view(dtype)
         self.ones = torch.ones(capacity, 1, dtype=torch.float32, device=device)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def _all_ok(self, ok: bool) -> bool:
+        """True when `ok` holds on every rank of the group (collective)."""
+        on_gpu = dist.get_backend(self.group) == "nccl"
+        t = torch.tensor([1 if ok else 0], dtype=torch.int32,
+                         device=self.device if on_gpu else "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(t.item())
+
+    def all_ok(self) -> bool:
+        """Collective: True when no rank's exchange kernels recorded an error."""
+        return self._all_ok(int(self.status.item()) == 0)
 
     def check(self) -> None:
         """Raises if a kernel of the exchange recorded an error (synchronises)."""
