@@ -262,6 +262,16 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
 int moe_fused_experts(const moe_problem_t* p, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* moe_fused_experts for top_k == 1 where only the rows of tokens with a
+ * valid expert id are wanted (the expert-parallel receive buffer): out[t] =
+ * w[t] * expert(x_t) for those tokens; rows of tokens whose id is dropped are
+ * unspecified (moe_fused_experts writes zeros there). When the down
+ * GEMM runs without a K split its epilogue writes these rows directly and
+ * no top-k sum is launched. No reference counterpart (an expert-parallel
+ * building block). */
+int moe_fused_experts_rows(const moe_problem_t* p, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* The stages of moe_fused_experts, one entry point each. Used by the expert-
  * parallel path (which inserts the token exchange between them) and by tests.

@@ -217,8 +217,11 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes) {
   return MOE_OK;
 }
 
-int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_bytes,
-                      void* stream) {
+// The forward of moe_fused_experts; with `rows_out` (top_k == 1 only) the
+// per-row expert outputs go straight to rows_out from the down GEMM when it
+// runs unsplit, and the top-k sum is skipped.
+static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t workspace_bytes,
+                              void* stream, void* rows_out) {
   int sms = 0;
   int st = check_device(&sms);
   if (st != MOE_OK) return st;
@@ -353,8 +356,15 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   gd.splits = P.splits;
   gd.block_n = P.dn_bn;
   gd.out_dtype = P.part_dtype;
+  const bool direct = rows_out != nullptr && P.splits == 1 && P.part_dtype == p->act_dtype;
+  if (direct) gd.out = rows_out;  // weighted rows in token order: the result itself
   st = gemm_down_launch(gd, s);
   if (st != MOE_OK) return st;
+  if (direct) {
+    KSW_MARK(MOE_STAGE_SUM);
+    KSW_MARK(MOE_NUM_STAGES);
+    return MOE_OK;
+  }
 
   SumArgs sa{};
   sa.part = at<void>(workspace, P.off_part);
@@ -366,7 +376,7 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   sa.ids = p->topk_ids;
   sa.ids_dtype = p->ids_dtype;
   sa.E = P.E;
-  sa.out = p->out;
+  sa.out = rows_out != nullptr ? rows_out : p->out;
   sa.out_dtype = p->act_dtype;
   KSW_MARK(MOE_STAGE_SUM);
   st = sum_topk_launch(sa, s);
@@ -374,6 +384,18 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   KSW_MARK(MOE_NUM_STAGES);
   return MOE_OK;
 #undef KSW_MARK
+}
+
+int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  return fused_experts_impl(p, workspace, workspace_bytes, stream, nullptr);
+}
+
+int moe_fused_experts_rows(const moe_problem_t* p, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  KSW_REQUIRE(p != nullptr, MOE_ERR_INVALID_ARG, "null problem");
+  KSW_REQUIRE(p->top_k == 1, MOE_ERR_INVALID_ARG, "moe_fused_experts_rows: top_k must be 1");
+  return fused_experts_impl(p, workspace, workspace_bytes, stream, p->out);
 }
 
 int moe_gather_rows(const void* src, int src_dtype, int64_t src_rows, int64_t hidden_size,

@@ -304,7 +304,8 @@ class ExpertParallelMoE:
                   fm._ptr(send_eid), fm._ptr(counts), fm._ptr(px.status), stream)
         fm.fused_experts(px.recv_rows, self.backend.prep, None, px.ones, px.recv_ids.view(-1, 1),
                          use_fp8_w8a8=self.quant == "fp8", use_int8_w8a8=self.quant == "int8",
-                         out=px.result_rows, status=px.status, stage_events=stage_events)
+                         out=px.result_rows, status=px.status, stage_events=stage_events,
+                         rows_only=True)
         out = torch.empty(T, H, dtype=hidden.dtype, device=dev)
         w = topk_weights.contiguous()
         _lib.call("moe_ep_peer_combine", px.handle, fm._ptr(inv), fm._ptr(w), fm._code(w), T, k,

@@ -300,8 +300,13 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
                   w2_scale: torch.Tensor | None = None, a1_scale: torch.Tensor | None = None,
                   a2_scale: torch.Tensor | None = None, block_shape: list[int] | None = None,
                   out: torch.Tensor | None = None, status: torch.Tensor | None = None,
-                  stage_events: ctypes.Array | None = None) -> torch.Tensor:
+                  stage_events: ctypes.Array | None = None,
+                  rows_only: bool = False) -> torch.Tensor:
     """out[t] = sum_j w[t,j] * W2[e] (silu(W1g[e] x_t) * W1u[e] x_t), e = ids[t,j].
+
+    rows_only (top_k == 1): rows of tokens whose expert id is dropped are left
+    unspecified instead of zeroed, which lets the down GEMM write the result
+    rows directly (moe_fused_experts_rows; the expert-parallel receive buffer).
 
     hidden_states [T, H] (f32/f16/bf16); w1 [E, 2I, H] and w2 [E, H, I] raw
     (cast or quantised once and cached) or `w1` a PreparedWeights and `w2`
@@ -353,8 +358,9 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
     _lib.check(lib.moe_fused_experts_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)),
                "moe_fused_experts_workspace_size")
     ws = _workspace(hidden.device, nbytes.value)
-    _lib.check(lib.moe_fused_experts(ctypes.byref(p), _ptr(ws), ws.numel(),
-                                     _stream(hidden.device)), "moe_fused_experts")
+    entry = "moe_fused_experts_rows" if rows_only else "moe_fused_experts"
+    _lib.check(getattr(lib, entry)(ctypes.byref(p), _ptr(ws), ws.numel(),
+                                   _stream(hidden.device)), entry)
     return out
 
 

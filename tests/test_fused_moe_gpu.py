@@ -187,3 +187,23 @@ def test_captured_graph_matches_eager(cuda_device):
         out = cap(hidden, logits)
         torch.cuda.synchronize()
         assert torch.equal(out, eager)
+
+
+@pytest.mark.parametrize("T", [5, 3000])
+def test_rows_only_matches_full_forward(cuda_device, T):
+    """moe_fused_experts_rows (top_k = 1, the expert-parallel receive buffer):
+    the rows of tokens with a valid id equal moe_fused_experts' bit for bit,
+    whether the down GEMM writes them directly (unsplit) or the sum does."""
+    H, I, E = 256, 512, 8
+    g = torch.Generator().manual_seed(T)
+    hidden = torch.randn(T, H, generator=g).to(torch.bfloat16).to(cuda_device)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) / H ** 0.5).to(torch.bfloat16).to(cuda_device)
+    w2 = (torch.randn(E, H, I, generator=g) / I ** 0.5).to(torch.bfloat16).to(cuda_device)
+    ids = torch.randint(-1, E, (T, 1), generator=g, dtype=torch.int32).to(cuda_device)
+    ones = torch.ones(T, 1, device=cuda_device)
+    prep = fm.prepare_weights(w1, w2, "none", torch.bfloat16)
+    full = fm.fused_experts(hidden, prep, None, ones, ids)
+    rows = torch.full_like(hidden, float("nan"))
+    fm.fused_experts(hidden, prep, None, ones, ids, out=rows, rows_only=True)
+    valid = (ids.view(-1) >= 0).cpu()
+    assert torch.equal(rows.cpu()[valid], full.cpu()[valid])
