@@ -7,8 +7,8 @@
 //   [ctrl: EpCtrl, 4 KB][recv ids: capacity int32][recv rows][result rows]
 //
 // One step, epoch e = ctrl.epoch + 1 (ctrl.epoch counts finished steps and
-// is advanced by the last kernel of the step, so the step is replayable from
-// a CUDA graph):
+// is advanced on the device by the last kernel of the step; the host keeps
+// no per-step state):
 //   dispatch  CTA 0 writes this rank's per-destination counts into row `me`
 //             of every rank's counts matrix, then arrive[me] = e on every
 //             rank. Every CTA waits for arrive[s] >= e from all ranks (this
@@ -28,8 +28,6 @@
 // is bounded (5 s of %globaltimer by default); on expiry the kernel records
 // MOE_ERR_TIMEOUT and skips its work instead of hanging.
 #include <cstring>
-#include <mutex>
-#include <vector>
 
 #include "common.cuh"
 
