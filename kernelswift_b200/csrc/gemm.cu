@@ -461,8 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   acc[m, n] += a_scale[m, kb] * b_scale[e, n / 128, kb] * P_kb[m, n]
 // TMEM holds 512 / BN such buffers (4 at BN = 128), so the MMAs of the next
 // k-blocks run while one is promoted; each epilogue warp copies its columns
-// out with one wait per 64 columns and releases the buffer before doing the
-// arithmetic, which keeps the buffer hand-off shorter than an MMA.
+// out in 16-column batches (one batch of 32 at BN = 128) and releases the
+// buffer as soon as the last batch is in registers, before its arithmetic.
 // Warp w (4..19) owns TMEM lane quarter w % 4 and column quarter (w - 4) / 4
 // (four warps per SM sub-partition hide the TMEM load latency);
 // warps whose 32 rows are all padding skip the arithmetic.
