@@ -50,6 +50,29 @@ struct GroupedGemmArgs {
   int early_meta;
 };
 
+// ----- decode.cu -----
+// Routed rows up to which moe_fused_experts streams the weights through
+// two CUDA-core kernels instead of the align/gather/GEMM pipeline.
+constexpr int64_t kDecodeMaxRows = 16;
+
+struct DecodeArgs {
+  int64_t T, H, I;
+  int top_k, E;
+  int act_dtype, ids_dtype, weights_dtype;
+  const void* hidden;   // [T, H] act dtype
+  const void* w13;      // [E, 2I, H] regrouped, act dtype
+  const void* w2;       // [E, H, I]
+  const void* ids;      // [T, top_k]
+  const void* weights;  // [T, top_k]
+  void* act;            // [T*top_k, I] scratch
+  void* out;            // [T, H]
+};
+
+bool decode_path_fits(int64_t T, int top_k, int64_t H, int64_t I, int act_dtype);
+bool decode_path_enabled();  // false when MOE_NO_DECODE_PATH=1
+// stage 0: gate-up + SiLU*up into act; stage 1: down + weighted top-k sum
+int decode_launch(const DecodeArgs& d, int stage, cudaStream_t s);
+
 int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s);
 int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s);
 int gemm_gate_up_split_launch(const GroupedGemmArgs& a, cudaStream_t s);

@@ -1,6 +1,7 @@
 // moe_fused_experts: the whole expert computation of
 // kernels/track1-triton/fused_moe/base.py:50-76 as six launches on the
-// caller's stream, with no host synchronisation:
+// caller's stream, with no host synchronisation (two weight-streaming
+// launches instead when at most 16 rows are routed, csrc/decode.cu):
 //
 //   1. align      topk_ids -> sorted_token_ids, expert_ids, num_post_pad
 //   2. gather     hidden rows in expert-sorted order (+cast / quantise)
@@ -255,6 +256,40 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
     st = mark(stage);             \
     if (st != MOE_OK) return st;  \
   } while (0)
+  // A handful of routed rows with 16-bit operands: stream the weights
+  // through the two decode kernels (csrc/decode.cu).
+  if (P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype && decode_path_enabled() &&
+      decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype)) {
+    DecodeArgs d{};
+    d.T = P.T;
+    d.H = P.H;
+    d.I = P.I;
+    d.top_k = P.k;
+    d.E = P.E;
+    d.act_dtype = p->act_dtype;
+    d.ids_dtype = p->ids_dtype;
+    d.weights_dtype = p->weights_dtype;
+    d.hidden = p->hidden;
+    d.w13 = p->w13;
+    d.w2 = p->w2;
+    d.ids = p->topk_ids;
+    d.weights = p->topk_weights;
+    d.act = at<void>(workspace, P.off_act);
+    d.out = rows_out != nullptr ? rows_out : p->out;
+    KSW_MARK(MOE_STAGE_ALIGN);
+    KSW_MARK(MOE_STAGE_GATHER);
+    KSW_MARK(MOE_STAGE_GATE_UP);
+    st = decode_launch(d, 0, s);
+    if (st != MOE_OK) return st;
+    KSW_MARK(MOE_STAGE_QUANT);
+    KSW_MARK(MOE_STAGE_DOWN);
+    st = decode_launch(d, 1, s);
+    if (st != MOE_OK) return st;
+    KSW_MARK(MOE_STAGE_SUM);
+    KSW_MARK(MOE_NUM_STAGES);
+    return MOE_OK;
+  }
+
   int32_t* sorted = at<int32_t>(workspace, P.off_sorted);
   int32_t* eids = at<int32_t>(workspace, P.off_eids);
   int32_t* npp = at<int32_t>(workspace, P.off_npp);

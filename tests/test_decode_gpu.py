@@ -1,0 +1,94 @@
+"""GPU: the decode path of moe_fused_experts (at most 16 routed rows, 16-bit
+activations, unquantised weights: two weight-streaming kernels instead of the
+align/gather/GEMM pipeline) against the fp32 oracle, with dropped slots,
+int32/int64 ids, f32/bf16 weights and fp16 activations; and the boundary
+with the tensor-core path (17 routed rows)."""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+from kernelswift_b200 import fused_moe as fm
+from oracle import moe_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+TOL = dict(rtol=2e-2, atol=2e-2)
+
+
+def problem(T, H, I, E, k, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    hidden = torch.randn(T, H, generator=g).to(dtype)
+    logits = torch.randn(T, E, generator=g)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) / H ** 0.5).to(dtype)
+    w2 = (torch.randn(E, H, I, generator=g) / I ** 0.5).to(dtype)
+    return hidden, logits, w1, w2
+
+
+@pytest.mark.parametrize("T,H,I,E,k,dtype", [
+    (1, 256, 128, 16, 8, torch.bfloat16),     # 8 routed rows (Qwen3-like top-8)
+    (2, 256, 128, 16, 8, torch.bfloat16),     # 16: the largest decode problem
+    (1, 512, 1024, 8, 2, torch.bfloat16),     # Mixtral-like top-2
+    (5, 384, 256, 8, 2, torch.float16),
+    (1, 128, 16, 4, 1, torch.bfloat16),       # smallest widths
+    (17, 256, 128, 16, 1, torch.bfloat16),    # 17 rows: tensor-core path
+])
+def test_decode_matches_oracle(cuda_device, T, H, I, E, k, dtype):
+    hidden, logits, w1, w2 = problem(T, H, I, E, k, dtype, seed=T * 131 + H)
+    w, ids = orc.route(logits, k)
+    ref = orc.fused_experts(hidden, w1, w2, w, ids)
+    prep = fm.prepare_weights(w1.to(cuda_device), w2.to(cuda_device), "none", dtype)
+    for ids_dt, w_dt in ((torch.int32, torch.float32), (torch.int64, dtype)):
+        out = fm.fused_experts(hidden.to(cuda_device), prep, None, w.to(w_dt).to(cuda_device),
+                               ids.to(ids_dt).to(cuda_device))
+        torch.testing.assert_close(out.float().cpu(), ref, **TOL)
+        again = fm.fused_experts(hidden.to(cuda_device), prep, None,
+                                 w.to(w_dt).to(cuda_device), ids.to(ids_dt).to(cuda_device))
+        assert torch.equal(out, again)  # fixed reduction order
+
+
+def test_decode_dropped_slots(cuda_device):
+    T, H, I, E, k = 2, 256, 128, 8, 4
+    hidden, logits, w1, w2 = problem(T, H, I, E, k, torch.bfloat16, seed=7)
+    w, ids = orc.route(logits, k)
+    ids[0, 1] = -1
+    ids[1, 3] = E  # out of range: dropped
+    keep = (ids >= 0) & (ids < E)
+    ref = orc.fused_experts(hidden, w1, w2, w * keep, ids.clamp(0, E - 1))
+    prep = fm.prepare_weights(w1.to(cuda_device), w2.to(cuda_device), "none", torch.bfloat16)
+    out = fm.fused_experts(hidden.to(cuda_device), prep, None, w.to(cuda_device),
+                           ids.to(torch.int32).to(cuda_device))
+    torch.testing.assert_close(out.float().cpu(), ref, **TOL)
+
+
+def test_decode_close_to_tensor_core_path(cuda_device, tmp_path):
+    """The same problem with MOE_NO_DECODE_PATH=1 (align/gather/GEMMs) in a
+    child process: the two paths agree within the bf16 tolerance."""
+    T, H, I, E, k = 1, 512, 256, 16, 8
+    code = f"""
+import sys, torch
+sys.path.insert(0, {str(Path(__file__).resolve().parent.parent)!r})
+sys.path.insert(0, {str(Path(__file__).resolve().parent)!r})
+from test_decode_gpu import run_case
+torch.save(run_case(), {str(tmp_path / 'tc.pt')!r})
+"""
+    env = dict(os.environ, MOE_NO_DECODE_PATH="1")
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    tc = torch.load(tmp_path / "tc.pt")
+    dec = run_case()
+    torch.testing.assert_close(dec.float(), tc.float(), **TOL)
+
+
+def run_case():
+    dev = torch.device("cuda", 0)
+    T, H, I, E, k = 1, 512, 256, 16, 8
+    hidden, logits, w1, w2 = problem(T, H, I, E, k, torch.bfloat16, seed=99)
+    w, ids = orc.route(logits, k)
+    prep = fm.prepare_weights(w1.to(dev), w2.to(dev), "none", torch.bfloat16)
+    out = fm.fused_experts(hidden.to(dev), prep, None, w.to(dev), ids.to(torch.int32).to(dev))
+    return out.cpu()
