@@ -7,18 +7,20 @@
 // SMs and the tensor-core path is bound by its fixed costs (seven launches,
 // pipeline fill, 128-row tiles that are almost all padding).
 //
-//   decode_gate_up_kernel  CTA = (routed slot, 32 rows of the regrouped w13):
+//   decode_gate_up_kernel  item = (routed slot, 32 rows of the regrouped w13):
 //                          16 gate rows and their 16 up rows; each warp dots
 //                          4 weight rows with the slot's token row (staged in
 //                          shared memory), then SiLU(gate) * up for 16 act
 //                          columns, rounded to the activation dtype
-//   decode_down_kernel     CTA = (token, 8 rows of w2): each warp dots one
-//                          w2 row of every slot's expert with that slot's act
-//                          row (all of the token's act rows staged) and sums
-//                          w_j * dot_j over the slots in slot order, in fp32
+//   decode_down_kernel     item = (token, 8 rows of w2): each warp streams one
+//                          w2 row of every slot's expert at once, dots each
+//                          with that slot's act row (the token's act rows are
+//                          staged) and sums w_j * dot_j in slot order, in fp32
+// Both run persistent grids (the CTAs that fit at once walk the items).
 //
 // Loads are 16-byte vectors, several in flight per lane. Slots whose id is
 // outside [0, E) contribute nothing. Deterministic: fixed reduction order.
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 
@@ -61,103 +63,152 @@ __device__ __forceinline__ void stage_row(T* dst, const T* src, int64_t n) {
 template <typename T, typename IdT>
 __global__ void __launch_bounds__(kThreadsDec)
     decode_gate_up_kernel(const T* __restrict__ hidden, const T* __restrict__ w13,
-                          const IdT* __restrict__ ids, int top_k, int E, int64_t H, int64_t I,
-                          T* __restrict__ act) {
+                          const IdT* __restrict__ ids, int64_t numel, int top_k, int E,
+                          int64_t H, int64_t I, T* __restrict__ act) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ uint4 smem_dec[];
-  T* a = reinterpret_cast<T*>(smem_dec);  // [H] token row
+  T* a = reinterpret_cast<T*>(smem_dec);  // [H] token row of the current slot
   __shared__ float res[kRowsGu];
-  const int64_t chunks = 2 * I / kRowsGu;
-  const int64_t slot = blockIdx.x / chunks;
-  const int64_t chunk = blockIdx.x - slot * chunks;
-  const int e = valid_expert(ids, slot, E);
-  if (e < 0) return;  // the act row of a dropped slot is never read
-  stage_row(a, hidden + (slot / top_k) * H, H);
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const T* w = w13 + (int64_t(e) * 2 * I + chunk * kRowsGu + warp * 4) * H;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  // two 256-column steps per iteration: 8 weight loads in flight per lane
-  for (int64_t k0 = int64_t(lane) * 8; k0 < H; k0 += 512) {
-    uint4 wv[2][4];
-    const bool second = k0 + 256 < H;
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      wv[0][r] = *reinterpret_cast<const uint4*>(w + r * H + k0);
-      if (second) wv[1][r] = *reinterpret_cast<const uint4*>(w + r * H + k0 + 256);
+  const int64_t chunks = 2 * I / kRowsGu;
+  int64_t staged = -1;  // token whose row is in shared memory
+  // persistent CTAs walk the (slot, 32-row chunk) items, so no partial last
+  // wave of CTAs is left streaming alone
+  for (int64_t item = blockIdx.x; item < numel * chunks; item += gridDim.x) {
+    const int64_t slot = item / chunks;
+    const int64_t chunk = item - slot * chunks;
+    const int e = valid_expert(ids, slot, E);
+    if (e < 0) continue;  // the act row of a dropped slot is never read
+    const int64_t tok = slot / top_k;
+    if (tok != staged) {
+      __syncthreads();  // everyone is done with the previous row
+      stage_row(a, hidden + tok * H, H);
+      staged = tok;
+      __syncthreads();
     }
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      if (s == 1 && !second) break;
-      float x[8];
-      unpack8<T>(*reinterpret_cast<const uint4*>(a + k0 + 256 * s), x);
+    const T* w = w13 + (int64_t(e) * 2 * I + chunk * kRowsGu + warp * 4) * H;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // two 256-column steps per iteration: 8 weight loads in flight per lane
+    for (int64_t k0 = int64_t(lane) * 8; k0 < H; k0 += 512) {
+      uint4 wv[2][4];
+      const bool second = k0 + 256 < H;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        float f[8];
-        unpack8<T>(wv[s][r], f);
+        wv[0][r] = *reinterpret_cast<const uint4*>(w + r * H + k0);
+        if (second) wv[1][r] = *reinterpret_cast<const uint4*>(w + r * H + k0 + 256);
+      }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[r] = fmaf(f[q], x[q], acc[r]);
+      for (int st = 0; st < 2; ++st) {
+        if (st == 1 && !second) break;
+        float x[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(a + k0 + 256 * st), x);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float f[8];
+          unpack8<T>(wv[st][r], f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[r] = fmaf(f[q], x[q], acc[r]);
+        }
       }
     }
-  }
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const float v = warp_sum(acc[r]);
-    if (lane == 0) res[warp * 4 + r] = v;
-  }
-  __syncthreads();
-  // rows 0-15 of the slice are gate rows, 16-31 the matching up rows
-  if (threadIdx.x < 16) {
-    const float g = res[threadIdx.x], u = res[16 + threadIdx.x];
-    act[slot * I + chunk * 16 + threadIdx.x] = from_f32<T>(g / (1.0f + __expf(-g)) * u);
+    for (int r = 0; r < 4; ++r) {
+      const float v = warp_sum(acc[r]);
+      if (lane == 0) res[warp * 4 + r] = v;
+    }
+    __syncthreads();
+    // rows 0-15 of the slice are gate rows, 16-31 the matching up rows
+    if (threadIdx.x < 16) {
+      const float g = res[threadIdx.x], u = res[16 + threadIdx.x];
+      act[slot * I + chunk * 16 + threadIdx.x] = from_f32<T>(g / (1.0f + __expf(-g)) * u);
+    }
+    __syncthreads();  // res is reused by the next item
   }
 }
 
-template <typename T, typename IdT, typename Tw>
+// One warp per output row; the rows of all the token's slots are streamed
+// together (one 16-byte load per slot per step, and U steps at a time when
+// there are few slots), so a warp keeps about eight loads in flight instead
+// of walking the slots one after another. KMAX >= top_k.
+template <typename T, typename IdT, typename Tw, int KMAX>
 __global__ void __launch_bounds__(kThreadsDec)
     decode_down_kernel(const T* __restrict__ act, const T* __restrict__ w2,
-                       const IdT* __restrict__ ids, const Tw* __restrict__ weights, int top_k,
-                       int E, int64_t H, int64_t I, T* __restrict__ out) {
+                       const IdT* __restrict__ ids, const Tw* __restrict__ weights,
+                       int64_t T_tokens, int top_k, int E, int64_t H, int64_t I,
+                       T* __restrict__ out) {
+  constexpr int U = KMAX >= 8 ? 1 : 8 / KMAX;
   pdl_wait();
   pdl_trigger();
   extern __shared__ uint4 smem_dec[];
-  T* a = reinterpret_cast<T*>(smem_dec);  // [top_k, I] the token's act rows
-  const int64_t row_blocks = H / kRowsDn;
-  const int64_t t = blockIdx.x / row_blocks;
-  const int64_t h0 = (blockIdx.x - t * row_blocks) * kRowsDn;
-  for (int j = 0; j < top_k; ++j)
-    if (valid_expert(ids, t * top_k + j, E) >= 0)
-      stage_row(a + int64_t(j) * I, act + (t * top_k + j) * I, I);
-  __syncthreads();
+  T* a = reinterpret_cast<T*>(smem_dec);  // [top_k, I] act rows of the current token
+  __shared__ int s_e[KMAX];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t h = h0 + warp;
-  float total = 0.f;
-  for (int j = 0; j < top_k; ++j) {
-    const int e = valid_expert(ids, t * top_k + j, E);
-    if (e < 0) continue;
-    const T* w = w2 + (int64_t(e) * H + h) * I;
-    const T* x = a + int64_t(j) * I;
-    float acc = 0.f;
-    for (int64_t k0 = int64_t(lane) * 8; k0 < I; k0 += 4 * 256) {
-      uint4 wv[4];
+  const int64_t row_blocks = H / kRowsDn;
+  int64_t staged = -1;
+  for (int64_t item = blockIdx.x; item < T_tokens * row_blocks; item += gridDim.x) {
+    const int64_t t = item / row_blocks;
+    const int64_t h = (item - t * row_blocks) * kRowsDn + warp;
+    if (t != staged) {
+      __syncthreads();
+      if (threadIdx.x < KMAX)
+        s_e[threadIdx.x] = threadIdx.x < top_k ? valid_expert(ids, t * top_k + threadIdx.x, E) : -1;
+      for (int j = 0; j < top_k; ++j)
+        if (valid_expert(ids, t * top_k + j, E) >= 0)
+          stage_row(a + int64_t(j) * I, act + (t * top_k + j) * I, I);
+      staged = t;
+      __syncthreads();
+    }
+    const T* wrow[KMAX];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (k0 + u * 256 < I) wv[u] = *reinterpret_cast<const uint4*>(w + k0 + u * 256);
+    for (int j = 0; j < KMAX; ++j)
+      wrow[j] = s_e[j] >= 0 ? w2 + (int64_t(s_e[j]) * H + h) * I : nullptr;
+    float acc[KMAX];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+    for (int j = 0; j < KMAX; ++j) acc[j] = 0.f;
+    for (int64_t k0 = int64_t(lane) * 8; k0 < I; k0 += 256 * U) {
+      uint4 wv[U][KMAX];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int j = 0; j < KMAX; ++j)
+          if (wrow[j] != nullptr && k0 + u * 256 < I)
+            wv[u][j] = *reinterpret_cast<const uint4*>(wrow[j] + k0 + u * 256);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
         if (k0 + u * 256 >= I) break;
-        float f[8], xv[8];
-        unpack8<T>(wv[u], f);
-        unpack8<T>(*reinterpret_cast<const uint4*>(x + k0 + u * 256), xv);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc = fmaf(f[q], xv[q], acc);
+        for (int j = 0; j < KMAX; ++j) {
+          if (wrow[j] == nullptr) continue;
+          float f[8], xv[8];
+          unpack8<T>(wv[u][j], f);
+          unpack8<T>(*reinterpret_cast<const uint4*>(a + int64_t(j) * I + k0 + u * 256), xv);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[j] = fmaf(f[q], xv[q], acc[j]);
+        }
       }
     }
-    acc = warp_sum(acc);
-    total = fmaf(to_f32(weights[t * top_k + j]), acc, total);
+    float total = 0.f;
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (wrow[j] == nullptr) continue;
+      const float dsum = warp_sum(acc[j]);
+      total = fmaf(to_f32(weights[t * top_k + j]), dsum, total);
+    }
+    if (lane == 0) out[t * H + h] = from_f32<T>(total);
   }
-  if (lane == 0) out[t * H + h] = from_f32<T>(total);
+}
+
+// CTAs of `kern` that fit on the GPU at once with `smem` bytes of dynamic
+// shared memory each: the persistent grid of the decode kernels.
+template <typename Kern>
+int grid_cap(Kern kern, size_t smem, int64_t* cap) {
+  int sms = 148, per_sm = 0;
+  int st = check_device(&sms);
+  if (st != MOE_OK) return st;
+  KSW_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreadsDec, smem));
+  *cap = int64_t(sms) * std::max(per_sm, 1);
+  return MOE_OK;
 }
 
 // Raises a kernel's dynamic shared-memory limit when a launch needs more
@@ -173,6 +224,24 @@ int ensure_smem(Kern k, size_t bytes, std::atomic<size_t>& granted) {
   return MOE_OK;
 }
 
+template <typename T, typename IdT, typename Tw, int KMAX>
+int launch_down(const DecodeArgs& d, cudaStream_t s) {
+  const size_t smem = size_t(d.top_k) * size_t(d.I) * sizeof(T);
+  auto k = decode_down_kernel<T, IdT, Tw, KMAX>;
+  static std::atomic<size_t> granted{0};
+  const int st = ensure_smem(k, smem, granted);
+  if (st != MOE_OK) return st;
+  const int64_t items = d.T * (d.H / kRowsDn);
+  int64_t cap = 0;
+  const int stc = grid_cap(k, smem, &cap);
+  if (stc != MOE_OK) return stc;
+  KSW_LAUNCH(k, dim3(unsigned(std::min<int64_t>(items, cap))), dim3(kThreadsDec),
+             smem, s, static_cast<const T*>(d.act), static_cast<const T*>(d.w2),
+             static_cast<const IdT*>(d.ids), static_cast<const Tw*>(d.weights), d.T, d.top_k,
+             d.E, d.H, d.I, static_cast<T*>(d.out));
+  return MOE_OK;
+}
+
 template <typename T, typename IdT, typename Tw>
 int launch_decode(const DecodeArgs& d, int stage, cudaStream_t s) {
   if (stage == 0) {
@@ -181,21 +250,21 @@ int launch_decode(const DecodeArgs& d, int stage, cudaStream_t s) {
     static std::atomic<size_t> granted{0};
     const int st = ensure_smem(k, smem, granted);
     if (st != MOE_OK) return st;
-    KSW_LAUNCH(k, dim3(unsigned(d.T * d.top_k * (2 * d.I / kRowsGu))), dim3(kThreadsDec), smem,
-               s, static_cast<const T*>(d.hidden), static_cast<const T*>(d.w13),
-               static_cast<const IdT*>(d.ids), d.top_k, d.E, d.H, d.I, static_cast<T*>(d.act));
+    const int64_t items = d.T * d.top_k * (2 * d.I / kRowsGu);
+    int64_t cap = 0;
+    const int stc = grid_cap(k, smem, &cap);
+    if (stc != MOE_OK) return stc;
+    KSW_LAUNCH(k, dim3(unsigned(std::min<int64_t>(items, cap))), dim3(kThreadsDec),
+               smem, s, static_cast<const T*>(d.hidden), static_cast<const T*>(d.w13),
+               static_cast<const IdT*>(d.ids), d.T * d.top_k, d.top_k, d.E, d.H, d.I,
+               static_cast<T*>(d.act));
     return MOE_OK;
   }
-  const size_t smem = size_t(d.top_k) * size_t(d.I) * sizeof(T);
-  auto k = decode_down_kernel<T, IdT, Tw>;
-  static std::atomic<size_t> granted{0};
-  const int st = ensure_smem(k, smem, granted);
-  if (st != MOE_OK) return st;
-  KSW_LAUNCH(k, dim3(unsigned(d.T * (d.H / kRowsDn))), dim3(kThreadsDec), smem, s,
-             static_cast<const T*>(d.act), static_cast<const T*>(d.w2),
-             static_cast<const IdT*>(d.ids), static_cast<const Tw*>(d.weights), d.top_k, d.E,
-             d.H, d.I, static_cast<T*>(d.out));
-  return MOE_OK;
+  if (d.top_k <= 1) return launch_down<T, IdT, Tw, 1>(d, s);
+  if (d.top_k <= 2) return launch_down<T, IdT, Tw, 2>(d, s);
+  if (d.top_k <= 4) return launch_down<T, IdT, Tw, 4>(d, s);
+  if (d.top_k <= 8) return launch_down<T, IdT, Tw, 8>(d, s);
+  return launch_down<T, IdT, Tw, 16>(d, s);
 }
 
 template <typename T, typename IdT>

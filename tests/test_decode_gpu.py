@@ -34,6 +34,7 @@ def problem(T, H, I, E, k, dtype, seed):
     (1, 512, 1024, 8, 2, torch.bfloat16),     # Mixtral-like top-2
     (5, 384, 256, 8, 2, torch.float16),
     (1, 128, 32, 4, 1, torch.bfloat16),       # smallest widths the planner takes
+    (1, 256, 128, 32, 12, torch.bfloat16),    # 12 slots of one token
     (17, 256, 128, 16, 1, torch.bfloat16),    # 17 rows: tensor-core path
 ])
 def test_decode_matches_oracle(cuda_device, T, H, I, E, k, dtype):
