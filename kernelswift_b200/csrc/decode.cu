@@ -281,7 +281,12 @@ int dispatch_w(const DecodeArgs& d, int stage, cudaStream_t s) {
 
 bool decode_path_fits(int64_t T, int top_k, int64_t H, int64_t I, int act_dtype) {
   const int64_t numel = T * top_k;
-  return numel >= 1 && numel <= kDecodeMaxRows &&
+  // Large experts stream better through the TMA-fed GEMMs (Mixtral-sized
+  // experts at T=1: 0.153 ms there against 0.168 ms here); the decode
+  // kernels win where the fixed costs dominate (Qwen3-sized experts at T=1:
+  // 35 us against 51 us). Split at 256 MB of weights streamed per call.
+  const double weight_bytes = double(numel) * 3.0 * double(H) * double(I) * 2.0;
+  return numel >= 1 && numel <= kDecodeMaxRows && weight_bytes <= 256.0 * 1024 * 1024 &&
          (act_dtype == MOE_DTYPE_BF16 || act_dtype == MOE_DTYPE_F16) && H % kRowsDn == 0 &&
          H % 8 == 0 && I % 16 == 0 && H * 2 <= 200 * 1024 &&
          int64_t(top_k) * I * 2 <= 200 * 1024;

@@ -52,7 +52,8 @@ struct GroupedGemmArgs {
 
 // ----- decode.cu -----
 // Routed rows up to which moe_fused_experts streams the weights through
-// two CUDA-core kernels instead of the align/gather/GEMM pipeline.
+// two CUDA-core kernels instead of the align/gather/GEMM pipeline (when the
+// weights it streams are also small: decode_path_fits).
 constexpr int64_t kDecodeMaxRows = 16;
 
 struct DecodeArgs {
