@@ -464,3 +464,70 @@ class CapturedMoE:
         self.hidden.copy_(hidden_states, non_blocking=True)
         self.logits.copy_(router_logits, non_blocking=True)
         return self.replay()
+
+
+class HostPipeline:
+    """Forwards over host (pinned) inputs with the copies of consecutive calls
+    overlapped: while the compute stream runs step i, a copy stream brings in
+    step i+1's inputs and another takes out step i-1's output. Device staging
+    buffers are double-buffered and handed between the streams with events.
+
+    `fn(hidden, logits) -> out` is the forward (a ModelNew, a CapturedMoE, an
+    expert-parallel step ...). `submit(hidden_host, logits_host, out_host)`
+    enqueues one step and returns at once; `out_host` holds that step's
+    output after `flush()` (or any later synchronisation). Work is ordered
+    after whatever the caller's current stream had enqueued when `submit` was
+    called, and `flush()` makes the caller's current stream wait for all of it.
+    """
+
+    def __init__(self, fn, num_tokens: int, hidden_size: int, num_experts: int,
+                 dtype: torch.dtype = torch.bfloat16, device=None, out_dtype=None):
+        dev = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.fn = fn
+        self.device = dev
+        self.h = [torch.empty(num_tokens, hidden_size, dtype=dtype, device=dev) for _ in range(2)]
+        self.l = [torch.empty(num_tokens, num_experts, dtype=torch.float32, device=dev)
+                  for _ in range(2)]
+        self.o = [torch.empty(num_tokens, hidden_size, dtype=out_dtype or dtype, device=dev)
+                  for _ in range(2)]
+        self.copy_in = torch.cuda.Stream(dev)
+        self.compute = torch.cuda.Stream(dev)
+        self.copy_out = torch.cuda.Stream(dev)
+        self.ev_in = [torch.cuda.Event() for _ in range(2)]      # inputs of slot landed
+        self.ev_used = [torch.cuda.Event() for _ in range(2)]    # compute done with inputs
+        self.ev_done = [torch.cuda.Event() for _ in range(2)]    # output staged
+        self.ev_taken = [torch.cuda.Event() for _ in range(2)]   # output copied out
+        for evs in (self.ev_used, self.ev_taken):
+            for ev in evs:
+                ev.record(torch.cuda.current_stream(dev))
+        self.i = 0
+
+    def submit(self, hidden_host: torch.Tensor, logits_host: torch.Tensor,
+               out_host: torch.Tensor) -> None:
+        slot = self.i % 2
+        self.i += 1
+        caller = torch.cuda.current_stream(self.device)
+        self.copy_in.wait_stream(caller)
+        self.copy_in.wait_event(self.ev_used[slot])
+        with torch.cuda.stream(self.copy_in):
+            self.h[slot].copy_(hidden_host, non_blocking=True)
+            self.l[slot].copy_(logits_host, non_blocking=True)
+            self.ev_in[slot].record(self.copy_in)
+        self.compute.wait_event(self.ev_in[slot])
+        self.compute.wait_event(self.ev_taken[slot])
+        with torch.cuda.stream(self.compute), torch.no_grad():
+            out = self.fn(self.h[slot], self.l[slot])
+            self.ev_used[slot].record(self.compute)
+            self.o[slot].copy_(out)
+            self.ev_done[slot].record(self.compute)
+        self.copy_out.wait_event(self.ev_done[slot])
+        with torch.cuda.stream(self.copy_out):
+            out_host.copy_(self.o[slot], non_blocking=True)
+            self.ev_taken[slot].record(self.copy_out)
+
+    def flush(self) -> None:
+        """Makes the caller's current stream wait for every submitted step."""
+        caller = torch.cuda.current_stream(self.device)
+        caller.wait_stream(self.copy_out)
+        caller.wait_stream(self.compute)

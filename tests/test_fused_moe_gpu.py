@@ -207,3 +207,28 @@ def test_rows_only_matches_full_forward(cuda_device, T):
     fm.fused_experts(hidden, prep, None, ones, ids, out=rows, rows_only=True)
     valid = (ids.view(-1) >= 0).cpu()
     assert torch.equal(rows.cpu()[valid], full.cpu()[valid])
+
+
+def test_host_pipeline_matches_direct_calls(cuda_device):
+    """HostPipeline: several steps with different host inputs and outputs,
+    copies overlapped across steps; each output equals a direct forward."""
+    T, H, I, E, k = 64, 256, 512, 8, 2
+    g = torch.Generator().manual_seed(5)
+    model = fm.ModelNew(E, k, H, I).to(cuda_device)
+    with torch.no_grad():
+        model.w1.copy_(torch.randn(E, 2 * I, H, generator=g) / H ** 0.5)
+        model.w2.copy_(torch.randn(E, H, I, generator=g) / I ** 0.5)
+    cap = fm.CapturedMoE(model, T, H, E, dtype=torch.bfloat16, device=cuda_device)
+    for fn in (model, cap):
+        pipe = fm.HostPipeline(fn, T, H, E, dtype=torch.bfloat16, device=cuda_device)
+        ins = [(torch.randn(T, H, generator=g).to(torch.bfloat16).pin_memory(),
+                torch.randn(T, E, generator=g).pin_memory()) for _ in range(5)]
+        outs = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(5)]
+        for (h, l), o in zip(ins, outs):
+            pipe.submit(h, l, o)
+        pipe.flush()
+        torch.cuda.synchronize()
+        for (h, l), o in zip(ins, outs):
+            with torch.no_grad():
+                ref = model(h.to(cuda_device), l.to(cuda_device))
+            assert torch.equal(o, ref.cpu())
