@@ -15,10 +15,12 @@ weights, N(0,1) router logits).
 between steps outside the timed windows, max over ranks). On one GPU a step
 is a replay of a CUDA graph that holds the whole forward (fused_moe.CapturedMoE;
 `--no-graph` launches every kernel eagerly instead); expert parallelism
-(N > 1) launches eagerly, since it syncs the host for the all_to_all split
-sizes. `e2e` is the same metric through the public API with pinned host
-inputs, including the H2D copies of hidden states and router logits and the
-D2H copy of the output.
+(N > 1) launches eagerly, exchanging rows through the NVLink peer-memory
+dispatch/combine kernels (`--ep-exchange nccl`: NCCL all_to_all). `e2e` is
+the same metric through the public API (fused_moe.HostPipeline) with pinned
+host buffers: every step copies its hidden states and router logits in and
+its output out, on copy streams that overlap the neighbouring steps'
+compute.
 `--impl reference` times the reference's CPU torch path (base.py:35-76,
 restated in the oracle) on the host cores instead.
 """
