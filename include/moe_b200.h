@@ -352,6 +352,22 @@ int moe_combine_rows(const void* rows, int rows_dtype, const int32_t* inv_index,
                      void* stream);
 
 /*
+ * Grouped top-k routing of kernels/track1-triton/groupedtopk/base.py:31-72
+ * (Model.forward): scores = softmax (scoring_func 0) or sigmoid (1) of
+ * gating_output [num_tokens, num_experts] (F32/F16/BF16); the experts form
+ * num_expert_group equal groups; the topk_group groups with the highest
+ * maximum score are kept and the top_k experts are chosen among them, in
+ * descending score order; topk_weights (fp32) = their scores, divided by
+ * their sum when renormalize, times routed_scaling_factor; topk_ids int32.
+ * Ties go to the lower index. num_experts <= 1024, num_expert_group <= 32,
+ * top_k <= min(32, topk_group * num_experts / num_expert_group).
+ */
+int moe_grouped_topk(const void* gating_output, int logits_dtype, int64_t num_tokens,
+                     int num_experts, int top_k, int renormalize, int num_expert_group,
+                     int topk_group, int scoring_func, float routed_scaling_factor,
+                     float* topk_weights, int32_t* topk_ids, void* stream);
+
+/*
  * Expert-parallel dispatch plan for this rank's routing (experts sharded in
  * contiguous blocks of num_experts / world per rank). For flat slot r with
  * expert id e = topk_ids[r] and destination rank d = e / (num_experts/world):

@@ -120,6 +120,33 @@ def fused_topk(hidden_states: torch.Tensor, gating_output: torch.Tensor, topk: i
     return w, ids
 
 
+def grouped_topk(hidden_states: torch.Tensor, gating_output: torch.Tensor, topk: int,
+                 renormalize: bool, num_expert_group: int, topk_group: int,
+                 scoring_func: str = "softmax", routed_scaling_factor: float = 1.0
+                 ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Grouped top-k routing of kernels/track1-triton/groupedtopk/base.py:31-72
+    in one kernel (moe_grouped_topk): softmax or sigmoid scores, the
+    `topk_group` expert groups with the best maximum score, the top-k experts
+    among them (descending, ties to the lower index), weights renormalised
+    when asked and scaled by `routed_scaling_factor`. Returns (topk_weights
+    fp32 [T, k], topk_ids int32 [T, k]) like the reference.
+    """
+    _check_cuda("gating_output", gating_output)
+    if gating_output.dim() != 2 or gating_output.shape[0] != hidden_states.shape[0]:
+        raise ValueError("gating_output must be [T, E] with T = hidden_states.shape[0]")
+    if scoring_func not in ("softmax", "sigmoid"):
+        raise ValueError(f"Unsupported scoring_func: {scoring_func}")
+    logits = _contig(gating_output)
+    T, E = logits.shape
+    dev = logits.device
+    w = torch.empty(T, topk, dtype=torch.float32, device=dev)
+    ids = torch.empty(T, topk, dtype=torch.int32, device=dev)
+    _lib.call("moe_grouped_topk", _ptr(logits), _code(logits), T, E, topk, int(renormalize),
+              num_expert_group, topk_group, 0 if scoring_func == "softmax" else 1,
+              float(routed_scaling_factor), _ptr(w), _ptr(ids), _stream(dev))
+    return w, ids
+
+
 # ---------------------------------------------------------------------------
 # moe_align_block_size
 # ---------------------------------------------------------------------------
@@ -464,6 +491,31 @@ class CapturedMoE:
         self.hidden.copy_(hidden_states, non_blocking=True)
         self.logits.copy_(router_logits, non_blocking=True)
         return self.replay()
+
+
+class GroupedTopK(nn.Module):
+    """Drop-in for kernels/track1-triton/groupedtopk/base.py's Model: same
+    constructor and forward(hidden_states, gating_output) -> (topk_weights
+    fp32 [T, k], topk_ids int32 [T, k]), computed by one kernel."""
+
+    def __init__(self, topk: int, renormalize: bool, num_expert_group: int, topk_group: int,
+                 scoring_func: str = "softmax", routed_scaling_factor: float = 1.0):
+        super().__init__()
+        if scoring_func not in ("softmax", "sigmoid"):
+            raise ValueError(f"Unsupported scoring_func: {scoring_func}")
+        self.topk = topk
+        self.renormalize = renormalize
+        self.num_expert_group = num_expert_group
+        self.topk_group = topk_group
+        self.scoring_func = scoring_func
+        self.routed_scaling_factor = routed_scaling_factor
+
+    def forward(self, hidden_states: torch.Tensor, gating_output: torch.Tensor):
+        if hidden_states.size(0) != gating_output.size(0):
+            raise ValueError("hidden_states and gating_output disagree on the token count")
+        return grouped_topk(hidden_states, gating_output, self.topk, self.renormalize,
+                            self.num_expert_group, self.topk_group, self.scoring_func,
+                            self.routed_scaling_factor)
 
 
 class HostPipeline:

@@ -66,3 +66,43 @@ def digest(*tensors: torch.Tensor) -> str:
     for t in tensors:
         h.update(t.contiguous().view(torch.uint8).numpy().tobytes())
     return h.hexdigest()
+
+
+# ---------------------------------------------------------------------------
+# Grouped top-k routing (kernels/track1-triton/groupedtopk/base.py)
+# ---------------------------------------------------------------------------
+
+@dataclass(frozen=True)
+class GroupedCase:
+    name: str
+    T: int
+    E: int
+    topk: int
+    renormalize: bool
+    num_expert_group: int
+    topk_group: int
+    scoring_func: str
+    routed_scaling_factor: float
+    seed: int
+
+
+GROUPED_CASES = [
+    # the reference's default problem (groupedtopk/base.py:75-89)
+    GroupedCase("gtk_default", 83, 256, 8, True, 8, 4, "softmax", 1.0, 61),
+    # DeepSeek-V3-style: sigmoid scores, scaled weights
+    GroupedCase("gtk_sigmoid_scaled", 64, 256, 8, True, 8, 4, "sigmoid", 2.5, 62),
+    GroupedCase("gtk_norenorm", 50, 64, 6, False, 4, 2, "softmax", 1.0, 63),
+    GroupedCase("gtk_one_group", 37, 32, 4, True, 4, 1, "sigmoid", 1.0, 64),
+    GroupedCase("gtk_wide", 19, 1024, 16, True, 32, 8, "softmax", 1.0, 65),
+]
+
+GROUPED_BY_NAME = {c.name: c for c in GROUPED_CASES}
+
+
+def make_grouped_inputs(c: GroupedCase):
+    """Returns (hidden_states [T, 16] f16 (only its row count is used),
+    gating_output [T, E] f32 ~ N(0, 1))."""
+    g = torch.Generator().manual_seed(c.seed)
+    hidden = torch.randn(c.T, 16, generator=g).to(torch.float16)
+    logits = torch.randn(c.T, c.E, generator=g)
+    return hidden, logits

@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 import torch
 
-from cases import CASES, digest, make_inputs
+from cases import CASES, GROUPED_CASES, digest, make_grouped_inputs, make_inputs
 from oracle import moe_oracle as orc
 
 GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden"
@@ -116,3 +116,16 @@ def test_w8a8_oracles_close_to_fp32():
     ref = orc.fused_experts(hidden, w1, w2, w, ids)
     assert orc.rel_l2(orc.fused_experts_fp8(hidden, w1, w2, w, ids), ref) < 0.1
     assert orc.rel_l2(orc.fused_experts_int8(hidden, w1, w2, w, ids), ref) < 3e-2
+
+
+@pytest.mark.parametrize("case", GROUPED_CASES, ids=lambda c: c.name)
+def test_grouped_topk_matches_reference(case):
+    """The grouped top-k restatement against the reference groupedtopk/base.py
+    outputs (same CPU torch ops, so bit for bit)."""
+    hidden, logits = make_grouped_inputs(case)
+    ref = np.load(GOLDEN / f"{case.name}.npz")
+    assert str(ref["digest"]) == digest(hidden, logits)
+    w, ids = orc.grouped_topk(logits, case.topk, case.renormalize, case.num_expert_group,
+                              case.topk_group, case.scoring_func, case.routed_scaling_factor)
+    assert torch.equal(ids, torch.from_numpy(ref["topk_ids"]))
+    assert torch.equal(w, torch.from_numpy(ref["topk_weights"]))

@@ -1,11 +1,14 @@
 """GPU: the fused routing kernel (moe_topk_softmax) against base.py's torch
-routing (softmax -> topk -> renormalise, base.py:44-48)."""
+routing (softmax -> topk -> renormalise, base.py:44-48), and the grouped
+top-k kernel (moe_grouped_topk) against the reference groupedtopk/base.py
+outputs (tests/golden/gtk_*.npz) and the oracle."""
 import numpy as np
 import pytest
 import torch
 
-from cases import CASES, make_inputs
+from cases import CASES, GROUPED_CASES, make_grouped_inputs, make_inputs
 from kernelswift_b200 import fused_moe as fm
+from oracle import moe_oracle as orc
 
 pytestmark = pytest.mark.gpu
 
@@ -94,3 +97,51 @@ def test_ties_go_to_the_lower_expert(cuda_device):
     hidden = torch.empty(3, 8, device=cuda_device)
     _, ids = fm.fused_topk(hidden, logits, 3, True)
     assert ids.cpu().tolist() == [[0, 1, 2], [5, 0, 1], [0, 1, 2]]
+
+
+# ---------------------------------------------------------------------------
+# grouped top-k (kernels/track1-triton/groupedtopk/base.py)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("case", GROUPED_CASES, ids=lambda c: c.name)
+def test_grouped_topk_matches_reference_golden(cuda_device, case):
+    """moe_grouped_topk against the reference operator's own outputs: ids
+    bit-exact, fp32 weights to a few ulp (exp/sigmoid evaluated on the GPU)."""
+    hidden, logits = make_grouped_inputs(case)
+    ref = np.load(GOLDEN / f"{case.name}.npz")
+    model = fm.GroupedTopK(case.topk, case.renormalize, case.num_expert_group,
+                           case.topk_group, case.scoring_func, case.routed_scaling_factor)
+    w, ids = model(hidden.to(cuda_device), logits.to(cuda_device))
+    assert w.dtype == torch.float32 and ids.dtype == torch.int32
+    assert torch.equal(ids.cpu(), torch.from_numpy(ref["topk_ids"]))
+    torch.testing.assert_close(w.cpu(), torch.from_numpy(ref["topk_weights"]),
+                               rtol=1e-5, atol=1e-6)
+
+
+def test_grouped_topk_respects_groups_and_order(cuda_device):
+    """Random problems against the oracle: every id lies in one of the
+    topk_group best groups, ids are in descending score order, equal to the
+    oracle's; 16-bit logits are accepted."""
+    g = torch.Generator().manual_seed(3)
+    for T, E, G, tg, k, sf in ((300, 128, 8, 3, 6, "sigmoid"), (1, 64, 2, 1, 4, "softmax"),
+                               (129, 96, 6, 2, 5, "softmax")):
+        logits = torch.randn(T, E, generator=g)
+        w, ids = fm.grouped_topk(torch.empty(T, 1, device=cuda_device), logits.to(cuda_device),
+                                 k, True, G, tg, sf)
+        rw, rids = orc.grouped_topk(logits, k, True, G, tg, sf)
+        assert torch.equal(ids.cpu(), rids)
+        torch.testing.assert_close(w.cpu(), rw, rtol=1e-5, atol=1e-6)
+    logits = torch.randn(40, 64, generator=g)
+    for dt in (torch.bfloat16, torch.float16):
+        w, ids = fm.grouped_topk(torch.empty(40, 1, device=cuda_device),
+                                 logits.to(dt).to(cuda_device), 4, True, 4, 2)
+        assert torch.isfinite(w).all() and ((ids >= 0) & (ids < 64)).all()
+
+
+def test_grouped_topk_rejects_impossible_k(cuda_device):
+    from kernelswift_b200._lib import MoeError
+
+    logits = torch.randn(4, 32, device=cuda_device)
+    with pytest.raises(MoeError):
+        # 1 kept group of 8 experts cannot supply 9
+        fm.grouped_topk(torch.empty(4, 1, device=cuda_device), logits, 9, True, 4, 1)
