@@ -76,6 +76,102 @@ struct TileCoord {
   int mb, nt, ks;
 };
 
+// ---------------------------------------------------------------------------
+// Expert-aligned tile groups. Tiles are enumerated group by group; inside a
+// group of m-blocks the n-tile varies slowest, so the CTAs that run the
+// group's m-blocks at the same time share each weight tile through L2.
+// Groups follow the experts: a run of m-blocks of one expert forms one group
+// (split into near-equal chunks of at most kGroupMax m-blocks), so an
+// expert's weights are streamed once per chunk instead of once more for
+// every fixed-size group boundary that falls inside the run. Entry m of the
+// table: (first m-block of m's group) << 16 | (the group's m-blocks).
+// ---------------------------------------------------------------------------
+constexpr int kGroupMax = 16;
+constexpr int kMaxTableMb = 4096;  // larger problems use the fixed groups below
+constexpr size_t kGroupTableBytes = size_t(kMaxTableMb) * 4 + 256;
+
+// Block-wide inclusive scan of v (max, or min when MIN) in thread order;
+// `carry` joins consecutive calls. All threads call it; scratch >= 33 ints.
+template <bool MIN>
+__device__ __forceinline__ int block_scan(int v, int& carry, int* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  auto op = [](int x, int y) { return MIN ? min(x, y) : max(x, y); };
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v = op(v, y);
+  }
+  if (lane == 31) scratch[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? scratch[lane] : (MIN ? INT_MAX : INT_MIN);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w = op(w, y);
+    }
+    scratch[lane] = w;
+  }
+  __syncthreads();
+  if (warp > 0) v = op(v, scratch[warp - 1]);
+  v = op(v, carry);
+  const int total = op(scratch[nw - 1], carry);
+  __syncthreads();
+  carry = total;
+  return v;
+}
+
+// Builds the group table for m-blocks [0, num_mb) (num_mb <= kMaxTableMb).
+// All threads of the block call it.
+__device__ void build_group_table(const int32_t* __restrict__ expert_ids, int num_mb,
+                                  uint32_t* tab, int* scratch) {
+  const int nthr = blockDim.x;
+  // pass 1: tab[m] = first m-block of m's run (max-scan of run starts)
+  int carry = 0;
+  for (int base = 0; base < num_mb; base += nthr) {
+    const int m = base + threadIdx.x;
+    int v = 0;
+    if (m < num_mb && (m == 0 || __ldg(expert_ids + m) != __ldg(expert_ids + m - 1))) v = m;
+    v = block_scan<false>(v, carry, scratch);
+    if (m < num_mb) tab[m] = uint32_t(v);
+  }
+  __syncthreads();
+  // pass 2: run end = the next run start after m (min-scan from the right);
+  // tab[m] = start | end << 16 (the low half, read by the neighbours, stays)
+  carry = num_mb;
+  for (int base = ((num_mb - 1) / nthr) * nthr; base >= 0; base -= nthr) {
+    const int m = base + (nthr - 1 - threadIdx.x);  // descending in thread order
+    int v = num_mb;
+    if (m + 1 < num_mb && m >= 0 && int(tab[m + 1] & 0xFFFFu) == m + 1) v = m + 1;
+    v = block_scan<true>(v, carry, scratch);
+    if (m >= 0 && m < num_mb) tab[m] = (tab[m] & 0xFFFFu) | (uint32_t(v) << 16);
+    __syncthreads();
+  }
+  // pass 3: chunk the run, store (group start, group size)
+  for (int m = threadIdx.x; m < num_mb; m += nthr) {
+    const int start = int(tab[m] & 0xFFFFu), end = int(tab[m] >> 16);
+    const int len = end - start;
+    const int chunks = (len + kGroupMax - 1) / kGroupMax;
+    const int csz = (len + chunks - 1) / chunks;
+    const int gs = start + ((m - start) / csz) * csz;
+    tab[m] = (uint32_t(gs) << 16) | uint32_t(min(csz, end - gs));
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ TileCoord tile_coord_tab(int t, int n_tiles, int splits,
+                                                    const uint32_t* tab) {
+  TileCoord c;
+  c.ks = t % splits;
+  const int u = t / splits;
+  const uint32_t e = tab[u / n_tiles];
+  const int gs = int(e >> 16), gsz = int(e & 0xFFFFu);
+  const int v = u - gs * n_tiles;
+  c.nt = v / gsz;
+  c.mb = gs + (v - c.nt * gsz);
+  return c;
+}
+
 __device__ __forceinline__ TileCoord tile_coord(int t, int num_mb, int n_tiles,
                                                 int splits) {
   TileCoord c;
@@ -120,7 +216,7 @@ struct GemmCfg {
   static constexpr int kStages = (192 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr size_t kSmemBytes =
-      1024 + size_t(kStages) * kStageBytes + 256;
+      1024 + size_t(kStages) * kStageBytes + 256 + kGroupTableBytes;
   static_assert(kStages >= 2, "pipeline needs at least two stages");
   static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM columns");
 };
@@ -177,11 +273,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   // Programmatic dependent launch: without early metadata every thread
-  // waits for the previous kernel here; with it, only the A loads (and so
-  // everything downstream of them) wait, after the first weight tiles have
-  // been requested.
+  // waits for the previous kernel here; with it, the align outputs are read
+  // first (they were written two launches earlier), and only the A loads
+  // (and so everything downstream of them) wait, after the first weight
+  // tiles have been requested.
   const bool producer = warp == 0 && lane == 0;
-  if (!p.early_meta || !producer) {
+  if (!p.early_meta) {
     pdl_wait();
     pdl_trigger();
   }
@@ -189,6 +286,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = p.n_total / BN;
   const int total_tiles = num_mb * n_tiles * p.splits;
   const uint64_t limit = p.wait_limit_ns;
+  uint32_t* gtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const bool use_tab = num_mb <= kMaxTableMb;
+  if (use_tab)
+    build_group_table(p.expert_ids, num_mb, gtab, reinterpret_cast<int*>(gtab + kMaxTableMb));
+  auto coord = [&](int t) {
+    return use_tab ? tile_coord_tab(t, n_tiles, p.splits, gtab)
+                   : tile_coord(t, num_mb, n_tiles, p.splits);
+  };
+  if (p.early_meta && !producer) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   if (producer) {
     // ---------------- TMA producer ----------------
@@ -201,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t pre = 0;
     if (p.early_meta) {
       for (int t = blockIdx.x; pre < uint32_t(STAGES) && t < total_tiles; t += gridDim.x) {
-        const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+        const TileCoord c = coord(t);
         const int e = __ldg(p.expert_ids + c.mb);
         if (e < 0 || e >= p.num_experts) continue;
         const int kb0 = c.ks * p.kb_per_split;
@@ -220,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t issued = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const TileCoord c = coord(t);
       const int e = __ldg(p.expert_ids + c.mb);
       if (e < 0 || e >= p.num_experts) continue;
       const int kb0 = c.ks * p.kb_per_split;
@@ -264,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const TileCoord c = coord(t);
       const int e = __ldg(p.expert_ids + c.mb);
       if (e < 0 || e >= p.num_experts) continue;
       const int kb0 = c.ks * p.kb_per_split;
@@ -313,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const TileCoord c = coord(t);
       const int e = __ldg(p.expert_ids + c.mb);
       if (e < 0 || e >= p.num_experts) continue;
       bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, limit);
@@ -546,11 +655,12 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   // Programmatic dependent launch: without early metadata every thread
-  // waits for the previous kernel here; with it, only the A loads (and so
-  // everything downstream of them) wait, after the first weight tiles have
-  // been requested.
+  // waits for the previous kernel here; with it, the align outputs are read
+  // first (they were written two launches earlier), and only the A loads
+  // (and so everything downstream of them) wait, after the first weight
+  // tiles have been requested.
   const bool producer = warp == 0 && lane == 0;
-  if (!p.early_meta || !producer) {
+  if (!p.early_meta) {
     pdl_wait();
     pdl_trigger();
   }
@@ -558,6 +668,18 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
   const int n_tiles = p.n_total / BN;
   const int total_tiles = num_mb * n_tiles * p.splits;
   const uint64_t limit = p.wait_limit_ns;
+  uint32_t* gtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const bool use_tab = num_mb <= kMaxTableMb;
+  if (use_tab)
+    build_group_table(p.expert_ids, num_mb, gtab, reinterpret_cast<int*>(gtab + kMaxTableMb));
+  auto coord = [&](int t) {
+    return use_tab ? tile_coord_tab(t, n_tiles, p.splits, gtab)
+                   : tile_coord(t, num_mb, n_tiles, p.splits);
+  };
+  if (p.early_meta && !producer) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   if (warp < 4) setmaxnreg_dec<kCtrlRegsF8>();
   if (producer) {
@@ -568,7 +690,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
     uint32_t pre = 0;
     if (p.early_meta) {
       for (int t = blockIdx.x; pre < uint32_t(STAGES) && t < total_tiles; t += gridDim.x) {
-        const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+        const TileCoord c = coord(t);
         const int e = __ldg(p.expert_ids + c.mb);
         if (e < 0 || e >= p.num_experts) continue;
         const int kb0 = c.ks * p.kb_per_split;
@@ -587,7 +709,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
     uint32_t issued = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const TileCoord c = coord(t);
       const int e = __ldg(p.expert_ids + c.mb);
       if (e < 0 || e >= p.num_experts) continue;
       const int kb0 = c.ks * p.kb_per_split;
@@ -627,7 +749,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
     uint32_t pphase = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const TileCoord c = coord(t);
       const int e = __ldg(p.expert_ids + c.mb);
       if (e < 0 || e >= p.num_experts) continue;
       const int kb0 = c.ks * p.kb_per_split;
@@ -672,7 +794,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
     uint32_t pphase = 0;
     bool aborted = false;
     for (int t = blockIdx.x; !aborted && t < total_tiles; t += gridDim.x) {
-      const TileCoord c = tile_coord(t, num_mb, n_tiles, p.splits);
+      const TileCoord c = coord(t);
       const int e = __ldg(p.expert_ids + c.mb);
       if (e < 0 || e >= p.num_experts) continue;
       const int kb0 = c.ks * p.kb_per_split;
