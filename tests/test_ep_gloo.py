@@ -4,7 +4,10 @@ The exchange (split sizes, packing order, the three all_to_alls, the inverse
 permutation of the combine) runs exactly as on GPUs; the device work is done
 by a test-only CPU backend built on the oracle. A second test makes one rank
 fail before its first collective and checks that the other rank's forward
-ends with an error within the process group's timeout instead of hanging.
+ends with an error within the process group's timeout instead of hanging. A
+third replays the peer-memory exchange's placement rule (counts matrix,
+destination offsets, combine addressing) on 2 and 4 ranks with uneven token
+counts.
 """
 import datetime
 import os
@@ -129,3 +132,93 @@ def test_ep_rank_failure_surfaces_as_error():
     assert res[1][0] == "error" and "planted failure" in res[1][1]
     # the surviving rank's first collective must fail, not hang
     assert res[0][0] == "error", res[0]
+
+
+# ---------------------------------------------------------------------------
+# The peer-memory exchange's placement rule, restated on gloo ranks: every
+# rank learns the full counts matrix (the kernels write rows of it into each
+# other's memory; here all_gather), a sender's rows for rank d start at
+# dst_off[d] = sum of what lower ranks send to d, and the combine reads slot
+# r's result from rank d at dst_off[d] + (send position - send_start[d]).
+# ---------------------------------------------------------------------------
+
+def peer_worker(rank, world, port, E, k, T, H, I, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        w1, w2 = problem(E, H, I, seed=0)
+        el = E // world
+        backend = CpuBackend(w1[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el])
+        g = torch.Generator().manual_seed(200 + rank)
+        Tr = T + 3 * rank  # uneven token counts
+        hidden = torch.randn(Tr, H, generator=g)
+        logits = torch.randn(Tr, E, generator=g) + torch.linspace(0, 1.5, E)
+        w, ids = orc.route(logits, k)
+        order, send_eid, inv, counts = backend.plan(ids, E, world)
+        # counts matrix on every rank
+        mat = [torch.zeros(world, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(mat, counts[:world].clone())
+        mat = torch.stack(mat)                        # [s, d]
+        send_start = torch.cat([torch.zeros(1, dtype=torch.int64), counts[:world].cumsum(0)])
+        dst_off = torch.stack([mat[:rank, d].sum() for d in range(world)])
+        n_recv = int(mat[:, rank].sum())
+        capacity = max(int(mat[:, d].sum()) for d in range(world))
+        # dispatch: rows land at dst_off[d] + i in rank d's receive buffer
+        rows = backend.pack(hidden, order, k)
+        recv = torch.zeros(capacity, H)
+        recv_id = torch.full((capacity,), -1, dtype=torch.int32)
+        for src in range(world):
+            # every rank's placement, replayed by every rank from the matrix
+            part = [torch.zeros(int(mat[src, d]), H) for d in range(world)]
+            pid = [torch.zeros(int(mat[src, d]), dtype=torch.int32) for d in range(world)]
+            if src == rank:
+                for d in range(world):
+                    part[d] = rows[int(send_start[d]):int(send_start[d + 1])]
+                    pid[d] = send_eid[int(send_start[d]):int(send_start[d + 1])]
+            for d in range(world):
+                dist.broadcast(part[d], src)
+                dist.broadcast(pid[d], src)
+            if mat[src, rank] > 0:
+                off = int(mat[:src, rank].sum())
+                recv[off:off + int(mat[src, rank])] = part[rank]
+                recv_id[off:off + int(mat[src, rank])] = pid[rank]
+        assert int((recv_id >= 0).sum()) == n_recv
+        valid = recv_id >= 0
+        res = torch.zeros(capacity, H)
+        res[valid] = backend.experts(recv[valid], recv_id[valid])
+        # combine: slot r reads rank d's result at dst_off[d] + (p - send_start[d])
+        results = [torch.zeros(capacity, H) for _ in range(world)]
+        dist.all_gather(results, res)
+        out = torch.zeros(Tr, H)
+        for r in range(Tr * k):
+            p = int(inv[r])
+            if p < 0:
+                continue
+            d = int(torch.searchsorted(send_start[1:], p, right=True))
+            row = int(dst_off[d]) + p - int(send_start[d])
+            out[r // k] += w.reshape(-1)[r] * results[d][row]
+        ref = orc.fused_experts(hidden, w1, w2, w, ids)
+        result_q.put((rank, "ok", float((out - ref).abs().max())))
+    except Exception as exc:
+        result_q.put((rank, "error", repr(exc)[:300]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,E,k", [(2, 8, 2), (4, 16, 4)])
+def test_peer_placement_rule_matches_oracle(world, E, k):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=peer_worker, args=(r, world, port, E, k, 21, 64, 32, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, status, info in res:
+        assert status == "ok", (rank, info)
+        assert info < 1e-4, (rank, info)
