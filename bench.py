@@ -557,16 +557,19 @@ def main():
                          f"restated in torch-CPU bf16 with its per-call weight casts "
                          f"(median of {n} calls, {med:.2f} s each)"}
 
-    # our kernels per step: routing, align (1 launch up to 8192 routed rows,
-    # else 3), gather, gate-up (+ swiglu_reduce when K-split), [activation
-    # quant], down, top-k sum
-    numel = rows_per_launch[0]
-    if world > 1 and ep.peer is not None:
-        numel = ep.peer.capacity  # align runs over the whole receive buffer
-    launches_per_step = 1 + (1 if numel <= 8192 else 3) + 4 + (0 if quant == "none" else 1)
-    if world > 1:
-        # plan, pack, combine (nccl) | plan, dispatch, signal, combine, step end (peer)
-        launches_per_step += 3 if ep.peer is None else 5
+    # our kernels per step: the routing kernel plus what the expert pass
+    # launches for this shape (the plan's own count), plus the exchange
+    if world == 1:
+        launches_per_step = 1 + fm.fused_experts_launches(T, H, I, E, k, quant)
+    elif ep.peer is None:
+        # plan, pack, expert pass over the received rows (top_k = 1), combine
+        launches_per_step = 1 + 2 + fm.fused_experts_launches(
+            rows_per_launch[0], H, I, E // world, 1, quant) + 1
+    else:
+        # plan, dispatch, expert pass over the receive buffer, signal,
+        # combine, step end
+        launches_per_step = 1 + 2 + fm.fused_experts_launches(
+            ep.peer.capacity, H, I, E // world, 1, quant, rows_only=True) + 3
     if rank == 0:
         line = {
             "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,

@@ -272,6 +272,11 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace,
 int moe_fused_experts_rows(const moe_problem_t* p, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Number of kernels moe_fused_experts (rows_only = 0) or
+ * moe_fused_experts_rows (rows_only = 1) launches for `p` (pointers unused;
+ * answers without a GPU). No reference counterpart (measurement aid). */
+int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launches);
+
 /* ------------------------------------------------------------------------ */
 /* The stages of moe_fused_experts, one entry point each. Used by the expert-
  * parallel path (which inserts the token exchange between them) and by tests.

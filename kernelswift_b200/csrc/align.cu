@@ -254,6 +254,8 @@ int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
 
 }  // namespace
 
+int64_t align_small_max() { return kSmallMax; }
+
 int64_t align_buffer_len(int64_t numel, int E, int BM) {
   return round_up(numel + int64_t(E) * (BM - 1), BM);
 }

@@ -10,6 +10,7 @@ namespace ksw {
 
 // ----- align.cu -----
 int64_t align_buffer_len(int64_t numel, int E, int BM);
+int64_t align_small_max();  // routed rows up to which align is one launch
 size_t align_workspace_bytes(int64_t numel, int E);
 int align_validate(int64_t numel, int E, int BM);
 int align_launch(const void* ids, int ids_dtype, int64_t numel, int E, int BM,

@@ -426,6 +426,32 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   return fused_experts_impl(p, workspace, workspace_bytes, stream, nullptr);
 }
 
+int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launches) {
+  KSW_REQUIRE(launches != nullptr, MOE_ERR_INVALID_ARG, "null launches pointer");
+  int sms = 148;
+  if (check_device(&sms) != MOE_OK) sms = 148;  // answers without a B200 present
+  Plan P;
+  const int st = make_plan(p, sms, &P);
+  if (st != MOE_OK) return st;
+  if (P.T == 0) {
+    *launches = 0;
+    return MOE_OK;
+  }
+  if (P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype && decode_path_enabled() &&
+      decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype)) {
+    *launches = 2;
+    return MOE_OK;
+  }
+  int n = (P.numel <= align_small_max() ? 1 : 3) + 1;  // align, gather
+  n += P.gu_splits > 1 ? 2 : 1;                         // gate-up (+ swiglu_reduce)
+  n += P.quant != MOE_QUANT_NONE ? 1 : 0;               // activation quantisation
+  n += 1;                                               // down
+  const bool direct = rows_only && p->top_k == 1 && P.splits == 1 && P.part_dtype == p->act_dtype;
+  n += direct ? 0 : 1;                                  // top-k sum
+  *launches = n;
+  return MOE_OK;
+}
+
 int moe_fused_experts_rows(const moe_problem_t* p, void* workspace, size_t workspace_bytes,
                            void* stream) {
   KSW_REQUIRE(p != nullptr, MOE_ERR_INVALID_ARG, "null problem");

@@ -309,6 +309,26 @@ def _problem(hidden, prep: PreparedWeights, topk_weights, topk_ids, out, status,
     return p
 
 
+def fused_experts_launches(num_tokens: int, hidden_size: int, intermediate_size: int,
+                           num_experts: int, top_k: int, quant: str = "none",
+                           dtype: torch.dtype = torch.bfloat16, rows_only: bool = False) -> int:
+    """Kernels one fused_experts call of this shape launches (the plan's
+    answer, moe_fused_experts_launches; no GPU needed)."""
+    p = _lib.MoeProblem()
+    p.num_tokens = num_tokens
+    p.hidden_size = hidden_size
+    p.inter_size = intermediate_size
+    p.num_experts = num_experts
+    p.top_k = top_k
+    p.act_dtype = _code(torch.empty(0, dtype=dtype))
+    p.quant = _QUANT[quant]
+    p.ids_dtype = _lib.DT_I32
+    p.weights_dtype = _lib.DT_F32
+    n = ctypes.c_int(0)
+    _lib.call("moe_fused_experts_launches", ctypes.byref(p), int(rows_only), ctypes.byref(n))
+    return n.value
+
+
 def stage_event_array(events) -> ctypes.Array:
     """cudaEvent_t[7] for moe_problem_t.stage_events from torch.cuda.Event
     objects (each must have been recorded once so that it exists)."""
