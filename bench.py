@@ -557,6 +557,21 @@ def main():
                          f"restated in torch-CPU bf16 with its per-call weight casts "
                          f"(median of {n} calls, {med:.2f} s each)"}
 
+    # align is launch-bound: its time (graph stage, with one event record)
+    # and the bytes it moves, ids in + sorted ids and block experts out
+    if world == 1:
+        n_ids = T * k
+    elif ep.peer is not None:
+        n_ids = ep.peer.capacity  # align runs over the whole receive buffer
+    else:
+        n_ids = int(rows_per_launch[0])
+    e_al = E if world == 1 else E // world
+    L_al = -(-(n_ids + e_al * 127) // 128) * 128
+    al_bytes = n_ids * 4 + (L_al + L_al // 128) * 4
+    al_ms = stage_ms.get("align", 0.0)
+    align_report = {"us": al_ms * 1e3, "bytes": al_bytes,
+                    "gbs": al_bytes / (al_ms * 1e-3) / 1e9 if al_ms > 0 else None}
+
     # our kernels per step: the routing kernel plus what the expert pass
     # launches for this shape (the plan's own count), plus the exchange
     if world == 1:
@@ -581,6 +596,7 @@ def main():
                                       None if world == 1 else ep.exchange),
             "tflops": tflops,
             "stage_ms": stage_ms,
+            "align": align_report,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -118,7 +118,7 @@ def run(world, fail_rank=-1, E=8, k=2, T=37, H=64, I=32):
     return results
 
 
-@pytest.mark.parametrize("world,E,k", [(2, 8, 2), (4, 16, 4)])
+@pytest.mark.parametrize("world,E,k", [(2, 8, 2), (4, 16, 4), (8, 16, 2)])
 def test_ep_matches_oracle(world, E, k):
     res = run(world, E=E, k=k)
     for rank in range(world):
