@@ -257,7 +257,12 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
  *          W2[e] . (silu(W1g[e] . x_t) * (W1u[e] . x_t)),  e = topk_ids[t, j]
  * Matmuls run on the tcgen05 tensor cores (bf16/fp16, e4m3 or int8 operands,
  * fp32/int32 accumulation in tensor memory); SiLU, scaling and the top-k sum
- * run in fp32. F32 activations are rounded to bf16 operands.
+ * run in fp32. F32 activations are rounded to bf16 operands. With at most
+ * 16 routed rows, 16-bit activations, unquantised weights and at most 256 MB
+ * of weights to stream, two weight-streaming CUDA-core kernels do the whole
+ * computation instead (fp32 dot products; MOE_NO_DECODE_PATH=1 disables
+ * them). Kernels are launched with programmatic dependent launch
+ * (MOE_NO_PDL=1 disables it).
  */
 int moe_fused_experts(const moe_problem_t* p, void* workspace,
                       size_t workspace_bytes, void* stream);
