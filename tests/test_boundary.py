@@ -8,6 +8,7 @@ import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
 V1 = ROOT / "kernelswift_b200" / "ks_fused_moe.py"
+V1_GTK = ROOT / "kernelswift_b200" / "ks_grouped_topk.py"
 
 
 def kept_by_auto_bench_filter(node):
@@ -16,8 +17,9 @@ def kept_by_auto_bench_filter(node):
                              ast.AsyncFunctionDef))
 
 
-def test_v1_module_is_all_kept_by_the_filter():
-    tree = ast.parse(V1.read_text())
+@pytest.mark.parametrize("path", [V1, V1_GTK], ids=lambda p: p.name)
+def test_v1_module_is_all_kept_by_the_filter(path):
+    tree = ast.parse(path.read_text())
     dropped = [type(n).__name__ for n in tree.body
                if not kept_by_auto_bench_filter(n) and not (
                    isinstance(n, ast.Expr) and isinstance(getattr(n, "value", None), ast.Constant))]
@@ -43,4 +45,28 @@ def test_v1_loads_through_the_real_harness_loader():
     harness = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(harness)
     mod = harness.load_ks_module(V1)
+    assert hasattr(mod, "ModelNew") and hasattr(mod, "get_inputs")
+
+
+def test_grouped_topk_module_defines_the_contract():
+    """ks_grouped_topk mirrors groupedtopk/base.py's constructor defaults."""
+    spec = importlib.util.spec_from_file_location("ks_gtk", V1_GTK)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.get_init_inputs() == [8, True, 8, 4]
+    m = mod.ModelNew(*mod.get_init_inputs())
+    assert (m.topk, m.renormalize, m.num_expert_group, m.topk_group) == (8, True, 8, 4)
+    assert m.scoring_func == "softmax" and m.routed_scaling_factor == 1.0
+    assert not list(m.state_dict())
+
+
+@pytest.mark.parametrize("path", [V1, V1_GTK], ids=lambda p: p.name)
+def test_loads_through_the_real_harness_loader(path):
+    ab = Path("/root/reference/auto_bench.py")
+    if not ab.exists():
+        pytest.skip("reference checkout not present")
+    spec = importlib.util.spec_from_file_location("ks_auto_bench2", ab)
+    harness = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(harness)
+    mod = harness.load_ks_module(path)
     assert hasattr(mod, "ModelNew") and hasattr(mod, "get_inputs")
