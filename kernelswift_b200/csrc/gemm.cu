@@ -20,9 +20,19 @@
 //   warps 2..9  epilogue: warp w reads TMEM lane quarter w % 4 and column
 //               half (w - 2) / 4, several 32-lane x 16-column tcgen05.ld per
 //               wait, fused math, 16-byte stores to global memory.
-// Tiles are (m-block, n-tile, k-split) triples handed out round-robin; within
-// a group of 8 m-blocks the n-tile index varies slowest, so the CTAs running
-// at the same time share weight tiles through L2.
+// Tiles are (m-block, n-tile, k-split) triples handed out round-robin, group
+// by group: a group is one expert's run of m-blocks (at most kGroupMax; a
+// longer run is split evenly) and inside it the n-tile index varies slowest,
+// so the CTAs running at the same time share each weight tile through L2
+// and an expert's weights stream from DRAM once per group.
+//
+// Launched with programmatic dependent launch: given early metadata (the
+// align outputs are two launches old), the producer requests the weight
+// tiles of its first stages before waiting on the kernel that wrote A.
+//
+// The fp8 block-scaled variant (moe_grouped_gemm_fp8_kernel, below) uses 20
+// warps: a per-k-block TMEM buffer is promoted into fp32 registers by 16
+// epilogue warps with the activation and weight block scales.
 //
 // Every barrier wait is bounded (one second): a role that runs out raises a
 // shared abort flag, every role leaves its loop, in-flight TMA loads and
