@@ -9,7 +9,7 @@ sum, over one batch of synthetic tokens (N(0,1) activations, N(0,1/fan_in)
 weights, N(0,1) router logits).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload mixtral|qwen3|dsv3-fp8|qwen3-int8] [--tokens T]
+                    [--workload mixtral|qwen3|dsv3-fp8|dsv3-fp8-ue8m0|qwen3-int8] [--tokens T]
 
 `value` is device time (CUDA events, inputs resident in HBM, L2 flushed
 between steps outside the timed windows, max over ranks). On one GPU a step
@@ -43,6 +43,8 @@ WORKLOADS = {
     "mixtral": (4096, 14336, 8, 2, "none", 4096, 0.0),
     "qwen3": (2048, 768, 128, 8, "none", 8192, 0.5),
     "dsv3-fp8": (7168, 2048, 256, 8, "fp8", 4096, 0.0),
+    # the same layer with power-of-two block scales applied by the tensor core
+    "dsv3-fp8-ue8m0": (7168, 2048, 256, 8, "fp8-ue8m0", 4096, 0.0),
     "qwen3-int8": (2048, 768, 128, 8, "int8", 8192, 0.5),
 }
 METRIC = "fused-MoE layer tokens/s"
@@ -300,7 +302,7 @@ def main():
         def step(stage_arr=None):
             tw, ti = fm.fused_topk(hidden, logits, k, weights_dtype=hidden.dtype)
             return fm.fused_experts(hidden, prep, None, tw, ti,
-                                    use_fp8_w8a8=quant == "fp8", use_int8_w8a8=quant == "int8",
+                                    use_fp8_w8a8=quant.startswith("fp8"), use_int8_w8a8=quant == "int8",
                                     stage_events=stage_arr)
     else:
         # expert parallel: this rank holds E/world experts, routes its own T
@@ -406,7 +408,7 @@ def main():
         # record nodes) for the per-kernel breakdown.
         def graph_fn(hd, ld, stage_arr=None):
             tw, ti = fm.fused_topk(hd, ld, k, weights_dtype=hd.dtype)
-            return fm.fused_experts(hd, prep, None, tw, ti, use_fp8_w8a8=quant == "fp8",
+            return fm.fused_experts(hd, prep, None, tw, ti, use_fp8_w8a8=quant.startswith("fp8"),
                                     use_int8_w8a8=quant == "int8", stage_events=stage_arr)
 
         graph = fm.CapturedMoE(graph_fn, T, H, E, dtype=torch.bfloat16, device=dev)
@@ -460,7 +462,7 @@ def main():
                 if world > 1:
                     return ep(hd, tw, ti)
                 return fm.fused_experts(hd, prep, None, tw, ti,
-                                        use_fp8_w8a8=quant == "fp8",
+                                        use_fp8_w8a8=quant.startswith("fp8"),
                                         use_int8_w8a8=quant == "int8")
 
         # the public host-I/O pipeline: each step's H2D and D2H copies run on
@@ -590,7 +592,7 @@ def main():
             "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16" if quant == "none" else ("e4m3" if quant == "fp8" else "int8"),
+            "dtype": "bf16" if quant == "none" else ("int8" if quant == "int8" else "e4m3"),
             "data": "synthetic",
             "config": workload_config(args.workload, H, I, E, k, quant, T, world,
                                       None if world == 1 else ep.exchange),

@@ -61,9 +61,34 @@ typedef enum moe_quant {
   MOE_QUANT_NONE = 0,         /* bf16/fp16 weights and activations            */
   MOE_QUANT_FP8_BLOCK = 1,    /* e4m3 W8A8: weight scales per 128x128 block,
                                  activation scales per token per 128 columns  */
-  MOE_QUANT_INT8_CHANNEL = 2  /* int8 W8A8: weight scale per output channel,
+  MOE_QUANT_INT8_CHANNEL = 2, /* int8 W8A8: weight scale per output channel,
                                  activation scale per token                   */
+  MOE_QUANT_FP8_UE8M0 = 3     /* e4m3 W8A8 with power-of-two (UE8M0) scales,
+                                 the FP8_BLOCK granularity, applied by the
+                                 tensor core; scales travel as scale-factor
+                                 images (below)                                */
 } moe_quant_t;
+
+/*
+ * MOE_QUANT_FP8_UE8M0 scales. A scale is one byte b meaning 2^(b - 127); it
+ * is the smallest power of two s with absmax / s <= 448 over its group (a
+ * 128x128 weight block, or 128 columns of one activation row), 127 (s = 1)
+ * for an all-zero group; q = e4m3_rn(x / s). The tensor core applies the
+ * scales itself (tcgen05.mma kind::mxf8f6f4.block_scale), so the products of
+ * every k-block accumulate in tensor memory with no per-block promotion.
+ *
+ * The scales of a matrix group g (expert g of a weight tensor; g = 0 for the
+ * gathered activations) with R rows and KB = C / 128 column blocks are stored
+ * as a "scale-factor image" of 512-byte chunks, one chunk per 128 rows and 4
+ * column blocks, in the order the tensor memory copy (tcgen05.cp 32x128b)
+ * takes them. The scale of row r, column block kb is the byte at
+ *   ((g * Q + kb / 4) * RS + r / 128) * 512
+ *     + 16 * (r % 32) + 4 * ((r % 128) / 32) + kb % 4
+ * with Q = ceil(KB / 4) and RS = ceil(R / 128). For the gate/up weights, r is
+ * the row of the regrouped w13 (each row carries the scale of its block in
+ * the original w1 layout).
+ */
+int64_t moe_ue8m0_scale_bytes(int64_t groups, int64_t rows, int64_t cols);
 
 /* ------------------------------------------------------------------------ */
 /* Status helpers                                                           */
@@ -189,6 +214,10 @@ int moe_align_block_size_noalloc(const void* topk_ids, int ids_dtype,
  * quant == MOE_QUANT_INT8_CHANNEL: src F32/F16/BF16 is quantised to int8 with
  *   one scale per output row, scale = absmax / 127; `scale_out` receives
  *   [E, 2I] fp32 in the regrouped row order.
+ * quant == MOE_QUANT_FP8_UE8M0: src F32/F16/BF16 is quantised to e4m3 with one
+ *   power-of-two scale per 128x128 block of the original layout; `scale_out`
+ *   (cast to float*, moe_ue8m0_scale_bytes(E, 2I, H) bytes) receives the
+ *   scale-factor image. Requires I % 128 == 0 and H % 128 == 0.
  * Requires I % 16 == 0 and H % 16 == 0.
  */
 int moe_prepare_w13(const void* w1, int src_dtype, const float* scale_in,
@@ -200,7 +229,8 @@ int moe_prepare_w13(const void* w1, int src_dtype, const float* scale_in,
  * w2 [E, H, I] (base.py:29-31) -> the down-projection operand, same layout.
  * quant NONE: cast. FP8_BLOCK: e4m3 + [E, ceil(H/128), ceil(I/128)] scales
  * (or pass-through of an already-e4m3 source with `scale_in`). INT8_CHANNEL:
- * int8 + [E, H] scales.
+ * int8 + [E, H] scales. FP8_UE8M0: e4m3 + the scale-factor image
+ * (moe_ue8m0_scale_bytes(E, H, I) bytes).
  */
 int moe_prepare_w2(const void* w2, int src_dtype, const float* scale_in,
                    int64_t num_experts, int64_t hidden_size,
@@ -296,7 +326,9 @@ int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launc
  * quant NONE: dst_dtype F16/BF16 (F32 sources are rounded).
  * quant FP8_BLOCK: dst e4m3 + dst_scale [buffer_len, ceil(H/128)],
  *   scale = absmax/448 per 128 columns. INT8_CHANNEL: dst int8 + dst_scale
- *   [buffer_len], scale = absmax/127 per row.
+ *   [buffer_len], scale = absmax/127 per row. FP8_UE8M0: dst e4m3 +
+ *   dst_scale (cast to float*) the scale-factor image of the rows,
+ *   moe_ue8m0_scale_bytes(1, buffer_len, H) bytes; H % 128 == 0.
  */
 int moe_gather_rows(const void* src, int src_dtype, int64_t src_rows,
                     int64_t hidden_size, int top_k,
@@ -308,8 +340,9 @@ int moe_gather_rows(const void* src, int src_dtype, int64_t src_rows,
 /*
  * act[m, :] = silu(gate) * up for every operand row m of a used block whose
  * slot is not padding, gate/up = a[m] . w13[e]^T (base.py:69-71).
- * act_out: [buffer_len, I] in compute_dtype (bf16 for INT8_CHANNEL).
- * block_n: 0 picks the N tile, else 64, 128 or 256.
+ * act_out: [buffer_len, I] in compute_dtype (bf16 for the W8A8 modes).
+ * FP8_UE8M0: a_scale and w13_scale are scale-factor images (cast to float*).
+ * block_n: 0 picks the N tile, else 64, 128 or 256 (128 or 256 for fp8).
  */
 int moe_gemm_gate_up(int quant, int compute_dtype, const void* a,
                      const float* a_scale, const void* w13,
@@ -326,6 +359,7 @@ int moe_gemm_gate_up(int quant, int compute_dtype, const void* a,
  * partial_out: [splits, numel, H] fp32; rows of dropped slots are not written.
  * `splits` must leave no split empty: with kb = ceil(I * elem_bytes / 128)
  * k-blocks, ceil(kb / ceil(kb / splits)) == splits.
+ * FP8_UE8M0: act_scale and w2_scale are scale-factor images (cast to float*).
  */
 int moe_gemm_down(int quant, int compute_dtype, const void* act,
                   const float* act_scale, const void* w2,

@@ -25,7 +25,7 @@ MOE_ERR_DEVICE = 6
 DT_F32, DT_F16, DT_BF16, DT_E4M3, DT_I8, DT_I32, DT_I64 = range(7)
 
 # moe_quant_t
-QUANT_NONE, QUANT_FP8_BLOCK, QUANT_INT8_CHANNEL = range(3)
+QUANT_NONE, QUANT_FP8_BLOCK, QUANT_INT8_CHANNEL, QUANT_FP8_UE8M0 = range(4)
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -73,6 +73,7 @@ SIGNATURES = {
     "moe_read_status": (_int, [_vp, _vp, _int, _vp]),
     "moe_topk_softmax": (_int, [_vp, _int, _i64, _int, _int, _int, _vp, _int, _vp, _int, _vp]),
     "moe_align_buffer_len": (_i64, [_i64, _int, _int]),
+    "moe_ue8m0_scale_bytes": (_i64, [_i64, _i64, _i64]),
     "moe_align_workspace_size": (_int, [_i64, _int, _int, ctypes.POINTER(_sz)]),
     "moe_align_block_size": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _sz, _vp]),
     "moe_align_block_size_noalloc": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp]),

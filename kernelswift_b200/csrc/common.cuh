@@ -302,6 +302,90 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
          (uint64_t(2) << 61);
 }
 
+// ----- block-scaled fp8 (kind::mxf8f6f4 with UE8M0 scale factors) -----
+
+// 1-D bulk copy global -> shared memory, completion counted on `bar` as
+// transaction bytes. Both addresses 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Instruction descriptor of tcgen05.mma kind::mxf8f6f4.block_scale with
+// e4m3 A and B (both K-major), UE8M0 scale factors and an f32 accumulator:
+//   [4,6) B scale-factor byte, [7,10) A format 0 (e4m3), [10,13) B format 0,
+//   [17,23) N >> 3, [23] scale format 1 (UE8M0), [24,29) M >> 4,
+//   [29,31) A scale-factor byte, [31] K = 32.
+__host__ __device__ constexpr uint32_t make_idesc_mx(int m, int n) {
+  return (uint32_t(n >> 3) << 17) | (1u << 23) | (uint32_t(m >> 4) << 24);
+}
+// Selects byte `id` (0..3) of the 32-bit scale-factor cells for A and B.
+__host__ __device__ constexpr uint32_t idesc_sf_ids(uint32_t idesc, uint32_t id) {
+  return idesc | (id << 29) | (id << 4);
+}
+
+// D[tmem] (+)= (A * sfA) * (B * sfB)^T for one K = 32 step: the scale
+// factor of A row m and of B row n live in tensor memory at sfa_tmem /
+// sfb_tmem (layout of tc_cp_sf below).
+__device__ __forceinline__ void tc_mma_mx(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t sfa_tmem,
+                                          uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], "
+      "p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Copies a 512-byte scale-factor chunk (32 rows of 16 bytes in shared
+// memory) into tensor memory: row l goes to lane l of the four columns at
+// `taddr`, replicated into each of the four 32-lane quarters. A chunk holds
+// the scales of 128 matrix rows: row r's four bytes (four consecutive
+// k-blocks) are the 32-bit cell of lane r % 32, column r / 32.
+__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// Shared-memory descriptor of one scale-factor chunk: no swizzle, 8-row x
+// 16-byte core matrices stored contiguously (stride byte offset 128 between
+// them), one core matrix across, version 1.
+__device__ __forceinline__ uint64_t make_sf_desc(uint32_t smem_addr) {
+  return (uint64_t((smem_addr >> 4) & 0x3FFFu)) | (uint64_t(128 >> 4) << 32) |
+         (uint64_t(1) << 46);
+}
+
+// UE8M0 scale byte of a group with absolute maximum `amax`: the smallest b
+// with amax <= 448 * 2^(b - 127). Writing amax = 1.f * 2^(E - 127) (f the
+// 23-bit fraction, E the biased exponent): 448 = 1.75 * 2^8, so b = E - 8
+// when 1.f <= 1.75 and E - 7 otherwise. Zero (and NaN) groups get 127
+// (scale 1); subnormal groups get 0.
+__device__ __forceinline__ uint32_t ue8m0_byte(float amax) {
+  if (!(amax > 0.0f)) return 127u;
+  const uint32_t bits = __float_as_uint(amax);
+  const int b = int((bits >> 23) & 0xFFu) - 8 + ((bits & 0x7FFFFFu) > 0x600000u ? 1 : 0);
+  return uint32_t(min(max(b, 0), 254));
+}
+// 1 / scale = 2^(127 - b), exactly (b <= 253).
+__device__ __forceinline__ float ue8m0_inv_scale(uint32_t b) {
+  return __uint_as_float((254u - b) << 23);
+}
+
+// Byte offset of the scale of row r, column block kb in a scale-factor image
+// with q_blocks = ceil(KB / 4) and row_slices = ceil(R / 128), for matrix
+// group g (the layout moe_ue8m0_scale_bytes documents).
+__host__ __device__ __forceinline__ int64_t sf_image_offset(int64_t g, int64_t r, int64_t kb,
+                                                            int64_t q_blocks,
+                                                            int64_t row_slices) {
+  return ((g * q_blocks + (kb >> 2)) * row_slices + (r >> 7)) * 512 + 16 * (r & 31) +
+         4 * ((r & 127) >> 5) + (kb & 3);
+}
+
 // Loads 16 consecutive 32-bit columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(

@@ -32,7 +32,10 @@
 //
 // The fp8 block-scaled variant (moe_grouped_gemm_fp8_kernel, below) uses 20
 // warps: a per-k-block TMEM buffer is promoted into fp32 registers by 16
-// epilogue warps with the activation and weight block scales.
+// epilogue warps with the activation and weight block scales. With
+// power-of-two (UE8M0) scales the tensor core applies them itself
+// (moe_grouped_gemm_mx_kernel, kind::mxf8f6f4.block_scale) and the tile
+// accumulates in TMEM like the bf16 kernel's.
 //
 // Every barrier wait is bounded (one second): a role that runs out raises a
 // shared abort flag, every role leaves its loop, in-flight TMA loads and
@@ -59,8 +62,8 @@ struct KParams {
   const int32_t* num_post_pad;
   const int32_t* expert_ids;
   const int32_t* sorted_ids;
-  const float* a_scale;     // INT8: [rows]
-  const float* b_scale;     // INT8: [E, n]
+  const float* a_scale;     // INT8: [rows]; FP8_UE8M0: scale-factor image (bytes)
+  const float* b_scale;     // INT8: [E, n]; FP8_UE8M0: scale-factor image (bytes)
   const void* row_weights;  // down: [numel]
   void* out;
   int32_t* status;
@@ -913,6 +916,346 @@ __global__ void __launch_bounds__(kThreadsF8, 1)
 }
 
 // ---------------------------------------------------------------------------
+// FP8 (e4m3) with power-of-two (UE8M0) block scales applied by the tensor
+// core: tcgen05.mma kind::mxf8f6f4.block_scale takes, for every K = 32 step,
+// one scale byte per A row and per B row from tensor memory, so all k-blocks
+// of a tile accumulate in one TMEM buffer as in the bf16 kernel, and the
+// epilogue is the bf16 kernel's (no per-k-block promotion).
+//
+// Per k-block the producer also brings the 512-byte scale-factor chunk of
+// the A tile's 128 rows and the BN / 128 chunks of the B tile (bulk copies
+// from the scale-factor images into the stage). The MMA thread copies them
+// into the stage's TMEM slot (tcgen05.cp; copies and MMAs issued by one
+// thread execute in order) and selects byte kb % 4 of each 32-bit cell
+// through the instruction descriptor. A slot is rewritten only after the
+// MMAs that read it have completed (the stage went through its empty
+// barrier first). A BN = 256 tile keeps one accumulator (its 256 columns and
+// the scale slots share the 512 TMEM columns), BN = 128 two.
+//
+// Image geometry (the moe_ue8m0_scale_bytes layout): A has rows / 128 row
+// slices and ceil(k_blocks / 4) chunk columns; B has n_total / 128 row
+// slices per expert.
+// ---------------------------------------------------------------------------
+template <int BN>
+struct MxCfg {
+  static constexpr int kNAcc = BN == 256 ? 1 : 2;
+  static constexpr int kBBytes = BN * kKBytes;
+  static constexpr int kSfaBytes = 512;
+  static constexpr int kSfbBytes = (BN / 128) * 512;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr size_t kFixedBytes = 1024 + 256 + kGroupTableBytes;
+  static constexpr int kStages = int((224 * 1024 - kFixedBytes) / kStageBytes);
+  static constexpr size_t kSmemBytes = kFixedBytes + size_t(kStages) * kStageBytes;
+  static constexpr int kSfCol0 = kNAcc * BN;          // first scale-slot column
+  static constexpr int kSfCols = 4 + 4 * (BN / 128);  // A chunk + B chunks per stage
+  static_assert(BN == 128 || BN == 256, "block-scaled tile width");
+  static_assert(kStages >= 2 && 8 * (2 * kStages + 5) + 8 <= 256, "pipeline depth");
+  static_assert(kSfCol0 + kStages * kSfCols <= 512, "TMEM columns");
+};
+
+template <int BN, int EPI, typename TOUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_grouped_gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA,
+                               const __grid_constant__ CUtensorMap tmB, const KParams p) {
+  using Cfg = MxCfg<BN>;
+  constexpr int STAGES = Cfg::kStages;
+  constexpr int NACC = Cfg::kNAcc;
+  constexpr uint32_t IDESC = make_idesc_mx(BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * kABytes;
+  uint8_t* sSfa = sB + STAGES * Cfg::kBBytes;
+  uint8_t* sSfb = sSfa + STAGES * Cfg::kSfaBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSfb + STAGES * Cfg::kSfbBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* final_bar = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < NACC; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 256);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // programmatic dependent launch, as in moe_grouped_gemm_kernel
+  const bool producer = warp == 0 && lane == 0;
+  if (!p.early_meta) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  const int num_mb = min(__ldg(p.num_post_pad) / BM, p.max_m_blocks);
+  const int n_tiles = p.n_total / BN;
+  const int total_tiles = num_mb * n_tiles * p.splits;
+  const uint64_t limit = p.wait_limit_ns;
+  uint32_t* gtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const bool use_tab = num_mb <= kMaxTableMb;
+  if (use_tab)
+    build_group_table(p.expert_ids, num_mb, gtab, reinterpret_cast<int*>(gtab + kMaxTableMb));
+  auto coord = [&](int t) {
+    return use_tab ? tile_coord_tab(t, n_tiles, p.splits, gtab)
+                   : tile_coord(t, num_mb, n_tiles, p.splits);
+  };
+  if (p.early_meta && !producer) {
+    pdl_wait();
+    pdl_trigger();
+  }
+
+  if (producer) {
+    // ---------------- TMA + scale-factor producer ----------------
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    const uint8_t* sfa_img = reinterpret_cast<const uint8_t*>(p.a_scale);
+    const uint8_t* sfb_img = reinterpret_cast<const uint8_t*>(p.b_scale);
+    const int64_t q_blocks = (p.k_blocks + 3) / 4;
+    const int64_t b_slices = p.n_total / 128;
+    auto sfa_src = [&](int mb, int kb) {
+      return sfa_img + (int64_t(kb >> 2) * p.max_m_blocks + mb) * 512;
+    };
+    auto sfb_src = [&](int e, int nt, int kb) {
+      return sfb_img + ((int64_t(e) * q_blocks + (kb >> 2)) * b_slices + nt * (BN / 128)) * 512;
+    };
+    uint32_t pre = 0;
+    if (p.early_meta) {
+      for (int t = blockIdx.x; pre < uint32_t(STAGES) && t < total_tiles; t += gridDim.x) {
+        const TileCoord c = coord(t);
+        const int e = __ldg(p.expert_ids + c.mb);
+        if (e < 0 || e >= p.num_experts) continue;
+        const int kb0 = c.ks * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        const int b_row = e * p.n_total + c.nt * BN;
+        for (int kb = kb0; kb < kb1 && pre < uint32_t(STAGES); ++kb, ++pre) {
+          mbar_arrive_expect_tx(&full[pre], Cfg::kStageBytes);
+          tma_load_2d(sB + pre * Cfg::kBBytes, &tmB, kb * kKBytes, b_row, &full[pre]);
+          bulk_load(sSfb + pre * Cfg::kSfbBytes, sfb_src(e, c.nt, kb), Cfg::kSfbBytes,
+                    &full[pre]);
+        }
+      }
+      pdl_wait();
+      pdl_trigger();
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      const TileCoord c = coord(t);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      const int kb0 = c.ks * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+      const int a_row = c.mb * BM;
+      const int b_row = e * p.n_total + c.nt * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (issued >= pre) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kb * kKBytes, b_row, &full[stage]);
+          bulk_load(sSfb + stage * Cfg::kSfbBytes, sfb_src(e, c.nt, kb), Cfg::kSfbBytes,
+                    &full[stage]);
+        }
+        tma_load_2d(sA + stage * kABytes, &tmA, kb * kKBytes, a_row, &full[stage]);
+        bulk_load(sSfa + stage * Cfg::kSfaBytes, sfa_src(c.mb, kb), Cfg::kSfaBytes,
+                  &full[stage]);
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    for (int s = 0; s < STAGES; ++s) {
+      const uint32_t n_s = issued / STAGES + (uint32_t(s) < issued % STAGES ? 1u : 0u);
+      if (n_s == 0) continue;
+      volatile int no_abort = 0;
+      mbar_wait_bounded(&full[s], (n_s - 1) & 1u, &no_abort, limit);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- scale-factor copies + MMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      const TileCoord c = coord(t);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      const int kb0 = c.ks * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+      if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, limit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sf_t = tmem_base + uint32_t(Cfg::kSfCol0 + stage * Cfg::kSfCols);
+        tc_cp_sf(sf_t, make_sf_desc(smem_u32(sSfa + stage * Cfg::kSfaBytes)));
+#pragma unroll
+        for (int j = 0; j < BN / 128; ++j)
+          tc_cp_sf(sf_t + 4 + 4 * j,
+                   make_sf_desc(smem_u32(sSfb + stage * Cfg::kSfbBytes + 512 * j)));
+        const uint32_t idesc = idesc_sf_ids(IDESC, uint32_t(kb & 3));
+        const uint32_t a0 = smem_u32(sA + stage * kABytes);
+        const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_mx(d_tmem, make_sw128_desc(a0 + kk * 32), make_sw128_desc(b0 + kk * 32),
+                    idesc, sf_t, sf_t + 4, (kb > kb0 || kk > 0) ? 1u : 0u);
+        tc_commit(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      tc_commit(&tfull[acc]);
+      if (++acc == NACC) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    tc_commit(final_bar);
+    volatile int no_abort = 0;
+    mbar_wait_bounded(final_bar, 0, &no_abort, limit);
+  } else if (warp >= 2) {
+    // ---------------- epilogue (8 warps), as in moe_grouped_gemm_kernel ----------------
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileCoord c = coord(t);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, limit);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int m = c.mb * BM + row;
+      const int r = __ldg(p.sorted_ids + m);
+      const bool valid = r < p.numel;
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+      if constexpr (EPI == kEpiSwiGLU) {
+        constexpr int G_HALF = BN / 64;
+        constexpr int GPI = G_HALF >= 2 ? 2 : 1;
+        TOUT* out_row = static_cast<TOUT*>(p.out) + int64_t(m) * p.out_ld + c.nt * (BN / 2);
+#pragma unroll 1
+        for (int gg = 0; gg < G_HALF; gg += GPI) {
+          uint32_t gv[GPI][16], uv[GPI][16];
+#pragma unroll
+          for (int u = 0; u < GPI; ++u) {
+            const int g = h * G_HALF + gg + u;
+            tmem_ld16(tbase + g * 32, gv[u]);
+            tmem_ld16(tbase + g * 32 + 16, uv[u]);
+          }
+          tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int u = 0; u < GPI; ++u) {
+              const int g = h * G_HALF + gg + u;
+              uint32_t packed[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                packed[j] = pack2<TOUT>(
+                    silu_mul(__uint_as_float(gv[u][2 * j]), __uint_as_float(uv[u][2 * j])),
+                    silu_mul(__uint_as_float(gv[u][2 * j + 1]),
+                             __uint_as_float(uv[u][2 * j + 1])));
+              uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
+              dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+              dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            }
+          }
+        }
+      } else {
+        constexpr int C_HALF = BN / 32;
+        constexpr int CPI = C_HALF >= 4 ? 4 : C_HALF;
+        const float w = valid ? load_weight(p.row_weights, p.row_weights_dtype, r) : 0.0f;
+        TOUT* out_row = static_cast<TOUT*>(p.out) +
+                        (int64_t(c.ks) * p.numel + (valid ? r : 0)) * p.out_ld + c.nt * BN;
+#pragma unroll 1
+        for (int cc = 0; cc < C_HALF; cc += CPI) {
+          uint32_t v[CPI][16];
+#pragma unroll
+          for (int u = 0; u < CPI; ++u) tmem_ld16(tbase + (h * C_HALF + cc + u) * 16, v[u]);
+          tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int u = 0; u < CPI; ++u) {
+              const int g = h * C_HALF + cc + u;
+              float x[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(v[u][j]) * w;
+              if constexpr (std::is_same<TOUT, float>::value) {
+                float4* dst = reinterpret_cast<float4*>(out_row + g * 16);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  dst[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+              } else {
+                uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+                  dst[j] = make_uint4(pack2<TOUT>(x[8 * j], x[8 * j + 1]),
+                                      pack2<TOUT>(x[8 * j + 2], x[8 * j + 3]),
+                                      pack2<TOUT>(x[8 * j + 4], x[8 * j + 5]),
+                                      pack2<TOUT>(x[8 * j + 6], x[8 * j + 7]));
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == NACC) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+  if (threadIdx.x == 0 && *abort_flag) report_status(p.status, MOE_ERR_TIMEOUT);
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -976,6 +1319,28 @@ int dispatch_fp8(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const KPa
   }
 }
 
+template <int BN, int EPI, typename TOUT>
+int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+              cudaStream_t s) {
+  using Cfg = MxCfg<BN>;
+  auto kern = moe_grouped_gemm_mx_kernel<BN, EPI, TOUT>;
+  static std::atomic<uint64_t> smem_set{0};
+  int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
+  if (st != MOE_OK) return st;
+  KSW_LAUNCH(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, s, ta, tb, kp);
+  return MOE_OK;
+}
+
+template <int EPI, typename TOUT>
+int dispatch_mx(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
+                int grid, cudaStream_t s) {
+  switch (bn) {
+    case 256: return launch_mx<256, EPI, TOUT>(ta, tb, kp, grid, s);
+    case 128: return launch_mx<128, EPI, TOUT>(ta, tb, kp, grid, s);
+    default: return fail(MOE_ERR_UNSUPPORTED, "fp8 ue8m0 GEMM: block_n must be 128 or 256");
+  }
+}
+
 template <int KIND, int AB_FMT, int EPI, typename TOUT>
 int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
                 const KParams& kp, int grid, cudaStream_t s) {
@@ -1031,7 +1396,8 @@ int operand_types(const GroupedGemmArgs& a, OperandTypes* ot) {
     ot->elem_bytes = 2;
     return MOE_OK;
   }
-  if (a.quant == MOE_QUANT_INT8_CHANNEL || a.quant == MOE_QUANT_FP8_BLOCK) {
+  if (a.quant == MOE_QUANT_INT8_CHANNEL || a.quant == MOE_QUANT_FP8_BLOCK ||
+      a.quant == MOE_QUANT_FP8_UE8M0) {
     KSW_REQUIRE(a.a_scale && a.b_scale, MOE_ERR_INVALID_ARG,
                 "W8A8 GEMM needs activation and weight scales");
     ot->tma_type = CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -1101,10 +1467,14 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   if (st != MOE_OK) return st;
   KSW_REQUIRE((a.k * ot.elem_bytes) % 16 == 0, MOE_ERR_UNSUPPORTED,
               "gate-up GEMM: hidden size * element size must be a multiple of 16 B");
-  const bool fp8 = a.quant == MOE_QUANT_FP8_BLOCK;
+  const bool mx = a.quant == MOE_QUANT_FP8_UE8M0;
+  const bool fp8 = a.quant == MOE_QUANT_FP8_BLOCK || mx;
   if (fp8)
     KSW_REQUIRE(a.n % 256 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 gate-up GEMM: I must be a multiple of 128");
+  if (mx)
+    KSW_REQUIRE(a.k % 128 == 0, MOE_ERR_UNSUPPORTED,
+                "fp8 ue8m0 gate-up GEMM: the hidden size must be a multiple of 128");
   const int bn = a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), 1, sms, !fp8);
   KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED,
               "gate-up GEMM: 2*I must be a multiple of 64");
@@ -1114,6 +1484,7 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   KParams kp = base_params(a, ot.elem_bytes);
   kp.out_ld = a.n / 2;
   const int grid = sms;
+  if (mx) return dispatch_mx<kEpiSwiGLU, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
   if (fp8) return dispatch_fp8<kEpiSwiGLU>(bn, ta, tb, kp, grid, s);
   if (a.quant == MOE_QUANT_INT8_CHANNEL) {
     // int8 products dequantise to bf16 activations
@@ -1161,11 +1532,15 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   KSW_REQUIRE(kp.splits == a.splits, MOE_ERR_INVALID_ARG,
               "down GEMM: splits leaves an empty K range; choose splits so that every split has k-blocks");
   const bool fp8 = a.quant == MOE_QUANT_FP8_BLOCK;
-  if (fp8)
+  const bool mx = a.quant == MOE_QUANT_FP8_UE8M0;
+  if (fp8 || mx)
     KSW_REQUIRE(a.n % 128 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 down GEMM: hidden size must be a multiple of 128");
-  const int bn =
-      a.block_n ? a.block_n : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms, !fp8);
+  if (mx)
+    KSW_REQUIRE(a.k % 128 == 0, MOE_ERR_UNSUPPORTED,
+                "fp8 ue8m0 down GEMM: the intermediate size must be a multiple of 128");
+  const int bn = a.block_n ? a.block_n
+                           : pick_block_n(a.n, est_m_blocks(a), kp.splits, sms, !(fp8 || mx));
   KSW_REQUIRE(bn > 0 && a.n % bn == 0, MOE_ERR_UNSUPPORTED, "down GEMM: bad block_n");
   CUtensorMap ta, tb;
   st = make_maps(a, ot, bn, &ta, &tb);
@@ -1178,6 +1553,12 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
               MOE_ERR_UNSUPPORTED,
               "down GEMM: 16-bit rows only without K split and without fp8");
   if (fp8) return dispatch_fp8<kEpiRows>(bn, ta, tb, kp, grid, s);
+  if (mx) {
+    if (a.out_dtype == MOE_DTYPE_BF16)
+      return dispatch_mx<kEpiRows, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
+    if (a.out_dtype == MOE_DTYPE_F32) return dispatch_mx<kEpiRows, float>(bn, ta, tb, kp, grid, s);
+    return fail(MOE_ERR_UNSUPPORTED, "down GEMM: fp8 ue8m0 rows are f32 or bf16");
+  }
   if (a.out_dtype == MOE_DTYPE_BF16) {
     if (a.quant == MOE_QUANT_INT8_CHANNEL)
       return dispatch_bn<kKindI8, 1, kEpiRows, __nv_bfloat16>(bn, ta, tb, kp, grid, s);

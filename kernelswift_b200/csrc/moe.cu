@@ -135,7 +135,7 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
     P.a_dtype = MOE_DTYPE_I8;
     P.act_dtype = MOE_DTYPE_BF16;
     kbpe = 1;
-  } else if (P.quant == MOE_QUANT_FP8_BLOCK) {
+  } else if (P.quant == MOE_QUANT_FP8_BLOCK || P.quant == MOE_QUANT_FP8_UE8M0) {
     KSW_REQUIRE(P.I % 128 == 0 && P.H % 128 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 block-scaled path needs hidden and intermediate sizes divisible by 128");
     P.a_dtype = MOE_DTYPE_E4M3;
@@ -146,12 +146,14 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   }
   const int64_t est_mb = est_m_blocks(P.numel, P.L, P.E);
   const bool fp8 = P.quant == MOE_QUANT_FP8_BLOCK;
+  const bool mx = P.quant == MOE_QUANT_FP8_UE8M0;
   const int max_bn = 256;
-  const Tiling dn = choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !fp8, max_bn);
+  const Tiling dn =
+      choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !(fp8 || mx), max_bn);
   // the split gate-up path has no fp8 epilogue (its block scales follow the
   // regrouped gate/up rows); fp8 keeps the fused SiLU*up epilogue
-  const Tiling gu =
-      choose_tiling(est_mb, P.numel, 2 * P.I, P.H * kbpe, sms, !fp8, !fp8, max_bn);
+  const Tiling gu = choose_tiling(est_mb, P.numel, 2 * P.I, P.H * kbpe, sms, !(fp8 || mx),
+                                  !(fp8 || mx), max_bn);
   KSW_REQUIRE(dn.bn > 0 && gu.bn > 0, MOE_ERR_UNSUPPORTED,
               "hidden size and 2*intermediate size must be multiples of 64 (128 for fp8)");
   P.splits = dn.splits;
@@ -178,10 +180,12 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.off_npp = take(4);
   P.off_align = take(P.align_ws);
   P.off_a = take(size_t(P.L) * P.H * elem_bytes(P.a_dtype));
-  // per-row scales: int8 one per row, fp8 one per row per 128 columns
+  // per-row scales: int8 one per row, fp8 one per row per 128 columns (fp32,
+  // or one byte in the scale-factor image for UE8M0)
   auto scale_bytes = [&](int64_t cols) -> size_t {
     if (P.quant == MOE_QUANT_INT8_CHANNEL) return size_t(P.L) * 4;
     if (P.quant == MOE_QUANT_FP8_BLOCK) return size_t(P.L) * size_t(ceil_div(cols, 128)) * 4;
+    if (P.quant == MOE_QUANT_FP8_UE8M0) return size_t(moe_ue8m0_scale_bytes(1, P.L, cols));
     return 0;
   };
   P.off_a_scale = take(scale_bytes(P.H));

@@ -11,6 +11,11 @@
 //              q = e4m3_rn(clamp(x / scale, -448, 448))
 //   int8 channel: per row, scale = absmax / 127 (1 if zero),
 //              q = rint(clamp(x / scale, -127, 127))
+//   fp8 UE8M0: per 128x128 block of the ORIGINAL layout, scale = the
+//              smallest power of two with absmax / scale <= 448 (1 if the
+//              block is zero), q = e4m3_rn(x / scale) (exact scaling); the
+//              scale byte is written into the scale-factor image at every
+//              row of the block (its regrouped row for w13)
 #include "common.cuh"
 
 namespace ksw {
@@ -93,6 +98,52 @@ __global__ void __launch_bounds__(256)
   if (t == 0) scale[(e * RB + rb) * CB + cb] = sc;
 }
 
+// fp8 block quantisation with power-of-two scales: one CTA of 256 threads per
+// 128x128 block (R and C multiples of 128); the block's scale byte goes into
+// the scale-factor image at each of its 128 rows.
+template <typename Tin>
+__global__ void __launch_bounds__(256)
+    prep_ue8m0_kernel(const Tin* __restrict__ src, int64_t E, int64_t R, int64_t C,
+                      int64_t I, bool regroup, uint8_t* __restrict__ dst,
+                      uint8_t* __restrict__ sf, int64_t q_blocks) {
+  __shared__ float red[8];
+  const int64_t RB = R / 128, CB = C / 128;
+  const int64_t blk = blockIdx.x;
+  const int64_t e = blk / (RB * CB);
+  const int64_t rb = (blk / CB) % RB;
+  const int64_t cb = blk % CB;
+  const int t = threadIdx.x;
+  const int r_in = t >> 4;          // 0..15
+  const int c_in = (t & 15) * 8;    // 0..120
+  float amax = 0.0f;
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = rb * 128 + r_in + 16 * i;
+    for (int j = 0; j < 8; ++j)
+      amax = fmaxf(amax, fabsf(ld(src + (e * R + r) * C + cb * 128 + c_in + j)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((t & 31) == 0) red[t >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+  for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
+  const uint32_t b = ue8m0_byte(amax);
+  const float inv = ue8m0_inv_scale(b);
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = rb * 128 + r_in + 16 * i;
+    uint8_t* d = dst + (e * R + map_row(r, I, regroup)) * C;
+    for (int j = 0; j < 8; ++j) {
+      const int64_t c = cb * 128 + c_in + j;
+      const float q = fminf(fmaxf(ld(src + (e * R + r) * C + c) * inv, -448.0f), 448.0f);
+      d[c] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3));
+    }
+  }
+  if (t < 128) {
+    const int64_t rr = map_row(rb * 128 + t, I, regroup);
+    sf[sf_image_offset(e, rr, cb, q_blocks, RB)] = static_cast<uint8_t>(b);
+  }
+}
+
 // int8 per-row quantisation: one warp per source row; the scale follows the
 // row to its regrouped position.
 template <typename Tin>
@@ -163,6 +214,17 @@ int prep_typed(const Tin* src, int64_t E, int64_t R, int64_t C, int64_t I,
     KSW_REQUIRE(nblk < (int64_t(1) << 31), MOE_ERR_UNSUPPORTED, "prepare: too many blocks");
     prep_fp8_kernel<Tin><<<unsigned(nblk), 256, 0, s>>>(
         src, E, R, C, I, regroup, static_cast<uint8_t*>(dst), scale);
+  } else if (quant == MOE_QUANT_FP8_UE8M0) {
+    KSW_REQUIRE(dst_dtype == MOE_DTYPE_E4M3 && scale, MOE_ERR_INVALID_ARG,
+                "prepare: fp8 ue8m0 needs an e4m3 destination and a scale-factor image");
+    KSW_REQUIRE(R % 128 == 0 && C % 128 == 0 && (!regroup || I % 128 == 0),
+                MOE_ERR_UNSUPPORTED,
+                "prepare: fp8 ue8m0 needs rows and columns (and I) divisible by 128");
+    const int64_t nblk = E * (R / 128) * (C / 128);
+    KSW_REQUIRE(nblk < (int64_t(1) << 31), MOE_ERR_UNSUPPORTED, "prepare: too many blocks");
+    prep_ue8m0_kernel<Tin><<<unsigned(nblk), 256, 0, s>>>(
+        src, E, R, C, I, regroup, static_cast<uint8_t*>(dst), reinterpret_cast<uint8_t*>(scale),
+        ceil_div(C / 128, 4));
   } else if (quant == MOE_QUANT_INT8_CHANNEL) {
     KSW_REQUIRE(dst_dtype == MOE_DTYPE_I8 && scale, MOE_ERR_INVALID_ARG,
                 "prepare: int8 needs an int8 destination and a scale buffer");
@@ -215,6 +277,11 @@ int prepare(const void* src, int src_dtype, const float* scale_in, int64_t E,
 }  // namespace ksw
 
 extern "C" {
+
+int64_t moe_ue8m0_scale_bytes(int64_t groups, int64_t rows, int64_t cols) {
+  if (groups < 0 || rows < 0 || cols < 0) return -1;
+  return groups * ksw::ceil_div(ksw::ceil_div(cols, 128), 4) * ksw::ceil_div(rows, 128) * 512;
+}
 
 int moe_prepare_w13(const void* w1, int src_dtype, const float* scale_in,
                     int64_t num_experts, int64_t inter_size, int64_t hidden_size,

@@ -2,7 +2,8 @@
 //   gather_rows: A[m] = hidden[sorted_ids[m] / top_k] in expert-sorted order
 //                (the replicate + boolean gather of base.py:52-58,68), with
 //                an optional cast (f32 -> bf16) or quantisation (e4m3 per
-//                128-column group, int8 per row).
+//                128-column group with an fp32 or a power-of-two scale, int8
+//                per row).
 //   quant_rows:  the same quantisations for the gate-up output (the second
 //                GEMM's operand).
 //   sum_topk:    out[t] = sum_s sum_j part[s, t*k + j] (the top-k reduction of
@@ -202,6 +203,58 @@ __global__ void __launch_bounds__(kWarps * 32)
         const float inv = 1.0f / sc;
         if (in) *reinterpret_cast<uint2*>(dst + m * H + h) = pack_e4m3x8(v[u], inv);
         if (in && (lane & 15) == 0) scale[m * groups + g] = sc;
+      }
+    }
+  }
+}
+
+// ---------------- gather + e4m3 with UE8M0 scales per (row, 128 columns) ---
+// The gather_fp8_kernel scheme with a power-of-two scale per group (H % 128
+// == 0): the scale byte goes into the scale-factor image of the operand rows
+// (row_slices = max_rows / 128 chunks per 4 column groups).
+template <typename Tin>
+__global__ void __launch_bounds__(kWarps * 32)
+    gather_ue8m0_kernel(const Tin* __restrict__ src, int64_t H, int top_k,
+                        const int32_t* __restrict__ sorted,
+                        const int32_t* __restrict__ num_post_pad, int64_t max_rows,
+                        int64_t numel, int64_t src_rows, uint8_t* __restrict__ dst,
+                        uint8_t* __restrict__ sf, int64_t q_blocks, int64_t row_slices) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = min(int64_t(__ldg(num_post_pad)), max_rows);
+  const int64_t groups = H / 128;
+  for (int64_t m = int64_t(blockIdx.x) * kWarps + warp; m < rows;
+       m += int64_t(gridDim.x) * kWarps) {
+    const int64_t sr = sorted ? source_row(sorted, m, numel, top_k) : m;
+    if (sr < 0 || sr >= src_rows) continue;
+    const Tin* s = src + sr * H;
+    for (int64_t gb = 0; gb < groups; gb += 2 * kBatch) {
+      float v[kBatch][8];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t g = gb + 2 * u + (lane >> 4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+        if (g < groups) load8(s + g * 128 + (lane & 15) * 8, v[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t g = gb + 2 * u + (lane >> 4);
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1)
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const uint32_t b = ue8m0_byte(amax);
+        const float inv = ue8m0_inv_scale(b);
+        if (g < groups) {
+          *reinterpret_cast<uint2*>(dst + m * H + g * 128 + (lane & 15) * 8) =
+              pack_e4m3x8(v[u], inv);
+          if ((lane & 15) == 0)
+            sf[sf_image_offset(0, m, g, q_blocks, row_slices)] = static_cast<uint8_t>(b);
+        }
       }
     }
   }
@@ -461,6 +514,27 @@ int gather_launch(const GatherArgs& a, cudaStream_t s) {
       KSW_LAUNCH(gather_fp8_kernel<__half>, dim3(grid), dim3(block), 0, s,
           static_cast<const __half*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<uint8_t*>(a.dst), a.scale);
+    else
+      return fail(MOE_ERR_UNSUPPORTED, "gather: unsupported source dtype");
+  } else if (a.quant == MOE_QUANT_FP8_UE8M0) {
+    KSW_REQUIRE(a.scale != nullptr, MOE_ERR_INVALID_ARG, "gather: null scale-factor image");
+    KSW_REQUIRE(a.H % 128 == 0 && a.max_rows % 128 == 0, MOE_ERR_UNSUPPORTED,
+                "gather: fp8 ue8m0 needs H and the buffer length divisible by 128");
+    uint8_t* sf = reinterpret_cast<uint8_t*>(a.scale);
+    const int64_t qb = ceil_div(a.H / 128, 4), rs = a.max_rows / 128;
+    if (a.src_dtype == MOE_DTYPE_F32)
+      KSW_LAUNCH(gather_ue8m0_kernel<float>, dim3(grid), dim3(block), 0, s,
+          static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<uint8_t*>(a.dst), sf, qb, rs);
+    else if (a.src_dtype == MOE_DTYPE_BF16)
+      KSW_LAUNCH(gather_ue8m0_kernel<__nv_bfloat16>, dim3(grid), dim3(block), 0, s,
+          static_cast<const __nv_bfloat16*>(a.src), a.H, a.top_k, a.sorted,
+          a.num_post_pad, a.max_rows, a.numel, a.src_rows,
+          static_cast<uint8_t*>(a.dst), sf, qb, rs);
+    else if (a.src_dtype == MOE_DTYPE_F16)
+      KSW_LAUNCH(gather_ue8m0_kernel<__half>, dim3(grid), dim3(block), 0, s,
+          static_cast<const __half*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<uint8_t*>(a.dst), sf, qb, rs);
     else
       return fail(MOE_ERR_UNSUPPORTED, "gather: unsupported source dtype");
   } else if (a.quant == MOE_QUANT_INT8_CHANNEL) {

@@ -21,7 +21,8 @@ struct GatherArgs {
   int quant;                    // moe_quant_t
   void* dst;                    // [max_rows, H] dst_dtype / e4m3 / int8
   int dst_dtype;                // for QUANT_NONE: F16 or BF16
-  float* scale;                 // FP8: [max_rows, ceil(H/128)], INT8: [max_rows]
+  float* scale;                 // FP8: [max_rows, ceil(H/128)], INT8: [max_rows],
+                                // FP8_UE8M0: the rows' scale-factor image (bytes)
 };
 
 struct SumArgs {

@@ -88,7 +88,7 @@ class CudaBackend:
                 stage_events=None) -> torch.Tensor:
         ones = torch.ones(rows.shape[0], 1, dtype=torch.float32, device=rows.device)
         return fm.fused_experts(rows, self.prep, None, ones, local_ids.view(-1, 1),
-                                use_fp8_w8a8=self.quant == "fp8",
+                                use_fp8_w8a8=self.quant.startswith("fp8"),
                                 use_int8_w8a8=self.quant == "int8", stage_events=stage_events)
 
     def combine(self, rows: torch.Tensor, inv: torch.Tensor, weights: torch.Tensor,
@@ -303,7 +303,7 @@ class ExpertParallelMoE:
         _lib.call("moe_ep_peer_dispatch", px.handle, fm._ptr(hidden), T, k, fm._ptr(order),
                   fm._ptr(send_eid), fm._ptr(counts), fm._ptr(px.status), stream)
         fm.fused_experts(px.recv_rows, self.backend.prep, None, px.ones, px.recv_ids.view(-1, 1),
-                         use_fp8_w8a8=self.quant == "fp8", use_int8_w8a8=self.quant == "int8",
+                         use_fp8_w8a8=self.quant.startswith("fp8"), use_int8_w8a8=self.quant == "int8",
                          out=px.result_rows, status=px.status, stage_events=stage_events,
                          rows_only=True)
         out = torch.empty(T, H, dtype=hidden.dtype, device=dev)

@@ -37,7 +37,8 @@ _DTYPE_CODE = {
     torch.int64: _lib.DT_I64,
 }
 
-_QUANT = {"none": _lib.QUANT_NONE, "fp8": _lib.QUANT_FP8_BLOCK, "int8": _lib.QUANT_INT8_CHANNEL}
+_QUANT = {"none": _lib.QUANT_NONE, "fp8": _lib.QUANT_FP8_BLOCK, "int8": _lib.QUANT_INT8_CHANNEL,
+          "fp8-ue8m0": _lib.QUANT_FP8_UE8M0}
 
 
 def _code(t: torch.Tensor) -> int:
@@ -196,7 +197,8 @@ class PreparedWeights:
     w2: torch.Tensor                # [E, H, I]
     w13_scale: torch.Tensor | None  # fp8: [E, 2I/128, H/128]; int8: [E, 2I]
     w2_scale: torch.Tensor | None   # fp8: [E, H/128, I/128];  int8: [E, H]
-    quant: str                      # "none" | "fp8" | "int8"
+    #                                 fp8-ue8m0: uint8 scale-factor images
+    quant: str                      # "none" | "fp8" | "int8" | "fp8-ue8m0"
     num_experts: int
     inter_size: int
     hidden_size: int
@@ -215,7 +217,10 @@ def prepare_weights(w1: torch.Tensor, w2: torch.Tensor, quant: str = "none",
     quant "none": cast to `compute_dtype` (bf16 or f16). quant "fp8": e4m3
     with one fp32 scale per 128x128 block (absmax / 448), or pass-through of
     already-e4m3 weights with `w1_scale`/`w2_scale`. quant "int8": int8 with
-    one scale per output row (absmax / 127).
+    one scale per output row (absmax / 127). quant "fp8-ue8m0": e4m3 with one
+    power-of-two scale per 128x128 block (the smallest with absmax / scale <=
+    448), kept as the scale-factor images the tensor core reads
+    (moe_ue8m0_scale_bytes layout); needs H and I divisible by 128.
     """
     _check_cuda("w1", w1)
     _check_cuda("w2", w2)
@@ -239,6 +244,15 @@ def prepare_weights(w1: torch.Tensor, w2: torch.Tensor, quant: str = "none",
         dst_dtype = torch.float8_e4m3fn
         s13 = torch.empty(E, -(-two_i // 128), -(-H // 128), dtype=torch.float32, device=dev)
         s2 = torch.empty(E, -(-H // 128), -(-inter // 128), dtype=torch.float32, device=dev)
+    elif quant == "fp8-ue8m0":
+        if H % 128 or inter % 128:
+            raise ValueError("fp8-ue8m0 needs hidden and intermediate sizes divisible by 128")
+        if w1c.dtype == torch.float8_e4m3fn:
+            raise ValueError("fp8-ue8m0 quantises f32/f16/bf16 weights itself")
+        dst_dtype = torch.float8_e4m3fn
+        lib = _lib.load()
+        s13 = torch.empty(lib.moe_ue8m0_scale_bytes(E, two_i, H), dtype=torch.uint8, device=dev)
+        s2 = torch.empty(lib.moe_ue8m0_scale_bytes(E, H, inter), dtype=torch.uint8, device=dev)
     else:
         dst_dtype = torch.int8
         s13 = torch.empty(E, two_i, dtype=torch.float32, device=dev)
@@ -248,6 +262,7 @@ def prepare_weights(w1: torch.Tensor, w2: torch.Tensor, quant: str = "none",
     o13 = torch.empty(E, two_i, H, dtype=dst_dtype, device=dev)
     o2 = torch.empty(E, H, inter, dtype=dst_dtype, device=dev)
     st = _stream(dev)
+    # the library takes every scale buffer as float* (UE8M0 images are bytes)
     sc1 = _contig(w1_scale.float()) if w1_scale is not None else None
     sc2 = _contig(w2_scale.float()) if w2_scale is not None else None
     _lib.call("moe_prepare_w13", _ptr(w1c), _code(w1c), _ptr(sc1), E, inter, H, q, _ptr(o13),
@@ -348,8 +363,12 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
                   a2_scale: torch.Tensor | None = None, block_shape: list[int] | None = None,
                   out: torch.Tensor | None = None, status: torch.Tensor | None = None,
                   stage_events: ctypes.Array | None = None,
-                  rows_only: bool = False) -> torch.Tensor:
+                  rows_only: bool = False, scale_format: str = "fp32") -> torch.Tensor:
     """out[t] = sum_j w[t,j] * W2[e] (silu(W1g[e] x_t) * W1u[e] x_t), e = ids[t,j].
+
+    scale_format (fp8 only): "fp32" (absmax / 448 block scales, promoted per
+    k-block) or "ue8m0" (power-of-two block scales applied by the tensor
+    core; weights prepared with quant "fp8-ue8m0").
 
     rows_only (top_k == 1): rows of tokens whose expert id is dropped are left
     unspecified instead of zeroed, which lets the down GEMM write the result
@@ -377,10 +396,16 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
         raise ValueError("expected hidden_states [T, H], topk_weights/topk_ids [T, k]")
     if topk_ids.shape[0] != hidden_states.shape[0]:
         raise ValueError("topk_ids and hidden_states disagree on the token count")
+    if scale_format not in ("fp32", "ue8m0"):
+        raise ValueError("scale_format must be 'fp32' or 'ue8m0'")
     quant = "fp8" if use_fp8_w8a8 else ("int8" if use_int8_w8a8 else "none")
+    if quant == "fp8" and scale_format == "ue8m0":
+        quant = "fp8-ue8m0"
     compute = torch.float16 if hidden_states.dtype == torch.float16 else torch.bfloat16
     if isinstance(w1, PreparedWeights):
         prep = w1
+        if quant == "fp8" and prep.quant == "fp8-ue8m0":
+            quant = prep.quant  # prepared fp8 weights carry their scale format
         if prep.quant != quant:
             raise ValueError(f"prepared weights are {prep.quant!r}, call asked for {quant!r}")
         if quant == "none" and prep.compute_dtype != compute:
