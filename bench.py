@@ -81,9 +81,10 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (0 = workload default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--ep-exchange", choices=("auto", "nccl", "peer"), default="auto",
+    ap.add_argument("--ep-exchange", choices=("auto", "nccl", "nccl-dedup", "peer"),
+                    default="auto",
                     help="expert-parallel row exchange for --gpus > 1 (auto: NVLink peer "
-                         "memory)")
+                         "memory; nccl-dedup: all_to_all sending a token to a rank once)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every step eagerly instead of replaying a CUDA graph of the "
                          "whole forward (1 GPU runs use the graph by default)")
@@ -245,7 +246,9 @@ def workload_config(name, H, I, E, k, quant, T, n, exchange=None):
             "tokens_per_gpu": T, "global_tokens": T * n,
             "parallelism": (f"ep{n} (E/{n} experts per GPU, " + (
                 "token rows exchanged by dispatch/combine kernels over NVLink peer memory)"
-                if exchange == "peer" else "NCCL all_to_all)")) if n > 1 else "single",
+                if exchange == "peer" else
+                "NCCL all_to_all, one row per token and destination rank)"
+                if exchange == "nccl-dedup" else "NCCL all_to_all)")) if n > 1 else "single",
             "l2": f"flushed between steps outside the timed windows ({L2_FLUSH_BYTES >> 20} MB "
                   f"write{', then a read of another ' + str(L2_FLUSH_BYTES >> 20) + ' MB that evicts the dirty lines' if L2Flush.evict else ''}); "
                   "weights also exceed L2"}
@@ -302,8 +305,8 @@ def main():
         def step(stage_arr=None):
             tw, ti = fm.fused_topk(hidden, logits, k, weights_dtype=hidden.dtype)
             return fm.fused_experts(hidden, prep, None, tw, ti,
-                                    use_fp8_w8a8=quant.startswith("fp8"), use_int8_w8a8=quant == "int8",
-                                    stage_events=stage_arr)
+                                    use_fp8_w8a8=quant.startswith("fp8"),
+                                    use_int8_w8a8=quant == "int8", stage_events=stage_arr)
     else:
         # expert parallel: this rank holds E/world experts, routes its own T
         # tokens over all E; rows move through the peer-memory dispatch and
@@ -316,8 +319,10 @@ def main():
         w1 = torch.randn(el, 2 * I, H, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(H)
         w2 = torch.randn(el, H, I, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(I)
         def make_ep(exchange):
-            return ExpertParallelMoE(w1, w2, E, k, quant=quant, exchange=exchange,
-                                     max_tokens=T, dtype=hidden.dtype)
+            dedup = exchange == "nccl-dedup"
+            return ExpertParallelMoE(w1, w2, E, k, quant=quant,
+                                     exchange="nccl" if dedup else exchange,
+                                     max_tokens=T, dtype=hidden.dtype, dedup=dedup)
 
         try:
             ep = make_ep(args.ep_exchange)
@@ -408,7 +413,8 @@ def main():
         # record nodes) for the per-kernel breakdown.
         def graph_fn(hd, ld, stage_arr=None):
             tw, ti = fm.fused_topk(hd, ld, k, weights_dtype=hd.dtype)
-            return fm.fused_experts(hd, prep, None, tw, ti, use_fp8_w8a8=quant.startswith("fp8"),
+            return fm.fused_experts(hd, prep, None, tw, ti,
+                                    use_fp8_w8a8=quant.startswith("fp8"),
                                     use_int8_w8a8=quant == "int8", stage_events=stage_arr)
 
         graph = fm.CapturedMoE(graph_fn, T, H, E, dtype=torch.bfloat16, device=dev)
@@ -565,6 +571,8 @@ def main():
         n_ids = T * k
     elif ep.peer is not None:
         n_ids = ep.peer.capacity  # align runs over the whole receive buffer
+    elif ep.dedup:
+        n_ids = ep.last_rows_received * k  # k slots per received token row
     else:
         n_ids = int(rows_per_launch[0])
     e_al = E if world == 1 else E // world
@@ -578,6 +586,11 @@ def main():
     # launches for this shape (the plan's own count), plus the exchange
     if world == 1:
         launches_per_step = 1 + fm.fused_experts_launches(T, H, I, E, k, quant)
+    elif ep.dedup:
+        # pack, expert pass over the received token rows (top_k = k),
+        # combine (the plan is torch ops)
+        launches_per_step = 1 + 1 + fm.fused_experts_launches(
+            ep.last_rows_received, H, I, E // world, k, quant) + 1
     elif ep.peer is None:
         # plan, pack, expert pass over the received rows (top_k = 1), combine
         launches_per_step = 1 + 2 + fm.fused_experts_launches(
@@ -595,7 +608,8 @@ def main():
             "dtype": "bf16" if quant == "none" else ("int8" if quant == "int8" else "e4m3"),
             "data": "synthetic",
             "config": workload_config(args.workload, H, I, E, k, quant, T, world,
-                                      None if world == 1 else ep.exchange),
+                                      None if world == 1 else
+                                      ("nccl-dedup" if ep.dedup else ep.exchange)),
             "tflops": tflops,
             "stage_ms": stage_ms,
             "align": align_report,

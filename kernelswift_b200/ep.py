@@ -28,6 +28,16 @@ object;
 `CudaBackend` runs the library's kernels and is the only backend this package
 provides.
 
+With dedup=True (NCCL exchange) a token is sent to a rank once, however
+many of its k slots that rank holds (top-8 of 256 experts over 8 ranks
+reaches about 5.3 ranks per token, so a third of the rows stay home): the
+send row carries the token's local expert ids on that rank (-1 for slots
+elsewhere) and their weights, the receiver runs moe_fused_experts with top_k
+= k (slots marked -1 are dropped) and returns one weighted, summed row per
+(token, rank), and the source adds the rows of the ranks it used
+(moe_combine_rows with unit weights). The plan is plain torch
+(`dedup_plan`).
+
 With exchange="peer" (ranks on one node, 2-8 GPUs) steps 2-4 and 6 are
 replaced by two kernels that move the rows themselves over NVLink
 (`PeerExchange`, the moe_ep_peer_* entry points): dispatch stores each row
@@ -48,6 +58,43 @@ import torch.distributed as dist
 
 from . import _lib
 from . import fused_moe as fm
+
+
+def dedup_plan(topk_ids: torch.Tensor, topk_weights: torch.Tensor, num_experts: int,
+               world: int):
+    """Send plan with one row per (token, destination rank) holding any of
+    the token's slots (dedup=True). Returns
+
+      tokens   int32 [n]      source token of send row p, rows grouped by
+                              destination rank (ascending), tokens ascending
+                              inside a rank
+      send_eid int32 [n, k]   the token's expert ids local to that rank, -1 for
+                              slots held elsewhere
+      send_w   f32   [n, k]   their weights (0 for slots held elsewhere)
+      inv      int32 [T, world] send row of (token, rank), -1 if none
+      counts   int64 [world + 1] rows per rank; counts[world] = tokens with an
+                              expert id outside [0, num_experts)
+
+    Plain torch ops, so the same code runs on the GPU and in CPU tests."""
+    T, k = topk_ids.shape
+    dev = topk_ids.device
+    el = num_experts // world
+    ids = topk_ids.long()
+    valid = (ids >= 0) & (ids < num_experts)
+    dest = torch.where(valid, torch.div(ids, el, rounding_mode="floor"),
+                       torch.full_like(ids, world))
+    present = torch.zeros(world + 1, T, dtype=torch.bool, device=dev)
+    present.scatter_(0, dest.t().contiguous(), True)
+    counts = present.sum(1)
+    d_idx, t_idx = present[:world].nonzero(as_tuple=True)
+    sel = dest[t_idx] == d_idx.unsqueeze(1)
+    send_eid = torch.where(sel, ids[t_idx] - d_idx.unsqueeze(1) * el,
+                           torch.full_like(ids[t_idx], -1)).to(torch.int32)
+    send_w = torch.where(sel, topk_weights[t_idx].float(),
+                         torch.zeros(sel.shape, dtype=torch.float32, device=dev))
+    inv = torch.full((T, world), -1, dtype=torch.int32, device=dev)
+    inv[t_idx, d_idx] = torch.arange(t_idx.numel(), dtype=torch.int32, device=dev)
+    return t_idx.to(torch.int32), send_eid, send_w, inv, counts
 
 
 class CudaBackend:
@@ -88,6 +135,13 @@ class CudaBackend:
                 stage_events=None) -> torch.Tensor:
         ones = torch.ones(rows.shape[0], 1, dtype=torch.float32, device=rows.device)
         return fm.fused_experts(rows, self.prep, None, ones, local_ids.view(-1, 1),
+                                use_fp8_w8a8=self.quant.startswith("fp8"),
+                                use_int8_w8a8=self.quant == "int8", stage_events=stage_events)
+
+    def experts_weighted(self, rows: torch.Tensor, local_ids: torch.Tensor,
+                         weights: torch.Tensor, stage_events=None) -> torch.Tensor:
+        """sum_j weights[:, j] * expert_{local_ids[:, j]}(rows) (ids -1 dropped)."""
+        return fm.fused_experts(rows, self.prep, None, weights, local_ids,
                                 use_fp8_w8a8=self.quant.startswith("fp8"),
                                 use_int8_w8a8=self.quant == "int8", stage_events=stage_events)
 
@@ -212,12 +266,15 @@ class ExpertParallelMoE:
     def __init__(self, w1_local: torch.Tensor | None, w2_local: torch.Tensor | None,
                  num_experts: int, top_k: int, group=None, quant: str = "none",
                  backend=None, exchange: str = "auto", max_tokens: int | None = None,
-                 dtype: torch.dtype = torch.bfloat16, wait_limit_ms: int = 0):
+                 dtype: torch.dtype = torch.bfloat16, wait_limit_ms: int = 0,
+                 dedup: bool = False):
         """exchange: "nccl" (all_to_all), "peer" (NVLink peer memory, needs
         max_tokens: the most tokens a rank passes to one forward) or "auto"
-        (peer when max_tokens is given, the CUDA backend is used and the group
-        has 2-8 ranks on GPUs, else nccl). `dtype` is the row dtype of the
-        peer exchange (the hidden states' dtype)."""
+        (peer when max_tokens is given, the CUDA backend is used, the group
+        has 2-8 ranks on GPUs and dedup is off, else nccl). `dtype` is the row
+        dtype of the peer exchange (the hidden states' dtype). dedup: send a
+        token to a rank once however many of its slots the rank holds (NCCL
+        exchange only)."""
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -235,10 +292,14 @@ class ExpertParallelMoE:
         self.quant = quant
         if exchange == "auto":
             exchange = ("peer" if max_tokens is not None and isinstance(backend, CudaBackend)
-                        and 2 <= self.world <= _lib.EP_MAX_RANKS else "nccl")
+                        and 2 <= self.world <= _lib.EP_MAX_RANKS and not dedup else "nccl")
         if exchange not in ("nccl", "peer"):
             raise ValueError(f"unknown exchange {exchange!r}")
+        if dedup and exchange != "nccl":
+            raise ValueError("dedup is implemented for the nccl exchange")
         self.exchange = exchange
+        self.dedup = dedup
+        self._last_recv_eid = None
         self.peer = None
         self.max_tokens = max_tokens
         self.last_rows_received = 0
@@ -256,6 +317,8 @@ class ExpertParallelMoE:
         the local expert computation."""
         if self.peer is not None:
             return self._forward_peer(hidden, topk_weights, topk_ids, stage_events)
+        if self.dedup:
+            return self._forward_dedup(hidden, topk_weights, topk_ids, stage_events)
         T, H = hidden.shape
         k = topk_ids.shape[1]
         dev = hidden.device
@@ -288,6 +351,39 @@ class ExpertParallelMoE:
         dist.all_to_all_single(back, out_rows, send_split, recv_split, group=self.group)
         return self.backend.combine(back, inv, topk_weights, T, k)
 
+    def _forward_dedup(self, hidden, topk_weights, topk_ids, stage_events=None):
+        T, H = hidden.shape
+        k = topk_ids.shape[1]
+        dev = hidden.device
+        tokens, send_eid, send_w, inv, counts = dedup_plan(topk_ids, topk_weights,
+                                                           self.num_experts, self.world)
+        recv_counts = torch.empty(self.world, dtype=counts.dtype, device=dev)
+        dist.all_to_all_single(recv_counts, counts[:self.world].contiguous(), group=self.group)
+        both = torch.cat([counts, recv_counts]).cpu()  # the one host sync
+        if int(both[self.world]) != 0:
+            raise ValueError("expert ids out of range")
+        send_split = both[:self.world].tolist()
+        recv_split = both[self.world + 1:].tolist()
+        n_recv = sum(recv_split)
+        send_rows = self.backend.pack(hidden, tokens, 1)
+        recv_rows = torch.empty(n_recv, H, dtype=hidden.dtype, device=dev)
+        recv_eid = torch.empty(n_recv, k, dtype=torch.int32, device=dev)
+        recv_w = torch.empty(n_recv, k, dtype=torch.float32, device=dev)
+        dist.all_to_all_single(recv_rows, send_rows, recv_split, send_split, group=self.group)
+        dist.all_to_all_single(recv_eid, send_eid, recv_split, send_split, group=self.group)
+        dist.all_to_all_single(recv_w, send_w, recv_split, send_split, group=self.group)
+        self.last_rows_received = n_recv
+        self._last_recv_eid = recv_eid
+        if stage_events is not None:
+            out_rows = self.backend.experts_weighted(recv_rows, recv_eid, recv_w,
+                                                     stage_events=stage_events)
+        else:
+            out_rows = self.backend.experts_weighted(recv_rows, recv_eid, recv_w)
+        back = torch.empty(tokens.numel(), H, dtype=out_rows.dtype, device=dev)
+        dist.all_to_all_single(back, out_rows, send_split, recv_split, group=self.group)
+        ones = torch.ones(T, self.world, dtype=torch.float32, device=dev)
+        return self.backend.combine(back, inv.reshape(-1), ones, T, self.world)
+
     def _forward_peer(self, hidden, topk_weights, topk_ids, stage_events=None):
         px = self.peer
         T, H = hidden.shape
@@ -303,8 +399,8 @@ class ExpertParallelMoE:
         _lib.call("moe_ep_peer_dispatch", px.handle, fm._ptr(hidden), T, k, fm._ptr(order),
                   fm._ptr(send_eid), fm._ptr(counts), fm._ptr(px.status), stream)
         fm.fused_experts(px.recv_rows, self.backend.prep, None, px.ones, px.recv_ids.view(-1, 1),
-                         use_fp8_w8a8=self.quant.startswith("fp8"), use_int8_w8a8=self.quant == "int8",
-                         out=px.result_rows, status=px.status, stage_events=stage_events,
+                         use_fp8_w8a8=self.quant.startswith("fp8"),
+                         use_int8_w8a8=self.quant == "int8", out=px.result_rows, status=px.status, stage_events=stage_events,
                          rows_only=True)
         out = torch.empty(T, H, dtype=hidden.dtype, device=dev)
         w = topk_weights.contiguous()
@@ -313,10 +409,13 @@ class ExpertParallelMoE:
         return out
 
     def rows_received(self) -> int:
-        """Rows this rank's experts processed in the last forward (synchronises
-        in the peer exchange)."""
+        """Rows this rank's experts processed in the last forward, i.e. routed
+        (token, slot) pairs (synchronises in the peer and dedup exchanges;
+        `last_rows_received` counts the token rows that crossed)."""
         if self.peer is not None:
             return int((self.peer.recv_ids >= 0).sum())
+        if self.dedup:
+            return int((self._last_recv_eid >= 0).sum())
         return self.last_rows_received
 
     def close(self) -> None:

@@ -2,7 +2,9 @@
 
 The exchange (split sizes, packing order, the three all_to_alls, the inverse
 permutation of the combine) runs exactly as on GPUs; the device work is done
-by a test-only CPU backend built on the oracle. A second test makes one rank
+by a test-only CPU backend built on the oracle. The deduplicated exchange
+(one row per token and destination rank) runs its torch plan unchanged. A
+second test makes one rank
 fail before its first collective and checks that the other rank's forward
 ends with an error within the process group's timeout instead of hanging. A
 third replays the peer-memory exchange's placement rule (counts matrix,
@@ -49,9 +51,20 @@ class CpuBackend:
         return orc.fused_experts(rows, self.w1, self.w2, ones,
                                  local_ids.view(-1, 1).long()).to(rows.dtype)
 
+    def experts_weighted(self, rows, local_ids, weights):
+        """sum_j w_j * expert_j(row), slots with id -1 dropped."""
+        keep = local_ids >= 0
+        return orc.fused_experts(rows, self.w1, self.w2, weights * keep,
+                                 local_ids.long().clamp_min(0)).to(rows.dtype)
+
     def combine(self, rows, inv, weights, num_tokens, top_k):
-        w = weights.reshape(-1, 1).float()
-        return (rows.float()[inv.long()] * w).view(num_tokens, top_k, -1).sum(1).to(rows.dtype)
+        """moe_combine_rows: slots with inv < 0 contribute nothing."""
+        inv = inv.long()
+        w = (weights.reshape(-1).float() * (inv >= 0)).unsqueeze(1)
+        if rows.shape[0] == 0:
+            return torch.zeros(num_tokens, rows.shape[1], dtype=rows.dtype)
+        picked = rows.float()[inv.clamp_min(0)] * w
+        return picked.view(num_tokens, top_k, -1).sum(1).to(rows.dtype)
 
 
 def free_port():
@@ -67,7 +80,7 @@ def problem(E, H, I, seed):
     return w1, w2
 
 
-def worker(rank, world, port, E, k, T, H, I, fail_rank, result_q):
+def worker(rank, world, port, E, k, T, H, I, fail_rank, result_q, dedup=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     from kernelswift_b200.ep import ExpertParallelMoE
@@ -83,12 +96,20 @@ def worker(rank, world, port, E, k, T, H, I, fail_rank, result_q):
         w, ids = orc.route(logits, k)
         ep = ExpertParallelMoE(None, None, E, k,
                                backend=CpuBackend(w1[rank * el:(rank + 1) * el],
-                                                  w2[rank * el:(rank + 1) * el]))
+                                                  w2[rank * el:(rank + 1) * el]),
+                               dedup=dedup)
         if rank == fail_rank:
             raise RuntimeError("planted failure before the first collective")
         out = ep(hidden, w, ids)
         ref = orc.fused_experts(hidden, w1, w2, w, ids)
         err = float((out - ref).abs().max())
+        if dedup:
+            # rows received = (token, rank) pairs routed here, over all senders
+            sent = torch.tensor([len({int(e) // el for e in row}) for row in ids])
+            n = torch.tensor([int(sent.sum()), ep.last_rows_received])
+            dist.all_reduce(n)
+            if int(n[0]) != int(n[1]):
+                raise AssertionError(f"rows sent {int(n[0])} != rows received {int(n[1])}")
         result_q.put((rank, "ok", err))
     except Exception as exc:  # reported to the parent
         result_q.put((rank, "error", repr(exc)[:200]))
@@ -99,11 +120,12 @@ def worker(rank, world, port, E, k, T, H, I, fail_rank, result_q):
             pass
 
 
-def run(world, fail_rank=-1, E=8, k=2, T=37, H=64, I=32):
+def run(world, fail_rank=-1, E=8, k=2, T=37, H=64, I=32, dedup=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=worker, args=(r, world, port, E, k, T, H, I, fail_rank, q))
+    procs = [ctx.Process(target=worker,
+                         args=(r, world, port, E, k, T, H, I, fail_rank, q, dedup))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -125,6 +147,52 @@ def test_ep_matches_oracle(world, E, k):
         status, info = res[rank]
         assert status == "ok", (rank, info)
         assert info < 1e-4, (rank, info)
+
+
+@pytest.mark.parametrize("world,E,k", [(2, 8, 2), (4, 16, 4), (8, 32, 8)])
+def test_ep_dedup_matches_oracle(world, E, k):
+    res = run(world, E=E, k=k, dedup=True)
+    for rank in range(world):
+        status, info = res[rank]
+        assert status == "ok", (rank, info)
+        assert info < 1e-4, (rank, info)
+
+
+def test_dedup_plan_rows():
+    """One send row per (token, rank) pair; its ids and weights are exactly the
+    token's slots on that rank; inv finds it; counts add up."""
+    from kernelswift_b200.ep import dedup_plan
+
+    g = torch.Generator().manual_seed(9)
+    T, E, k, world = 53, 32, 8, 4
+    w, ids = orc.route(torch.randn(T, E, generator=g) + torch.linspace(0, 2, E), k)
+    tokens, eid, sw, inv, counts = dedup_plan(ids, w, E, world)
+    el = E // world
+    pairs = [(d, t) for d in range(world) for t in range(T)
+             if any(int(e) // el == d for e in ids[t])]
+    assert tokens.numel() == len(pairs) == int(counts[:world].sum())
+    assert int(counts[world]) == 0
+    for p, (d, t) in enumerate(pairs):
+        assert int(tokens[p]) == t and int(inv[t, d]) == p
+        for j in range(k):
+            on_d = int(ids[t, j]) // el == d
+            assert int(eid[p, j]) == (int(ids[t, j]) - d * el if on_d else -1)
+            assert float(sw[p, j]) == (float(w[t, j]) if on_d else 0.0)
+    assert int((inv >= 0).sum()) == len(pairs)
+    for d in range(world):
+        assert int(counts[d]) == sum(1 for dd, _ in pairs if dd == d)
+
+
+def test_dedup_plan_counts_invalid_ids():
+    from kernelswift_b200.ep import dedup_plan
+
+    ids = torch.tensor([[0, 5], [7, 1], [-1, 2]])  # 4 experts on 2 ranks
+    w = torch.ones(3, 2)
+    tokens, eid, sw, inv, counts = dedup_plan(ids, w, 4, 2)
+    # rank 0: tokens 0, 1; rank 1: token 2; all three have an invalid slot
+    assert counts.tolist() == [2, 1, 3]
+    assert inv.tolist() == [[0, -1], [1, -1], [-1, 2]]
+    assert eid.tolist() == [[0, -1], [-1, 1], [-1, 0]]
 
 
 def test_ep_rank_failure_surfaces_as_error():

@@ -30,14 +30,14 @@ def worker(rank, world, port, cfg, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
     try:
-        E, k, T, H, I, quant = cfg
+        E, k, T, H, I, quant, dedup = cfg
         g = torch.Generator().manual_seed(0)
         w1 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
         w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
         el = E // world
         ep = ExpertParallelMoE(w1[rank * el:(rank + 1) * el].to(dev),
                                w2[rank * el:(rank + 1) * el].to(dev), E, k, quant=quant,
-                               exchange="nccl")
+                               exchange="nccl", dedup=dedup)
         gt = torch.Generator().manual_seed(10 + rank)
         hidden = torch.randn(T, H, generator=gt).to(torch.bfloat16)
         w, ids = orc.route(torch.randn(T, E, generator=gt), k)
@@ -55,12 +55,13 @@ def worker(rank, world, port, cfg, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("quant", ["none", "fp8"])
-def test_ep_matches_oracle(cuda_device, quant):
+@pytest.mark.parametrize("quant,dedup", [("none", False), ("fp8", False), ("none", True)])
+def test_ep_matches_oracle(cuda_device, quant, dedup):
+    """NCCL exchange; dedup sends each token to a rank once."""
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 4)
-    cfg = (16, 4, 200, 256, 256, quant)
+    cfg = (16, 4, 200, 256, 256, quant, dedup)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
