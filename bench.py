@@ -9,7 +9,7 @@ sum, over one batch of synthetic tokens (N(0,1) activations, N(0,1/fan_in)
 weights, N(0,1) router logits).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload mixtral|qwen3|dsv3-fp8|dsv3-fp8-ue8m0|qwen3-int8] [--tokens T]
+                    [--workload mixtral|qwen3|dsv3|dsv3-fp8|dsv3-fp8-ue8m0|qwen3-int8] [--tokens T]
 
 `value` is device time (CUDA events, inputs resident in HBM, L2 flushed
 between steps outside the timed windows, max over ranks). On one GPU a step
@@ -42,6 +42,7 @@ WORKLOADS = {
     # name: (H, I, E, k, quant, default T, logit bias std)
     "mixtral": (4096, 14336, 8, 2, "none", 4096, 0.0),
     "qwen3": (2048, 768, 128, 8, "none", 8192, 0.5),
+    "dsv3": (7168, 2048, 256, 8, "none", 8192, 0.0),
     "dsv3-fp8": (7168, 2048, 256, 8, "fp8", 4096, 0.0),
     # the same layer with power-of-two block scales applied by the tensor core
     "dsv3-fp8-ue8m0": (7168, 2048, 256, 8, "fp8-ue8m0", 4096, 0.0),
