@@ -509,6 +509,15 @@ int moe_ep_peer_destroy(moe_ep_peer_t* ep);
 int moe_selftest_wait_timeout(int32_t* device_status, int limit_us,
                               void* stream);
 
+/* Self-test of the MOE_QUANT_FP8_UE8M0 scale-factor path: copies one
+ * 512-byte chunk (`chunk`, device, 16-byte aligned) into tensor memory as the
+ * block-scaled GEMM does and reads the four columns of all 128 lanes back
+ * into out[lane * 4 + column] (uint32, device). A correct copy gives
+ * out[l * 4 + c] = 32-bit word 4 * (l % 32) + c of the chunk. A bounded wait
+ * that runs out stores MOE_ERR_TIMEOUT in `device_status`. */
+int moe_selftest_sf_copy(const void* chunk, uint32_t* out, int32_t* device_status,
+                         void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

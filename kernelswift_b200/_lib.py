@@ -96,6 +96,7 @@ SIGNATURES = {
                                 ctypes.c_float, _vp, _vp, _vp]),
     "moe_combine_rows": (_int, [_vp, _int, _vp, _vp, _int, _i64, _int, _i64, _vp, _int, _vp]),
     "moe_selftest_wait_timeout": (_int, [_vp, _int, _vp]),
+    "moe_selftest_sf_copy": (_int, [_vp, _vp, _vp, _vp]),
     "moe_ep_peer_create": (_int, [_int, _int, _i64, _i64, _int, _int, _vp, _vp]),
     "moe_ep_peer_connect": (_int, [_vp, _vp]),
     "moe_ep_peer_buffers": (_int, [_vp, _vp, _vp, _vp]),

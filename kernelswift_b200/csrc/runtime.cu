@@ -122,6 +122,56 @@ __global__ void selftest_wait_kernel(int32_t* status, uint64_t limit_ns) {
   __syncthreads();
 }
 
+// Copies one 512-byte scale-factor chunk into tensor memory the way the
+// block-scaled GEMM does (shared memory, tcgen05.cp 32x128b.warpx4) and reads
+// all 128 lanes of the four columns back: out[lane * 4 + c].
+__global__ void __launch_bounds__(128, 1)
+    selftest_sf_copy_kernel(const uint32_t* __restrict__ chunk, uint32_t* __restrict__ out,
+                            int32_t* status, uint64_t limit_ns) {
+  __shared__ alignas(128) uint32_t s_chunk[128];
+  __shared__ alignas(8) uint64_t bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  s_chunk[threadIdx.x] = chunk[threadIdx.x];
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  // the copy reads shared memory through the async proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_slot;
+  if (threadIdx.x == 0) {
+    tc_cp_sf(tbase, make_sf_desc(smem_u32(s_chunk)));
+    tc_commit(&bar);
+  }
+  const bool ok = mbar_wait_bounded(&bar, 0, &abort_flag, limit_ns);
+  tc_fence_after();
+  if (__all_sync(0xffffffffu, ok)) {
+    uint32_t v[4];
+    tmem_ld4(tbase + (uint32_t(warp * 32) << 16), v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) out[(warp * 32 + lane) * 4 + c] = v[c];
+  } else if (lane == 0) {
+    report_status(status, MOE_ERR_TIMEOUT);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 32);
+  }
+}
+
 }  // namespace ksw
 
 using namespace ksw;
@@ -170,6 +220,21 @@ int moe_selftest_wait_timeout(int32_t* device_status, int limit_us,
   if (st != MOE_OK) return st;
   selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
       device_status, uint64_t(limit_us) * 1000ull);
+  KSW_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+int moe_selftest_sf_copy(const void* chunk, uint32_t* out, int32_t* device_status,
+                         void* stream) {
+  KSW_REQUIRE(chunk != nullptr && out != nullptr && device_status != nullptr,
+              MOE_ERR_INVALID_ARG, "moe_selftest_sf_copy: null pointer");
+  KSW_REQUIRE((reinterpret_cast<uintptr_t>(chunk) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+              MOE_ERR_INVALID_ARG, "moe_selftest_sf_copy: buffers must be 16-byte aligned");
+  int st = check_device(nullptr);
+  if (st != MOE_OK) return st;
+  selftest_sf_copy_kernel<<<1, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint32_t*>(chunk), out, device_status, kWaitLimitNs);
   KSW_CUDA(cudaGetLastError());
   return MOE_OK;
 }

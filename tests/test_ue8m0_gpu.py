@@ -53,6 +53,23 @@ def expected_row_bytes(block_bytes, rows_total, regroup):
     return orc.regroup_w13(per_row) if regroup else per_row
 
 
+def test_scale_factor_copy_layout(cuda_device):
+    """tcgen05.cp 32x128b.warpx4 of one chunk: lane l, column c holds word
+    4 * (l % 32) + c, in all four 32-lane quarters."""
+    g = torch.Generator().manual_seed(0)
+    chunk = torch.randint(0, 2 ** 31 - 1, (128,), generator=g, dtype=torch.int64)
+    chunk_dev = chunk.to(torch.int32).to(cuda_device)
+    out = torch.zeros(128 * 4, dtype=torch.int32, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    _lib.call("moe_selftest_sf_copy", p(chunk_dev), p(out), p(status), stream())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    lanes = torch.arange(128).unsqueeze(1)
+    cols = torch.arange(4).unsqueeze(0)
+    want = chunk.to(torch.int32)[4 * (lanes % 32) + cols]
+    assert torch.equal(out.cpu().view(128, 4), want)
+
+
 @pytest.mark.parametrize("E,H,I", [(4, 256, 128), (3, 384, 256)])
 def test_prepare_matches_oracle(cuda_device, E, H, I):
     w1, w2 = weights(E, H, I, seed=E * H, dev=cuda_device)
