@@ -106,3 +106,46 @@ def test_power_of_two_scales_cost_no_accuracy():
     fp32 = orc.rel_l2(orc.fused_experts_fp8(hidden, w1, w2, w, ids), ref)
     assert pow2 < 0.08 and fp32 < 0.08
     assert pow2 < 1.15 * fp32
+
+
+def _kernel_sfa_chunk(mb, kb, max_m_blocks):
+    """moe_grouped_gemm_mx_kernel's sfa_src: chunk (kb / 4, mb) of the
+    activation image ([q][row slice] with one group)."""
+    return (kb >> 2) * max_m_blocks + mb
+
+
+def _kernel_sfb_chunk(e, nt, kb, q_blocks, b_slices, bn):
+    """... and sfb_src: chunk (e, kb / 4, nt * BN / 128) of a weight image; a
+    256-wide tile takes this chunk and the next."""
+    return (e * q_blocks + (kb >> 2)) * b_slices + nt * (bn // 128)
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("E,N,K,rows", [(3, 512, 640, 384), (2, 1024, 2048, 256)])
+def test_kernel_chunk_addressing_matches_image_layout(bn, E, N, K, rows):
+    """Every bulk copy of the block-scaled GEMM lands inside its image, and
+    the chunk it copies holds, at the byte the MMA selects (row r % 32 / cell
+    (r % 128) / 32 / byte kb % 4), exactly the scale of each row of the tile
+    for that k-block."""
+    KB = K // 128
+    q_blocks = -(-KB // 4)
+    max_m_blocks = rows // 128
+    b_slices = N // 128
+    a_bytes = orc.sf_image_bytes(1, rows, K)
+    b_bytes = orc.sf_image_bytes(E, N, K)
+    for kb in range(KB):
+        for mb in range(max_m_blocks):
+            c = _kernel_sfa_chunk(mb, kb, max_m_blocks)
+            assert 0 <= c * 512 and (c + 1) * 512 <= a_bytes
+            for r in range(mb * 128, mb * 128 + 128):
+                off = orc.sf_image_offset(0, r, kb, q_blocks, max_m_blocks)
+                rr = r % 128
+                assert off == c * 512 + 16 * (rr % 32) + 4 * (rr // 32) + kb % 4
+        for e in range(E):
+            for nt in range(N // bn):
+                c = _kernel_sfb_chunk(e, nt, kb, q_blocks, b_slices, bn)
+                assert (c + bn // 128) * 512 <= b_bytes
+                for n in range(nt * bn, nt * bn + bn):
+                    off = orc.sf_image_offset(e, n, kb, q_blocks, b_slices)
+                    j, nn = divmod(n - nt * bn, 128)  # which of the tile's chunks
+                    assert off == (c + j) * 512 + 16 * (nn % 32) + 4 * (nn // 32) + kb % 4
