@@ -41,6 +41,7 @@
 // shared abort flag, every role leaves its loop, in-flight TMA loads and
 // MMAs are waited for, TMEM is freed and MOE_ERR_TIMEOUT is reported.
 #include <atomic>
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -236,7 +237,12 @@ struct GemmCfg {
 
 // KIND: kKindF16 (AB_FMT 0 = f16, 1 = bf16) or kKindI8 (AB_FMT 1 = s8).
 // TOUT: element type of the gate-up output (f16/bf16).
-template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
+// HALF: an m-block whose rows 64..127 are all padding (valid rows come first
+// in every expert's blocks, so sorted_ids[block + 64] is the sentinel) runs
+// M = 64 MMAs, half the tensor work. Their accumulator rows sit in the first
+// 16 lanes of each 32-lane quarter (row 16 q + l at lane 32 q + l), so the
+// epilogue maps its rows accordingly.
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF = false>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB,
@@ -245,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGES = Cfg::kStages;
   constexpr uint32_t D_FMT = (KIND == kKindI8) ? 2u : 1u;
   constexpr uint32_t IDESC = make_idesc(D_FMT, AB_FMT, BM, BN);
+  constexpr uint32_t IDESC_HALF = make_idesc(D_FMT, AB_FMT, BM / 2, BN);
   constexpr bool kScaled = (KIND == kKindI8);
 
   extern __shared__ uint8_t smem_raw[];
@@ -397,6 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+      uint32_t idesc = IDESC;
+      if constexpr (HALF)
+        if (__ldg(p.sorted_ids + c.mb * BM + BM / 2) >= p.numel) idesc = IDESC_HALF;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag, limit)) {
           ok = false;
@@ -408,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           tc_mma<KIND>(d_tmem, make_sw128_desc(a0 + kk * 32),
-                       make_sw128_desc(b0 + kk * 32), IDESC,
+                       make_sw128_desc(b0 + kk * 32), idesc,
                        (kb > kb0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(&empty[stage]);
@@ -441,9 +451,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, limit);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int m = c.mb * BM + row;
-      const int r = __ldg(p.sorted_ids + m);
-      const bool valid = r < p.numel;
+      int m, r;
+      bool valid;
+      if constexpr (HALF) {
+        // an M = 64 tile: lanes 0-15 of quarter q hold rows 16 q .. 16 q + 15
+        const bool half = __ldg(p.sorted_ids + c.mb * BM + BM / 2) >= p.numel;
+        m = c.mb * BM + (half ? q * 16 + (lane & 15) : row);
+        r = __ldg(p.sorted_ids + m);
+        valid = (!half || lane < 16) && r < p.numel;
+      } else {
+        m = c.mb * BM + row;
+        r = __ldg(p.sorted_ids + m);
+        valid = r < p.numel;
+      }
       const uint32_t tbase =
           tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
       float a_s = 1.0f;
@@ -1275,16 +1295,34 @@ int set_smem_once(Kern kern, size_t bytes, std::atomic<uint64_t>& done) {
   return MOE_OK;
 }
 
-template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
-int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
-                  const KParams& kp, int grid, cudaStream_t s) {
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF>
+int launch_kernel_v(const CUtensorMap& ta, const CUtensorMap& tb,
+                    const KParams& kp, int grid, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
-  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT>;
+  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT, HALF>;
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
   KSW_LAUNCH(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, s, ta, tb, kp);
   return MOE_OK;
+}
+
+// MOE_HALF_TILES=1 selects the variant with M = 64 MMAs for half-empty
+// m-blocks (not yet measured; the default keeps M = 128 throughout).
+bool half_tiles_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_HALF_TILES");
+    return v && v[0] && v[0] != '0';
+  }();
+  return on;
+}
+
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
+                  const KParams& kp, int grid, cudaStream_t s) {
+  if (half_tiles_enabled())
+    return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, true>(ta, tb, kp, grid, s);
+  return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, false>(ta, tb, kp, grid, s);
 }
 
 template <int BN, int EPI>
