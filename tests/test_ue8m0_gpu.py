@@ -6,13 +6,10 @@ tensor core (quant "fp8-ue8m0", moe_grouped_gemm_mx_kernel).
   - activation gather: e4m3 rows and image bytes bit-exact for every routed
     row;
   - the whole layer: relative L2 <= 5e-2 against the fp32 dequantised oracle,
-    both N tiles, K-split and dropped slots, deterministic repeats.
-
-The path has not yet been run on a B200, so these tests only run with
-MOE_TEST_UE8M0=1 until it has passed them there once.
+    both N tiles, K-split and dropped slots, deterministic repeats;
+  - the tensor-memory layout of one scale-factor chunk copy on its own.
 """
 import ctypes
-import os
 
 import pytest
 import torch
@@ -21,12 +18,7 @@ from kernelswift_b200 import _lib
 from kernelswift_b200 import fused_moe as fm
 from oracle import moe_oracle as orc
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("MOE_TEST_UE8M0") != "1",
-                       reason="UE8M0 tensor-core path not yet run on a B200; "
-                              "set MOE_TEST_UE8M0=1 to run it"),
-]
+pytestmark = pytest.mark.gpu
 
 REL_L2 = 5e-2
 
@@ -40,9 +32,11 @@ def stream():
 
 
 def weights(E, H, I, seed, dev):
-    g = torch.Generator().manual_seed(seed)
-    w1 = (torch.randn(E, 2 * I, H, generator=g) / H ** 0.5).to(dev)
-    w2 = (torch.randn(E, H, I, generator=g) / I ** 0.5).to(dev)
+    """N(0, 1/fan_in) expert weights drawn on the device (the DeepSeek-V3
+    shape is 45 GB of fp32)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w1 = torch.randn(E, 2 * I, H, generator=g, device=dev) / H ** 0.5
+    w2 = torch.randn(E, H, I, generator=g, device=dev) / I ** 0.5
     return w1, w2
 
 
