@@ -292,7 +292,10 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
  * of weights to stream, two weight-streaming CUDA-core kernels do the whole
  * computation instead (fp32 dot products; MOE_NO_DECODE_PATH=1 disables
  * them). Kernels are launched with programmatic dependent launch
- * (MOE_NO_PDL=1 disables it).
+ * (MOE_NO_PDL=1 disables it). Opt-in variants of the bf16/f16/int8 GEMMs:
+ * MOE_HALF_TILES=1 (M = 64 MMAs for blocks whose second half is padding) and
+ * MOE_TAIL_SPLIT=1 (the down GEMM splits the tiles of its last partial wave
+ * along K; deterministic, int8 bit-exact with the default).
  */
 int moe_fused_experts(const moe_problem_t* p, void* workspace,
                       size_t workspace_bytes, void* stream);
@@ -311,6 +314,14 @@ int moe_fused_experts_rows(const moe_problem_t* p, void* workspace,
  * moe_fused_experts_rows (rows_only = 1) launches for `p` (pointers unused;
  * answers without a GPU). No reference counterpart (measurement aid). */
 int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launches);
+
+/* The plan moe_fused_experts makes for `p` (pointers unused; answers without
+ * a GPU, for 148 SMs): info[0] gate-up tile width, [1] gate-up K splits,
+ * [2] down tile width, [3] down K splits, [4] dtype of the down GEMM's rows,
+ * [5] 1 when the down GEMM splits its last partial wave along K
+ * (MOE_TAIL_SPLIT=1), [6] 1 when the decode kernels run instead of the GEMM
+ * pipeline, [7] SMs planned for. No reference counterpart (inspection aid). */
+int moe_fused_experts_plan(const moe_problem_t* p, int32_t* info);
 
 /* ------------------------------------------------------------------------ */
 /* The stages of moe_fused_experts, one entry point each. Used by the expert-

@@ -84,6 +84,7 @@ SIGNATURES = {
     "moe_fused_experts_rows": (_int, [ctypes.POINTER(MoeProblem), _vp, _sz, _vp]),
     "moe_fused_experts_launches": (_int, [ctypes.POINTER(MoeProblem), _int,
                                           ctypes.POINTER(_int)]),
+    "moe_fused_experts_plan": (_int, [ctypes.POINTER(MoeProblem), _vp]),
     "moe_gather_rows": (_int, [_vp, _int, _i64, _i64, _int, _vp, _vp, _i64, _i64, _int, _vp,
                                _int, _vp, _vp]),
     "moe_gemm_gate_up": (_int, [_int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int,

@@ -344,6 +344,28 @@ def fused_experts_launches(num_tokens: int, hidden_size: int, intermediate_size:
     return n.value
 
 
+def fused_experts_plan(num_tokens: int, hidden_size: int, intermediate_size: int,
+                       num_experts: int, top_k: int, quant: str = "none",
+                       dtype: torch.dtype = torch.bfloat16) -> dict:
+    """The tile widths and K splits fused_experts picks for this shape
+    (moe_fused_experts_plan; no GPU needed)."""
+    p = _lib.MoeProblem()
+    p.num_tokens = num_tokens
+    p.hidden_size = hidden_size
+    p.inter_size = intermediate_size
+    p.num_experts = num_experts
+    p.top_k = top_k
+    p.act_dtype = _code(torch.empty(0, dtype=dtype))
+    p.quant = _QUANT[quant]
+    p.ids_dtype = _lib.DT_I32
+    p.weights_dtype = _lib.DT_F32
+    info = (ctypes.c_int32 * 8)()
+    _lib.call("moe_fused_experts_plan", ctypes.byref(p), info)
+    keys = ("gate_up_block_n", "gate_up_splits", "down_block_n", "down_splits",
+            "down_rows_dtype", "down_tail_split", "decode_path", "sms")
+    return dict(zip(keys, list(info)))
+
+
 def stage_event_array(events) -> ctypes.Array:
     """cudaEvent_t[7] for moe_problem_t.stage_events from torch.cuda.Event
     objects (each must have been recorded once so that it exists)."""

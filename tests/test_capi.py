@@ -1,6 +1,7 @@
 """CPU tests of the C ABI: the library loads, exports every function that
 include/*.h declares, and answers size queries without a GPU."""
 import ctypes
+import os
 import re
 from pathlib import Path
 
@@ -100,3 +101,26 @@ def test_launch_count_query_without_gpu():
     assert fm.fused_experts_launches(20000, 512, 256, 8, 1) == 7        # 3-launch align
     assert fm.fused_experts_launches(16384, 4096, 14336, 4, 1, rows_only=True) == 6
     assert fm.fused_experts_launches(0, 512, 256, 8, 2) == 0
+
+
+def test_plan_query_without_gpu():
+    """moe_fused_experts_plan: tile widths divide the GEMMs' widths, fp8 keeps
+    128/256-wide tiles and no gate-up split, decode shapes take the decode
+    kernels, and the tail split is off unless MOE_TAIL_SPLIT=1."""
+    from kernelswift_b200 import fused_moe as fm
+
+    for T, H, I, E, k, quant in [(4096, 4096, 14336, 8, 2, "none"), (64, 2048, 768, 128, 8, "none"),
+                                 (4096, 7168, 2048, 256, 8, "fp8"),
+                                 (4096, 7168, 2048, 256, 8, "fp8-ue8m0"),
+                                 (8192, 2048, 768, 128, 8, "int8")]:
+        plan = fm.fused_experts_plan(T, H, I, E, k, quant)
+        assert (2 * I) % plan["gate_up_block_n"] == 0 and H % plan["down_block_n"] == 0
+        assert plan["gate_up_splits"] >= 1 and plan["down_splits"] >= 1
+        assert plan["sms"] == 148 and plan["decode_path"] == 0
+        if quant.startswith("fp8"):
+            assert plan["gate_up_splits"] == 1
+            assert plan["gate_up_block_n"] in (128, 256) and plan["down_block_n"] in (128, 256)
+        if os.environ.get("MOE_TAIL_SPLIT", "0") in ("", "0"):
+            assert plan["down_tail_split"] == 0
+    assert fm.fused_experts_plan(1, 2048, 768, 128, 8)["decode_path"] == 1
+    assert fm.fused_experts_plan(4096, 4096, 14336, 8, 2)["down_rows_dtype"] == _lib.DT_BF16
