@@ -1,9 +1,12 @@
-"""CPU: the index arithmetic of the down GEMM's tail split (the
-moe_grouped_gemm_kernel TAIL variant), restated and exercised over many tile
-counts before it runs on a GPU: the work items cover every (tile, k-block)
-once, tail items land on distinct CTAs within the grid's last round,
-workspace slots stay inside the gridDim.x slots and are unique, no part is
-empty, and adding the parts in part order equals the whole-tile sum."""
+"""CPU: the index arithmetic of the grouped GEMM's opt-in variants, restated
+and exercised before they run on a GPU.
+
+Tail split (TAIL): over many tile counts the work items cover every (tile,
+k-block) once, tail items land on distinct CTAs within the grid's last
+round, workspace slots stay inside the gridDim.x slots and are unique, no
+part is empty, and adding the parts in part order equals the whole-tile sum.
+Half tiles (HALF): the half-empty test of an m-block agrees with align's
+layout."""
 import random
 
 import pytest
@@ -95,3 +98,27 @@ def test_part_order_sum_equals_whole_tile_sum():
                 for q2 in range(parts):
                     total += partials[q2]
                 assert total == sum(per_kb)
+
+
+def test_half_tile_rule_matches_align_layout():
+    """The M = 64 variant treats an m-block as half-empty when its row 64 is
+    the padding sentinel. That is exact because align packs an expert's rows
+    at the front of its blocks: in every block the valid rows form a prefix,
+    so a sentinel at row 64 means rows 64..127 are all padding, and the
+    valid rows (< 64) are the rows an M = 64 MMA computes."""
+    import torch
+
+    from oracle import moe_oracle as orc
+
+    g = torch.Generator().manual_seed(3)
+    for T, E, k in [(37, 8, 2), (300, 16, 4), (1000, 64, 8), (5, 128, 8)]:
+        _, ids = orc.route(torch.randn(T, E, generator=g), k)
+        sorted_ids, expert_ids, npp = orc.moe_align(ids, E, 128)
+        numel = T * k
+        s = torch.as_tensor(sorted_ids)
+        for b in range(int(npp) // 128):
+            blk = s[b * 128:(b + 1) * 128]
+            valid = blk < numel
+            n = int(valid.sum())
+            assert n > 0 and bool(valid[:n].all()), "valid rows are not a prefix"
+            assert (int(blk[64]) >= numel) == (n <= 64)
