@@ -302,6 +302,14 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
          (uint64_t(2) << 61);
 }
 
+// Asks L2 to fetch `bytes` (a multiple of 16) of global memory starting at a
+// 16-byte aligned address; no data reaches the thread and nothing waits.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* gsrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                   reinterpret_cast<uint64_t>(gsrc)),
+               "r"(bytes));
+}
+
 // ----- block-scaled fp8 (kind::mxf8f6f4 with UE8M0 scale factors) -----
 
 // 1-D bulk copy global -> shared memory, completion counted on `bar` as

@@ -15,7 +15,10 @@
 //   decode_down_kernel     item = (token, 8 rows of w2): each warp streams one
 //                          w2 row of every slot's expert at once, dots each
 //                          with that slot's act row (the token's act rows are
-//                          staged) and sums w_j * dot_j in slot order, in fp32
+//                          staged) and sums w_j * dot_j in slot order, in fp32;
+//                          before waiting for the gate-up kernel it has L2
+//                          prefetch the w2 rows of its first item (the ids
+//                          are already final)
 // Both run persistent grids (the CTAs that fit at once walk the items).
 //
 // Loads are 16-byte vectors, several in flight per lane. Slots whose id is
@@ -138,13 +141,30 @@ __global__ void __launch_bounds__(kThreadsDec)
                        int64_t T_tokens, int top_k, int E, int64_t H, int64_t I,
                        T* __restrict__ out) {
   constexpr int U = KMAX >= 8 ? 1 : 8 / KMAX;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row_blocks = H / kRowsDn;
+  // The routing ids were final before the previous launch (the gate-up
+  // kernel) passed its own wait, so before waiting for it this CTA asks L2 for
+  // the w2 rows of its first item (kRowsDn contiguous rows per slot; at decode
+  // sizes most CTAs have one item); that weight stream then overlaps the
+  // gate-up kernel. Only a prefetch: the ids are read again after the wait.
+  // Kept to the many-slot instantiations (top-8 and up), whose register use
+  // it leaves as it was; in the few-slot ones it would cost occupancy.
+  if constexpr (KMAX >= 8) {
+    if (warp == 0 && lane < top_k && int64_t(blockIdx.x) < T_tokens * row_blocks) {
+      const int64_t t = int64_t(blockIdx.x) / row_blocks;
+      const int e = valid_expert(ids, t * top_k + lane, E);
+      if (e >= 0)
+        l2_prefetch_bulk(
+            w2 + (int64_t(e) * H + (int64_t(blockIdx.x) - t * row_blocks) * kRowsDn) * I,
+            uint32_t(kRowsDn * I * sizeof(T)));
+    }
+  }
   pdl_wait();
   pdl_trigger();
   extern __shared__ uint4 smem_dec[];
   T* a = reinterpret_cast<T*>(smem_dec);  // [top_k, I] act rows of the current token
   __shared__ int s_e[KMAX];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row_blocks = H / kRowsDn;
   int64_t staged = -1;
   for (int64_t item = blockIdx.x; item < T_tokens * row_blocks; item += gridDim.x) {
     const int64_t t = item / row_blocks;
