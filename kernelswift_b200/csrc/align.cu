@@ -62,6 +62,21 @@ __device__ __forceinline__ int block_excl_scan(int v, int* tmp, int* total) {
   return excl;
 }
 
+// Adds ids[base, min(base + 1024, end)) (one per thread) to the expert
+// histogram with one shared-memory atomic per distinct expert per warp (the
+// warp's lanes with the same expert are grouped by __match_any_sync), instead
+// of one per id: with few experts per-id atomics all contend on a handful of
+// counters. `base` is the same for every thread of the block.
+template <typename IdT>
+__device__ __forceinline__ void count_subchunk(const IdT* ids, int64_t base, int64_t end,
+                                               int E, int* counts) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = base + threadIdx.x;
+  const int e = (i < end) ? load_id(ids, i, E) : -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  if (e >= 0 && lane == __ffs(peers) - 1) atomicAdd(&counts[e], __popc(peers));
+}
+
 // Places ids[base, min(base + 1024, end)) (one per thread) at their final
 // slots. running[e] is expert e's next free slot; warp_cnt[32][E] must be
 // all zero on entry and is all zero again on exit.
@@ -128,10 +143,8 @@ __global__ void __launch_bounds__(kThreads)
   for (int p = tid; p < 32 * E; p += kThreads) warp_cnt[p] = 0;
   __syncthreads();
 
-  for (int64_t i = tid; i < numel; i += kThreads) {
-    const int e = load_id(ids, i, E);
-    if (e >= 0) atomicAdd(&counts[e], 1);
-  }
+  for (int64_t base = 0; base < numel; base += kThreads)
+    count_subchunk(ids, base, numel, E, counts);
   __syncthreads();
 
   const int cnt = tid < E ? counts[tid] : 0;
@@ -164,10 +177,8 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   const int64_t begin = int64_t(blockIdx.x) * kChunk;
   const int64_t end = min(numel, begin + kChunk);
-  for (int64_t i = begin + tid; i < end; i += kThreads) {
-    const int e = load_id(ids, i, E);
-    if (e >= 0) atomicAdd(&counts[e], 1);
-  }
+  for (int64_t base = begin; base < end; base += kThreads)
+    count_subchunk(ids, base, end, E, counts);
   __syncthreads();
   for (int e = tid; e < E; e += kThreads)
     chunk_counts[int64_t(blockIdx.x) * E + e] = counts[e];

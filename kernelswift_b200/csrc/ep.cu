@@ -45,9 +45,13 @@ __global__ void __launch_bounds__(kThreads)
     *local = static_cast<int>(v - int64_t(d) * e_local);
     return d;
   };
-  for (int64_t i = tid; i < numel; i += kThreads) {
+  // histogram with one shared-memory atomic per distinct bucket per warp
+  for (int64_t base = 0; base < numel; base += kThreads) {
+    const int64_t i = base + tid;
     int loc;
-    atomicAdd(&cnt[bucket_of(i, &loc)], 1);
+    const int d = i < numel ? bucket_of(i, &loc) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    if (d >= 0 && lane == __ffs(peers) - 1) atomicAdd(&cnt[d], __popc(peers));
   }
   __syncthreads();
   // exclusive scan over the (<= 129) buckets by warp 0..4
