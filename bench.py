@@ -281,7 +281,17 @@ def workload_config(name, H, I, E, k, quant, T, n, exchange=None):
                 if exchange == "nccl-dedup" else "NCCL all_to_all)")) if n > 1 else "single",
             "l2": f"flushed between steps outside the timed windows ({L2_FLUSH_BYTES >> 20} MB "
                   f"write{', then a read of another ' + str(L2_FLUSH_BYTES >> 20) + ' MB that evicts the dirty lines' if L2Flush.evict else ''}); "
-                  "weights also exceed L2"}
+                  "weights also exceed L2",
+            "switches": active_switches()}
+
+
+def active_switches() -> dict:
+    """The library's environment switches as this run saw them."""
+    def on(name, default):
+        v = os.environ.get(name)
+        return default if not v else v[0] != "0"  # the library's reading
+    return {"pdl": not on("MOE_NO_PDL", False), "decode_path": not on("MOE_NO_DECODE_PATH", False),
+            "half_tiles": on("MOE_HALF_TILES", False), "tail_split": on("MOE_TAIL_SPLIT", False)}
 
 
 # ---------------------------------------------------------------------------
