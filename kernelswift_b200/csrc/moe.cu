@@ -14,6 +14,7 @@
 // moe_gemm_down, moe_sum_topk) for callers that build their own pipeline
 // (expert parallelism) and for stage-level tests.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -162,6 +163,15 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.dn_bn = dn.bn;
   P.gu_splits = gu.splits;
   P.gu_bn = gu.bn;
+  // MOE_BLOCK_N=64/128/256 overrides the tile width of each GEMM it divides
+  // (and that allows it: fp8 tiles are 128 or 256 wide), for timing studies
+  if (const char* v = std::getenv("MOE_BLOCK_N")) {
+    const int bn = std::atoi(v);
+    if ((bn == 128 || bn == 256 || (bn == 64 && !fp8 && !mx)) && bn <= max_bn) {
+      if (P.H % bn == 0) P.dn_bn = bn;
+      if ((2 * P.I) % bn == 0) P.gu_bn = bn;
+    }
+  }
   // Without a K split each weighted row is final: keep it in the 16-bit
   // activation dtype (as base.py:72,75 does) and halve the row traffic;
   // K-split partial sums and fp32 activations stay fp32.
