@@ -17,7 +17,9 @@ from . import fused_moe as fm
 WORKLOADS = {
     "mixtral": (4096, 14336, 8, 2, "none", 0.0),
     "qwen3": (2048, 768, 128, 8, "none", 0.5),
+    "dsv3": (7168, 2048, 256, 8, "none", 0.0),
     "dsv3-fp8": (7168, 2048, 256, 8, "fp8", 0.0),
+    "dsv3-fp8-ue8m0": (7168, 2048, 256, 8, "fp8-ue8m0", 0.0),
     "qwen3-int8": (2048, 768, 128, 8, "int8", 0.5),
 }
 
@@ -45,7 +47,8 @@ def main() -> None:
     for _ in range(args.steps):
         tw, ti = fm.fused_topk(hidden, logits, k)
         out = fm.fused_experts(hidden, prep, None, tw.to(hidden.dtype), ti,
-                               use_fp8_w8a8=quant == "fp8", use_int8_w8a8=quant == "int8")
+                               use_fp8_w8a8=quant.startswith("fp8"),
+                               use_int8_w8a8=quant == "int8")
     torch.cuda.synchronize()
     print(f"profile_case {args.workload} T={args.tokens}: out {tuple(out.shape)} "
           f"finite={bool(torch.isfinite(out).all())}")
