@@ -124,3 +124,34 @@ def test_plan_query_without_gpu():
             assert plan["down_tail_split"] == 0
     assert fm.fused_experts_plan(1, 2048, 768, 128, 8)["decode_path"] == 1
     assert fm.fused_experts_plan(4096, 4096, 14336, 8, 2)["down_rows_dtype"] == _lib.DT_BF16
+
+
+def test_plan_switches_in_a_child_process():
+    """MOE_TAIL_SPLIT=1 plans the tail split for unsplit bf16/int8 down GEMMs
+    (not for fp8, not with a K split); MOE_BLOCK_N forces the tile width it
+    divides (fp8 keeps 128/256)."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    code = ("import json, sys; sys.path.insert(0, %r)\n"
+            "from kernelswift_b200 import fused_moe as fm\n"
+            "print(json.dumps([fm.fused_experts_plan(*a) for a in [\n"
+            "  (4096, 4096, 14336, 8, 2), (512, 4096, 14336, 8, 2),\n"
+            "  (4096, 7168, 2048, 256, 8, 'fp8'), (8192, 2048, 768, 128, 8, 'int8')]]))\n"
+            % str(root))
+
+    def plans(**env):
+        res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                             env=dict(os.environ, **env), timeout=300)
+        assert res.returncode == 0, res.stderr[-2000:]
+        return json.loads(res.stdout.strip().splitlines()[-1])
+
+    tail = plans(MOE_TAIL_SPLIT="1", MOE_BLOCK_N="")
+    assert [p["down_tail_split"] for p in tail] == [1, 0, 0, 1]  # K split at T=512; fp8
+    forced = plans(MOE_TAIL_SPLIT="0", MOE_BLOCK_N="128")
+    assert all(p["down_block_n"] == 128 and p["gate_up_block_n"] == 128 for p in forced)
+    narrow = plans(MOE_TAIL_SPLIT="0", MOE_BLOCK_N="64")
+    assert narrow[0]["down_block_n"] == 64 and narrow[2]["down_block_n"] in (128, 256)
