@@ -1,0 +1,73 @@
+"""CPU: bench.py's host-side pieces the benchmark contract rests on: the
+workload table, the config block of the JSON line, the CPU baseline's host
+memory cap, the switch record, and the reference arm's JSON line (run on a
+tiny sample so it finishes in seconds)."""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+import bench  # noqa: E402
+
+
+def test_workloads_cover_the_configs():
+    names = set(bench.WORKLOADS)
+    assert {"mixtral", "qwen3", "dsv3", "dsv3-fp8", "qwen3-int8"} <= names
+    H, I, E, k, quant, T, bias = bench.WORKLOADS["mixtral"]
+    assert (H, I, E, k, quant, T) == (4096, 14336, 8, 2, "none", 4096)
+    assert bench.WORKLOADS["dsv3-fp8"][4] == "fp8" and bench.WORKLOADS["qwen3"][6] > 0
+
+
+def test_config_block():
+    cfg = bench.workload_config("mixtral", 4096, 14336, 8, 2, "none", 4096, 1)
+    assert cfg["parallelism"] == "single" and cfg["tokens_per_gpu"] == 4096
+    assert "flushed" in cfg["l2"] and set(cfg["switches"]) >= {"pdl", "tail_split"}
+    ep = bench.workload_config("mixtral", 4096, 14336, 8, 2, "none", 4096, 8, "peer")
+    assert ep["global_tokens"] == 8 * 4096 and "peer memory" in ep["parallelism"]
+    dd = bench.workload_config("dsv3", 7168, 2048, 256, 8, "none", 8192, 4, "nccl-dedup")
+    assert "one row per token and destination rank" in dd["parallelism"]
+
+
+def test_cpu_baseline_memory_cap():
+    # Mixtral's masters fit; DeepSeek-V3's 256 experts do not
+    assert bench.cpu_experts(4096, 14336, 8, 2) == 8
+    sub = bench.cpu_experts(7168, 2048, 256, 8)
+    assert 8 <= sub < 256
+    assert sub * 1.5 * 12 * 7168 * 2048 <= bench.CPU_WEIGHT_BUDGET
+    assert bench.cpu_expert_note(4096, 14336, 8, 2) == ""
+    assert "upper bound" in bench.cpu_expert_note(7168, 2048, 256, 8)
+
+
+def test_switch_record(monkeypatch):
+    for name in ("MOE_NO_PDL", "MOE_NO_DECODE_PATH", "MOE_HALF_TILES", "MOE_TAIL_SPLIT",
+                 "MOE_BLOCK_N"):
+        monkeypatch.delenv(name, raising=False)
+    assert bench.active_switches() == {"pdl": True, "decode_path": True, "half_tiles": False,
+                                       "tail_split": False, "block_n": "planner"}
+    monkeypatch.setenv("MOE_NO_PDL", "1")
+    monkeypatch.setenv("MOE_TAIL_SPLIT", "0")
+    monkeypatch.setenv("MOE_HALF_TILES", "1")
+    sw = bench.active_switches()
+    assert not sw["pdl"] and not sw["tail_split"] and sw["half_tiles"]
+
+
+def test_reference_arm_json_line():
+    """--impl reference prints one JSON line with the contract's keys (the
+    reference's CPU path on the qwen3 layer, a small token count)."""
+    res = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference",
+                          "--workload", "qwen3", "--tokens", "16", "--steps", "1",
+                          "--warmup", "0"], capture_output=True, text=True, timeout=600,
+                         cwd=str(ROOT), env=dict(os.environ, OMP_NUM_THREADS="4"))
+    assert res.returncode == 0, res.stderr[-2000:]
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
