@@ -45,6 +45,8 @@ def worker(rank, world, port, cfg, q):
         torch.cuda.synchronize()
         if quant == "fp8":
             ref = orc.fused_experts_fp8(hidden, w1, w2, w, ids)
+        elif quant == "fp8-ue8m0":
+            ref = orc.fused_experts_fp8_ue8m0(hidden, w1, w2, w, ids)
         else:
             ref = orc.fused_experts(hidden, w1, w2, w, ids)
         close = bool(torch.allclose(out.cpu().float(), ref, rtol=2e-2, atol=2e-2))
@@ -55,7 +57,8 @@ def worker(rank, world, port, cfg, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("quant,dedup", [("none", False), ("fp8", False), ("none", True)])
+@pytest.mark.parametrize("quant,dedup", [("none", False), ("fp8", False), ("none", True),
+                                         ("fp8-ue8m0", False)])
 def test_ep_matches_oracle(cuda_device, quant, dedup):
     """NCCL exchange; dedup sends each token to a rank once."""
     import torch.multiprocessing as mp
@@ -73,7 +76,7 @@ def test_ep_matches_oracle(cuda_device, quant, dedup):
         p.join(timeout=60)
     for rank, status, rel, close in res:
         assert status == "ok", (rank, rel)
-        if quant == "fp8":
+        if quant.startswith("fp8"):
             assert rel <= 5e-2, (rank, rel)  # relative L2 vs the dequantised oracle
         else:
             assert close, (rank, rel)  # rtol 2e-2 / atol 2e-2 vs the fp32 oracle
