@@ -11,20 +11,27 @@
 // element's position, so the output is bit-identical run to run.
 //
 // Paths:
-//   numel <= kSmallMax: one CTA does fill + histogram + scan + scatter.
-//   otherwise: three launches over chunks of kChunk ids:
+//   numel <= small_max: one CTA does fill + histogram + scan + scatter.
+//   otherwise: three launches over chunks of `chunk` ids:
 //     hist (per-chunk histogram, sentinel fill) -> scan (one CTA: offsets,
 //     expert_ids, num_tokens_post_pad, per-chunk bases) -> scatter.
+// moe_align_block_size and moe_fused_experts use 1024 for both (the single
+// CTA handles its ids in 1024-id rounds, each a few block barriers, so larger
+// problems are faster spread over CTAs); moe_align_block_size_noalloc keeps
+// 8192 / 4096, the limits its header documents for the static scratch.
 #include <mutex>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace ksw {
 namespace {
 
 constexpr int kThreads = 1024;
-constexpr int kChunk = 4096;          // ids per CTA on the multi-CTA path
-constexpr int64_t kSmallMax = 8192;   // single-CTA path up to this many ids
+constexpr int kChunk = 1024;          // ids per CTA on the multi-CTA path
+constexpr int64_t kSmallMax = 1024;   // single-CTA path up to this many ids
+constexpr int kChunkNoAlloc = 4096;   // the same for moe_align_block_size_noalloc
+constexpr int64_t kSmallMaxNoAlloc = 8192;
 constexpr int kMaxExperts = 1024;
 
 template <typename IdT>
@@ -163,7 +170,7 @@ __global__ void __launch_bounds__(kThreads)
 template <typename IdT>
 __global__ void __launch_bounds__(kThreads)
     align_hist_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
-                      int64_t L, int32_t* __restrict__ sorted,
+                      int64_t L, int chunk, int32_t* __restrict__ sorted,
                       int32_t* __restrict__ chunk_counts) {
   pdl_wait();
   pdl_trigger();
@@ -175,8 +182,8 @@ __global__ void __launch_bounds__(kThreads)
     sorted[p] = static_cast<int32_t>(numel);
   for (int e = tid; e < E; e += kThreads) counts[e] = 0;
   __syncthreads();
-  const int64_t begin = int64_t(blockIdx.x) * kChunk;
-  const int64_t end = min(numel, begin + kChunk);
+  const int64_t begin = int64_t(blockIdx.x) * chunk;
+  const int64_t end = min(numel, begin + chunk);
   for (int64_t base = begin; base < end; base += kThreads)
     count_subchunk(ids, base, end, E, counts);
   __syncthreads();
@@ -215,7 +222,7 @@ __global__ void __launch_bounds__(kThreads)
 
 template <typename IdT>
 __global__ void __launch_bounds__(kThreads)
-    align_scatter_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
+    align_scatter_kernel(const IdT* __restrict__ ids, int64_t numel, int E, int chunk,
                          const int32_t* __restrict__ chunk_base,
                          int32_t* __restrict__ sorted) {
   pdl_wait();
@@ -228,8 +235,8 @@ __global__ void __launch_bounds__(kThreads)
     running[e] = chunk_base[int64_t(blockIdx.x) * E + e];
   for (int p = tid; p < 32 * E; p += kThreads) warp_cnt[p] = 0;
   __syncthreads();
-  const int64_t begin = int64_t(blockIdx.x) * kChunk;
-  const int64_t end = min(numel, begin + kChunk);
+  const int64_t begin = int64_t(blockIdx.x) * chunk;
+  const int64_t end = min(numel, begin + chunk);
   for (int64_t base = begin; base < end; base += kThreads)
     scatter_subchunk(ids, base, end, E, running, warp_cnt, sorted);
 }
@@ -237,8 +244,8 @@ __global__ void __launch_bounds__(kThreads)
 template <typename IdT>
 int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
                  int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
-                 int32_t* ws, cudaStream_t s) {
-  if (numel <= kSmallMax) {
+                 int32_t* ws, int chunk, int64_t small_max, cudaStream_t s) {
+  if (numel <= small_max) {
     const size_t smem = size_t(2 * E + 64 + 32 * E) * sizeof(int);
     auto k = align_small_kernel<IdT>;
     if (smem > 48 * 1024)
@@ -248,9 +255,9 @@ int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
                expert_ids, num_post_pad);
     return MOE_OK;
   }
-  const int nchunks = static_cast<int>(ceil_div(numel, kChunk));
+  const int nchunks = static_cast<int>(ceil_div(numel, chunk));
   KSW_LAUNCH(align_hist_kernel<IdT>, dim3(nchunks), dim3(kThreads),
-             size_t(E) * sizeof(int), s, ids, numel, E, L, sorted, ws);
+             size_t(E) * sizeof(int), s, ids, numel, E, L, chunk, sorted, ws);
   KSW_LAUNCH(align_scan_kernel, dim3(1), dim3(kThreads), 0, s, nchunks, E, BM, L, ws,
              expert_ids, num_post_pad);
   const size_t smem = size_t(E + 32 * E) * sizeof(int);
@@ -258,9 +265,40 @@ int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
   if (smem > 48 * 1024)
     KSW_CUDA(cudaFuncSetAttribute(
         k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  KSW_LAUNCH(k, dim3(nchunks), dim3(kThreads), smem, s, ids, numel, E,
+  KSW_LAUNCH(k, dim3(nchunks), dim3(kThreads), smem, s, ids, numel, E, chunk,
              static_cast<const int32_t*>(ws), sorted);
   return MOE_OK;
+}
+
+size_t workspace_bytes(int64_t numel, int E, int chunk, int64_t small_max) {
+  if (numel <= small_max) return 0;
+  return align256(size_t(ceil_div(numel, chunk)) * size_t(E) * sizeof(int32_t));
+}
+
+// align_launch with the given path thresholds.
+int align_launch_cfg(const void* ids, int ids_dtype, int64_t numel, int E, int BM,
+                     int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
+                     void* workspace, size_t ws_bytes, int chunk, int64_t small_max,
+                     cudaStream_t s) {
+  int st = align_validate(numel, E, BM);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE(ids_dtype == MOE_DTYPE_I32 || ids_dtype == MOE_DTYPE_I64,
+              MOE_ERR_INVALID_ARG, "topk_ids dtype must be int32 or int64");
+  KSW_REQUIRE(sorted && expert_ids && num_post_pad, MOE_ERR_INVALID_ARG,
+              "null output pointer");
+  KSW_REQUIRE(numel == 0 || ids != nullptr, MOE_ERR_INVALID_ARG,
+              "null topk_ids");
+  const size_t need = workspace_bytes(numel, E, chunk, small_max);
+  KSW_REQUIRE(ws_bytes >= need && (need == 0 || workspace != nullptr),
+              MOE_ERR_WORKSPACE, "align workspace too small");
+  const int64_t L = align_buffer_len(numel, E, BM);
+  if (ids_dtype == MOE_DTYPE_I32)
+    return launch_align(static_cast<const int32_t*>(ids), numel, E, BM, L,
+                        sorted, expert_ids, num_post_pad,
+                        static_cast<int32_t*>(workspace), chunk, small_max, s);
+  return launch_align(static_cast<const int64_t*>(ids), numel, E, BM, L, sorted,
+                      expert_ids, num_post_pad,
+                      static_cast<int32_t*>(workspace), chunk, small_max, s);
 }
 
 }  // namespace
@@ -272,8 +310,7 @@ int64_t align_buffer_len(int64_t numel, int E, int BM) {
 }
 
 size_t align_workspace_bytes(int64_t numel, int E) {
-  if (numel <= kSmallMax) return 0;
-  return align256(size_t(ceil_div(numel, kChunk)) * size_t(E) * sizeof(int32_t));
+  return workspace_bytes(numel, E, kChunk, kSmallMax);
 }
 
 int align_validate(int64_t numel, int E, int BM) {
@@ -290,25 +327,8 @@ int align_validate(int64_t numel, int E, int BM) {
 int align_launch(const void* ids, int ids_dtype, int64_t numel, int E, int BM,
                  int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
                  void* workspace, size_t ws_bytes, cudaStream_t s) {
-  int st = align_validate(numel, E, BM);
-  if (st != MOE_OK) return st;
-  KSW_REQUIRE(ids_dtype == MOE_DTYPE_I32 || ids_dtype == MOE_DTYPE_I64,
-              MOE_ERR_INVALID_ARG, "topk_ids dtype must be int32 or int64");
-  KSW_REQUIRE(sorted && expert_ids && num_post_pad, MOE_ERR_INVALID_ARG,
-              "null output pointer");
-  KSW_REQUIRE(numel == 0 || ids != nullptr, MOE_ERR_INVALID_ARG,
-              "null topk_ids");
-  const size_t need = align_workspace_bytes(numel, E);
-  KSW_REQUIRE(ws_bytes >= need && (need == 0 || workspace != nullptr),
-              MOE_ERR_WORKSPACE, "align workspace too small");
-  const int64_t L = align_buffer_len(numel, E, BM);
-  if (ids_dtype == MOE_DTYPE_I32)
-    return launch_align(static_cast<const int32_t*>(ids), numel, E, BM, L,
-                        sorted, expert_ids, num_post_pad,
-                        static_cast<int32_t*>(workspace), s);
-  return launch_align(static_cast<const int64_t*>(ids), numel, E, BM, L, sorted,
-                      expert_ids, num_post_pad,
-                      static_cast<int32_t*>(workspace), s);
+  return align_launch_cfg(ids, ids_dtype, numel, E, BM, sorted, expert_ids, num_post_pad,
+                          workspace, ws_bytes, kChunk, kSmallMax, s);
 }
 
 }  // namespace ksw
@@ -408,7 +428,7 @@ extern "C" int moe_align_block_size_noalloc(const void* topk_ids, int ids_dtype,
   if (st != MOE_OK) return st;
   st = align_validate(numel, num_experts, block_m);
   if (st != MOE_OK) return st;
-  const size_t need = align_workspace_bytes(numel, num_experts);
+  const size_t need = workspace_bytes(numel, num_experts, kChunkNoAlloc, kSmallMaxNoAlloc);
   if (need > kNoAllocScratchBytes)
     return fail(MOE_ERR_UNSUPPORTED,
                 "moe_align_block_size_noalloc: this problem needs " + std::to_string(need) +
@@ -419,7 +439,7 @@ extern "C" int moe_align_block_size_noalloc(const void* topk_ids, int ids_dtype,
   int32_t* scratch = nullptr;
   st = noalloc_scratch_address(&scratch);
   if (st != MOE_OK) return st;
-  return align_launch(topk_ids, ids_dtype, numel, num_experts, block_m, sorted_token_ids,
-                      expert_ids, num_tokens_post_pad, scratch, kNoAllocScratchBytes,
-                      static_cast<cudaStream_t>(stream));
+  return align_launch_cfg(topk_ids, ids_dtype, numel, num_experts, block_m, sorted_token_ids,
+                          expert_ids, num_tokens_post_pad, scratch, kNoAllocScratchBytes,
+                          kChunkNoAlloc, kSmallMaxNoAlloc, static_cast<cudaStream_t>(stream));
 }

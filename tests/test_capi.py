@@ -94,13 +94,15 @@ def test_launch_count_query_without_gpu():
     """moe_fused_experts_launches answers from the plan alone."""
     from kernelswift_b200 import fused_moe as fm
 
-    assert fm.fused_experts_launches(4096, 4096, 14336, 8, 2) == 5      # align..sum
+    assert fm.fused_experts_launches(4096, 4096, 14336, 8, 2) == 7      # 3-launch align..sum
     assert fm.fused_experts_launches(1, 2048, 768, 128, 8) == 2         # decode kernels
     assert fm.fused_experts_launches(64, 2048, 768, 128, 8) == 6        # split gate-up
     assert fm.fused_experts_launches(64, 7168, 2048, 256, 8, "fp8") == 6
     assert fm.fused_experts_launches(20000, 512, 256, 8, 1) == 7        # 3-launch align
     assert fm.fused_experts_launches(16384, 4096, 14336, 4, 1, rows_only=True) == 6
     assert fm.fused_experts_launches(0, 512, 256, 8, 2) == 0
+    assert fm.fused_experts_launches(512, 4096, 14336, 8, 2) == 5       # 1024 ids: 1-launch align
+    assert fm.fused_experts_launches(513, 4096, 14336, 8, 2) == 7       # 1026 ids: 3-launch align
 
 
 def test_plan_query_without_gpu():
