@@ -15,10 +15,11 @@
 //   otherwise: three launches over chunks of `chunk` ids:
 //     hist (per-chunk histogram, sentinel fill) -> scan (one CTA: offsets,
 //     expert_ids, num_tokens_post_pad, per-chunk bases) -> scatter.
-// moe_align_block_size and moe_fused_experts use 1024 for both (the single
-// CTA handles its ids in 1024-id rounds, each a few block barriers, so larger
-// problems are faster spread over CTAs); moe_align_block_size_noalloc keeps
-// 8192 / 4096, the limits its header documents for the static scratch.
+// moe_align_block_size and moe_fused_experts take the single CTA up to 2048
+// ids and chunks of 1024 above (the single CTA handles its ids in 1024-id
+// rounds of a few block barriers each, so larger problems are faster spread
+// over CTAs); moe_align_block_size_noalloc keeps 8192 / 4096, the limits its
+// header documents for the static scratch.
 #include <mutex>
 
 #include "common.cuh"
@@ -29,7 +30,7 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kChunk = 1024;          // ids per CTA on the multi-CTA path
-constexpr int64_t kSmallMax = 1024;   // single-CTA path up to this many ids
+constexpr int64_t kSmallMax = 2048;   // single-CTA path up to this many ids
 constexpr int kChunkNoAlloc = 4096;   // the same for moe_align_block_size_noalloc
 constexpr int64_t kSmallMaxNoAlloc = 8192;
 constexpr int kMaxExperts = 1024;

@@ -51,8 +51,8 @@ SHAPES = [
     ("one_expert", 300, 2, 8, 128),
     ("uniform", 1000, 1, 1, 32),
     ("with_invalid", 500, 4, 16, 64),
-    ("topk", 512, 2, 8, 128),       # single-CTA path, full (1024 ids)
-    ("topk", 513, 2, 8, 128),       # crosses into the multi-CTA path
+    ("topk", 1024, 2, 8, 128),      # single-CTA path, full (2048 ids)
+    ("topk", 1025, 2, 8, 128),      # crosses into the multi-CTA path
     ("topk", 4096, 2, 8, 128),      # multi-CTA, 8 chunks of 1024 (Mixtral T=4096)
     ("topk", 4097, 2, 8, 128),      # 8 chunks and a 2-id one
     ("skewed", 8192, 8, 128, 128),  # multi-CTA, Qwen3 T=8192

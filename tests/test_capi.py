@@ -101,8 +101,8 @@ def test_launch_count_query_without_gpu():
     assert fm.fused_experts_launches(20000, 512, 256, 8, 1) == 7        # 3-launch align
     assert fm.fused_experts_launches(16384, 4096, 14336, 4, 1, rows_only=True) == 6
     assert fm.fused_experts_launches(0, 512, 256, 8, 2) == 0
-    assert fm.fused_experts_launches(512, 4096, 14336, 8, 2) == 5       # 1024 ids: 1-launch align
-    assert fm.fused_experts_launches(513, 4096, 14336, 8, 2) == 7       # 1026 ids: 3-launch align
+    assert fm.fused_experts_launches(1024, 4096, 14336, 8, 2) == 5      # 2048 ids: 1-launch align
+    assert fm.fused_experts_launches(1025, 4096, 14336, 8, 2) == 7      # 2050 ids: 3-launch align
 
 
 def test_plan_query_without_gpu():
