@@ -228,7 +228,12 @@ __global__ void __launch_bounds__(kWarps * 32)
        m += int64_t(gridDim.x) * kWarps) {
     const int64_t sr = sorted ? source_row(sorted, m, numel, top_k) : m;
     if (sr < 0 || sr >= src_rows) continue;
-    const Tin* s = src + sr * H;
+    const Tin* s = src + sr * H + (lane & 15) * 8;
+    uint8_t* d = dst + m * H + (lane & 15) * 8;
+    // this row's bytes in the image: group g at sf_row + (g / 4) * q_stride + g % 4
+    // (the sf_image_offset layout)
+    uint8_t* sf_row = sf + (m >> 7) * 512 + 16 * (m & 31) + 4 * ((m & 127) >> 5);
+    const int64_t q_stride = row_slices * 512;
     for (int64_t gb = 0; gb < groups; gb += 2 * kBatch) {
       float v[kBatch][8];
 #pragma unroll
@@ -236,7 +241,7 @@ __global__ void __launch_bounds__(kWarps * 32)
         const int64_t g = gb + 2 * u + (lane >> 4);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
-        if (g < groups) load8(s + g * 128 + (lane & 15) * 8, v[u]);
+        if (g < groups) load8(s + g * 128, v[u]);
       }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
@@ -250,10 +255,8 @@ __global__ void __launch_bounds__(kWarps * 32)
         const uint32_t b = ue8m0_byte(amax);
         const float inv = ue8m0_inv_scale(b);
         if (g < groups) {
-          *reinterpret_cast<uint2*>(dst + m * H + g * 128 + (lane & 15) * 8) =
-              pack_e4m3x8(v[u], inv);
-          if ((lane & 15) == 0)
-            sf[sf_image_offset(0, m, g, q_blocks, row_slices)] = static_cast<uint8_t>(b);
+          *reinterpret_cast<uint2*>(d + g * 128) = pack_e4m3x8(v[u], inv);
+          if ((lane & 15) == 0) sf_row[(g >> 2) * q_stride + (g & 3)] = static_cast<uint8_t>(b);
         }
       }
     }
