@@ -17,7 +17,7 @@
 //     expert_ids, num_tokens_post_pad, per-chunk bases) -> scatter.
 // moe_align_block_size and moe_fused_experts take the single CTA up to 2048
 // ids and chunks of 1024 above (the single CTA handles its ids in 1024-id
-// rounds of a few block barriers each, so larger problems are faster spread
+// passes of a few block barriers each, so larger problems are faster spread
 // over CTAs); moe_align_block_size_noalloc keeps 8192 / 4096, the limits its
 // header documents for the static scratch.
 #include <mutex>

@@ -3,7 +3,7 @@ and exercised before they run on a GPU.
 
 Tail split (TAIL): over many tile counts the work items cover every (tile,
 k-block) once, tail items land on distinct CTAs within the grid's last
-round, workspace slots stay inside the gridDim.x slots and are unique, no
+pass, workspace slots stay inside the gridDim.x slots and are unique, no
 part is empty, and adding the parts in part order equals the whole-tile sum.
 Half tiles (HALF): the half-empty test of an m-block agrees with align's
 layout."""
@@ -62,7 +62,7 @@ def test_items_cover_each_tile_k_block_once(total_tiles, grid, k_blocks):
             assert slot not in slots
             slots.add(slot)
     assert len(covered) == total_tiles * k_blocks
-    # every CTA runs the whole-tile rounds, then at most one tail item
+    # every CTA runs the whole-tile passes, then at most one tail item
     for parts_seen in per_cta.values():
         assert sum(1 for q in parts_seen if q >= 0) <= 1
     if parts > 1:
