@@ -442,6 +442,16 @@ int moe_ep_plan(const void* topk_ids, int ids_dtype, int64_t numel,
                 int num_experts, int world, int32_t* order, int32_t* send_eid,
                 int32_t* inv_index, int64_t* counts, void* stream);
 
+/* moe_ep_plan with the slots spread over CTAs when there are more than 8192
+ * (three launches: per-chunk histograms, a scan, the placement; one CTA
+ * otherwise). Same outputs, bit for bit. `workspace` holds
+ * moe_ep_plan_workspace_size bytes (0 up to 8192 slots). */
+int moe_ep_plan_workspace_size(int64_t numel, int world, size_t* bytes);
+int moe_ep_plan_ws(const void* topk_ids, int ids_dtype, int64_t numel,
+                   int num_experts, int world, int32_t* order, int32_t* send_eid,
+                   int32_t* inv_index, int64_t* counts, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Expert parallelism over NVLink peer memory. No reference counterpart (the */
 /* reference has no expert parallelism): it replaces, across the ranks of    */

@@ -93,6 +93,8 @@ SIGNATURES = {
                              _i64, _i64, _vp, _int, _int, _vp, _int, _vp, _vp]),
     "moe_sum_topk": (_int, [_vp, _int, _i64, _int, _i64, _vp, _int, _int, _vp, _int, _vp]),
     "moe_ep_plan": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp]),
+    "moe_ep_plan_workspace_size": (_int, [_i64, _int, ctypes.POINTER(_sz)]),
+    "moe_ep_plan_ws": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "moe_grouped_topk": (_int, [_vp, _int, _i64, _int, _int, _int, _int, _int, _int,
                                 ctypes.c_float, _vp, _vp, _vp]),
     "moe_combine_rows": (_int, [_vp, _int, _vp, _vp, _int, _i64, _int, _i64, _vp, _int, _vp]),

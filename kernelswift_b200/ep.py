@@ -4,8 +4,9 @@ Experts are sharded in contiguous blocks: with E experts over `world` ranks,
 rank r holds experts [r*E/world, (r+1)*E/world). Tokens stay data-parallel:
 every rank routes its own tokens. One forward is
 
-  1. plan (moe_ep_plan, one launch): dest[r] = topk_ids[r] // E_local for
-     every flat slot r = t*k + j; `order` = the slots sorted by destination
+  1. plan (moe_ep_plan_ws: one launch up to 8192 slots, three above):
+     dest[r] = topk_ids[r] // E_local for every flat slot r = t*k + j;
+     `order` = the slots sorted by destination
      rank (stable), the destination-local expert ids in that order, the
      inverse permutation and the per-destination counts
   2. all_to_all of the per-destination counts (the only host sync: NCCL's
@@ -103,9 +104,11 @@ class CudaBackend:
     def __init__(self, prepared: fm.PreparedWeights, quant: str = "none"):
         self.prep = prepared
         self.quant = quant
+        self._plan_ws = None
 
     def plan(self, topk_ids: torch.Tensor, num_experts: int, world: int):
-        """(order, send_eid, inv, counts) of moe_ep_plan for this rank's ids."""
+        """(order, send_eid, inv, counts) of moe_ep_plan for this rank's ids
+        (moe_ep_plan_ws: more than 8192 slots are spread over CTAs)."""
         ids = topk_ids.reshape(-1).contiguous()
         n = ids.numel()
         dev = ids.device
@@ -113,9 +116,13 @@ class CudaBackend:
         send_eid = torch.empty(n, dtype=torch.int32, device=dev)
         inv = torch.empty(n, dtype=torch.int32, device=dev)
         counts = torch.empty(world + 1, dtype=torch.int64, device=dev)
-        _lib.call("moe_ep_plan", fm._ptr(ids), fm._code(ids), n, num_experts, world,
+        nbytes = ctypes.c_size_t(0)
+        _lib.call("moe_ep_plan_workspace_size", n, world, ctypes.byref(nbytes))
+        if self._plan_ws is None or self._plan_ws.numel() < nbytes.value:
+            self._plan_ws = torch.empty(max(nbytes.value, 256), dtype=torch.uint8, device=dev)
+        _lib.call("moe_ep_plan_ws", fm._ptr(ids), fm._code(ids), n, num_experts, world,
                   fm._ptr(order), fm._ptr(send_eid), fm._ptr(inv), fm._ptr(counts),
-                  fm._stream(dev))
+                  fm._ptr(self._plan_ws), self._plan_ws.numel(), fm._stream(dev))
         return order, send_eid, inv, counts
 
     def pack(self, hidden: torch.Tensor, order: torch.Tensor, top_k: int) -> torch.Tensor:
@@ -400,8 +407,8 @@ class ExpertParallelMoE:
                   fm._ptr(send_eid), fm._ptr(counts), fm._ptr(px.status), stream)
         fm.fused_experts(px.recv_rows, self.backend.prep, None, px.ones, px.recv_ids.view(-1, 1),
                          use_fp8_w8a8=self.quant.startswith("fp8"),
-                         use_int8_w8a8=self.quant == "int8", out=px.result_rows, status=px.status, stage_events=stage_events,
-                         rows_only=True)
+                         use_int8_w8a8=self.quant == "int8", out=px.result_rows,
+                         status=px.status, stage_events=stage_events, rows_only=True)
         out = torch.empty(T, H, dtype=hidden.dtype, device=dev)
         w = topk_weights.contiguous()
         _lib.call("moe_ep_peer_combine", px.handle, fm._ptr(inv), fm._ptr(w), fm._code(w), T, k,

@@ -157,3 +157,14 @@ def test_plan_switches_in_a_child_process():
     assert all(p["down_block_n"] == 128 and p["gate_up_block_n"] == 128 for p in forced)
     narrow = plans(MOE_TAIL_SPLIT="0", MOE_BLOCK_N="64")
     assert narrow[0]["down_block_n"] == 64 and narrow[2]["down_block_n"] in (128, 256)
+
+
+def test_ep_plan_workspace_query_without_gpu():
+    lib = _lib.load()
+    n = ctypes.c_size_t(123)
+    assert lib.moe_ep_plan_workspace_size(8192, 8, ctypes.byref(n)) == 0 and n.value == 0
+    assert lib.moe_ep_plan_workspace_size(8193, 8, ctypes.byref(n)) == 0
+    assert n.value == 9 * 9 * 4  # ceil(8193 / 1024) chunks x (world + 1) buckets
+    assert lib.moe_ep_plan_workspace_size(65536, 128, ctypes.byref(n)) == 0
+    assert n.value == 64 * 129 * 4
+    assert lib.moe_ep_plan_workspace_size(100, 129, ctypes.byref(n)) == _lib.MOE_ERR_UNSUPPORTED
