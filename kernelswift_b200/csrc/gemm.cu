@@ -1145,7 +1145,10 @@ struct MxCfg {
   static_assert(kSfCol0 + kStages * kSfCols <= 512, "TMEM columns");
 };
 
-template <int BN, int EPI, typename TOUT>
+// HALF: as in moe_grouped_gemm_kernel, M = 64 MMAs for m-blocks whose rows
+// 64..127 are padding; their A scale factors are the first two columns of
+// the same slot (rows 0-63 of the chunk).
+template <int BN, int EPI, typename TOUT, bool HALF = false>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_grouped_gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA,
                                const __grid_constant__ CUtensorMap tmB, const KParams p) {
@@ -1153,6 +1156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGES = Cfg::kStages;
   constexpr int NACC = Cfg::kNAcc;
   constexpr uint32_t IDESC = make_idesc_mx(BM, BN);
+  constexpr uint32_t IDESC_HALF = make_idesc_mx(BM / 2, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -1308,6 +1312,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+      uint32_t idesc_tile = IDESC;
+      if constexpr (HALF)
+        if (__ldg(p.sorted_ids + c.mb * BM + BM / 2) >= p.numel) idesc_tile = IDESC_HALF;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag, limit)) {
           ok = false;
@@ -1320,7 +1327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < BN / 128; ++j)
           tc_cp_sf(sf_t + 4 + 4 * j,
                    make_sf_desc(smem_u32(sSfb + stage * Cfg::kSfbBytes + 512 * j)));
-        const uint32_t idesc = idesc_sf_ids(IDESC, uint32_t(kb & 3));
+        const uint32_t idesc = idesc_sf_ids(idesc_tile, uint32_t(kb & 3));
         const uint32_t a0 = smem_u32(sA + stage * kABytes);
         const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
 #pragma unroll
@@ -1357,9 +1364,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, limit);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int m = c.mb * BM + row;
-      const int r = __ldg(p.sorted_ids + m);
-      const bool valid = r < p.numel;
+      int m, r;
+      bool valid;
+      if constexpr (HALF) {
+        const bool half = __ldg(p.sorted_ids + c.mb * BM + BM / 2) >= p.numel;
+        m = c.mb * BM + (half ? q * 16 + (lane & 15) : row);
+        r = __ldg(p.sorted_ids + m);
+        valid = (!half || lane < 16) && r < p.numel;
+      } else {
+        m = c.mb * BM + row;
+        r = __ldg(p.sorted_ids + m);
+        valid = r < p.numel;
+      }
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
       if constexpr (EPI == kEpiSwiGLU) {
         constexpr int G_HALF = BN / 64;
@@ -1551,16 +1567,25 @@ int dispatch_fp8(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const KPa
   }
 }
 
-template <int BN, int EPI, typename TOUT>
-int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
-              cudaStream_t s) {
+template <int BN, int EPI, typename TOUT, bool HALF>
+int launch_mx_v(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+                cudaStream_t s) {
   using Cfg = MxCfg<BN>;
-  auto kern = moe_grouped_gemm_mx_kernel<BN, EPI, TOUT>;
+  auto kern = moe_grouped_gemm_mx_kernel<BN, EPI, TOUT, HALF>;
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
   KSW_LAUNCH(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, s, ta, tb, kp);
   return MOE_OK;
+}
+
+bool half_tiles_enabled();
+
+template <int BN, int EPI, typename TOUT>
+int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+              cudaStream_t s) {
+  if (half_tiles_enabled()) return launch_mx_v<BN, EPI, TOUT, true>(ta, tb, kp, grid, s);
+  return launch_mx_v<BN, EPI, TOUT, false>(ta, tb, kp, grid, s);
 }
 
 template <int EPI, typename TOUT>

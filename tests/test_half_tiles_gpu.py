@@ -1,5 +1,6 @@
 """GPU: the M = 64 tile variant of the grouped GEMMs (MOE_HALF_TILES=1): an
-m-block whose rows 64..127 are all padding runs half-height MMAs. The layer
+m-block whose rows 64..127 are all padding runs half-height MMAs (bf16,
+int8 and the UE8M0 block-scaled kernel). The layer
 must match the fp32 oracle within the bf16 tolerance and agree with the
 default M = 128 path (run in a child process without the switch).
 
@@ -31,6 +32,7 @@ CASES = [
     (1024, 512, 256, 64, 8, "none"),
     (300, 256, 256, 16, 4, "int8"),
     (20, 512, 512, 8, 2, "none"),
+    (200, 256, 256, 16, 4, "fp8-ue8m0"),  # the block-scaled kernel's M = 64 tiles
 ]
 
 
@@ -45,7 +47,8 @@ def run_case(T, H, I, E, k, quant):
     w1 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
     w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
     out = fm.fused_experts(hidden.to(dev), w1.to(dev), w2.to(dev), w.to(dev), ids.to(dev),
-                           use_int8_w8a8=quant == "int8")
+                           use_int8_w8a8=quant == "int8", use_fp8_w8a8=quant == "fp8-ue8m0",
+                           scale_format="ue8m0")
     torch.cuda.synchronize()
     return out.cpu(), hidden, w1, w2, w, ids
 
@@ -69,8 +72,9 @@ def test_half_tiles_match_oracle_and_default(cuda_device, tmp_path, case):
     half = child(case, tmp_path / "half.pt", True)
     full = child(case, tmp_path / "full.pt", False)
     _, hidden, w1, w2, w, ids = run_case(*case)
-    if case[5] == "int8":
-        ref = orc.fused_experts_int8(hidden, w1, w2, w, ids)
+    if case[5] in ("int8", "fp8-ue8m0"):
+        f = orc.fused_experts_int8 if case[5] == "int8" else orc.fused_experts_fp8_ue8m0
+        ref = f(hidden, w1, w2, w, ids)
         assert orc.rel_l2(half, ref) <= 5e-2
     else:
         ref = orc.fused_experts(hidden.float(), w1, w2, w, ids)
