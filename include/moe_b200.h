@@ -296,6 +296,10 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
  * MOE_HALF_TILES=1 (M = 64 MMAs for blocks whose second half is padding) and
  * MOE_TAIL_SPLIT=1 (the down GEMM splits the tiles of its last partial wave
  * along K; deterministic, int8 bit-exact with the default).
+ * hidden, w13, w2, out, workspace and the INT8_CHANNEL / FP8_UE8M0 weight
+ * scales must be 16-byte aligned (the kernels move them in 16-byte vectors
+ * and bulk copies; FP8_BLOCK scales need only float alignment); otherwise
+ * MOE_ERR_INVALID_ARG, checked before anything else.
  */
 int moe_fused_experts(const moe_problem_t* p, void* workspace,
                       size_t workspace_bytes, void* stream);

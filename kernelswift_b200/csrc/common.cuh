@@ -43,6 +43,7 @@ int check_device(int* num_sms);
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
 // Default wait limit for on-chip barrier waits: one second.
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;

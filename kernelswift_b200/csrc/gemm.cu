@@ -1628,6 +1628,11 @@ int pick_block_n(int64_t n, int64_t est_m_blocks, int64_t splits, int sms,
 int common_checks(const GroupedGemmArgs& a) {
   KSW_REQUIRE(a.a && a.b && a.sorted_ids && a.expert_ids && a.num_post_pad && a.out,
               MOE_ERR_INVALID_ARG, "grouped GEMM: null pointer");
+  // TMA operands, 16-byte epilogue stores, float4 / bulk-copied scales
+  KSW_REQUIRE(aligned16(a.a) && aligned16(a.b) && aligned16(a.out) &&
+                  (a.quant == MOE_QUANT_FP8_BLOCK ||
+                   (aligned16(a.a_scale) && aligned16(a.b_scale))),
+              MOE_ERR_INVALID_ARG, "grouped GEMM: operands must be 16-byte aligned");
   KSW_REQUIRE(a.rows > 0 && a.rows % BM == 0, MOE_ERR_INVALID_ARG,
               "grouped GEMM: rows must be a positive multiple of 128");
   KSW_REQUIRE(a.num_experts >= 1 && a.n > 0 && a.k > 0, MOE_ERR_INVALID_ARG,

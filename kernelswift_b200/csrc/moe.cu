@@ -244,6 +244,17 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes) {
 // runs unsplit, and the top-k sum is skipped.
 static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t workspace_bytes,
                               void* stream, void* rows_out) {
+  // 16-byte vectors and bulk copies: a misaligned operand would fault the
+  // context, so it is refused here, before the device is touched
+  // (fp8 128x128 block scales are read one float at a time)
+  KSW_REQUIRE(p != nullptr, MOE_ERR_INVALID_ARG, "null problem");
+  const bool vec_scales = p->quant != MOE_QUANT_FP8_BLOCK;
+  KSW_REQUIRE(aligned16(p->hidden) && aligned16(p->w13) && aligned16(p->w2) &&
+                  aligned16(p->out) && aligned16(rows_out) && aligned16(workspace) &&
+                  (!vec_scales || (aligned16(p->w13_scale) && aligned16(p->w2_scale))),
+              MOE_ERR_INVALID_ARG,
+              "moe_fused_experts: hidden, w13, w2, out, workspace and the int8 / UE8M0 "
+              "weight scales must be 16-byte aligned");
   int sms = 0;
   int st = check_device(&sms);
   if (st != MOE_OK) return st;

@@ -90,6 +90,40 @@ def test_compute_entry_points_fail_cleanly_without_gpu():
         _lib.call("moe_selftest_wait_timeout", None, 10, None)
 
 
+def test_fused_experts_refuses_misaligned_operands():
+    """A pointer off a 16-byte boundary is refused on the host, before any
+    device call (the pointers here are never dereferenced)."""
+    lib = _lib.load()
+
+    def problem(quant=_lib.QUANT_NONE, **ptr):
+        p = _lib.MoeProblem()
+        p.num_tokens, p.hidden_size, p.inter_size = 64, 512, 256
+        p.num_experts, p.top_k = 8, 2
+        p.act_dtype, p.quant = _lib.DT_BF16, quant
+        p.ids_dtype, p.weights_dtype = _lib.DT_I32, _lib.DT_BF16
+        for name in ("hidden", "w13", "w2", "topk_weights", "topk_ids", "out"):
+            setattr(p, name, ptr.get(name, 0x10000))
+        if quant != _lib.QUANT_NONE:
+            p.w13_scale = ptr.get("w13_scale", 0x20000)
+            p.w2_scale = ptr.get("w2_scale", 0x20000)
+        return p
+
+    ws = ctypes.c_void_p(0x30000)
+    for field in ("hidden", "w13", "w2", "out"):
+        p = problem(**{field: 0x10008})
+        assert lib.moe_fused_experts(ctypes.byref(p), ws, 1 << 30, None) \
+            == _lib.MOE_ERR_INVALID_ARG, field
+        assert "16-byte aligned" in lib.moe_last_error().decode()
+    p = problem()
+    assert lib.moe_fused_experts(ctypes.byref(p), ctypes.c_void_p(0x30004), 1 << 30, None) \
+        == _lib.MOE_ERR_INVALID_ARG
+    # int8 per-channel scales are read as float4; fp8 block scales one float at a time
+    p = problem(_lib.QUANT_INT8_CHANNEL, w2_scale=0x20004)
+    assert lib.moe_fused_experts(ctypes.byref(p), ws, 1 << 30, None) == _lib.MOE_ERR_INVALID_ARG
+    p = problem(_lib.QUANT_FP8_BLOCK, w2_scale=0x20004)
+    assert lib.moe_fused_experts(ctypes.byref(p), ws, 1 << 30, None) != _lib.MOE_ERR_INVALID_ARG
+
+
 def test_launch_count_query_without_gpu():
     """moe_fused_experts_launches answers from the plan alone."""
     from kernelswift_b200 import fused_moe as fm
