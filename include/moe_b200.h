@@ -11,6 +11,10 @@
  *
  * Conventions shared by every entry point:
  *   - All tensor arguments are raw device pointers to dense row-major arrays.
+ *     Row, weight, output and workspace pointers are 16-byte aligned (the
+ *     kernels move them in 16-byte vectors, TMA and bulk copies); the
+ *     compute entry points refuse others with MOE_ERR_INVALID_ARG. Ids,
+ *     routing weights and fp32 block scales need only element alignment.
  *   - Memory is owned by the caller. Entry points that need temporary device
  *     memory take a `workspace` pointer and its size; the matching
  *     *_workspace_size() query returns the required number of bytes.

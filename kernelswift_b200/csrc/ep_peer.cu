@@ -437,6 +437,8 @@ extern "C" int moe_ep_peer_dispatch(moe_ep_peer_t* ep, const void* hidden, int64
   KSW_REQUIRE(num_tokens >= 0 && top_k >= 1, MOE_ERR_INVALID_ARG, "ep_peer_dispatch: bad sizes");
   KSW_REQUIRE(counts && (num_tokens == 0 || (hidden && order && send_eid)), MOE_ERR_INVALID_ARG,
               "ep_peer_dispatch: null pointer");
+  KSW_REQUIRE(aligned16(hidden), MOE_ERR_INVALID_ARG,
+              "ep_peer_dispatch: hidden must be 16-byte aligned");
   const int64_t numel = num_tokens * top_k;
   const int64_t rows_per_cta = kThreadsEp / 32;
   const int grid = int(std::max<int64_t>(
@@ -456,6 +458,7 @@ extern "C" int moe_ep_peer_combine(moe_ep_peer_t* ep, const int32_t* inv_index,
   KSW_REQUIRE(num_tokens >= 0 && top_k >= 1, MOE_ERR_INVALID_ARG, "ep_peer_combine: bad sizes");
   KSW_REQUIRE(num_tokens == 0 || (inv_index && weights && out), MOE_ERR_INVALID_ARG,
               "ep_peer_combine: null pointer");
+  KSW_REQUIRE(aligned16(out), MOE_ERR_INVALID_ARG, "ep_peer_combine: out must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const EpView v = view_of(ep);
   KSW_LAUNCH(ep_signal_done_kernel, dim3(1), dim3(32), 0, s, v);

@@ -474,6 +474,8 @@ int grid_for_rows(int64_t rows) {
 
 int gather_launch(const GatherArgs& a, cudaStream_t s) {
   KSW_REQUIRE(a.src && a.dst && a.num_post_pad, MOE_ERR_INVALID_ARG, "gather: null pointer");
+  KSW_REQUIRE(aligned16(a.src) && aligned16(a.dst), MOE_ERR_INVALID_ARG,
+              "gather: src and dst must be 16-byte aligned");
   KSW_REQUIRE(a.sorted || a.quant != MOE_QUANT_NONE, MOE_ERR_INVALID_ARG,
               "gather: null sorted ids");
   KSW_REQUIRE(a.sorted || a.top_k == 0, MOE_ERR_INVALID_ARG,
@@ -566,6 +568,8 @@ int gather_launch(const GatherArgs& a, cudaStream_t s) {
 
 int sum_topk_launch(const SumArgs& a, cudaStream_t s) {
   KSW_REQUIRE(a.part && a.out, MOE_ERR_INVALID_ARG, "sum_topk: null pointer");
+  KSW_REQUIRE(aligned16(a.part) && aligned16(a.out), MOE_ERR_INVALID_ARG,
+              "sum_topk: partial and out must be 16-byte aligned");
   KSW_REQUIRE(a.H % 8 == 0, MOE_ERR_UNSUPPORTED, "sum_topk: H % 8 != 0");
   KSW_REQUIRE(a.splits >= 1 && a.top_k >= 1, MOE_ERR_INVALID_ARG, "sum_topk: bad sizes");
   KSW_REQUIRE(a.part_dtype == MOE_DTYPE_F32 || a.part_dtype == a.out_dtype, MOE_ERR_UNSUPPORTED,
@@ -622,6 +626,8 @@ int combine_launch(const CombineArgs& a, cudaStream_t s) {
   KSW_REQUIRE(a.inv && a.weights && a.out && (a.rows || a.T == 0), MOE_ERR_INVALID_ARG,
               "combine: null pointer");
   KSW_REQUIRE(a.H % 8 == 0 && a.top_k >= 1, MOE_ERR_UNSUPPORTED, "combine: bad sizes");
+  KSW_REQUIRE(aligned16(a.rows) && aligned16(a.out), MOE_ERR_INVALID_ARG,
+              "combine: rows and out must be 16-byte aligned");
   if (a.T == 0) return MOE_OK;
   const int64_t total = a.T * (a.H / 8);
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 148 * 32)));
