@@ -401,7 +401,8 @@ class ExpertParallelMoE:
             raise ValueError(f"hidden states are {hidden.dtype}, the exchange moves {px.dtype}")
         dev = hidden.device
         stream = fm._stream(dev)
-        hidden = hidden.contiguous()
+        # a misaligned view is copied: no rank's dispatch is refused while its peers wait
+        hidden = fm._contig(hidden)
         order, send_eid, inv, counts = self.backend.plan(topk_ids, self.num_experts, self.world)
         _lib.call("moe_ep_peer_dispatch", px.handle, fm._ptr(hidden), T, k, fm._ptr(order),
                   fm._ptr(send_eid), fm._ptr(counts), fm._ptr(px.status), stream)

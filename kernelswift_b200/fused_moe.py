@@ -62,7 +62,12 @@ def _check_cuda(name: str, t: torch.Tensor) -> None:
 
 
 def _contig(t: torch.Tensor) -> torch.Tensor:
-    return t if t.is_contiguous() else t.contiguous()
+    """A dense tensor whose data starts on a 16-byte boundary (the kernels
+    move rows in 16-byte vectors): `t` itself when it already is one, else a
+    copy (a view that starts mid-row of a larger tensor, for instance)."""
+    if t.is_contiguous() and t.data_ptr() % 16 == 0:
+        return t
+    return t.clone(memory_format=torch.contiguous_format)
 
 
 # ---------------------------------------------------------------------------
@@ -444,8 +449,9 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
     ti = _contig(topk_ids)
     if out is None:
         out = torch.empty_like(hidden)
-    elif out.shape != hidden.shape or out.dtype != hidden.dtype or not out.is_contiguous():
-        raise ValueError("out must be a contiguous tensor like hidden_states")
+    elif (out.shape != hidden.shape or out.dtype != hidden.dtype or not out.is_contiguous()
+          or out.data_ptr() % 16):
+        raise ValueError("out must be a contiguous, 16-byte aligned tensor like hidden_states")
     p = _problem(hidden, prep, tw, ti, out, status, stage_events)
     lib = _lib.load()
     nbytes = ctypes.c_size_t(0)
