@@ -124,6 +124,25 @@ def test_fused_experts_refuses_misaligned_operands():
     assert lib.moe_fused_experts(ctypes.byref(p), ws, 1 << 30, None) != _lib.MOE_ERR_INVALID_ARG
 
 
+def test_python_wrapper_copies_misaligned_views():
+    """fused_moe hands the library only 16-byte aligned dense tensors: an
+    aligned dense tensor passes through, a view starting mid-vector or a
+    strided view is copied."""
+    import torch
+
+    from kernelswift_b200 import fused_moe as fm
+
+    base = torch.zeros(4 * 64 + 8, dtype=torch.bfloat16)
+    assert base.data_ptr() % 16 == 0
+    assert fm._contig(base) is base
+    off = base[1:1 + 4 * 64].view(4, 64)  # starts 2 bytes past a boundary
+    got = fm._contig(off)
+    assert got is not off and got.data_ptr() % 16 == 0 and torch.equal(got, off)
+    strided = base[:256].view(64, 4).t()
+    got = fm._contig(strided)
+    assert got.is_contiguous() and torch.equal(got, strided)
+
+
 def test_launch_count_query_without_gpu():
     """moe_fused_experts_launches answers from the plan alone."""
     from kernelswift_b200 import fused_moe as fm
