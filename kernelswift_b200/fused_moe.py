@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
+import weakref
 from dataclasses import dataclass
 
 import torch
@@ -282,7 +283,13 @@ _prep_cache: dict = {}
 
 
 def _cached_prepare(w1, w2, quant, compute_dtype, w1_scale, w2_scale) -> PreparedWeights:
-    """prepare_weights memoised on the identity and version of the inputs."""
+    """prepare_weights memoised on the identity and version of the inputs.
+
+    An entry holds weak references to the tensors it was made from and is
+    used only while they still name those same tensor objects: once a
+    source tensor is freed, a new tensor that the caching allocator places
+    at the same address (same shape, version 0) does not match it."""
+    srcs = (w1, w2, w1_scale, w2_scale)
     key = (w1.data_ptr(), w1._version, tuple(w1.shape), w1.dtype,
            w2.data_ptr(), w2._version, tuple(w2.shape), w2.dtype, quant, compute_dtype,
            None if w1_scale is None else (w1_scale.data_ptr(), w1_scale._version),
@@ -290,12 +297,16 @@ def _cached_prepare(w1, w2, quant, compute_dtype, w1_scale, w2_scale) -> Prepare
     with _prep_lock:
         hit = _prep_cache.get(key)
     if hit is not None:
-        return hit
+        prep, refs = hit
+        if all((r is None and t is None) or (r is not None and r() is t)
+               for r, t in zip(refs, srcs)):
+            return prep
     prep = prepare_weights(w1, w2, quant, compute_dtype, w1_scale, w2_scale)
+    refs = tuple(None if t is None else weakref.ref(t) for t in srcs)
     with _prep_lock:
         if len(_prep_cache) > 8:
             _prep_cache.clear()
-        _prep_cache[key] = prep
+        _prep_cache[key] = (prep, refs)
     return prep
 
 

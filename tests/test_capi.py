@@ -143,6 +143,31 @@ def test_python_wrapper_copies_misaligned_views():
     assert got.is_contiguous() and torch.equal(got, strided)
 
 
+def test_prepared_weights_cache_checks_the_source_tensors(monkeypatch):
+    """fused_experts' prepared-weight cache answers only for the very tensors
+    (and versions) it prepared: another tensor object at the same address
+    (here a view; after a free, a new allocation) and an in-place update
+    both prepare again."""
+    import torch
+
+    from kernelswift_b200 import fused_moe as fm
+
+    calls = []
+    monkeypatch.setattr(fm, "prepare_weights", lambda *a, **k: calls.append(a) or object())
+    monkeypatch.setattr(fm, "_prep_cache", {})
+    w1, w2 = torch.zeros(2, 8, 64), torch.zeros(2, 64, 4)
+    p1 = fm._cached_prepare(w1, w2, "none", torch.bfloat16, None, None)
+    assert fm._cached_prepare(w1, w2, "none", torch.bfloat16, None, None) is p1
+    assert len(calls) == 1
+    alias = w1.view(w1.shape)  # same data_ptr, shape and version counter
+    assert alias.data_ptr() == w1.data_ptr() and alias._version == w1._version
+    assert fm._cached_prepare(alias, w2, "none", torch.bfloat16, None, None) is not p1
+    assert len(calls) == 2
+    w2.add_(1.0)
+    fm._cached_prepare(alias, w2, "none", torch.bfloat16, None, None)
+    assert len(calls) == 3
+
+
 def test_launch_count_query_without_gpu():
     """moe_fused_experts_launches answers from the plan alone."""
     from kernelswift_b200 import fused_moe as fm
