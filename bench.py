@@ -292,6 +292,7 @@ def active_switches() -> dict:
         return default if not v else v[0] != "0"  # the library's reading
     return {"pdl": not on("MOE_NO_PDL", False), "decode_path": not on("MOE_NO_DECODE_PATH", False),
             "half_tiles": on("MOE_HALF_TILES", False), "tail_split": on("MOE_TAIL_SPLIT", False),
+            "gather_tma": on("MOE_GATHER_TMA", False),
             "block_n": os.environ.get("MOE_BLOCK_N") or "planner"}
 
 

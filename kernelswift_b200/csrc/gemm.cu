@@ -86,6 +86,7 @@ struct KParams {
   uint64_t wait_limit_ns;
   float* tail_ws;           // TAIL: gridDim.x * BM * BN words of part tiles
   int32_t* tail_cnt;        // TAIL: gridDim.x counters, zero at launch
+  int32_t gather_top_k;     // GATHER: operand row m is token sorted_ids[m] / gather_top_k
 };
 
 struct TileCoord {
@@ -251,8 +252,15 @@ struct GemmCfg {
 // parts in part order, so results do not depend on timing, and runs the
 // epilogue. Workspace: gridDim.x slots of BM x BN 32-bit words, and one
 // counter per slot, zero at launch.
+// GATHER (16-bit gate-up): tmA maps the token matrix [T, K] with a box one
+// row high, and the whole of warp 0 produces: lane l loads operand rows
+// 4l..4l+3 of every A tile (token sorted_ids[m] / gather_top_k; padding
+// slots load token 0, whose products the epilogue drops) with one
+// tile::gather4 per k-block, so no gathered copy of the rows is written.
+// The align outputs come from the previous launch, so every thread waits
+// for it first (no early metadata).
 template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF = false,
-          bool TAIL = false>
+          bool TAIL = false, bool GATHER = false>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB,
@@ -316,7 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (and so everything downstream of them) wait, after the first weight
   // tiles have been requested.
   const bool producer = warp == 0 && lane == 0;
-  if (!p.early_meta) {
+  const bool early = p.early_meta && !GATHER;
+  if (!early) {
     pdl_wait();
     pdl_trigger();
   }
@@ -368,12 +377,72 @@ __global__ void __launch_bounds__(kThreads, 1)
     kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
     return -1;
   };
-  if (p.early_meta && !producer) {
+  if (early && !producer) {
     pdl_wait();
     pdl_trigger();
   }
 
-  if (producer) {
+  if (GATHER && warp == 0) {
+    // ---------------- TMA producer, A rows gathered from the tokens ----------------
+    static_assert(!GATHER || (KIND == kKindF16 && EPI == kEpiSwiGLU && !TAIL),
+                  "gathered A rows: 16-bit gate-up only");
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+    }
+    constexpr int kColsPerKb = kKBytes / 2;
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_items; t += gridDim.x) {
+      TileCoord c;
+      int kb0, kb1;
+      item(t, c, kb0, kb1);
+      const int e = __ldg(p.expert_ids + c.mb);
+      if (e < 0 || e >= p.num_experts) continue;
+      // this lane's four operand rows -> their token rows
+      int32_t rows[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = __ldg(p.sorted_ids + c.mb * BM + 4 * lane + j);
+        rows[j] = (r >= 0 && r < p.numel) ? r / p.gather_top_k : 0;
+      }
+      const int b_row = e * p.n_total + c.nt * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int kcol = kb * kColsPerKb;
+        bool free_slot = true;
+        if (lane == 0)
+          free_slot = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit);
+        if (!__shfl_sync(0xffffffffu, free_slot, 0)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kcol, b_row, &full[stage]);
+        }
+        __syncwarp();  // the stage's byte count is posted before any row lands
+        // rows 4 lane .. 4 lane + 3 of the tile: kKBytes per row
+        tma_gather4(sA + stage * kABytes + 4 * lane * kKBytes, &tmA, kcol, rows, &full[stage]);
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // Drain (lane 0): every load issued into a stage has landed before exit.
+    if (lane == 0) {
+      for (int s = 0; s < STAGES; ++s) {
+        const uint32_t n_s = issued / STAGES + (uint32_t(s) < issued % STAGES ? 1u : 0u);
+        if (n_s == 0) continue;
+        volatile int no_abort = 0;
+        mbar_wait_bounded(&full[s], (n_s - 1) & 1u, &no_abort, limit);
+      }
+    }
+    __syncwarp();
+  } else if (producer) {
     // ---------------- TMA producer ----------------
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -1483,11 +1552,12 @@ int set_smem_once(Kern kern, size_t bytes, std::atomic<uint64_t>& done) {
   return MOE_OK;
 }
 
-template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF, bool TAIL = false>
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF, bool TAIL = false,
+          bool GATHER = false>
 int launch_kernel_v(const CUtensorMap& ta, const CUtensorMap& tb,
                     const KParams& kp, int grid, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
-  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT, HALF, TAIL>;
+  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT, HALF, TAIL, GATHER>;
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
@@ -1508,6 +1578,15 @@ bool half_tiles_enabled() {
 template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
                   const KParams& kp, int grid, cudaStream_t s) {
+  if constexpr (EPI == kEpiSwiGLU && KIND == kKindF16) {
+    // A rows gathered from the token matrix by the kernel itself
+    if (kp.gather_top_k > 0) {
+      if (half_tiles_enabled())
+        return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, true, false, true>(ta, tb, kp, grid,
+                                                                               s);
+      return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, false, false, true>(ta, tb, kp, grid, s);
+    }
+  }
   if constexpr (EPI == kEpiRows) {
     // the tail split's workspace is sized for one slot per CTA
     if (kp.tail_ws != nullptr && kp.tail_cnt != nullptr && kp.splits == 1) {
@@ -1526,6 +1605,15 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
 bool tail_split_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("MOE_TAIL_SPLIT");
+    return v && v[0] && v[0] != '0';
+  }();
+  return on;
+}
+// MOE_GATHER_TMA=1: the 16-bit gate-up GEMM loads its A rows from the token
+// matrix with tile::gather4 instead of after a gather pass (not yet measured).
+bool gather_tma_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_GATHER_TMA");
     return v && v[0] && v[0] != '0';
   }();
   return on;
@@ -1672,8 +1760,11 @@ int operand_types(const GroupedGemmArgs& a, OperandTypes* ot) {
 int make_maps(const GroupedGemmArgs& a, const OperandTypes& ot, int bn,
               CUtensorMap* ta, CUtensorMap* tb) {
   const uint32_t box_k = uint32_t(kKBytes / ot.elem_bytes);
+  // gathered A: the token matrix, loaded four one-row boxes at a time
+  const bool gather = a.gather_top_k > 0;
   int st = encode_tma_2d(ta, ot.tma_type, ot.elem_bytes, a.a, uint64_t(a.k),
-                         uint64_t(a.rows), uint64_t(a.k), box_k, BM);
+                         uint64_t(gather ? a.a_rows : a.rows), uint64_t(a.k), box_k,
+                         gather ? 1u : uint32_t(BM));
   if (st != MOE_OK) return st;
   return encode_tma_2d(tb, ot.tma_type, ot.elem_bytes, a.b, uint64_t(a.k),
                        uint64_t(a.num_experts) * uint64_t(a.n), uint64_t(a.k),
@@ -1706,6 +1797,7 @@ KParams base_params(const GroupedGemmArgs& a, int elem_bytes) {
   kp.wait_limit_ns = kWaitLimitNs;
   kp.tail_ws = a.tail_ws;
   kp.tail_cnt = a.tail_cnt;
+  kp.gather_top_k = a.gather_top_k;
   return kp;
 }
 
@@ -1733,6 +1825,10 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
               "gate-up GEMM: hidden size * element size must be a multiple of 16 B");
   const bool mx = a.quant == MOE_QUANT_FP8_UE8M0;
   const bool fp8 = a.quant == MOE_QUANT_FP8_BLOCK || mx;
+  if (a.gather_top_k > 0)
+    KSW_REQUIRE(a.quant == MOE_QUANT_NONE && a.a_rows >= 1 && a.a_rows < (int64_t(1) << 31),
+                MOE_ERR_INVALID_ARG,
+                "gate-up GEMM: gathered A rows need 16-bit operands and 1 <= token rows < 2^31");
   if (fp8)
     KSW_REQUIRE(a.n % 256 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 gate-up GEMM: I must be a multiple of 128");

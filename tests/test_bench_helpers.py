@@ -45,10 +45,11 @@ def test_cpu_baseline_memory_cap():
 
 def test_switch_record(monkeypatch):
     for name in ("MOE_NO_PDL", "MOE_NO_DECODE_PATH", "MOE_HALF_TILES", "MOE_TAIL_SPLIT",
-                 "MOE_BLOCK_N"):
+                 "MOE_GATHER_TMA", "MOE_BLOCK_N"):
         monkeypatch.delenv(name, raising=False)
     assert bench.active_switches() == {"pdl": True, "decode_path": True, "half_tiles": False,
-                                       "tail_split": False, "block_n": "planner"}
+                                       "tail_split": False, "gather_tma": False,
+                                       "block_n": "planner"}
     monkeypatch.setenv("MOE_NO_PDL", "1")
     monkeypatch.setenv("MOE_TAIL_SPLIT", "0")
     monkeypatch.setenv("MOE_HALF_TILES", "1")
