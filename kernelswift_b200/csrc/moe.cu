@@ -4,7 +4,9 @@
 // launches instead when at most 16 rows are routed, csrc/decode.cu):
 //
 //   1. align      topk_ids -> sorted_token_ids, expert_ids, num_post_pad
-//   2. gather     hidden rows in expert-sorted order (+cast / quantise)
+//   2. gather     hidden rows in expert-sorted order (+cast / quantise);
+//                 skipped under MOE_GATHER_TMA=1 for 16-bit activations, where
+//                 the gate-up GEMM loads the token rows itself
 //   3. gate-up    grouped tcgen05 GEMM, SiLU(gate)*up fused      [L, I]
 //   4. (quant)    per-row quantisation of the activation (W8A8 modes)
 //   5. down       grouped tcgen05 GEMM, topk weight fused, optional K split
