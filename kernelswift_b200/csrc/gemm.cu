@@ -1876,6 +1876,8 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
                   a.row_weights_dtype == MOE_DTYPE_BF16,
               MOE_ERR_INVALID_ARG, "down GEMM: row weights must be f32/f16/bf16");
   KSW_REQUIRE(a.splits >= 1, MOE_ERR_INVALID_ARG, "down GEMM: splits must be >= 1");
+  KSW_REQUIRE(a.gather_top_k == 0, MOE_ERR_INVALID_ARG,
+              "down GEMM (and split gate-up): A rows must be pre-gathered");
   OperandTypes ot;
   st = operand_types(a, &ot);
   if (st != MOE_OK) return st;
