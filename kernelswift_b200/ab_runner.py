@@ -24,8 +24,10 @@ from __future__ import annotations
 
 import argparse
 import ast
+import atexit
 import importlib.util
 import json
+import shutil
 import statistics
 import sys
 import tempfile
@@ -81,6 +83,7 @@ def _ensure_torch_mlu_stub() -> None:
         pass
     if _STUB_DIR is None:
         _STUB_DIR = Path(tempfile.mkdtemp(prefix="torch_mlu_stub_"))
+        atexit.register(shutil.rmtree, str(_STUB_DIR), True)  # removed when the process ends
         pkg = _STUB_DIR / "torch_mlu"
         (pkg / "utils").mkdir(parents=True)
         (pkg / "__init__.py").write_text("")

@@ -18,7 +18,9 @@ Usage (needs the reference checkout; the outputs are committed):
 """
 from __future__ import annotations
 
+import atexit
 import importlib.util
+import shutil
 import sys
 import tempfile
 from pathlib import Path
@@ -44,6 +46,7 @@ def _stub_torch_mlu(root: Path) -> None:
 
 def load_reference_base(ref_root: Path):
     tmp = Path(tempfile.mkdtemp(prefix="torch_mlu_stub_"))
+    atexit.register(shutil.rmtree, str(tmp), True)  # removed when the process ends
     _stub_torch_mlu(tmp)
     sys.path.insert(0, str(tmp))
     spec = importlib.util.spec_from_file_location("ks_fused_moe_base", ref_root / BASE_REL)
