@@ -227,12 +227,29 @@ def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1
     return sample_tokens / med, med, torch.get_num_threads(), len(times)
 
 
-def cpu_sample_tokens(H, I, E, k, T, bias, target_s=3.0):
-    """Tokens per CPU call so that one call of the reference path takes about
-    `target_s` seconds on this host (at most the GPU batch T)."""
-    probe = min(T, 256)
-    rate, _, _, _ = cpu_reference_rate(H, I, E, k, "none", bias, probe, repeats=1, warmup=1)
-    return int(max(16, min(T, rate * target_s)))
+# Tokens per CPU call of each workload: one fixed sample, the same for the
+# cpu_baseline leg and the --impl reference arm, so both legs time the same
+# batch (about 0.2-1 s per call on a 16-core host).
+CPU_SAMPLE_TOKENS = {"mixtral": 2048, "qwen3": 1024, "qwen3-int8": 1024, "dsv3": 512,
+                     "dsv3-fp8": 512, "dsv3-fp8-ue8m0": 512}
+
+
+def cpu_sample_tokens(workload: str, T: int) -> int:
+    """Tokens per CPU call of the reference path (at most the GPU batch T)."""
+    return max(1, min(T, CPU_SAMPLE_TOKENS[workload]))
+
+
+def cpu_model() -> str:
+    """The host CPU's model string (/proc/cpuinfo), for the baseline record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
 
 
 def cpu_expert_note(H, I, E, k) -> str:
@@ -248,7 +265,7 @@ def run_reference(args, H, I, E, k, quant, T, bias, rank):
     """--impl reference: the reference's CPU torch path, rank 0 only."""
     if rank != 0:
         return
-    sample = cpu_sample_tokens(H, I, E, k, T, bias)
+    sample = cpu_sample_tokens(args.workload, T)
     rate, med, cores, n = cpu_reference_rate(H, I, E, k, quant, bias, sample,
                                              repeats=max(1, args.steps), warmup=max(0, args.warmup))
     line = {
@@ -259,6 +276,7 @@ def run_reference(args, H, I, E, k, quant, T, bias, rank):
         "config": dict(workload_config(args.workload, H, I, E, k, quant, T, args.gpus),
                        l2="not applicable: host CPU run", parallelism="single host process"),
         "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "cpu_model": cpu_model(),
                          "sample": f"{sample} tokens per step of the {args.workload} layer, "
                                    "base.py forward restated in torch-CPU bf16 with the "
                                    "per-call fp32->bf16 weight casts"
@@ -292,7 +310,6 @@ def active_switches() -> dict:
         return default if not v else v[0] != "0"  # the library's reading
     return {"pdl": not on("MOE_NO_PDL", False), "decode_path": not on("MOE_NO_DECODE_PATH", False),
             "half_tiles": on("MOE_HALF_TILES", False), "tail_split": on("MOE_TAIL_SPLIT", False),
-            "gather_tma": on("MOE_GATHER_TMA", False),
             "block_n": os.environ.get("MOE_BLOCK_N") or "planner"}
 
 
@@ -602,10 +619,11 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sample = cpu_sample_tokens(H, I, E, k, T, bias)
+        sample = cpu_sample_tokens(args.workload, T)
         rate, med, cores, n = cpu_reference_rate(H, I, E, k, quant, bias, sample, repeats=3,
                                                  min_seconds=10.0)
         cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "cpu_model": cpu_model(),
                "sample": f"{sample} tokens of the same layer per call, base.py forward "
                          f"restated in torch-CPU bf16 with its per-call weight casts "
                          f"(median of {n} calls, {med:.2f} s each)"

@@ -299,10 +299,7 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
  * (MOE_NO_PDL=1 disables it). Opt-in variants of the bf16/f16/int8 GEMMs:
  * MOE_HALF_TILES=1 (M = 64 MMAs for blocks whose second half is padding) and
  * MOE_TAIL_SPLIT=1 (the down GEMM splits the tiles of its last partial wave
- * along K; deterministic, int8 bit-exact with the default) and
- * MOE_GATHER_TMA=1 (16-bit activations: the gate-up GEMM loads its rows from
- * `hidden` with TMA tile::gather4, and the gather launch is skipped;
- * bit-exact with the default).
+ * along K; deterministic, int8 bit-exact with the default).
  * hidden, w13, w2, out, workspace and the INT8_CHANNEL / FP8_UE8M0 weight
  * scales must be 16-byte aligned (the kernels move them in 16-byte vectors
  * and bulk copies; FP8_BLOCK scales need only float alignment); otherwise

@@ -205,20 +205,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst,
       : "memory");
 }
 
-// Four rows of a 2-D tensor map whose box is one row high (rows[0..3] of the
-// outer dimension, box-width columns from c0) -> four consecutive box rows at
-// smem_dst, completion counted on `bar` (tile::gather4; no multicast). The
-// swizzle follows the destination address, as for a tiled load.
-__device__ __forceinline__ void tma_gather4(void* smem_dst, const CUtensorMap* tm, int32_t c0,
-                                            const int32_t (&rows)[4], uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::"
-      "bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(rows[0]), "r"(rows[1]), "r"(rows[2]),
-      "r"(rows[3]), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // ---------------------------------------------------------------------------
 // tcgen05 (tensor memory + 5th-generation tensor core MMA)
 // ---------------------------------------------------------------------------

@@ -86,7 +86,6 @@ struct KParams {
   uint64_t wait_limit_ns;
   float* tail_ws;           // TAIL: gridDim.x * BM * BN words of part tiles
   int32_t* tail_cnt;        // TAIL: gridDim.x counters, zero at launch
-  int32_t gather_top_k;     // GATHER: operand row m is token sorted_ids[m] / gather_top_k
 };
 
 struct TileCoord {
@@ -252,15 +251,8 @@ struct GemmCfg {
 // parts in part order, so results do not depend on timing, and runs the
 // epilogue. Workspace: gridDim.x slots of BM x BN 32-bit words, and one
 // counter per slot, zero at launch.
-// GATHER (16-bit gate-up): tmA maps the token matrix [T, K] with a box one
-// row high, and the whole of warp 0 produces: lane l loads operand rows
-// 4l..4l+3 of every A tile (token sorted_ids[m] / gather_top_k; padding
-// slots load token 0, whose products the epilogue drops) with one
-// tile::gather4 per k-block, so no gathered copy of the rows is written.
-// The align outputs come from the previous launch, so every thread waits
-// for it first (no early metadata).
 template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF = false,
-          bool TAIL = false, bool GATHER = false>
+          bool TAIL = false>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB,
@@ -324,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (and so everything downstream of them) wait, after the first weight
   // tiles have been requested.
   const bool producer = warp == 0 && lane == 0;
-  const bool early = p.early_meta && !GATHER;
+  const bool early = p.early_meta;
   if (!early) {
     pdl_wait();
     pdl_trigger();
@@ -382,67 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_trigger();
   }
 
-  if (GATHER && warp == 0) {
-    // ---------------- TMA producer, A rows gathered from the tokens ----------------
-    static_assert(!GATHER || (KIND == kKindF16 && EPI == kEpiSwiGLU && !TAIL),
-                  "gathered A rows: 16-bit gate-up only");
-    if (lane == 0) {
-      tma_prefetch_desc(&tmA);
-      tma_prefetch_desc(&tmB);
-    }
-    constexpr int kColsPerKb = kKBytes / 2;
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t issued = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < total_items; t += gridDim.x) {
-      TileCoord c;
-      int kb0, kb1;
-      item(t, c, kb0, kb1);
-      const int e = __ldg(p.expert_ids + c.mb);
-      if (e < 0 || e >= p.num_experts) continue;
-      // this lane's four operand rows -> their token rows
-      int32_t rows[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = __ldg(p.sorted_ids + c.mb * BM + 4 * lane + j);
-        rows[j] = (r >= 0 && r < p.numel) ? r / p.gather_top_k : 0;
-      }
-      const int b_row = e * p.n_total + c.nt * BN;
-      for (int kb = kb0; kb < kb1; ++kb) {
-        const int kcol = kb * kColsPerKb;
-        bool free_slot = true;
-        if (lane == 0)
-          free_slot = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, limit);
-        if (!__shfl_sync(0xffffffffu, free_slot, 0)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kcol, b_row, &full[stage]);
-        }
-        __syncwarp();  // the stage's byte count is posted before any row lands
-        // rows 4 lane .. 4 lane + 3 of the tile: kKBytes per row
-        tma_gather4(sA + stage * kABytes + 4 * lane * kKBytes, &tmA, kcol, rows, &full[stage]);
-        ++issued;
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-    }
-    // Drain (lane 0): every load issued into a stage has landed before exit.
-    if (lane == 0) {
-      for (int s = 0; s < STAGES; ++s) {
-        const uint32_t n_s = issued / STAGES + (uint32_t(s) < issued % STAGES ? 1u : 0u);
-        if (n_s == 0) continue;
-        volatile int no_abort = 0;
-        mbar_wait_bounded(&full[s], (n_s - 1) & 1u, &no_abort, limit);
-      }
-    }
-    __syncwarp();
-  } else if (producer) {
+  if (producer) {
     // ---------------- TMA producer ----------------
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -1214,10 +1146,9 @@ struct MxCfg {
   static_assert(kSfCol0 + kStages * kSfCols <= 512, "TMEM columns");
 };
 
-// HALF: as in moe_grouped_gemm_kernel, M = 64 MMAs for m-blocks whose rows
-// 64..127 are padding; their A scale factors are the first two columns of
-// the same slot (rows 0-63 of the chunk).
-template <int BN, int EPI, typename TOUT, bool HALF = false>
+// Block-scaled MMAs exist with M = 128 only (one CTA), so every m-block runs
+// full-height tiles here, padding rows included.
+template <int BN, int EPI, typename TOUT>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_grouped_gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA,
                                const __grid_constant__ CUtensorMap tmB, const KParams p) {
@@ -1225,7 +1156,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGES = Cfg::kStages;
   constexpr int NACC = Cfg::kNAcc;
   constexpr uint32_t IDESC = make_idesc_mx(BM, BN);
-  constexpr uint32_t IDESC_HALF = make_idesc_mx(BM / 2, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -1381,9 +1311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-      uint32_t idesc_tile = IDESC;
-      if constexpr (HALF)
-        if (__ldg(p.sorted_ids + c.mb * BM + BM / 2) >= p.numel) idesc_tile = IDESC_HALF;
+      const uint32_t idesc_tile = IDESC;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag, limit)) {
           ok = false;
@@ -1433,18 +1361,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, limit);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      int m, r;
-      bool valid;
-      if constexpr (HALF) {
-        const bool half = __ldg(p.sorted_ids + c.mb * BM + BM / 2) >= p.numel;
-        m = c.mb * BM + (half ? q * 16 + (lane & 15) : row);
-        r = __ldg(p.sorted_ids + m);
-        valid = (!half || lane < 16) && r < p.numel;
-      } else {
-        m = c.mb * BM + row;
-        r = __ldg(p.sorted_ids + m);
-        valid = r < p.numel;
-      }
+      const int m = c.mb * BM + row;
+      const int r = __ldg(p.sorted_ids + m);
+      const bool valid = r < p.numel;
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
       if constexpr (EPI == kEpiSwiGLU) {
         constexpr int G_HALF = BN / 64;
@@ -1552,12 +1471,11 @@ int set_smem_once(Kern kern, size_t bytes, std::atomic<uint64_t>& done) {
   return MOE_OK;
 }
 
-template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF, bool TAIL = false,
-          bool GATHER = false>
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF, bool TAIL = false>
 int launch_kernel_v(const CUtensorMap& ta, const CUtensorMap& tb,
                     const KParams& kp, int grid, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
-  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT, HALF, TAIL, GATHER>;
+  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT, HALF, TAIL>;
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
@@ -1578,15 +1496,6 @@ bool half_tiles_enabled() {
 template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
                   const KParams& kp, int grid, cudaStream_t s) {
-  if constexpr (EPI == kEpiSwiGLU && KIND == kKindF16) {
-    // A rows gathered from the token matrix by the kernel itself
-    if (kp.gather_top_k > 0) {
-      if (half_tiles_enabled())
-        return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, true, false, true>(ta, tb, kp, grid,
-                                                                               s);
-      return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, false, false, true>(ta, tb, kp, grid, s);
-    }
-  }
   if constexpr (EPI == kEpiRows) {
     // the tail split's workspace is sized for one slot per CTA
     if (kp.tail_ws != nullptr && kp.tail_cnt != nullptr && kp.splits == 1) {
@@ -1605,15 +1514,6 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
 bool tail_split_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("MOE_TAIL_SPLIT");
-    return v && v[0] && v[0] != '0';
-  }();
-  return on;
-}
-// MOE_GATHER_TMA=1: the 16-bit gate-up GEMM loads its A rows from the token
-// matrix with tile::gather4 instead of after a gather pass (not yet measured).
-bool gather_tma_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("MOE_GATHER_TMA");
     return v && v[0] && v[0] != '0';
   }();
   return on;
@@ -1655,25 +1555,16 @@ int dispatch_fp8(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const KPa
   }
 }
 
-template <int BN, int EPI, typename TOUT, bool HALF>
-int launch_mx_v(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
-                cudaStream_t s) {
+template <int BN, int EPI, typename TOUT>
+int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+              cudaStream_t s) {
   using Cfg = MxCfg<BN>;
-  auto kern = moe_grouped_gemm_mx_kernel<BN, EPI, TOUT, HALF>;
+  auto kern = moe_grouped_gemm_mx_kernel<BN, EPI, TOUT>;
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
   KSW_LAUNCH(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, s, ta, tb, kp);
   return MOE_OK;
-}
-
-bool half_tiles_enabled();
-
-template <int BN, int EPI, typename TOUT>
-int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
-              cudaStream_t s) {
-  if (half_tiles_enabled()) return launch_mx_v<BN, EPI, TOUT, true>(ta, tb, kp, grid, s);
-  return launch_mx_v<BN, EPI, TOUT, false>(ta, tb, kp, grid, s);
 }
 
 template <int EPI, typename TOUT>
@@ -1760,11 +1651,8 @@ int operand_types(const GroupedGemmArgs& a, OperandTypes* ot) {
 int make_maps(const GroupedGemmArgs& a, const OperandTypes& ot, int bn,
               CUtensorMap* ta, CUtensorMap* tb) {
   const uint32_t box_k = uint32_t(kKBytes / ot.elem_bytes);
-  // gathered A: the token matrix, loaded four one-row boxes at a time
-  const bool gather = a.gather_top_k > 0;
-  int st = encode_tma_2d(ta, ot.tma_type, ot.elem_bytes, a.a, uint64_t(a.k),
-                         uint64_t(gather ? a.a_rows : a.rows), uint64_t(a.k), box_k,
-                         gather ? 1u : uint32_t(BM));
+  int st = encode_tma_2d(ta, ot.tma_type, ot.elem_bytes, a.a, uint64_t(a.k), uint64_t(a.rows),
+                         uint64_t(a.k), box_k, uint32_t(BM));
   if (st != MOE_OK) return st;
   return encode_tma_2d(tb, ot.tma_type, ot.elem_bytes, a.b, uint64_t(a.k),
                        uint64_t(a.num_experts) * uint64_t(a.n), uint64_t(a.k),
@@ -1797,7 +1685,6 @@ KParams base_params(const GroupedGemmArgs& a, int elem_bytes) {
   kp.wait_limit_ns = kWaitLimitNs;
   kp.tail_ws = a.tail_ws;
   kp.tail_cnt = a.tail_cnt;
-  kp.gather_top_k = a.gather_top_k;
   return kp;
 }
 
@@ -1825,10 +1712,6 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
               "gate-up GEMM: hidden size * element size must be a multiple of 16 B");
   const bool mx = a.quant == MOE_QUANT_FP8_UE8M0;
   const bool fp8 = a.quant == MOE_QUANT_FP8_BLOCK || mx;
-  if (a.gather_top_k > 0)
-    KSW_REQUIRE(a.quant == MOE_QUANT_NONE && a.a_rows >= 1 && a.a_rows < (int64_t(1) << 31),
-                MOE_ERR_INVALID_ARG,
-                "gate-up GEMM: gathered A rows need 16-bit operands and 1 <= token rows < 2^31");
   if (fp8)
     KSW_REQUIRE(a.n % 256 == 0, MOE_ERR_UNSUPPORTED,
                 "fp8 gate-up GEMM: I must be a multiple of 128");
@@ -1876,8 +1759,6 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
                   a.row_weights_dtype == MOE_DTYPE_BF16,
               MOE_ERR_INVALID_ARG, "down GEMM: row weights must be f32/f16/bf16");
   KSW_REQUIRE(a.splits >= 1, MOE_ERR_INVALID_ARG, "down GEMM: splits must be >= 1");
-  KSW_REQUIRE(a.gather_top_k == 0, MOE_ERR_INVALID_ARG,
-              "down GEMM (and split gate-up): A rows must be pre-gathered");
   OperandTypes ot;
   st = operand_types(a, &ot);
   if (st != MOE_OK) return st;

@@ -54,19 +54,10 @@ struct GroupedGemmArgs {
   // must be zero at launch), or null
   float* tail_ws;
   int32_t* tail_cnt;
-  // gate-up GEMM with 16-bit operands only: when > 0, `a` is the token
-  // matrix [a_rows, K] itself and operand row m is token
-  // sorted_ids[m] / gather_top_k, loaded by TMA tile::gather4 (no gather
-  // pass); 0: `a` holds the operand rows in expert-sorted order
-  int gather_top_k;
-  int64_t a_rows;
 };
 
 // Tail splitting of the down GEMM (MOE_TAIL_SPLIT=1; off by default).
 bool tail_split_enabled();
-// Gate-up A rows gathered by TMA from the token rows (MOE_GATHER_TMA=1; off
-// by default).
-bool gather_tma_enabled();
 size_t tail_ws_bytes(int sms, int bn);   // part tiles
 size_t tail_cnt_bytes(int sms);          // counters
 

@@ -4,9 +4,7 @@
 // launches instead when at most 16 rows are routed, csrc/decode.cu):
 //
 //   1. align      topk_ids -> sorted_token_ids, expert_ids, num_post_pad
-//   2. gather     hidden rows in expert-sorted order (+cast / quantise);
-//                 skipped under MOE_GATHER_TMA=1 for 16-bit activations, where
-//                 the gate-up GEMM loads the token rows itself
+//   2. gather     hidden rows in expert-sorted order (+cast / quantise)
 //   3. gate-up    grouped tcgen05 GEMM, SiLU(gate)*up fused      [L, I]
 //   4. (quant)    per-row quantisation of the activation (W8A8 modes)
 //   5. down       grouped tcgen05 GEMM, topk weight fused, optional K split
@@ -38,7 +36,6 @@ struct Plan {
   int part_dtype;        // dtype of the down GEMM's weighted rows
   size_t align_ws;
   bool tail;             // down GEMM splits its last partial wave along K
-  bool gather_fused;     // the gate-up GEMM gathers its A rows itself (no gather pass)
   int sms;
   size_t off_sorted, off_eids, off_npp, off_align, off_a, off_a_scale, off_act,
       off_act_q, off_act_scale, off_part, off_gu_part, off_tail_ws, off_tail_cnt, total;
@@ -210,8 +207,6 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.off_part = take(size_t(P.splits) * P.numel * P.H * elem_bytes(P.part_dtype));
   P.off_gu_part = take(P.gu_splits > 1 ? size_t(P.gu_splits) * P.numel * 2 * P.I * 4 : 0);
   P.sms = sms;
-  P.gather_fused = gather_tma_enabled() && P.quant == MOE_QUANT_NONE &&
-                   p->act_dtype == P.compute_dtype && P.gu_splits == 1;
   P.tail = tail_split_enabled() && P.splits == 1 && P.quant != MOE_QUANT_FP8_BLOCK &&
            P.quant != MOE_QUANT_FP8_UE8M0;
   P.off_tail_ws = take(P.tail ? tail_ws_bytes(sms, P.dn_bn) : 0);
@@ -353,10 +348,8 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   g.dst_dtype = P.a_dtype;
   g.scale = P.quant == MOE_QUANT_NONE ? nullptr : at<float>(workspace, P.off_a_scale);
   KSW_MARK(MOE_STAGE_GATHER);
-  if (!P.gather_fused) {
-    st = gather_launch(g, s);
-    if (st != MOE_OK) return st;
-  }
+  st = gather_launch(g, s);
+  if (st != MOE_OK) return st;
 
   KSW_MARK(MOE_STAGE_GATE_UP);
   GroupedGemmArgs ga{};
@@ -378,13 +371,6 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   ga.splits = 1;
   ga.status = p->status;
   ga.early_meta = 1;  // align ran two launches earlier (the gather is between)
-  if (P.gather_fused) {
-    // the GEMM reads the token rows itself, right after align
-    ga.a = p->hidden;
-    ga.gather_top_k = P.k;
-    ga.a_rows = P.T;
-    ga.early_meta = 0;
-  }
   if (P.gu_splits > 1) {
     // decode-sized: split K, unweighted fp32 partial rows, then SiLU*up
     GroupedGemmArgs gs = ga;
@@ -495,7 +481,7 @@ int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launc
     return MOE_OK;
   }
   int n = (P.numel <= align_small_max() ? 1 : 3);      // align
-  n += P.gather_fused ? 0 : 1;                          // gather
+  n += 1;                                               // gather
   n += P.gu_splits > 1 ? 2 : 1;                         // gate-up (+ swiglu_reduce)
   n += P.quant != MOE_QUANT_NONE ? 1 : 0;               // activation quantisation
   n += 1;                                               // down

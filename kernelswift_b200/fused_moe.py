@@ -506,14 +506,23 @@ class ModelNew(nn.Module):
         self._prepared: dict = {}
 
     def prepared(self, act_dtype: torch.dtype, quant: str = "none") -> PreparedWeights:
+        """The prepared weights for this activation dtype, made once per
+        weight version. An entry also holds weak references to the w1/w2
+        objects it was made from, so a parameter replaced by a new tensor
+        that happens to reuse the old address (version 0 again) is
+        prepared afresh instead of matching the stale entry."""
         compute = torch.float16 if act_dtype == torch.float16 else torch.bfloat16
-        key = (quant, compute, self.w1.data_ptr(), self.w1._version, self.w2.data_ptr(),
-               self.w2._version)
-        prep = self._prepared.get(key)
-        if prep is None:
-            self._prepared.clear()
-            prep = prepare_weights(self.w1, self.w2, quant, compute)
-            self._prepared[key] = prep
+        w1, w2 = self.w1, self.w2
+        key = (quant, compute, w1.data_ptr(), w1._version, tuple(w1.shape), w1.dtype,
+               w2.data_ptr(), w2._version, tuple(w2.shape), w2.dtype)
+        hit = self._prepared.get(key)
+        if hit is not None:
+            prep, r1, r2 = hit
+            if r1() is w1 and r2() is w2:
+                return prep
+        self._prepared.clear()
+        prep = prepare_weights(w1, w2, quant, compute)
+        self._prepared[key] = (prep, weakref.ref(w1), weakref.ref(w2))
         return prep
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:

@@ -14,12 +14,13 @@ a leftover import; a stub package is written to a temporary directory and put
 on sys.path so the module loads under stock torch.
 
 Usage (needs the reference checkout; the outputs are committed):
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py <reference checkout>  (or set KS_REFERENCE_ROOT)
 """
 from __future__ import annotations
 
 import atexit
 import importlib.util
+import os
 import shutil
 import sys
 import tempfile
@@ -32,8 +33,16 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
 from cases import CASES, digest, make_inputs  # noqa: E402
 
-DEFAULT_REF = Path("/root/reference")
 BASE_REL = Path("kernels/track1-triton/fused_moe/base.py")
+
+
+def reference_checkout() -> Path:
+    """The reference checkout: the first argument, else KS_REFERENCE_ROOT."""
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KS_REFERENCE_ROOT")
+    if not arg:
+        raise SystemExit("usage: give the reference checkout as the first argument "
+                         "or in KS_REFERENCE_ROOT")
+    return Path(arg)
 
 
 def _stub_torch_mlu(root: Path) -> None:
@@ -56,7 +65,7 @@ def load_reference_base(ref_root: Path):
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REF
+    ref_root = reference_checkout()
     base = load_reference_base(ref_root)
     torch.set_num_threads(8)
     for c in CASES:

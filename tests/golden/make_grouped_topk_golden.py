@@ -8,11 +8,12 @@ cases.GROUPED_CASES and stores, per case:
   digest        SHA-256 of the regenerated inputs
 
 Usage (needs the reference checkout; the outputs are committed):
-    python tests/golden/make_grouped_topk_golden.py [/path/to/reference]
+    python tests/golden/make_grouped_topk_golden.py <reference checkout>  (or set KS_REFERENCE_ROOT)
 """
 from __future__ import annotations
 
 import importlib.util
+import os
 import sys
 from pathlib import Path
 
@@ -23,12 +24,20 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
 from cases import GROUPED_CASES, digest, make_grouped_inputs  # noqa: E402
 
-DEFAULT_REF = Path("/root/reference")
 BASE_REL = Path("kernels/track1-triton/groupedtopk/base.py")
 
 
+def reference_checkout() -> Path:
+    """The reference checkout: the first argument, else KS_REFERENCE_ROOT."""
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KS_REFERENCE_ROOT")
+    if not arg:
+        raise SystemExit("usage: give the reference checkout as the first argument "
+                         "or in KS_REFERENCE_ROOT")
+    return Path(arg)
+
+
 def main() -> None:
-    ref_root = Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REF
+    ref_root = reference_checkout()
     spec = importlib.util.spec_from_file_location("ks_grouped_topk_base", ref_root / BASE_REL)
     base = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(base)

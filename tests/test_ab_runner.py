@@ -6,6 +6,8 @@ from pathlib import Path
 import pytest
 import torch
 
+from conftest import reference_file
+
 from kernelswift_b200 import ab_runner
 
 V0 = '''
@@ -66,14 +68,11 @@ def test_compare_semantics():
     assert ab_runner.compare(a, a[:1], 1e-2, 1e-2)
 
 
-REF = Path("/root/reference/kernels/track1-triton/fused_moe/base.py")
-
-
-@pytest.mark.skipif(not REF.exists(), reason="reference checkout not present")
 def test_loads_the_reference_operator_module():
     """fused_moe/base.py under the filter, with the torch_mlu stub: its Model
     builds and runs on the CPU."""
-    mod = ab_runner.load_module(REF, "ref_fused_moe")
+    ref = reference_file("kernels/track1-triton/fused_moe/base.py")
+    mod = ab_runner.load_module(ref, "ref_fused_moe")
     m = mod.Model(*mod.get_init_inputs())
     x = ab_runner._cpu_inputs(mod)
     with torch.no_grad():

@@ -45,11 +45,10 @@ def test_cpu_baseline_memory_cap():
 
 def test_switch_record(monkeypatch):
     for name in ("MOE_NO_PDL", "MOE_NO_DECODE_PATH", "MOE_HALF_TILES", "MOE_TAIL_SPLIT",
-                 "MOE_GATHER_TMA", "MOE_BLOCK_N"):
+                 "MOE_BLOCK_N"):
         monkeypatch.delenv(name, raising=False)
     assert bench.active_switches() == {"pdl": True, "decode_path": True, "half_tiles": False,
-                                       "tail_split": False, "gather_tma": False,
-                                       "block_n": "planner"}
+                                       "tail_split": False, "block_n": "planner"}
     monkeypatch.setenv("MOE_NO_PDL", "1")
     monkeypatch.setenv("MOE_TAIL_SPLIT", "0")
     monkeypatch.setenv("MOE_HALF_TILES", "1")
@@ -72,3 +71,14 @@ def test_reference_arm_json_line():
         assert key in line, key
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
+
+
+def test_cpu_sample_is_fixed_per_workload():
+    """Both CPU legs (cpu_baseline and --impl reference) time the same fixed
+    batch of each workload, capped at the GPU batch."""
+    assert set(bench.CPU_SAMPLE_TOKENS) == set(bench.WORKLOADS)
+    for name, (_, _, _, _, _, T, _) in bench.WORKLOADS.items():
+        n = bench.cpu_sample_tokens(name, T)
+        assert 1 <= n <= T and n == bench.cpu_sample_tokens(name, T)
+    assert bench.cpu_sample_tokens("mixtral", 64) == 64
+    assert isinstance(bench.cpu_model(), str) and bench.cpu_model()

@@ -6,6 +6,8 @@ from pathlib import Path
 
 import pytest
 
+from conftest import reference_file
+
 ROOT = Path(__file__).resolve().parent.parent
 V1 = ROOT / "kernelswift_b200" / "ks_fused_moe.py"
 V1_GTK = ROOT / "kernelswift_b200" / "ks_grouped_topk.py"
@@ -38,9 +40,7 @@ def test_v1_module_defines_the_contract():
 def test_v1_loads_through_the_real_harness_loader():
     """If the reference checkout is present, load the v1 file with
     auto_bench's own loader (its AST filter and exec)."""
-    ab = Path("/root/reference/auto_bench.py")
-    if not ab.exists():
-        pytest.skip("reference checkout not present")
+    ab = reference_file("auto_bench.py")
     spec = importlib.util.spec_from_file_location("ks_auto_bench", ab)
     harness = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(harness)
@@ -62,9 +62,7 @@ def test_grouped_topk_module_defines_the_contract():
 
 @pytest.mark.parametrize("path", [V1, V1_GTK], ids=lambda p: p.name)
 def test_loads_through_the_real_harness_loader(path):
-    ab = Path("/root/reference/auto_bench.py")
-    if not ab.exists():
-        pytest.skip("reference checkout not present")
+    ab = reference_file("auto_bench.py")
     spec = importlib.util.spec_from_file_location("ks_auto_bench2", ab)
     harness = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(harness)

@@ -237,36 +237,6 @@ def test_plan_switches_in_a_child_process():
     assert narrow[0]["down_block_n"] == 64 and narrow[2]["down_block_n"] in (128, 256)
 
 
-def test_gather_tma_switch_drops_the_gather_launch():
-    """MOE_GATHER_TMA=1: the 16-bit gate-up GEMM gathers its own A rows, so
-    the forward has no gather launch; quantised paths (their gather also
-    quantises), f32 activations (cast in the gather) and the split gate-up
-    keep it."""
-    import json
-    import subprocess
-    import sys
-    from pathlib import Path
-
-    root = Path(__file__).resolve().parent.parent
-    code = ("import json, sys, torch; sys.path.insert(0, %r)\n"
-            "from kernelswift_b200 import fused_moe as fm\n"
-            "print(json.dumps([fm.fused_experts_launches(*a) for a in [\n"
-            "  (4096, 4096, 14336, 8, 2), (8192, 2048, 768, 128, 8),\n"
-            "  (4096, 7168, 2048, 256, 8, 'fp8'), (8192, 2048, 768, 128, 8, 'int8'),\n"
-            "  (64, 2048, 768, 128, 8)]] + [fm.fused_experts_launches(\n"
-            "  4096, 4096, 14336, 8, 2, dtype=torch.float32)]))\n" % str(root))
-
-    def launches(**env):
-        res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
-                             env=dict(os.environ, **env), timeout=300)
-        assert res.returncode == 0, res.stderr[-2000:]
-        return json.loads(res.stdout.strip().splitlines()[-1])
-
-    plain = launches(MOE_GATHER_TMA="0")
-    fused = launches(MOE_GATHER_TMA="1")
-    assert [a - b for a, b in zip(plain, fused)] == [1, 1, 0, 0, 0, 0]
-
-
 def test_ep_plan_workspace_query_without_gpu():
     lib = _lib.load()
     n = ctypes.c_size_t(123)

@@ -3,9 +3,6 @@ more than 8192 slots) against the single-CTA plan (moe_ep_plan) bit for
 bit, and against a CPU restatement, for several rank counts, int32/int64
 ids and ids outside [0, E). The plan is a pure function of the ids, so one
 GPU covers any rank count.
-
-The multi-CTA plan has not yet been run on a B200, so these tests only run
-with MOE_TEST_EP_PLAN=1 until it has passed them there once.
 """
 import ctypes
 import os
@@ -15,12 +12,7 @@ import torch
 
 from kernelswift_b200 import _lib
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("MOE_TEST_EP_PLAN") != "1",
-                       reason="multi-CTA EP plan not yet run on a B200; "
-                              "set MOE_TEST_EP_PLAN=1 to run it"),
-]
+pytestmark = pytest.mark.gpu
 
 
 def p(t):

@@ -6,8 +6,7 @@ k-block) once, tail items land on distinct CTAs within the grid's last
 pass, workspace slots stay inside the gridDim.x slots and are unique, no
 part is empty, and adding the parts in part order equals the whole-tile sum.
 Half tiles (HALF): the half-empty test of an m-block agrees with align's
-layout. Gathered A rows (GATHER): the producer lanes' gather4 loads cover an
-A tile's rows and bytes once, with token rows in range."""
+layout."""
 import random
 
 import pytest
@@ -123,31 +122,3 @@ def test_half_tile_rule_matches_align_layout():
             n = int(valid.sum())
             assert n > 0 and bool(valid[:n].all()), "valid rows are not a prefix"
             assert (int(blk[64]) >= numel) == (n <= 64)
-
-
-def test_gathered_a_rows_cover_the_tile_once():
-    """GATHER: lane l of the producer warp loads operand rows 4l..4l+3 of an
-    A tile with one tile::gather4 into bytes [512 l, 512 l + 512) of the
-    stage (128-byte rows, 16 KB stage): the 32 lanes cover the 128 rows and
-    the stage exactly once, and every row index handed to the tensor map is
-    a token row in [0, T) (padding slots read token 0)."""
-    import torch
-
-    from oracle import moe_oracle as orc
-
-    BM, ROW_BYTES, STAGE_BYTES = 128, 128, 128 * 128
-    rows_seen, bytes_seen = [], []
-    for lane in range(32):
-        rows_seen += [4 * lane + j for j in range(4)]
-        dst = 4 * lane * ROW_BYTES
-        bytes_seen += list(range(dst, dst + 4 * ROW_BYTES))
-    assert sorted(rows_seen) == list(range(BM))
-    assert sorted(bytes_seen) == list(range(STAGE_BYTES))
-    g = torch.Generator().manual_seed(7)
-    for T, E, k in [(1, 8, 2), (37, 8, 2), (300, 16, 4), (1000, 64, 8)]:
-        _, ids = orc.route(torch.randn(T, E, generator=g), k)
-        sorted_ids, _, npp = orc.moe_align(ids, E, BM)
-        numel = T * k
-        s = torch.as_tensor(sorted_ids)[:int(npp)]
-        tok = torch.where((s >= 0) & (s < numel), s // k, torch.zeros_like(s))
-        assert int(tok.min()) >= 0 and int(tok.max()) < T

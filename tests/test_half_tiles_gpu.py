@@ -1,11 +1,9 @@
 """GPU: the M = 64 tile variant of the grouped GEMMs (MOE_HALF_TILES=1): an
-m-block whose rows 64..127 are all padding runs half-height MMAs (bf16,
-int8 and the UE8M0 block-scaled kernel). The layer
-must match the fp32 oracle within the bf16 tolerance and agree with the
-default M = 128 path (run in a child process without the switch).
-
-The variant has not yet been run on a B200, so these tests only run with
-MOE_TEST_HALF_TILES=1 until it has passed them there once.
+m-block whose rows 64..127 are all padding runs half-height MMAs (bf16, f16
+and int8; block-scaled MMAs exist with M = 128 only, so the UE8M0 kernel
+ignores the switch, which a UE8M0 case checks). The layer must match the
+fp32 oracle within the bf16 tolerance and agree with the default M = 128
+path (run in a child process without the switch).
 """
 import os
 import subprocess
@@ -15,12 +13,7 @@ from pathlib import Path
 import pytest
 import torch
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("MOE_TEST_HALF_TILES") != "1",
-                       reason="M = 64 tile variant not yet run on a B200; "
-                              "set MOE_TEST_HALF_TILES=1 to run it"),
-]
+pytestmark = pytest.mark.gpu
 
 TOL = dict(rtol=2e-2, atol=2e-2)
 ROOT = Path(__file__).resolve().parent.parent

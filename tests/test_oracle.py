@@ -129,3 +129,16 @@ def test_grouped_topk_matches_reference(case):
                               case.topk_group, case.scoring_func, case.routed_scaling_factor)
     assert torch.equal(ids, torch.from_numpy(ref["topk_ids"]))
     assert torch.equal(w, torch.from_numpy(ref["topk_weights"]))
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: c.name)
+def test_native_forward_matches_reference(case):
+    """model_forward_native -- base.py's forward restated op for op in the
+    activation dtype, the CPU path bench.py times as the reference arm --
+    gives base.py's own outputs: the same torch ops in the same order on
+    the same inputs, so bit for bit."""
+    hidden, logits, w1, w2 = make_inputs(case)
+    out = orc.model_forward_native(hidden, logits, w1, w2, case.k, case.renormalize)
+    ref = torch.from_numpy(load(case)["out"])
+    assert out.dtype == case.dtype
+    assert torch.equal(out.float(), ref)

@@ -4,9 +4,6 @@ that completes a tile last adds the parts in part order. The layer must match
 the fp32 oracle within the bf16 tolerance (int8: 5e-2 relative L2 against
 the dequantised oracle), agree with the default path (child process without
 the switch), and repeat bit for bit.
-
-The variant has not yet been run on a B200, so these tests only run with
-MOE_TEST_TAIL_SPLIT=1 until it has passed them there once.
 """
 import os
 import subprocess
@@ -16,12 +13,7 @@ from pathlib import Path
 import pytest
 import torch
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("MOE_TEST_TAIL_SPLIT") != "1",
-                       reason="tail split not yet run on a B200; "
-                              "set MOE_TEST_TAIL_SPLIT=1 to run it"),
-]
+pytestmark = pytest.mark.gpu
 
 TOL = dict(rtol=2e-2, atol=2e-2)
 ROOT = Path(__file__).resolve().parent.parent
