@@ -309,7 +309,6 @@ def active_switches() -> dict:
         v = os.environ.get(name)
         return default if not v else v[0] != "0"  # the library's reading
     return {"pdl": not on("MOE_NO_PDL", False), "decode_path": not on("MOE_NO_DECODE_PATH", False),
-            "half_tiles": on("MOE_HALF_TILES", False), "tail_split": on("MOE_TAIL_SPLIT", False),
             "block_n": os.environ.get("MOE_BLOCK_N") or "planner"}
 
 

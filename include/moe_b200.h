@@ -187,9 +187,12 @@ int moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel,
  * MOE_ERR_UNSUPPORTED and a message; up to 8192 ids need no scratch at all.
  * The first call on each device looks up the array's device address with
  * cudaGetSymbolAddress (that device must be current) and should come before
- * any stream capture. All calls share the array: calls whose work overlaps
- * on the GPU race on it, so order them on one stream or with events. Nothing
- * in the array has to start at zero.
+ * any stream capture. The address is kept for the life of the process: after
+ * cudaDeviceReset of a device (or any teardown of its primary context) the
+ * library may be loaded again at another address, so do not call this entry
+ * point on that device again in the same process. All calls share the
+ * array: calls whose work overlaps on the GPU race on it, so order them on
+ * one stream or with events. Nothing in the array has to start at zero.
  */
 #define MOE_ALIGN_NOALLOC_SCRATCH_BYTES (1u << 20)
 int moe_align_block_size_noalloc(const void* topk_ids, int ids_dtype,
@@ -296,10 +299,7 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
  * of weights to stream, two weight-streaming CUDA-core kernels do the whole
  * computation instead (fp32 dot products; MOE_NO_DECODE_PATH=1 disables
  * them). Kernels are launched with programmatic dependent launch
- * (MOE_NO_PDL=1 disables it). Opt-in variants of the bf16/f16/int8 GEMMs:
- * MOE_HALF_TILES=1 (M = 64 MMAs for blocks whose second half is padding) and
- * MOE_TAIL_SPLIT=1 (the down GEMM splits the tiles of its last partial wave
- * along K; deterministic, int8 bit-exact with the default).
+ * (MOE_NO_PDL=1 disables it).
  * hidden, w13, w2, out, workspace and the INT8_CHANNEL / FP8_UE8M0 weight
  * scales must be 16-byte aligned (the kernels move them in 16-byte vectors
  * and bulk copies; FP8_BLOCK scales need only float alignment); otherwise
@@ -326,8 +326,7 @@ int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launc
 /* The plan moe_fused_experts makes for `p` (pointers unused; answers without
  * a GPU, for 148 SMs): info[0] gate-up tile width, [1] gate-up K splits,
  * [2] down tile width, [3] down K splits, [4] dtype of the down GEMM's rows,
- * [5] 1 when the down GEMM splits its last partial wave along K
- * (MOE_TAIL_SPLIT=1), [6] 1 when the decode kernels run instead of the GEMM
+ * [5] reserved (0), [6] 1 when the decode kernels run instead of the GEMM
  * pipeline, [7] SMs planned for. No reference counterpart (inspection aid). */
 int moe_fused_experts_plan(const moe_problem_t* p, int32_t* info);
 

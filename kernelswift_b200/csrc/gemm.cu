@@ -84,8 +84,6 @@ struct KParams {
   int32_t up_offset;        // gate-up: original row of the first up row (= I)
   int32_t early_meta;       // see GroupedGemmArgs::early_meta
   uint64_t wait_limit_ns;
-  float* tail_ws;           // TAIL: gridDim.x * BM * BN words of part tiles
-  int32_t* tail_cnt;        // TAIL: gridDim.x counters, zero at launch
 };
 
 struct TileCoord {
@@ -239,20 +237,7 @@ struct GemmCfg {
 
 // KIND: kKindF16 (AB_FMT 0 = f16, 1 = bf16) or kKindI8 (AB_FMT 1 = s8).
 // TOUT: element type of the gate-up output (f16/bf16).
-// HALF: an m-block whose rows 64..127 are all padding (valid rows come first
-// in every expert's blocks, so sorted_ids[block + 64] is the sentinel) runs
-// M = 64 MMAs, half the tensor work. Their accumulator rows sit in the first
-// 16 lanes of each 32-lane quarter (row 16 q + l at lane 32 q + l), so the
-// epilogue maps its rows accordingly.
-// TAIL (weighted-rows epilogue without K split): the tiles of the last,
-// partial wave are split along K over the SMs that would idle (stream-K for
-// the tail). Each part stores its raw accumulator tile in a workspace slot;
-// the part that completes a tile last (an atomic counter per tile) adds the
-// parts in part order, so results do not depend on timing, and runs the
-// epilogue. Workspace: gridDim.x slots of BM x BN 32-bit words, and one
-// counter per slot, zero at launch.
-template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF = false,
-          bool TAIL = false>
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB,
@@ -261,7 +246,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGES = Cfg::kStages;
   constexpr uint32_t D_FMT = (KIND == kKindI8) ? 2u : 1u;
   constexpr uint32_t IDESC = make_idesc(D_FMT, AB_FMT, BM, BN);
-  constexpr uint32_t IDESC_HALF = make_idesc(D_FMT, AB_FMT, BM / 2, BN);
   constexpr bool kScaled = (KIND == kKindI8);
 
   extern __shared__ uint8_t smem_raw[];
@@ -276,10 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* final_bar = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // TAIL: [0] all epilogue threads stored their part, [1] the counter was read
-  uint64_t* tail_bar = reinterpret_cast<uint64_t*>(tmem_slot + 2);
-  volatile int* tail_last = reinterpret_cast<volatile int*>(tail_bar + 2);
-  static_assert(8 * (2 * STAGES + 5) + 8 + 16 + 4 <= 256, "barrier area");
+  static_assert(8 * (2 * STAGES + 5) + 8 <= 256, "barrier area");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -294,10 +275,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[b], 256);
     }
     mbar_init(final_bar, 1);
-    if constexpr (TAIL) {
-      mbar_init(&tail_bar[0], 256);
-      mbar_init(&tail_bar[1], 1);
-    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -333,41 +310,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     return use_tab ? tile_coord_tab(t, n_tiles, p.splits, gtab)
                    : tile_coord(t, num_mb, n_tiles, p.splits);
   };
-  // Work items: the tiles, except that with TAIL the R tiles of the last
-  // partial wave become R * parts items of about k_blocks / parts k-blocks
-  // each (R * parts <= gridDim.x: one item per otherwise idle CTA). Every
-  // CTA derives the same split from num_mb.
-  int tail_start = total_tiles, parts = 1, per_part = 0;
-  if constexpr (TAIL) {
-    const int G = int(gridDim.x);
-    const int R = total_tiles % G;
-    if (p.tail_ws != nullptr && p.splits == 1 && R > 0) {
-      const int f = min(G / R, p.k_blocks);
-      if (f >= 2) {
-        per_part = (p.k_blocks + f - 1) / f;
-        const int fe = (p.k_blocks + per_part - 1) / per_part;  // no empty part
-        if (fe >= 2) {
-          parts = fe;
-          tail_start = total_tiles - R;
-        }
-      }
-    }
-  }
-  const int total_items = tail_start + (total_tiles - tail_start) * parts;
-  // item i -> tile coordinates, its k-block range and its part (-1: a whole tile)
-  auto item = [&](int i, TileCoord& c, int& kb0, int& kb1) -> int {
-    if (TAIL && i >= tail_start) {
-      const int j = (i - tail_start) / parts;
-      const int part = (i - tail_start) - j * parts;
-      c = coord(tail_start + j);
-      kb0 = part * per_part;
-      kb1 = min(kb0 + per_part, p.k_blocks);
-      return part;
-    }
+  // tile t -> its coordinates and k-block range
+  const int total_items = total_tiles;
+  auto item = [&](int i, TileCoord& c, int& kb0, int& kb1) {
     c = coord(i);
     kb0 = c.ks * p.kb_per_split;
     kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
-    return -1;
   };
   if (early && !producer) {
     pdl_wait();
@@ -459,9 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-      uint32_t idesc = IDESC;
-      if constexpr (HALF)
-        if (__ldg(p.sorted_ids + c.mb * BM + BM / 2) >= p.numel) idesc = IDESC_HALF;
+      const uint32_t idesc = IDESC;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag, limit)) {
           ok = false;
@@ -499,150 +445,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    uint32_t tail_phase = 0;
     for (int t = blockIdx.x; t < total_items; t += gridDim.x) {
       TileCoord c;
       int kb0, kb1;
-      const int part = item(t, c, kb0, kb1);
+      item(t, c, kb0, kb1);
       const int e = __ldg(p.expert_ids + c.mb);
       if (e < 0 || e >= p.num_experts) continue;
       bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, limit);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      int m, r;
-      bool valid;
-      if constexpr (HALF) {
-        // an M = 64 tile: lanes 0-15 of quarter q hold rows 16 q .. 16 q + 15
-        const bool half = __ldg(p.sorted_ids + c.mb * BM + BM / 2) >= p.numel;
-        m = c.mb * BM + (half ? q * 16 + (lane & 15) : row);
-        r = __ldg(p.sorted_ids + m);
-        valid = (!half || lane < 16) && r < p.numel;
-      } else {
-        m = c.mb * BM + row;
-        r = __ldg(p.sorted_ids + m);
-        valid = r < p.numel;
-      }
+      const int m = c.mb * BM + row;
+      const int r = __ldg(p.sorted_ids + m);
+      const bool valid = r < p.numel;
       const uint32_t tbase =
           tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
       float a_s = 1.0f;
       if constexpr (kScaled) a_s = valid ? __ldg(p.a_scale + m) : 0.0f;
       const float* bsc =
           kScaled ? p.b_scale + int64_t(e) * p.n_total + c.nt * BN : nullptr;
-
-      if constexpr (TAIL && EPI == kEpiRows) {
-        if (part >= 0) {
-          constexpr int C_HALF = BN / 32;
-          constexpr int CPI = C_HALF >= 4 ? 4 : C_HALF;
-          const int j = (t - tail_start) / parts;  // tail tile
-          // (1) this part's raw accumulator words -> workspace slot (j, part),
-          // indexed by TMEM lane and column, then TMEM goes back to the MMA
-          uint32_t* slot = reinterpret_cast<uint32_t*>(p.tail_ws) +
-                           (int64_t(j * parts + part) * BM + row) * BN;
-#pragma unroll 1
-          for (int cc = 0; cc < C_HALF; cc += CPI) {
-            uint32_t v[CPI][16];
-#pragma unroll
-            for (int u = 0; u < CPI; ++u) tmem_ld16(tbase + (h * C_HALF + cc + u) * 16, v[u]);
-            tmem_ld_wait();
-#pragma unroll
-            for (int u = 0; u < CPI; ++u) {
-              uint4* dst = reinterpret_cast<uint4*>(slot + (h * C_HALF + cc + u) * 16);
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                dst[i] = make_uint4(v[u][4 * i], v[u][4 * i + 1], v[u][4 * i + 2],
-                                    v[u][4 * i + 3]);
-            }
-          }
-          tc_fence_before();
-          mbar_arrive(&tempty[acc]);
-          acc ^= 1;
-          if (acc == 0) acc_phase ^= 1u;
-          __threadfence();
-          // (2) once all 256 epilogue threads stored, one of them counts the
-          // part; the part that makes the count `parts` finishes the tile
-          mbar_arrive(&tail_bar[0]);
-          bool ok2 = mbar_wait_bounded(&tail_bar[0], tail_phase, abort_flag, limit);
-          if (threadIdx.x == 64) {
-            int last = 0;
-            if (ok2) {
-              last = atomicAdd(p.tail_cnt + j, 1) == parts - 1;
-              __threadfence();
-            }
-            *tail_last = last;
-            mbar_arrive(&tail_bar[1]);
-          }
-          ok2 = mbar_wait_bounded(&tail_bar[1], tail_phase, abort_flag, limit) && ok2;
-          tail_phase ^= 1u;
-          if (!__all_sync(0xffffffffu, ok2)) break;
-          if (*tail_last && valid) {
-            // (3) sum the parts in part order (int32 exactly for kind::i8),
-            // scale, store the weighted row as the epilogue below does
-            const float w = load_weight(p.row_weights, p.row_weights_dtype, r);
-            TOUT* out_row = static_cast<TOUT*>(p.out) + int64_t(r) * p.out_ld + c.nt * BN;
-            const uint32_t* base = reinterpret_cast<const uint32_t*>(p.tail_ws) +
-                                   (int64_t(j * parts) * BM + row) * BN;
-#pragma unroll 1
-            for (int gi = 0; gi < C_HALF; ++gi) {
-              const int g = h * C_HALF + gi;
-              uint32_t sum[16];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const uint4 w4 = __ldcg(reinterpret_cast<const uint4*>(base + g * 16) + i);
-                sum[4 * i] = w4.x; sum[4 * i + 1] = w4.y; sum[4 * i + 2] = w4.z;
-                sum[4 * i + 3] = w4.w;
-              }
-              for (int q2 = 1; q2 < parts; ++q2) {
-                const uint32_t* src = base + int64_t(q2) * BM * BN + g * 16;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const uint4 w4 = __ldcg(reinterpret_cast<const uint4*>(src) + i);
-                  const uint32_t in[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-                  for (int z = 0; z < 4; ++z) {
-                    if constexpr (KIND == kKindI8)
-                      sum[4 * i + z] = uint32_t(int32_t(sum[4 * i + z]) + int32_t(in[z]));
-                    else
-                      sum[4 * i + z] =
-                          __float_as_uint(__uint_as_float(sum[4 * i + z]) + __uint_as_float(in[z]));
-                  }
-                }
-              }
-              float x[16];
-#pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                float s4[4] = {w, w, w, w};
-                if constexpr (kScaled) {
-                  const float s = a_s * w;
-                  const float4 b4 = __ldg(reinterpret_cast<const float4*>(bsc + g * 16) + jj);
-                  s4[0] = s * b4.x;
-                  s4[1] = s * b4.y;
-                  s4[2] = s * b4.z;
-                  s4[3] = s * b4.w;
-                }
-#pragma unroll
-                for (int q2 = 0; q2 < 4; ++q2)
-                  x[4 * jj + q2] = acc_to_f32<KIND>(sum[4 * jj + q2]) * s4[q2];
-              }
-              if constexpr (std::is_same<TOUT, float>::value) {
-                float4* dst = reinterpret_cast<float4*>(out_row + g * 16);
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj)
-                  dst[jj] = make_float4(x[4 * jj], x[4 * jj + 1], x[4 * jj + 2], x[4 * jj + 3]);
-              } else {
-                uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
-#pragma unroll
-                for (int jj = 0; jj < 2; ++jj)
-                  dst[jj] = make_uint4(pack2<TOUT>(x[8 * jj], x[8 * jj + 1]),
-                                       pack2<TOUT>(x[8 * jj + 2], x[8 * jj + 3]),
-                                       pack2<TOUT>(x[8 * jj + 4], x[8 * jj + 5]),
-                                       pack2<TOUT>(x[8 * jj + 6], x[8 * jj + 7]));
-              }
-            }
-          }
-          if (*tail_last && threadIdx.x == 64) p.tail_cnt[j] = 0;  // ready for the next launch
-          continue;
-        }
-      }
 
       if constexpr (EPI == kEpiSwiGLU) {
         constexpr int G_HALF = BN / 64;              // 32-column groups per half
@@ -1471,57 +1291,17 @@ int set_smem_once(Kern kern, size_t bytes, std::atomic<uint64_t>& done) {
   return MOE_OK;
 }
 
-template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT, bool HALF, bool TAIL = false>
-int launch_kernel_v(const CUtensorMap& ta, const CUtensorMap& tb,
-                    const KParams& kp, int grid, cudaStream_t s) {
+template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
+                  const KParams& kp, int grid, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
-  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT, HALF, TAIL>;
+  auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT>;
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
   KSW_LAUNCH(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, s, ta, tb, kp);
   return MOE_OK;
 }
-
-// MOE_HALF_TILES=1 selects the variant with M = 64 MMAs for half-empty
-// m-blocks (not yet measured; the default keeps M = 128 throughout).
-bool half_tiles_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("MOE_HALF_TILES");
-    return v && v[0] && v[0] != '0';
-  }();
-  return on;
-}
-
-template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
-int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
-                  const KParams& kp, int grid, cudaStream_t s) {
-  if constexpr (EPI == kEpiRows) {
-    // the tail split's workspace is sized for one slot per CTA
-    if (kp.tail_ws != nullptr && kp.tail_cnt != nullptr && kp.splits == 1) {
-      if (half_tiles_enabled())
-        return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, true, true>(ta, tb, kp, grid, s);
-      return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, false, true>(ta, tb, kp, grid, s);
-    }
-  }
-  if (half_tiles_enabled())
-    return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, true>(ta, tb, kp, grid, s);
-  return launch_kernel_v<KIND, AB_FMT, BN, EPI, TOUT, false>(ta, tb, kp, grid, s);
-}
-
-}  // namespace
-
-bool tail_split_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("MOE_TAIL_SPLIT");
-    return v && v[0] && v[0] != '0';
-  }();
-  return on;
-}
-size_t tail_ws_bytes(int sms, int bn) { return size_t(sms) * BM * size_t(bn) * 4; }
-size_t tail_cnt_bytes(int sms) { return size_t(sms) * 4; }
-
-namespace {
 
 template <int BN, int EPI>
 int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
@@ -1683,8 +1463,6 @@ KParams base_params(const GroupedGemmArgs& a, int elem_bytes) {
   kp.up_offset = int32_t(a.n / 2);
   kp.early_meta = a.early_meta;
   kp.wait_limit_ns = kWaitLimitNs;
-  kp.tail_ws = a.tail_ws;
-  kp.tail_cnt = a.tail_cnt;
   return kp;
 }
 

@@ -49,17 +49,8 @@ struct GroupedGemmArgs {
   // them, and request its first weight tiles, before waiting on the kernel
   // that produced its A operand (programmatic dependent launch).
   int early_meta;
-  // down GEMM without K split: workspace for splitting the last partial
-  // wave's tiles along K (tail_ws_bytes and tail_cnt_bytes; the counters
-  // must be zero at launch), or null
-  float* tail_ws;
-  int32_t* tail_cnt;
 };
 
-// Tail splitting of the down GEMM (MOE_TAIL_SPLIT=1; off by default).
-bool tail_split_enabled();
-size_t tail_ws_bytes(int sms, int bn);   // part tiles
-size_t tail_cnt_bytes(int sms);          // counters
 
 // ----- decode.cu -----
 // Routed rows up to which moe_fused_experts streams the weights through

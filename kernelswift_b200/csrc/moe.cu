@@ -35,10 +35,9 @@ struct Plan {
   int dn_bn, gu_bn;      // N tile widths
   int part_dtype;        // dtype of the down GEMM's weighted rows
   size_t align_ws;
-  bool tail;             // down GEMM splits its last partial wave along K
   int sms;
   size_t off_sorted, off_eids, off_npp, off_align, off_a, off_a_scale, off_act,
-      off_act_q, off_act_scale, off_part, off_gu_part, off_tail_ws, off_tail_cnt, total;
+      off_act_q, off_act_scale, off_part, off_gu_part, total;
 };
 
 int elem_bytes(int dtype) {
@@ -207,10 +206,6 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.off_part = take(size_t(P.splits) * P.numel * P.H * elem_bytes(P.part_dtype));
   P.off_gu_part = take(P.gu_splits > 1 ? size_t(P.gu_splits) * P.numel * 2 * P.I * 4 : 0);
   P.sms = sms;
-  P.tail = tail_split_enabled() && P.splits == 1 && P.quant != MOE_QUANT_FP8_BLOCK &&
-           P.quant != MOE_QUANT_FP8_UE8M0;
-  P.off_tail_ws = take(P.tail ? tail_ws_bytes(sms, P.dn_bn) : 0);
-  P.off_tail_cnt = take(P.tail ? tail_cnt_bytes(sms) : 0);
   P.total = off;
   return MOE_OK;
 }
@@ -330,8 +325,6 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   st = align_launch(p->topk_ids, p->ids_dtype, P.numel, P.E, kBlockM, sorted, eids, npp,
                     at<void>(workspace, P.off_align), P.align_ws, s);
   if (st != MOE_OK) return st;
-  if (P.tail)  // the down GEMM's tail counters start at zero
-    KSW_CUDA(cudaMemsetAsync(at<void>(workspace, P.off_tail_cnt), 0, tail_cnt_bytes(P.sms), s));
 
   GatherArgs g{};
   g.src = p->hidden;
@@ -425,10 +418,6 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   gd.splits = P.splits;
   gd.block_n = P.dn_bn;
   gd.out_dtype = P.part_dtype;
-  if (P.tail) {
-    gd.tail_ws = at<float>(workspace, P.off_tail_ws);
-    gd.tail_cnt = at<int32_t>(workspace, P.off_tail_cnt);
-  }
   const bool direct = rows_out != nullptr && P.splits == 1 && P.part_dtype == p->act_dtype;
   if (direct) gd.out = rows_out;  // weighted rows in token order: the result itself
   st = gemm_down_launch(gd, s);
@@ -505,7 +494,7 @@ int moe_fused_experts_plan(const moe_problem_t* p, int32_t* info) {
   info[2] = P.dn_bn;
   info[3] = P.splits;
   info[4] = P.part_dtype;
-  info[5] = P.tail ? 1 : 0;
+  info[5] = 0;
   info[6] = decode ? 1 : 0;
   info[7] = sms;
   return MOE_OK;

@@ -378,8 +378,8 @@ def fused_experts_plan(num_tokens: int, hidden_size: int, intermediate_size: int
     info = (ctypes.c_int32 * 8)()
     _lib.call("moe_fused_experts_plan", ctypes.byref(p), info)
     keys = ("gate_up_block_n", "gate_up_splits", "down_block_n", "down_splits",
-            "down_rows_dtype", "down_tail_split", "decode_path", "sms")
-    return dict(zip(keys, list(info)))
+            "down_rows_dtype", None, "decode_path", "sms")  # info[5] is reserved
+    return {k: v for k, v in zip(keys, list(info)) if k is not None}
 
 
 def stage_event_array(events) -> ctypes.Array:

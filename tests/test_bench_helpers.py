@@ -26,7 +26,7 @@ def test_workloads_cover_the_configs():
 def test_config_block():
     cfg = bench.workload_config("mixtral", 4096, 14336, 8, 2, "none", 4096, 1)
     assert cfg["parallelism"] == "single" and cfg["tokens_per_gpu"] == 4096
-    assert "flushed" in cfg["l2"] and set(cfg["switches"]) >= {"pdl", "tail_split"}
+    assert "flushed" in cfg["l2"] and set(cfg["switches"]) >= {"pdl", "decode_path", "block_n"}
     ep = bench.workload_config("mixtral", 4096, 14336, 8, 2, "none", 4096, 8, "peer")
     assert ep["global_tokens"] == 8 * 4096 and "peer memory" in ep["parallelism"]
     dd = bench.workload_config("dsv3", 7168, 2048, 256, 8, "none", 8192, 4, "nccl-dedup")
@@ -44,16 +44,14 @@ def test_cpu_baseline_memory_cap():
 
 
 def test_switch_record(monkeypatch):
-    for name in ("MOE_NO_PDL", "MOE_NO_DECODE_PATH", "MOE_HALF_TILES", "MOE_TAIL_SPLIT",
-                 "MOE_BLOCK_N"):
+    for name in ("MOE_NO_PDL", "MOE_NO_DECODE_PATH", "MOE_BLOCK_N"):
         monkeypatch.delenv(name, raising=False)
-    assert bench.active_switches() == {"pdl": True, "decode_path": True, "half_tiles": False,
-                                       "tail_split": False, "block_n": "planner"}
+    assert bench.active_switches() == {"pdl": True, "decode_path": True, "block_n": "planner"}
     monkeypatch.setenv("MOE_NO_PDL", "1")
-    monkeypatch.setenv("MOE_TAIL_SPLIT", "0")
-    monkeypatch.setenv("MOE_HALF_TILES", "1")
+    monkeypatch.setenv("MOE_NO_DECODE_PATH", "0")
+    monkeypatch.setenv("MOE_BLOCK_N", "128")
     sw = bench.active_switches()
-    assert not sw["pdl"] and not sw["tail_split"] and sw["half_tiles"]
+    assert not sw["pdl"] and sw["decode_path"] and sw["block_n"] == "128"
 
 
 def test_reference_arm_json_line():

@@ -186,7 +186,7 @@ def test_launch_count_query_without_gpu():
 def test_plan_query_without_gpu():
     """moe_fused_experts_plan: tile widths divide the GEMMs' widths, fp8 keeps
     128/256-wide tiles and no gate-up split, decode shapes take the decode
-    kernels, and the tail split is off unless MOE_TAIL_SPLIT=1."""
+    kernels."""
     from kernelswift_b200 import fused_moe as fm
 
     for T, H, I, E, k, quant in [(4096, 4096, 14336, 8, 2, "none"), (64, 2048, 768, 128, 8, "none"),
@@ -200,16 +200,12 @@ def test_plan_query_without_gpu():
         if quant.startswith("fp8"):
             assert plan["gate_up_splits"] == 1
             assert plan["gate_up_block_n"] in (128, 256) and plan["down_block_n"] in (128, 256)
-        if os.environ.get("MOE_TAIL_SPLIT", "0") in ("", "0"):
-            assert plan["down_tail_split"] == 0
     assert fm.fused_experts_plan(1, 2048, 768, 128, 8)["decode_path"] == 1
     assert fm.fused_experts_plan(4096, 4096, 14336, 8, 2)["down_rows_dtype"] == _lib.DT_BF16
 
 
 def test_plan_switches_in_a_child_process():
-    """MOE_TAIL_SPLIT=1 plans the tail split for unsplit bf16/int8 down GEMMs
-    (not for fp8, not with a K split); MOE_BLOCK_N forces the tile width it
-    divides (fp8 keeps 128/256)."""
+    """MOE_BLOCK_N forces the tile width it divides (fp8 keeps 128/256)."""
     import json
     import subprocess
     import sys
@@ -229,11 +225,9 @@ def test_plan_switches_in_a_child_process():
         assert res.returncode == 0, res.stderr[-2000:]
         return json.loads(res.stdout.strip().splitlines()[-1])
 
-    tail = plans(MOE_TAIL_SPLIT="1", MOE_BLOCK_N="")
-    assert [p["down_tail_split"] for p in tail] == [1, 0, 0, 1]  # K split at T=512; fp8
-    forced = plans(MOE_TAIL_SPLIT="0", MOE_BLOCK_N="128")
+    forced = plans(MOE_BLOCK_N="128")
     assert all(p["down_block_n"] == 128 and p["gate_up_block_n"] == 128 for p in forced)
-    narrow = plans(MOE_TAIL_SPLIT="0", MOE_BLOCK_N="64")
+    narrow = plans(MOE_BLOCK_N="64")
     assert narrow[0]["down_block_n"] == 64 and narrow[2]["down_block_n"] in (128, 256)
 
 

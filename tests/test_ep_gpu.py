@@ -219,3 +219,100 @@ def test_ep_peer_absent_rank_times_out(cuda_device):
     assert all(r[1] == "ok" for r in res), res
     assert res[0][2] == _lib.MOE_ERR_TIMEOUT, res
     assert res[0][3] == 4.0
+
+
+class ExpertBank:
+    """DeepSeek-V3-sized expert weights drawn per expert from a seeded device
+    generator, so any rank can make any expert: rank r builds its E/N
+    experts for the layer, and the oracle check builds the experts its
+    sampled tokens hit, a chunk at a time. bank[idx] -> [len(idx), ...]."""
+
+    def __init__(self, which, E, H, I, device, seed=0):
+        self.which, self.H, self.I, self.device, self.seed = which, H, I, device, seed
+        rows, cols = (2 * I, H) if which == "w1" else (H, I)
+        self.shape = (E, rows, cols)
+
+    def expert(self, e):
+        g = torch.Generator(device=self.device).manual_seed(
+            self.seed * 100003 + 2 * int(e) + (self.which == "w2"))
+        _, rows, cols = self.shape
+        return (torch.randn(rows, cols, generator=g, device=self.device) / cols ** 0.5).to(
+            torch.bfloat16)
+
+    def __getitem__(self, idx):
+        return torch.stack([self.expert(e) for e in idx.tolist()])
+
+
+def dsv3_worker(rank, world, port, cfg, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from kernelswift_b200.ep import ExpertParallelMoE
+    from oracle import moe_oracle as orc
+    from sampled import cover_tokens, oracle_on_tokens
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    ep = None
+    try:
+        E, k, T, H, I, quant, exchange, extra = cfg
+        b1, b2 = ExpertBank("w1", E, H, I, dev), ExpertBank("w2", E, H, I, dev)
+        el = E // world
+        local = torch.arange(rank * el, (rank + 1) * el)
+        ep = ExpertParallelMoE(b1[local], b2[local], E, k, quant=quant, exchange=exchange,
+                               max_tokens=T)
+        torch.cuda.empty_cache()
+        gt = torch.Generator().manual_seed(1000 + rank)
+        hidden = torch.randn(T, H, generator=gt).to(torch.bfloat16)
+        w, ids = orc.route(torch.randn(T, E, generator=gt), k)
+        out = ep(hidden.to(dev), w.to(dev), ids.to(dev))
+        torch.cuda.synchronize()
+        if ep.peer is not None:
+            ep.peer.check()
+        tokens = cover_tokens(ids, extra, seed=rank)
+        ref = oracle_on_tokens(quant, hidden, b1, b2, w, ids, tokens)
+        got = out.cpu()[tokens]
+        rel = orc.rel_l2(got, ref)
+        close = bool(torch.allclose(got.float(), ref, rtol=2e-2, atol=2e-2))
+        q.put((rank, "ok", rel, close, int(tokens.numel())))
+    except Exception as exc:
+        q.put((rank, "error", repr(exc)[:300], False, 0))
+    finally:
+        if ep is not None:
+            ep.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("quant,exchange", [("none", "peer"), ("none", "nccl"), ("fp8", "peer")])
+def test_ep_dsv3_config(cuda_device, quant, exchange):
+    """The expert-parallel DeepSeek-V3 configuration: H=7168, I=2048, 256
+    experts sharded E/N per GPU, top-8, 8192 tokens per rank (65,536 slots,
+    so the multi-CTA dispatch plan runs), on every GPU of the box up to 8.
+    Each rank checks at least 256 of its tokens against the oracle: the
+    first token of every expert its batch hits, plus 64 random tokens
+    (bf16: rtol 2e-2 / atol 2e-2; fp8: relative L2 <= 5e-2)."""
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs two GPUs: one rank would exchange nothing")
+    cfg = (256, 8, 8192, 7168, 2048, quant, exchange, 64)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=dsv3_worker, args=(r, world, port, cfg, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=900) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, status, rel, close, n in res:
+        assert status == "ok", (rank, rel)
+        assert n >= 256, (rank, n)
+        if quant == "fp8":
+            assert rel <= 5e-2, (rank, rel)
+        else:
+            assert close, (rank, rel)

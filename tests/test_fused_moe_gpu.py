@@ -7,6 +7,7 @@ import torch
 from cases import CASES, make_inputs
 from kernelswift_b200 import fused_moe as fm
 from oracle import moe_oracle as orc
+from sampled import cover_tokens, oracle_on_tokens
 
 pytestmark = pytest.mark.gpu
 
@@ -74,33 +75,40 @@ def random_problem(T, H, I, E, k, dtype, seed, bias=0.0, device="cuda"):
 
 def oracle_subset(hidden, w1, w2, w, ids, tokens):
     """fp32 oracle on the given tokens, moving only the hit experts."""
-    sub_ids = ids[tokens]
-    hit = torch.unique(sub_ids)
-    remap = torch.full((w1.shape[0],), -1, dtype=torch.int64)
-    remap[hit] = torch.arange(hit.numel())
-    return orc.fused_experts(hidden[tokens].cpu(), w1[hit.to(w1.device)].cpu(),
-                             w2[hit.to(w2.device)].cpu(), w[tokens], remap[sub_ids])
+    return oracle_on_tokens("none", hidden, w1, w2, w, ids, tokens)
 
 
+# Every token/size pair of the bf16 configurations: Mixtral-8x7B (H=4096,
+# I=14336, E=8, top-2) at T in {1, 16, 64, 512, 4096, 16384}, Qwen3-30B-A3B
+# (H=2048, I=768, E=128, top-8, skewed routing) at T in {1, 64, 1024, 8192},
+# DeepSeek-V3 (H=7168, I=2048, E=256, top-8) in bf16 at T=64 and at the
+# expert-parallel configuration's 8192 tokens per GPU with all 256 experts
+# on one GPU. Up to 64 tokens every token is checked; above, the first token
+# of every hit expert plus `extra` random tokens.
 SHAPES = [
-    # name, T, H, I, E, k, bias, tokens checked against the CPU oracle
-    ("mixtral_T1", 1, 4096, 14336, 8, 2, 0.0, 1),
-    ("mixtral_T16", 16, 4096, 14336, 8, 2, 0.0, 16),
+    # name, T, H, I, E, k, logit bias std, extra random tokens
+    ("mixtral_T1", 1, 4096, 14336, 8, 2, 0.0, 0),
+    ("mixtral_T16", 16, 4096, 14336, 8, 2, 0.0, 0),
+    ("mixtral_T64", 64, 4096, 14336, 8, 2, 0.0, 0),
     ("mixtral_T512", 512, 4096, 14336, 8, 2, 0.0, 48),
-    ("qwen3_T1", 1, 2048, 768, 128, 8, 0.5, 1),
-    ("qwen3_T64", 64, 2048, 768, 128, 8, 0.5, 64),
-    ("qwen3_T1024", 1024, 2048, 768, 128, 8, 0.5, 48),
-    ("dsv3_T64_bf16", 64, 7168, 2048, 256, 8, 0.0, 4),
+    ("mixtral_T4096", 4096, 4096, 14336, 8, 2, 0.0, 64),
+    ("mixtral_T16384", 16384, 4096, 14336, 8, 2, 0.0, 64),
+    ("qwen3_T1", 1, 2048, 768, 128, 8, 0.5, 0),
+    ("qwen3_T64", 64, 2048, 768, 128, 8, 0.5, 0),
+    ("qwen3_T1024", 1024, 2048, 768, 128, 8, 0.5, 64),
+    ("qwen3_T8192", 8192, 2048, 768, 128, 8, 0.5, 128),
+    ("dsv3_T64_bf16", 64, 7168, 2048, 256, 8, 0.0, 0),
+    ("dsv3_T8192_bf16", 8192, 7168, 2048, 256, 8, 0.0, 64),
 ]
 
 
-@pytest.mark.parametrize("name,T,H,I,E,k,bias,n_check", SHAPES, ids=[s[0] for s in SHAPES])
-def test_config_shapes_bf16(cuda_device, name, T, H, I, E, k, bias, n_check):
+@pytest.mark.parametrize("name,T,H,I,E,k,bias,extra", SHAPES, ids=[s[0] for s in SHAPES])
+def test_config_shapes_bf16(cuda_device, name, T, H, I, E, k, bias, extra):
     hidden, w1, w2, w, ids = random_problem(T, H, I, E, k, torch.bfloat16, seed=T + E,
                                             bias=bias)
     out = fm.fused_experts(hidden, w1, w2, w.to(cuda_device), ids.to(cuda_device))
     torch.cuda.synchronize()
-    tokens = torch.randperm(T, generator=torch.Generator().manual_seed(0))[:n_check]
+    tokens = torch.arange(T) if T <= 64 else cover_tokens(ids, extra)
     ref = oracle_subset(hidden, w1, w2, w, ids, tokens)
     torch.testing.assert_close(out.cpu()[tokens].float(), ref, **TOL)
 

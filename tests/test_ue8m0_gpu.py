@@ -17,6 +17,7 @@ import torch
 from kernelswift_b200 import _lib
 from kernelswift_b200 import fused_moe as fm
 from oracle import moe_oracle as orc
+from sampled import cover_tokens, oracle_on_tokens
 
 pytestmark = pytest.mark.gpu
 
@@ -121,7 +122,9 @@ LAYER_SHAPES = [
     ("decode_T1", 1, 512, 256, 32, 8, 1),     # K-split down GEMM
     ("tail_blocks", 129, 384, 128, 8, 2, 129),
     ("wide", 700, 1024, 512, 8, 2, 64),       # 256-wide tiles
-    ("dsv3_T64", 64, 7168, 2048, 256, 8, 4),
+    ("dsv3_T64", 64, 7168, 2048, 256, 8, 64),
+    # DeepSeek-V3 at T=4096: the first token of every hit expert + 32 more
+    ("dsv3_T4096", 4096, 7168, 2048, 256, 8, -32),
 ]
 
 
@@ -138,8 +141,12 @@ def test_layer_matches_oracle(cuda_device, name, T, H, I, E, k, n_check):
                              use_fp8_w8a8=True)
     torch.cuda.synchronize()
     assert torch.equal(out, again)
-    tokens = torch.randperm(T, generator=torch.Generator().manual_seed(0))[:n_check]
-    ref = oracle_rows(hidden, w1, w2, w, ids, tokens)
+    if n_check < 0:  # every hit expert, plus -n_check random tokens
+        tokens = cover_tokens(ids, -n_check)
+        ref = oracle_on_tokens("fp8-ue8m0", hidden, w1, w2, w, ids, tokens)
+    else:
+        tokens = torch.randperm(T, generator=torch.Generator().manual_seed(0))[:n_check]
+        ref = oracle_rows(hidden, w1, w2, w, ids, tokens)
     assert orc.rel_l2(out.cpu()[tokens], ref) <= REL_L2
 
 
