@@ -293,7 +293,8 @@ def workload_config(name, H, I, E, k, quant, T, n, exchange=None):
             "hidden": H, "intermediate": I, "experts": E, "top_k": k, "quant": quant,
             "tokens_per_gpu": T, "global_tokens": T * n,
             "parallelism": (f"ep{n} (E/{n} experts per GPU, " + (
-                "token rows exchanged by dispatch/combine kernels over NVLink peer memory)"
+                "one row per token and destination rank, moved by dispatch/combine kernels "
+                "over NVLink peer memory)"
                 if exchange == "peer" else
                 "NCCL all_to_all, one row per token and destination rank)"
                 if exchange == "nccl-dedup" else "NCCL all_to_all)")) if n > 1 else "single",
@@ -364,10 +365,9 @@ def main():
         prep = model.prepared(torch.bfloat16, quant)
 
         def step(stage_arr=None):
-            tw, ti = fm.fused_topk(hidden, logits, k, weights_dtype=hidden.dtype)
-            return fm.fused_experts(hidden, prep, None, tw, ti,
-                                    use_fp8_w8a8=quant.startswith("fp8"),
-                                    use_int8_w8a8=quant == "int8", stage_events=stage_arr)
+            return fm.fused_moe(hidden, prep, None, logits, k,
+                                use_fp8_w8a8=quant.startswith("fp8"),
+                                use_int8_w8a8=quant == "int8", stage_events=stage_arr)
     else:
         # expert parallel: this rank holds E/world experts, routes its own T
         # tokens over all E; rows move through the peer-memory dispatch and
@@ -473,10 +473,8 @@ def main():
         # no host launch gaps. A second capture carries stage events (event
         # record nodes) for the per-kernel breakdown.
         def graph_fn(hd, ld, stage_arr=None):
-            tw, ti = fm.fused_topk(hd, ld, k, weights_dtype=hd.dtype)
-            return fm.fused_experts(hd, prep, None, tw, ti,
-                                    use_fp8_w8a8=quant.startswith("fp8"),
-                                    use_int8_w8a8=quant == "int8", stage_events=stage_arr)
+            return fm.fused_moe(hd, prep, None, ld, k, use_fp8_w8a8=quant.startswith("fp8"),
+                                use_int8_w8a8=quant == "int8", stage_events=stage_arr)
 
         graph = fm.CapturedMoE(graph_fn, T, H, E, dtype=torch.bfloat16, device=dev)
         graph.hidden.copy_(hidden)
@@ -525,12 +523,11 @@ def main():
             model_call = model
         else:
             def model_call(hd, ld):
-                tw, ti = fm.fused_topk(hd, ld, k, weights_dtype=hd.dtype)
                 if world > 1:
+                    tw, ti = fm.fused_topk(hd, ld, k, weights_dtype=hd.dtype)
                     return ep(hd, tw, ti)
-                return fm.fused_experts(hd, prep, None, tw, ti,
-                                        use_fp8_w8a8=quant.startswith("fp8"),
-                                        use_int8_w8a8=quant == "int8")
+                return fm.fused_moe(hd, prep, None, ld, k, use_fp8_w8a8=quant.startswith("fp8"),
+                                    use_int8_w8a8=quant == "int8")
 
         # the public host-I/O pipeline: each step's H2D and D2H copies run on
         # their own streams, overlapping the neighbouring steps' compute
@@ -564,7 +561,7 @@ def main():
                + logits.numel() * logits.element_size(),
                "d2h_bytes_per_step": T * H * 2,
                "path": "HostPipeline over " + (
-                   "CapturedMoE (CUDA graph of fused_topk + fused_experts)" if use_graph
+                   "CapturedMoE (CUDA graph of fused_moe: routing + experts)" if use_graph
                    else "ModelNew.forward (drop-in module)" if world == 1 and quant == "none"
                    else "fused_topk + " + ("ExpertParallelMoE.forward" if world > 1
                                            else "fused_experts"))
@@ -615,6 +612,19 @@ def main():
                                f"{gu_bytes / 1e9:.4g} GB ({hit} experts' w13 + rows in + act out) "
                                "per launch",
                 "launch_ms": gu_ms}
+    if world == 1 and quant == "none" and fm.fused_experts_plan(T, H, I, E, k)["decode_path"]:
+        # decode sizes: the weight-streaming gate-up kernel (its stage) reads
+        # the hit experts' w13 and the token rows, writes the act rows
+        dec_bytes = hit * 2 * I * H * 2 + T * H * 2 + rows * I * 2
+        achieved = dec_bytes / (gu_ms / 1e3) / 1e9
+        roofline = {"kernel": "decode_gate_up_kernel (SiLU fused)", "bound": "hbm",
+                    "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                    "frac": achieved / hbm_peak, "peak_source": f"copy bandwidth, {peak_src}",
+                    "traffic": traffic,
+                    "traffic_unit": "DRAM bytes per launch (ncu capture, profiles/)",
+                    "algorithmic": f"{dec_bytes / 1e6:.4g} MB ({hit} experts' w13 + tokens in + "
+                                   "act out) per launch",
+                    "launch_ms": gu_ms}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -633,7 +643,8 @@ def main():
     if world == 1:
         n_ids = T * k
     elif ep.peer is not None:
-        n_ids = ep.peer.capacity  # align runs over the whole receive buffer
+        # align takes the received rows' k slots (the device-side count)
+        n_ids = int(ep.peer.recv_count.item()) * k
     elif ep.dedup:
         n_ids = ep.last_rows_received * k  # k slots per received token row
     else:
@@ -648,21 +659,22 @@ def main():
     # our kernels per step: the routing kernel plus what the expert pass
     # launches for this shape (the plan's own count), plus the exchange
     if world == 1:
-        launches_per_step = 1 + fm.fused_experts_launches(T, H, I, E, k, quant)
+        launches_per_step = fm.fused_moe_launches(T, H, I, E, k, quant)
+    elif ep.peer is not None:
+        # routing, plan, dispatch, expert pass over the receive buffer
+        # (top_k = k, bounded by the received count), signal, combine, step end
+        launches_per_step = 1 + 2 + fm.fused_experts_launches(
+            ep.peer.capacity, H, I, E // world, k, quant) + 3
     elif ep.dedup:
-        # pack, expert pass over the received token rows (top_k = k),
-        # combine (the plan is torch ops)
-        launches_per_step = 1 + 1 + fm.fused_experts_launches(
+        # routing, plan, pack, expert pass over the received token rows
+        # (top_k = k), combine
+        launches_per_step = 1 + 2 + fm.fused_experts_launches(
             ep.last_rows_received, H, I, E // world, k, quant) + 1
-    elif ep.peer is None:
-        # plan, pack, expert pass over the received rows (top_k = 1), combine
+    else:
+        # routing, plan, pack, expert pass over the received rows (top_k = 1),
+        # combine
         launches_per_step = 1 + 2 + fm.fused_experts_launches(
             rows_per_launch[0], H, I, E // world, 1, quant) + 1
-    else:
-        # plan, dispatch, expert pass over the receive buffer, signal,
-        # combine, step end
-        launches_per_step = 1 + 2 + fm.fused_experts_launches(
-            ep.peer.capacity, H, I, E // world, 1, quant, rows_only=True) + 3
     if rank == 0:
         line = {
             "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
@@ -672,7 +684,8 @@ def main():
             "data": "synthetic",
             "config": workload_config(args.workload, H, I, E, k, quant, T, world,
                                       None if world == 1 else
-                                      ("nccl-dedup" if ep.dedup else ep.exchange)),
+                                      (ep.exchange if ep.exchange == "peer" else
+                                       "nccl-dedup" if ep.dedup else "nccl")),
             "tflops": tflops,
             "stage_ms": stage_ms,
             "align": align_report,

@@ -39,7 +39,7 @@
 extern "C" {
 #endif
 
-#define MOE_B200_ABI_VERSION 1
+#define MOE_B200_ABI_VERSION 2
 
 typedef enum moe_status {
   MOE_OK = 0,
@@ -275,6 +275,14 @@ typedef struct moe_problem {
                                i is recorded on `stream` before stage i and
                                event MOE_NUM_STAGES after the last one, for
                                per-kernel timing (may be NULL)               */
+  const int32_t* num_tokens_dev; /* optional device int: only tokens
+                               t < *num_tokens_dev (<= num_tokens) take part;
+                               the rest are neither read nor written. Lets an
+                               expert-parallel receive buffer sized for the
+                               worst case be processed at the size it got
+                               this step without a host sync (NULL: all
+                               num_tokens). Not with the decode path's sizes
+                               (at most 16 routed rows).                     */
 } moe_problem_t;
 
 /* Stages of moe_fused_experts, in launch order (for stage_events). */
@@ -307,6 +315,19 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
  */
 int moe_fused_experts(const moe_problem_t* p, void* workspace,
                       size_t workspace_bytes, void* stream);
+
+/*
+ * The whole forward of base.py:35-76 in one call: routing of
+ * router_logits [T, num_experts] (F32, F16 or BF16) as moe_topk_softmax does
+ * it (softmax in fp32, top-k, renormalised when `renormalize`; base.py:44-48)
+ * into p->topk_weights / p->topk_ids -- OUTPUTS here, [T, k] in
+ * p->weights_dtype / p->ids_dtype -- then moe_fused_experts with those
+ * weights (moe_topk_softmax's kernel, then moe_fused_experts' launches, on
+ * `stream`). Workspace as for moe_fused_experts_workspace_size. Replaces
+ * Model.forward (base.py:35-76).
+ */
+int moe_fused_moe(const moe_problem_t* p, const void* router_logits, int logits_dtype,
+                  int renormalize, void* workspace, size_t workspace_bytes, void* stream);
 
 /* moe_fused_experts for top_k == 1 where only the rows of tokens with a
  * valid expert id are wanted (the expert-parallel receive buffer): out[t] =
@@ -459,6 +480,27 @@ int moe_ep_plan_ws(const void* topk_ids, int ids_dtype, int64_t numel,
                    int32_t* inv_index, int64_t* counts, void* workspace,
                    size_t workspace_bytes, void* stream);
 
+/*
+ * Deduplicated send plan: one send row per (token, destination rank) that
+ * holds any of the token's k slots, so a token crosses to a rank once
+ * however many of its experts live there (top-8 of 256 experts over 8 ranks
+ * reaches about 5.3 ranks per token). Rows are grouped by rank (ascending),
+ * tokens ascending inside a rank; for send row p:
+ *   send_token[p]        the token (row of hidden_states)
+ *   send_eid[p*k + j]    topk_ids[t, j] - d * E_local when slot j is on rank d,
+ *                        else -1
+ *   send_w[p*k + j]      topk_weights[t, j] (as f32) for those slots, else 0
+ * inv_index[t*world + d] = the row of (t, d), -1 when the token has no slot
+ * on d; counts[d] = rows for rank d (d < world), counts[world] = tokens with
+ * an id outside [0, num_experts). Outputs hold num_tokens * world rows at
+ * most. One CTA; deterministic. Replaces the cross-rank grouping of
+ * base.py:64-68. 1 <= world <= 32, num_experts % world == 0.
+ */
+int moe_ep_plan_dedup(const void* topk_ids, int ids_dtype, const void* topk_weights,
+                      int weights_dtype, int64_t num_tokens, int top_k, int num_experts,
+                      int world, int32_t* send_token, int32_t* send_eid, float* send_w,
+                      int32_t* inv_index, int64_t* counts, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Expert parallelism over NVLink peer memory. No reference counterpart (the */
 /* reference has no expert parallelism): it replaces, across the ranks of    */
@@ -485,40 +527,45 @@ int moe_ep_plan_ws(const void* topk_ids, int ids_dtype, int64_t numel,
 
 typedef struct moe_ep_peer moe_ep_peer_t;
 
-/* Allocates this rank's buffer; writes its IPC handle (MOE_EP_HANDLE_BYTES)
- * to handle_out. 2 <= world <= MOE_EP_MAX_RANKS. wait_limit_ms bounds every
- * wait on another rank (0: 5000 ms). After a timeout the object is unusable
- * (ranks may disagree on the step) and must be destroyed. */
-int moe_ep_peer_create(int world, int rank, int64_t capacity, int64_t hidden_size,
+/* Allocates this rank's buffer for `capacity` received token rows (the most
+ * a step can bring: max tokens per rank * world) with top_k id and weight
+ * slots each; writes its IPC handle (MOE_EP_HANDLE_BYTES) to handle_out.
+ * 2 <= world <= MOE_EP_MAX_RANKS. wait_limit_ms bounds every wait on
+ * another rank (0: 5000 ms). After a timeout the object is unusable (ranks
+ * may disagree on the step) and must be destroyed. */
+int moe_ep_peer_create(int world, int rank, int64_t capacity, int64_t hidden_size, int top_k,
                        int act_dtype, int wait_limit_ms, moe_ep_peer_t** out,
                        void* handle_out);
 
 /* Opens the other ranks' buffers: `handles` holds world handles, rank order. */
 int moe_ep_peer_connect(moe_ep_peer_t* ep, const void* handles);
 
-/* This rank's received rows [capacity, hidden_size], received expert ids
- * [capacity] (int32, destination-local) and result rows [capacity,
- * hidden_size]. */
+/* This rank's received rows [capacity, hidden_size], their expert ids
+ * [capacity, top_k] (int32, local to this rank, -1 for slots held elsewhere)
+ * and weights [capacity, top_k] (f32), the result rows [capacity,
+ * hidden_size], and the device int that holds how many rows the last
+ * dispatch delivered (pass it as moe_problem_t.num_tokens_dev). */
 int moe_ep_peer_buffers(const moe_ep_peer_t* ep, void** recv_rows, int32_t** recv_ids,
-                        void** result_rows);
+                        float** recv_weights, void** result_rows, int32_t** recv_count);
 
-/* Sends this rank's rows: for send position p (moe_ep_plan's order,
- * send_eid and counts), row hidden[order[p] / top_k] and id send_eid[p] go
- * to the destination rank's buffer; returns (on the stream) once every rank's
- * rows for this rank have arrived. hidden is [num_tokens, hidden_size] in the
- * buffer's act dtype. */
-int moe_ep_peer_dispatch(moe_ep_peer_t* ep, const void* hidden, int64_t num_tokens, int top_k,
-                         const int32_t* order, const int32_t* send_eid, const int64_t* counts,
-                         int32_t* status, void* stream);
+/* Sends this rank's rows: for send row p of moe_ep_plan_dedup (send_token,
+ * send_eid, send_w, counts), row hidden[send_token[p]] with its top_k ids
+ * and weights goes to the destination rank's buffer; returns (on the
+ * stream) once every rank's rows for this rank have arrived, with the
+ * received count in the recv_count word. hidden is [num_tokens,
+ * hidden_size] in the buffer's act dtype. */
+int moe_ep_peer_dispatch(moe_ep_peer_t* ep, const void* hidden, int64_t num_tokens,
+                         const int32_t* send_token, const int32_t* send_eid,
+                         const float* send_w, const int64_t* counts, int32_t* status,
+                         void* stream);
 
-/* Signals that this rank's result rows are complete, waits for the other
- * ranks' signals and computes out[t] = sum_j w[t,j] * result row of slot
- * t*top_k + j (read from the rank that computed it; slots with
- * inv_index < 0 contribute nothing). out is [num_tokens, hidden_size] in
- * the act dtype; weights F32/F16/BF16. Ends the step. */
-int moe_ep_peer_combine(moe_ep_peer_t* ep, const int32_t* inv_index, const void* weights,
-                        int weights_dtype, int64_t num_tokens, int top_k, void* out,
-                        int32_t* status, void* stream);
+/* Signals that this rank's result rows (each already the weighted sum over
+ * its slots) are complete, waits for the other ranks' signals and computes
+ * out[t] = sum over ranks d, ascending, with inv_index[t*world + d] >= 0 of
+ * the result row d computed for (t, d), read from d's buffer, in fp32. out
+ * is [num_tokens, hidden_size] in the act dtype. Ends the step. */
+int moe_ep_peer_combine(moe_ep_peer_t* ep, const int32_t* inv_index, int64_t num_tokens,
+                        void* out, int32_t* status, void* stream);
 
 /* Closes the mappings of the other ranks' buffers. */
 int moe_ep_peer_disconnect(moe_ep_peer_t* ep);

@@ -58,6 +58,7 @@ class MoeProblem(ctypes.Structure):
         ("out", _vp),
         ("status", _vp),
         ("stage_events", _vp),
+        ("num_tokens_dev", _vp),
     ]
 
 
@@ -82,6 +83,7 @@ SIGNATURES = {
     "moe_fused_experts_workspace_size": (_int, [ctypes.POINTER(MoeProblem), ctypes.POINTER(_sz)]),
     "moe_fused_experts": (_int, [ctypes.POINTER(MoeProblem), _vp, _sz, _vp]),
     "moe_fused_experts_rows": (_int, [ctypes.POINTER(MoeProblem), _vp, _sz, _vp]),
+    "moe_fused_moe": (_int, [ctypes.POINTER(MoeProblem), _vp, _int, _int, _vp, _sz, _vp]),
     "moe_fused_experts_launches": (_int, [ctypes.POINTER(MoeProblem), _int,
                                           ctypes.POINTER(_int)]),
     "moe_fused_experts_plan": (_int, [ctypes.POINTER(MoeProblem), _vp]),
@@ -95,16 +97,18 @@ SIGNATURES = {
     "moe_ep_plan": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp]),
     "moe_ep_plan_workspace_size": (_int, [_i64, _int, ctypes.POINTER(_sz)]),
     "moe_ep_plan_ws": (_int, [_vp, _int, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "moe_ep_plan_dedup": (_int, [_vp, _int, _vp, _int, _i64, _int, _int, _int, _vp, _vp, _vp,
+                                 _vp, _vp, _vp]),
     "moe_grouped_topk": (_int, [_vp, _int, _i64, _int, _int, _int, _int, _int, _int,
                                 ctypes.c_float, _vp, _vp, _vp]),
     "moe_combine_rows": (_int, [_vp, _int, _vp, _vp, _int, _i64, _int, _i64, _vp, _int, _vp]),
     "moe_selftest_wait_timeout": (_int, [_vp, _int, _vp]),
     "moe_selftest_sf_copy": (_int, [_vp, _vp, _vp, _vp]),
-    "moe_ep_peer_create": (_int, [_int, _int, _i64, _i64, _int, _int, _vp, _vp]),
+    "moe_ep_peer_create": (_int, [_int, _int, _i64, _i64, _int, _int, _int, _vp, _vp]),
     "moe_ep_peer_connect": (_int, [_vp, _vp]),
-    "moe_ep_peer_buffers": (_int, [_vp, _vp, _vp, _vp]),
-    "moe_ep_peer_dispatch": (_int, [_vp, _vp, _i64, _int, _vp, _vp, _vp, _vp, _vp]),
-    "moe_ep_peer_combine": (_int, [_vp, _vp, _vp, _int, _i64, _int, _vp, _vp, _vp]),
+    "moe_ep_peer_buffers": (_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "moe_ep_peer_dispatch": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "moe_ep_peer_combine": (_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
     "moe_ep_peer_disconnect": (_int, [_vp]),
     "moe_ep_peer_destroy": (_int, [_vp]),
 }

@@ -35,6 +35,15 @@ constexpr int kChunkNoAlloc = 4096;   // the same for moe_align_block_size_noall
 constexpr int64_t kSmallMaxNoAlloc = 8192;
 constexpr int kMaxExperts = 1024;
 
+// Flat ids at or past the valid count are dropped: *valid_dev * mult of the
+// numel ids when the caller gives a device-side count (the rows an
+// expert-parallel receive buffer actually got this step), else all of them.
+__device__ __forceinline__ int64_t valid_ids(int64_t numel, const int32_t* valid_dev, int mult) {
+  if (valid_dev == nullptr) return numel;
+  const int64_t v = int64_t(max(*valid_dev, 0)) * mult;
+  return v < numel ? v : numel;
+}
+
 template <typename IdT>
 __device__ __forceinline__ int load_id(const IdT* ids, int64_t i, int E) {
   const long long v = static_cast<long long>(ids[i]);
@@ -136,9 +145,11 @@ __global__ void __launch_bounds__(kThreads)
     align_small_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
                        int BM, int64_t L, int32_t* __restrict__ sorted,
                        int32_t* __restrict__ expert_ids,
-                       int32_t* __restrict__ num_post_pad) {
+                       int32_t* __restrict__ num_post_pad, const int32_t* valid_dev,
+                       int valid_mult) {
   pdl_wait();
   pdl_trigger();
+  const int64_t nv = valid_ids(numel, valid_dev, valid_mult);
   extern __shared__ int sm[];
   int* counts = sm;                 // E
   int* running = counts + E;        // E
@@ -151,8 +162,8 @@ __global__ void __launch_bounds__(kThreads)
   for (int p = tid; p < 32 * E; p += kThreads) warp_cnt[p] = 0;
   __syncthreads();
 
-  for (int64_t base = 0; base < numel; base += kThreads)
-    count_subchunk(ids, base, numel, E, counts);
+  for (int64_t base = 0; base < nv; base += kThreads)
+    count_subchunk(ids, base, nv, E, counts);
   __syncthreads();
 
   const int cnt = tid < E ? counts[tid] : 0;
@@ -164,17 +175,19 @@ __global__ void __launch_bounds__(kThreads)
   if (tid == 0) *num_post_pad = total;
   __syncthreads();
 
-  for (int64_t base = 0; base < numel; base += kThreads)
-    scatter_subchunk(ids, base, numel, E, running, warp_cnt, sorted);
+  for (int64_t base = 0; base < nv; base += kThreads)
+    scatter_subchunk(ids, base, nv, E, running, warp_cnt, sorted);
 }
 
 template <typename IdT>
 __global__ void __launch_bounds__(kThreads)
     align_hist_kernel(const IdT* __restrict__ ids, int64_t numel, int E,
                       int64_t L, int chunk, int32_t* __restrict__ sorted,
-                      int32_t* __restrict__ chunk_counts) {
+                      int32_t* __restrict__ chunk_counts, const int32_t* valid_dev,
+                      int valid_mult) {
   pdl_wait();
   pdl_trigger();
+  const int64_t nv = valid_ids(numel, valid_dev, valid_mult);
   extern __shared__ int sm[];
   int* counts = sm;  // E
   const int tid = threadIdx.x;
@@ -184,7 +197,7 @@ __global__ void __launch_bounds__(kThreads)
   for (int e = tid; e < E; e += kThreads) counts[e] = 0;
   __syncthreads();
   const int64_t begin = int64_t(blockIdx.x) * chunk;
-  const int64_t end = min(numel, begin + chunk);
+  const int64_t end = min(nv, begin + chunk);
   for (int64_t base = begin; base < end; base += kThreads)
     count_subchunk(ids, base, end, E, counts);
   __syncthreads();
@@ -225,9 +238,11 @@ template <typename IdT>
 __global__ void __launch_bounds__(kThreads)
     align_scatter_kernel(const IdT* __restrict__ ids, int64_t numel, int E, int chunk,
                          const int32_t* __restrict__ chunk_base,
-                         int32_t* __restrict__ sorted) {
+                         int32_t* __restrict__ sorted, const int32_t* valid_dev,
+                         int valid_mult) {
   pdl_wait();
   pdl_trigger();
+  const int64_t nv = valid_ids(numel, valid_dev, valid_mult);
   extern __shared__ int sm[];
   int* running = sm;           // E
   int* warp_cnt = running + E; // 32 * E
@@ -237,7 +252,8 @@ __global__ void __launch_bounds__(kThreads)
   for (int p = tid; p < 32 * E; p += kThreads) warp_cnt[p] = 0;
   __syncthreads();
   const int64_t begin = int64_t(blockIdx.x) * chunk;
-  const int64_t end = min(numel, begin + chunk);
+  const int64_t end = min(nv, begin + chunk);
+  if (begin >= end) return;  // nothing valid in this chunk
   for (int64_t base = begin; base < end; base += kThreads)
     scatter_subchunk(ids, base, end, E, running, warp_cnt, sorted);
 }
@@ -245,7 +261,8 @@ __global__ void __launch_bounds__(kThreads)
 template <typename IdT>
 int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
                  int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
-                 int32_t* ws, int chunk, int64_t small_max, cudaStream_t s) {
+                 int32_t* ws, int chunk, int64_t small_max, cudaStream_t s,
+                 const int32_t* valid_dev, int valid_mult) {
   if (numel <= small_max) {
     const size_t smem = size_t(2 * E + 64 + 32 * E) * sizeof(int);
     auto k = align_small_kernel<IdT>;
@@ -253,12 +270,13 @@ int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
       KSW_CUDA(cudaFuncSetAttribute(
           k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     KSW_LAUNCH(k, dim3(1), dim3(kThreads), smem, s, ids, numel, E, BM, L, sorted,
-               expert_ids, num_post_pad);
+               expert_ids, num_post_pad, valid_dev, valid_mult);
     return MOE_OK;
   }
   const int nchunks = static_cast<int>(ceil_div(numel, chunk));
   KSW_LAUNCH(align_hist_kernel<IdT>, dim3(nchunks), dim3(kThreads),
-             size_t(E) * sizeof(int), s, ids, numel, E, L, chunk, sorted, ws);
+             size_t(E) * sizeof(int), s, ids, numel, E, L, chunk, sorted, ws, valid_dev,
+             valid_mult);
   KSW_LAUNCH(align_scan_kernel, dim3(1), dim3(kThreads), 0, s, nchunks, E, BM, L, ws,
              expert_ids, num_post_pad);
   const size_t smem = size_t(E + 32 * E) * sizeof(int);
@@ -267,7 +285,7 @@ int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
     KSW_CUDA(cudaFuncSetAttribute(
         k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   KSW_LAUNCH(k, dim3(nchunks), dim3(kThreads), smem, s, ids, numel, E, chunk,
-             static_cast<const int32_t*>(ws), sorted);
+             static_cast<const int32_t*>(ws), sorted, valid_dev, valid_mult);
   return MOE_OK;
 }
 
@@ -280,7 +298,8 @@ size_t workspace_bytes(int64_t numel, int E, int chunk, int64_t small_max) {
 int align_launch_cfg(const void* ids, int ids_dtype, int64_t numel, int E, int BM,
                      int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
                      void* workspace, size_t ws_bytes, int chunk, int64_t small_max,
-                     cudaStream_t s) {
+                     cudaStream_t s, const int32_t* valid_dev = nullptr,
+                     int valid_mult = 1) {
   int st = align_validate(numel, E, BM);
   if (st != MOE_OK) return st;
   KSW_REQUIRE(ids_dtype == MOE_DTYPE_I32 || ids_dtype == MOE_DTYPE_I64,
@@ -296,10 +315,12 @@ int align_launch_cfg(const void* ids, int ids_dtype, int64_t numel, int E, int B
   if (ids_dtype == MOE_DTYPE_I32)
     return launch_align(static_cast<const int32_t*>(ids), numel, E, BM, L,
                         sorted, expert_ids, num_post_pad,
-                        static_cast<int32_t*>(workspace), chunk, small_max, s);
+                        static_cast<int32_t*>(workspace), chunk, small_max, s, valid_dev,
+                        valid_mult);
   return launch_align(static_cast<const int64_t*>(ids), numel, E, BM, L, sorted,
                       expert_ids, num_post_pad,
-                      static_cast<int32_t*>(workspace), chunk, small_max, s);
+                      static_cast<int32_t*>(workspace), chunk, small_max, s, valid_dev,
+                      valid_mult);
 }
 
 }  // namespace
@@ -327,9 +348,10 @@ int align_validate(int64_t numel, int E, int BM) {
 
 int align_launch(const void* ids, int ids_dtype, int64_t numel, int E, int BM,
                  int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
-                 void* workspace, size_t ws_bytes, cudaStream_t s) {
+                 void* workspace, size_t ws_bytes, cudaStream_t s, const int32_t* valid_dev,
+                 int valid_mult) {
   return align_launch_cfg(ids, ids_dtype, numel, E, BM, sorted, expert_ids, num_post_pad,
-                          workspace, ws_bytes, kChunk, kSmallMax, s);
+                          workspace, ws_bytes, kChunk, kSmallMax, s, valid_dev, valid_mult);
 }
 
 }  // namespace ksw

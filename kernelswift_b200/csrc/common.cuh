@@ -151,14 +151,21 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                : "memory");
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// is parked by the hardware until it completes or the hint (1 ms) passes,
+// instead of polling the barrier's shared-memory word in a tight loop (which
+// takes shared-memory bandwidth from the loads and the bulk copies it waits
+// for). The callers re-check their time limit and abort flag between calls.
+constexpr uint32_t kMbarSuspendHintNs = 1000000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kMbarSuspendHintNs)
       : "memory");
   return ok != 0;
 }

@@ -246,6 +246,107 @@ int launch_plan_multi(const IdT* ids, int64_t numel, int num_experts, int world,
   return MOE_OK;
 }
 
+// ---- the deduplicated plan (moe_ep_plan_dedup): one send row per (token,
+// destination rank) holding any of the token's slots. Rows are grouped by
+// rank, tokens ascending inside a rank. One CTA walks the tokens in 1024-token
+// passes; a token's position among the rank's rows is the ballot count of
+// earlier lanes in its warp plus the totals of earlier warps and passes, so
+// the plan is deterministic. ----
+constexpr int kDedupMaxWorld = 32;
+
+__device__ __forceinline__ float weight_as_f32(const void* w, int dtype, int64_t i) {
+  if (dtype == MOE_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]);
+  if (dtype == MOE_DTYPE_F16) return __half2float(static_cast<const __half*>(w)[i]);
+  return static_cast<const float*>(w)[i];
+}
+
+// Bit d of the result: the token has a slot on rank d; bit `world`: it has a
+// slot whose id is outside [0, num_experts).
+template <typename IdT>
+__device__ __forceinline__ uint64_t token_ranks(const IdT* ids, int64_t t, int k, int E,
+                                                int e_local, int world) {
+  uint64_t m = 0;
+  for (int j = 0; j < k; ++j) {
+    const long long v = static_cast<long long>(ids[t * k + j]);
+    m |= (v >= 0 && v < E) ? (uint64_t(1) << (v / e_local)) : (uint64_t(1) << world);
+  }
+  return m;
+}
+
+template <typename IdT>
+__global__ void __launch_bounds__(kThreads)
+    ep_plan_dedup_kernel(const IdT* __restrict__ ids, const void* __restrict__ w, int w_dtype,
+                         int64_t T, int k, int E, int e_local, int world,
+                         int32_t* __restrict__ send_token, int32_t* __restrict__ send_eid,
+                         float* __restrict__ send_w, int32_t* __restrict__ inv,
+                         int64_t* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int cnt[kDedupMaxWorld + 1];
+  __shared__ int running[kDedupMaxWorld];
+  __shared__ int warp_tot[32][kDedupMaxWorld];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid <= world) cnt[tid] = 0;
+  __syncthreads();
+  // pass 1: rows per rank, and tokens with an invalid slot
+  for (int64_t base = 0; base < T; base += kThreads) {
+    const int64_t t = base + tid;
+    const uint64_t m = t < T ? token_ranks(ids, t, k, E, e_local, world) : 0;
+    for (int d = 0; d <= world; ++d) {
+      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
+      if (lane == 0 && b) atomicAdd(&cnt[d], __popc(b));
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int d = 0; d < world; ++d) {
+      running[d] = run;
+      run += cnt[d];
+    }
+  }
+  if (tid <= world) counts[tid] = cnt[tid];
+  __syncthreads();
+  // pass 2: placement
+  for (int64_t base = 0; base < T; base += kThreads) {
+    const int64_t t = base + tid;
+    const uint64_t m = t < T ? token_ranks(ids, t, k, E, e_local, world) : 0;
+    for (int d = 0; d < world; ++d) {
+      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
+      if (lane == 0) warp_tot[warp][d] = __popc(b);
+    }
+    __syncthreads();
+    for (int d = 0; d < world; ++d) {  // warp-uniform: every lane takes each ballot
+      const bool on = (m >> d) & 1u;
+      const unsigned b = __ballot_sync(0xffffffffu, on);
+      if (t >= T) continue;
+      if (!on) {
+        inv[t * world + d] = -1;
+        continue;
+      }
+      int prefix = 0;
+      for (int w2 = 0; w2 < warp; ++w2) prefix += warp_tot[w2][d];
+      const int pos = running[d] + prefix + __popc(b & lanemask_lt());
+      send_token[pos] = static_cast<int32_t>(t);
+      inv[t * world + d] = pos;
+      for (int j = 0; j < k; ++j) {
+        const long long v = static_cast<long long>(ids[t * k + j]);
+        const bool here = v >= 0 && v < E && v / e_local == d;
+        send_eid[int64_t(pos) * k + j] = here ? static_cast<int32_t>(v - int64_t(d) * e_local) : -1;
+        send_w[int64_t(pos) * k + j] = here ? weight_as_f32(w, w_dtype, t * k + j) : 0.0f;
+      }
+    }
+    __syncthreads();
+    if (tid < world) {
+      int sum = 0;
+      for (int w2 = 0; w2 < 32; ++w2) sum += warp_tot[w2][tid];
+      running[tid] += sum;
+    }
+    __syncthreads();
+  }
+}
+
+
 }  // namespace
 }  // namespace ksw
 
@@ -318,4 +419,42 @@ extern "C" int moe_ep_plan_ws(const void* topk_ids, int ids_dtype, int64_t numel
                              order, send_eid, inv_index, counts, ws, s);
   return launch_plan_multi(static_cast<const int64_t*>(topk_ids), numel, num_experts, world,
                            order, send_eid, inv_index, counts, ws, s);
+}
+
+extern "C" int moe_ep_plan_dedup(const void* topk_ids, int ids_dtype, const void* topk_weights,
+                                 int weights_dtype, int64_t num_tokens, int top_k,
+                                 int num_experts, int world, int32_t* send_token,
+                                 int32_t* send_eid, float* send_w, int32_t* inv_index,
+                                 int64_t* counts, void* stream) {
+  using namespace ksw;
+  int st = check_device(nullptr);
+  if (st != MOE_OK) return st;
+  KSW_REQUIRE(world >= 1 && world <= kDedupMaxWorld, MOE_ERR_UNSUPPORTED,
+              "ep_plan_dedup: world must be in [1, 32]");
+  KSW_REQUIRE(num_experts >= world && num_experts % world == 0, MOE_ERR_INVALID_ARG,
+              "ep_plan_dedup: num_experts must be a positive multiple of world");
+  KSW_REQUIRE(top_k >= 1 && top_k <= 64, MOE_ERR_INVALID_ARG, "ep_plan_dedup: top_k in [1, 64]");
+  KSW_REQUIRE(num_tokens >= 0 && num_tokens * world < (int64_t(1) << 31), MOE_ERR_UNSUPPORTED,
+              "ep_plan_dedup: num_tokens out of range");
+  KSW_REQUIRE(ids_dtype == MOE_DTYPE_I32 || ids_dtype == MOE_DTYPE_I64, MOE_ERR_INVALID_ARG,
+              "ep_plan_dedup: ids dtype must be int32 or int64");
+  KSW_REQUIRE(weights_dtype == MOE_DTYPE_F32 || weights_dtype == MOE_DTYPE_BF16 ||
+                  weights_dtype == MOE_DTYPE_F16,
+              MOE_ERR_INVALID_ARG, "ep_plan_dedup: weights must be f32, bf16 or f16");
+  KSW_REQUIRE(counts && (num_tokens == 0 || (topk_ids && topk_weights && send_token &&
+                                             send_eid && send_w && inv_index)),
+              MOE_ERR_INVALID_ARG, "ep_plan_dedup: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int e_local = num_experts / world;
+  if (ids_dtype == MOE_DTYPE_I32)
+    KSW_LAUNCH(ep_plan_dedup_kernel<int32_t>, dim3(1), dim3(kThreads), 0, s,
+               static_cast<const int32_t*>(topk_ids), topk_weights, weights_dtype, num_tokens,
+               top_k, num_experts, e_local, world, send_token, send_eid, send_w, inv_index,
+               counts);
+  else
+    KSW_LAUNCH(ep_plan_dedup_kernel<int64_t>, dim3(1), dim3(kThreads), 0, s,
+               static_cast<const int64_t*>(topk_ids), topk_weights, weights_dtype, num_tokens,
+               top_k, num_experts, e_local, world, send_token, send_eid, send_w, inv_index,
+               counts);
+  return MOE_OK;
 }

@@ -236,9 +236,13 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes) {
 
 // The forward of moe_fused_experts; with `rows_out` (top_k == 1 only) the
 // per-row expert outputs go straight to rows_out from the down GEMM when it
-// runs unsplit, and the top-k sum is skipped.
+// runs unsplit, and the top-k sum is skipped. With `logits` (moe_fused_moe)
+// the tokens are routed first into p->topk_weights / p->topk_ids: inside
+// the decode kernel when it runs and the logits are fp32 over at most 256
+// experts, else by moe_topk_softmax.
 static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t workspace_bytes,
-                              void* stream, void* rows_out) {
+                              void* stream, void* rows_out, const void* logits = nullptr,
+                              int logits_dtype = MOE_DTYPE_F32, int renorm = 1) {
   // 16-byte vectors and bulk copies: a misaligned operand would fault the
   // context, so it is refused here, before the device is touched
   // (fp8 128x128 block scales are read one float at a time)
@@ -265,6 +269,15 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   if (P.quant != MOE_QUANT_NONE)
     KSW_REQUIRE(p->w13_scale && p->w2_scale, MOE_ERR_INVALID_ARG, "null weight scales");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool decode = P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype &&
+                      p->num_tokens_dev == nullptr && decode_path_enabled() &&
+                      decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype);
+  if (logits != nullptr) {
+    st = moe_topk_softmax(logits, logits_dtype, P.T, P.E, P.k, renorm,
+                          const_cast<void*>(p->topk_weights), p->weights_dtype,
+                          const_cast<void*>(p->topk_ids), p->ids_dtype, stream);
+    if (st != MOE_OK) return st;
+  }
   // Stage events: inside a stream capture they become event-record nodes of
   // the graph (external records), so a replayed graph can be timed per stage.
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -285,8 +298,7 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   } while (0)
   // A handful of routed rows with 16-bit operands: stream the weights
   // through the two decode kernels (csrc/decode.cu).
-  if (P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype && decode_path_enabled() &&
-      decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype)) {
+  if (decode) {
     DecodeArgs d{};
     d.T = P.T;
     d.H = P.H;
@@ -323,7 +335,7 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
 
   KSW_MARK(MOE_STAGE_ALIGN);
   st = align_launch(p->topk_ids, p->ids_dtype, P.numel, P.E, kBlockM, sorted, eids, npp,
-                    at<void>(workspace, P.off_align), P.align_ws, s);
+                    at<void>(workspace, P.off_align), P.align_ws, s, p->num_tokens_dev, P.k);
   if (st != MOE_OK) return st;
 
   GatherArgs g{};
@@ -440,6 +452,7 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   sa.E = P.E;
   sa.out = rows_out != nullptr ? rows_out : p->out;
   sa.out_dtype = p->act_dtype;
+  sa.count_dev = p->num_tokens_dev;
   KSW_MARK(MOE_STAGE_SUM);
   st = sum_topk_launch(sa, s);
   if (st != MOE_OK) return st;
@@ -453,6 +466,16 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace, size_t workspace_
   return fused_experts_impl(p, workspace, workspace_bytes, stream, nullptr);
 }
 
+int moe_fused_moe(const moe_problem_t* p, const void* router_logits, int logits_dtype,
+                  int renormalize, void* workspace, size_t workspace_bytes, void* stream) {
+  KSW_REQUIRE(router_logits != nullptr, MOE_ERR_INVALID_ARG, "moe_fused_moe: null logits");
+  KSW_REQUIRE(logits_dtype == MOE_DTYPE_F32 || logits_dtype == MOE_DTYPE_F16 ||
+                  logits_dtype == MOE_DTYPE_BF16,
+              MOE_ERR_INVALID_ARG, "moe_fused_moe: logits must be f32, f16 or bf16");
+  return fused_experts_impl(p, workspace, workspace_bytes, stream, nullptr, router_logits,
+                            logits_dtype, renormalize ? 1 : 0);
+}
+
 int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launches) {
   KSW_REQUIRE(launches != nullptr, MOE_ERR_INVALID_ARG, "null launches pointer");
   int sms = 148;
@@ -464,9 +487,10 @@ int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launc
     *launches = 0;
     return MOE_OK;
   }
-  if (P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype && decode_path_enabled() &&
+  if (P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype &&
+      p->num_tokens_dev == nullptr && decode_path_enabled() &&
       decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype)) {
-    *launches = 2;
+    *launches = 2;  // the two decode kernels
     return MOE_OK;
   }
   int n = (P.numel <= align_small_max() ? 1 : 3);      // align
@@ -488,7 +512,8 @@ int moe_fused_experts_plan(const moe_problem_t* p, int32_t* info) {
   const int st = make_plan(p, sms, &P);
   if (st != MOE_OK) return st;
   const bool decode = P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype &&
-                      decode_path_enabled() && decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype);
+                      p->num_tokens_dev == nullptr && decode_path_enabled() &&
+                      decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype);
   info[0] = P.gu_bn;
   info[1] = P.gu_splits;
   info[2] = P.dn_bn;

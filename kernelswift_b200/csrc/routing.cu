@@ -9,29 +9,12 @@
 // exp(l_e - max), then divided by the sum of the k selected weights when
 // renormalising. All arithmetic is fp32.
 #include "common.cuh"
+#include "routing.cuh"
 
 namespace ksw {
 namespace {
 
 constexpr int kWarpsPerBlock = 8;
-
-// Warp-wide argmax of (value, index): larger value wins, then lower index.
-__device__ __forceinline__ void warp_argmax(float& v, int& i) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
-    if (ov > v || (ov == v && oi < i)) {
-      v = ov;
-      i = oi;
-    }
-  }
-}
-
-template <typename Tin>
-__device__ __forceinline__ float ld_logit(const Tin* p) {
-  return to_f32(*p);
-}
 
 template <int PER_LANE, typename Tin, typename Tw, typename Tid>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
@@ -42,51 +25,11 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int64_t t = int64_t(blockIdx.x) * kWarpsPerBlock + warp; t < T;
        t += int64_t(gridDim.x) * kWarpsPerBlock) {
-    const Tin* row = logits + t * E;
-    float v[PER_LANE];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < PER_LANE; ++j) {
-      const int e = lane + 32 * j;
-      v[j] = e < E ? ld_logit(row + e) : -INFINITY;
-      mx = fmaxf(mx, v[j]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.0f;
-#pragma unroll
-    for (int j = 0; j < PER_LANE; ++j)
-      if (lane + 32 * j < E) sum += expf(v[j] - mx);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-
-    uint32_t taken = 0;  // bit j: this lane's j-th logit already selected
-    float sel_w = 0.0f;  // lane j < k keeps the j-th selected weight
-    int sel_i = 0;
-    float wsum = 0.0f;
-    for (int s = 0; s < k; ++s) {
-      float bv = -INFINITY;
-      int bi = INT32_MAX;
-#pragma unroll
-      for (int j = 0; j < PER_LANE; ++j) {
-        const int e = lane + 32 * j;
-        if (e < E && !(taken >> j & 1u) && (v[j] > bv || (v[j] == bv && e < bi))) {
-          bv = v[j];
-          bi = e;
-        }
-      }
-      warp_argmax(bv, bi);
-      if (bi < E && (bi & 31) == lane) taken |= 1u << (bi >> 5);
-      const float w = expf(bv - mx) / sum;
-      wsum += w;
-      if (lane == s) {
-        sel_w = w;
-        sel_i = bi;
-      }
-    }
+    float sel_w;
+    int sel_i;
+    route_token_warp<PER_LANE>(logits + t * E, E, k, renorm, lane, sel_w, sel_i);
     if (lane < k) {
-      const float w = renorm ? sel_w / wsum : sel_w;
-      weights[t * k + lane] = from_f32<Tw>(w);
+      weights[t * k + lane] = from_f32<Tw>(sel_w);
       ids[t * k + lane] = static_cast<Tid>(sel_i);
     }
   }

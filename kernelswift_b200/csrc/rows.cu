@@ -324,11 +324,14 @@ template <typename Tout, typename IdT, typename Tp>
 __global__ void __launch_bounds__(256)
     sum_topk_kernel(const Tp* __restrict__ part, int splits, int64_t T,
                     int top_k, int64_t H, int64_t numel, const IdT* __restrict__ ids,
-                    int E, Tout* __restrict__ out) {
+                    int E, Tout* __restrict__ out, const int32_t* count_dev) {
   pdl_wait();
   pdl_trigger();
   const int64_t vec_per_row = H / 8;
-  const int64_t total = T * vec_per_row;
+  // rows past the device-side count (the rows a receive buffer actually got)
+  // are neither read nor written
+  const int64_t rows = count_dev != nullptr ? min(T, int64_t(max(*count_dev, 0))) : T;
+  const int64_t total = rows * vec_per_row;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t t = i / vec_per_row;
@@ -582,11 +585,11 @@ int sum_topk_launch(const SumArgs& a, cudaStream_t s) {
   if (a.part_dtype == MOE_DTYPE_F32)                                                         \
     KSW_LAUNCH(sum_topk_kernel<TOUT, IDT, float>, dim3(grid), dim3(256), 0, s,                                   \
         static_cast<const float*>(a.part), a.splits, a.T, a.top_k, a.H, numel,               \
-        static_cast<const IDT*>(a.ids), a.E, static_cast<TOUT*>(a.out));                     \
+        static_cast<const IDT*>(a.ids), a.E, static_cast<TOUT*>(a.out), a.count_dev);        \
   else                                                                                       \
     KSW_LAUNCH(sum_topk_kernel<TOUT, IDT, TOUT>, dim3(grid), dim3(256), 0, s,                                    \
         static_cast<const TOUT*>(a.part), a.splits, a.T, a.top_k, a.H, numel,                \
-        static_cast<const IDT*>(a.ids), a.E, static_cast<TOUT*>(a.out))
+        static_cast<const IDT*>(a.ids), a.E, static_cast<TOUT*>(a.out), a.count_dev)
   const bool i64 = a.ids_dtype == MOE_DTYPE_I64;
   if (a.out_dtype == MOE_DTYPE_BF16) {
     if (i64) { KSW_SUM(__nv_bfloat16, int64_t); } else { KSW_SUM(__nv_bfloat16, int32_t); }

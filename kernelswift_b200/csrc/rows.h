@@ -37,6 +37,7 @@ struct SumArgs {
   int E;
   void* out;                    // [T, H]
   int out_dtype;
+  const int32_t* count_dev;     // optional: only rows t < *count_dev are written
 };
 
 struct CombineArgs {

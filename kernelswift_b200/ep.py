@@ -29,26 +29,28 @@ object;
 `CudaBackend` runs the library's kernels and is the only backend this package
 provides.
 
-With dedup=True (NCCL exchange) a token is sent to a rank once, however
-many of its k slots that rank holds (top-8 of 256 experts over 8 ranks
-reaches about 5.3 ranks per token, so a third of the rows stay home): the
-send row carries the token's local expert ids on that rank (-1 for slots
+Deduplicated exchange: a token is sent to a rank once, however many of its
+k slots that rank holds (top-8 of 256 experts over 8 ranks reaches about 5.3
+ranks per token, so a third of the rows stay home). The plan is one kernel
+(moe_ep_plan_dedup; `dedup_plan` restates it in torch for CPU backends): the
+send row carries the token's expert ids local to that rank (-1 for slots
 elsewhere) and their weights, the receiver runs moe_fused_experts with top_k
 = k (slots marked -1 are dropped) and returns one weighted, summed row per
-(token, rank), and the source adds the rows of the ranks it used
-(moe_combine_rows with unit weights). The plan is plain torch
-(`dedup_plan`).
+(token, rank), and the source adds the rows of the ranks it used. The NCCL
+exchange does this with dedup=True; the peer exchange always does.
 
-With exchange="peer" (ranks on one node, 2-8 GPUs) steps 2-4 and 6 are
+With exchange="peer" (ranks on one node, 2-8 GPUs) the all_to_alls are
 replaced by two kernels that move the rows themselves over NVLink
-(`PeerExchange`, the moe_ep_peer_* entry points): dispatch stores each row
-into the destination GPU's receive buffer (mapped with CUDA IPC) at an
-offset every rank derives from a counts matrix the ranks write into each
-other's memory, and combine loads each result row from the GPU that computed
-it. The ranks hand off through flags in each other's memory, so a step needs
-no host synchronisation and no NCCL call. The local expert pass then runs
-over the whole receive buffer (`capacity` rows; unused slots carry id -1 and
-are dropped by align).
+(`PeerExchange`, the moe_ep_peer_* entry points): dispatch stores each
+deduplicated row with its ids and weights into the destination GPU's
+receive buffer (mapped with CUDA IPC) at an offset every rank derives from a
+counts matrix the ranks write into each other's memory, and combine loads
+each rank's result row from the GPU that computed it. The ranks hand off
+through flags in each other's memory, so a step needs no host
+synchronisation and no NCCL call. The receive buffer is sized for the worst
+case (max_tokens * world rows); the local expert pass reads the count the
+dispatch stored on the device (num_tokens_dev) and touches only the rows
+that arrived.
 """
 from __future__ import annotations
 
@@ -125,6 +127,26 @@ class CudaBackend:
                   fm._ptr(self._plan_ws), self._plan_ws.numel(), fm._stream(dev))
         return order, send_eid, inv, counts
 
+    def plan_dedup(self, topk_ids: torch.Tensor, topk_weights: torch.Tensor, num_experts: int,
+                   world: int):
+        """dedup_plan's outputs from one kernel (moe_ep_plan_dedup); row
+        buffers are sized for num_tokens * world rows, counts[:world] says
+        how many are used."""
+        T, k = topk_ids.shape
+        dev = topk_ids.device
+        ids = topk_ids.contiguous()
+        w = topk_weights.contiguous()
+        n = T * world
+        tokens = torch.empty(n, dtype=torch.int32, device=dev)
+        send_eid = torch.empty(n, k, dtype=torch.int32, device=dev)
+        send_w = torch.empty(n, k, dtype=torch.float32, device=dev)
+        inv = torch.empty(T, world, dtype=torch.int32, device=dev)
+        counts = torch.empty(world + 1, dtype=torch.int64, device=dev)
+        _lib.call("moe_ep_plan_dedup", fm._ptr(ids), fm._code(ids), fm._ptr(w), fm._code(w), T,
+                  k, num_experts, world, fm._ptr(tokens), fm._ptr(send_eid), fm._ptr(send_w),
+                  fm._ptr(inv), fm._ptr(counts), fm._stream(dev))
+        return tokens, send_eid, send_w, inv, counts
+
     def pack(self, hidden: torch.Tensor, order: torch.Tensor, top_k: int) -> torch.Tensor:
         n = order.numel()
         rows = torch.empty(n, hidden.shape[1], dtype=hidden.dtype, device=hidden.device)
@@ -184,7 +206,7 @@ class PeerExchange:
     """
 
     def __init__(self, group, world: int, rank: int, capacity: int, hidden_size: int,
-                 dtype: torch.dtype, device: torch.device, wait_limit_ms: int = 0):
+                 top_k: int, dtype: torch.dtype, device: torch.device, wait_limit_ms: int = 0):
         if dtype not in (torch.bfloat16, torch.float16):
             raise ValueError("the peer exchange moves f16/bf16 rows")
         self.group = group
@@ -198,7 +220,7 @@ class PeerExchange:
         # every step below is agreed on by all ranks, so that a failure on one
         # rank raises on all of them instead of leaving the others in a
         # collective
-        st = lib.moe_ep_peer_create(world, rank, capacity, hidden_size,
+        st = lib.moe_ep_peer_create(world, rank, capacity, hidden_size, top_k,
                                     fm._code(torch.empty(0, dtype=dtype)), wait_limit_ms,
                                     ctypes.byref(handle), raw)
         detail = lib.moe_last_error().decode() if st else ""
@@ -216,17 +238,22 @@ class PeerExchange:
             lib.moe_ep_peer_destroy(handle)
             raise RuntimeError(f"peer exchange unavailable (rank {rank}: {detail or 'ok'})")
         self.handle = handle
-        rows, ids, res = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        rows, ids, wts, res, cnt = (ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p(),
+                                    ctypes.c_void_p(), ctypes.c_void_p())
         _lib.call("moe_ep_peer_buffers", handle, ctypes.byref(rows), ctypes.byref(ids),
-                  ctypes.byref(res))
+                  ctypes.byref(wts), ctypes.byref(res), ctypes.byref(cnt))
         shape = (capacity, hidden_size)
+        self.top_k = top_k
         self.recv_rows = torch.as_tensor(_DeviceArray(rows.value, shape, "<i2"),
                                          device=device).view(dtype)
-        self.recv_ids = torch.as_tensor(_DeviceArray(ids.value, (capacity,), "<i4"),
+        self.recv_ids = torch.as_tensor(_DeviceArray(ids.value, (capacity, top_k), "<i4"),
                                         device=device)
+        self.recv_weights = torch.as_tensor(_DeviceArray(wts.value, (capacity, top_k), "<f4"),
+                                            device=device)
         self.result_rows = torch.as_tensor(_DeviceArray(res.value, shape, "<i2"),
                                            device=device).view(dtype)
-        self.ones = torch.ones(capacity, 1, dtype=torch.float32, device=device)
+        # rows the last dispatch delivered (written by the dispatch kernel)
+        self.recv_count = torch.as_tensor(_DeviceArray(cnt.value, (1,), "<i4"), device=device)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
 
     def _all_ok(self, ok: bool) -> bool:
@@ -256,7 +283,8 @@ class PeerExchange:
         dist.barrier(group=self.group)
         _lib.load().moe_ep_peer_disconnect(self.handle)
         dist.barrier(group=self.group)
-        self.recv_rows = self.recv_ids = self.result_rows = None
+        self.recv_rows = self.recv_ids = self.recv_weights = self.result_rows = None
+        self.recv_count = None
         _lib.call("moe_ep_peer_destroy", self.handle)
         self.handle = None
 
@@ -277,11 +305,11 @@ class ExpertParallelMoE:
                  dedup: bool = False):
         """exchange: "nccl" (all_to_all), "peer" (NVLink peer memory, needs
         max_tokens: the most tokens a rank passes to one forward) or "auto"
-        (peer when max_tokens is given, the CUDA backend is used, the group
-        has 2-8 ranks on GPUs and dedup is off, else nccl). `dtype` is the row
-        dtype of the peer exchange (the hidden states' dtype). dedup: send a
-        token to a rank once however many of its slots the rank holds (NCCL
-        exchange only)."""
+        (peer when max_tokens is given, the CUDA backend is used and the
+        group has 2-8 ranks on GPUs, else nccl). `dtype` is the row dtype of
+        the peer exchange (the hidden states' dtype). dedup: send a token to
+        a rank once however many of its slots the rank holds (the NCCL
+        exchange's option; the peer exchange always does)."""
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -299,13 +327,11 @@ class ExpertParallelMoE:
         self.quant = quant
         if exchange == "auto":
             exchange = ("peer" if max_tokens is not None and isinstance(backend, CudaBackend)
-                        and 2 <= self.world <= _lib.EP_MAX_RANKS and not dedup else "nccl")
+                        and 2 <= self.world <= _lib.EP_MAX_RANKS else "nccl")
         if exchange not in ("nccl", "peer"):
             raise ValueError(f"unknown exchange {exchange!r}")
-        if dedup and exchange != "nccl":
-            raise ValueError("dedup is implemented for the nccl exchange")
         self.exchange = exchange
-        self.dedup = dedup
+        self.dedup = dedup or exchange == "peer"
         self._last_recv_eid = None
         self.peer = None
         self.max_tokens = max_tokens
@@ -314,9 +340,9 @@ class ExpertParallelMoE:
             if max_tokens is None or not isinstance(backend, CudaBackend):
                 raise ValueError("the peer exchange needs max_tokens and the CUDA backend")
             dev = backend.prep.w13.device
-            # worst case: every token of every rank routed to this rank's experts
-            self.peer = PeerExchange(group, self.world, self.rank, max_tokens * top_k * self.world,
-                                     backend.prep.hidden_size, dtype, dev, wait_limit_ms)
+            # worst case: every token of every rank has a slot on this rank
+            self.peer = PeerExchange(group, self.world, self.rank, max_tokens * self.world,
+                                     backend.prep.hidden_size, top_k, dtype, dev, wait_limit_ms)
 
     def forward(self, hidden: torch.Tensor, topk_weights: torch.Tensor,
                 topk_ids: torch.Tensor, stage_events=None) -> torch.Tensor:
@@ -362,8 +388,12 @@ class ExpertParallelMoE:
         T, H = hidden.shape
         k = topk_ids.shape[1]
         dev = hidden.device
-        tokens, send_eid, send_w, inv, counts = dedup_plan(topk_ids, topk_weights,
-                                                           self.num_experts, self.world)
+        if hasattr(self.backend, "plan_dedup"):
+            tokens, send_eid, send_w, inv, counts = self.backend.plan_dedup(
+                topk_ids, topk_weights, self.num_experts, self.world)
+        else:
+            tokens, send_eid, send_w, inv, counts = dedup_plan(topk_ids, topk_weights,
+                                                               self.num_experts, self.world)
         recv_counts = torch.empty(self.world, dtype=counts.dtype, device=dev)
         dist.all_to_all_single(recv_counts, counts[:self.world].contiguous(), group=self.group)
         both = torch.cat([counts, recv_counts]).cpu()  # the one host sync
@@ -372,6 +402,8 @@ class ExpertParallelMoE:
         send_split = both[:self.world].tolist()
         recv_split = both[self.world + 1:].tolist()
         n_recv = sum(recv_split)
+        n_send = sum(send_split)
+        tokens, send_eid, send_w = tokens[:n_send], send_eid[:n_send], send_w[:n_send]
         send_rows = self.backend.pack(hidden, tokens, 1)
         recv_rows = torch.empty(n_recv, H, dtype=hidden.dtype, device=dev)
         recv_eid = torch.empty(n_recv, k, dtype=torch.int32, device=dev)
@@ -399,21 +431,27 @@ class ExpertParallelMoE:
             raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens}")
         if hidden.dtype != px.dtype:
             raise ValueError(f"hidden states are {hidden.dtype}, the exchange moves {px.dtype}")
+        if k != px.top_k:
+            raise ValueError(f"top_k {k} differs from the exchange's {px.top_k}")
         dev = hidden.device
         stream = fm._stream(dev)
         # a misaligned view is copied: no rank's dispatch is refused while its peers wait
         hidden = fm._contig(hidden)
-        order, send_eid, inv, counts = self.backend.plan(topk_ids, self.num_experts, self.world)
-        _lib.call("moe_ep_peer_dispatch", px.handle, fm._ptr(hidden), T, k, fm._ptr(order),
-                  fm._ptr(send_eid), fm._ptr(counts), fm._ptr(px.status), stream)
-        fm.fused_experts(px.recv_rows, self.backend.prep, None, px.ones, px.recv_ids.view(-1, 1),
+        tokens, send_eid, send_w, inv, counts = self.backend.plan_dedup(
+            topk_ids, topk_weights, self.num_experts, self.world)
+        _lib.call("moe_ep_peer_dispatch", px.handle, fm._ptr(hidden), T, fm._ptr(tokens),
+                  fm._ptr(send_eid), fm._ptr(send_w), fm._ptr(counts), fm._ptr(px.status),
+                  stream)
+        # the received rows: one per (token, this rank), k local ids and
+        # weights each; only the first recv_count rows (on the device) exist
+        fm.fused_experts(px.recv_rows, self.backend.prep, None, px.recv_weights, px.recv_ids,
                          use_fp8_w8a8=self.quant.startswith("fp8"),
                          use_int8_w8a8=self.quant == "int8", out=px.result_rows,
-                         status=px.status, stage_events=stage_events, rows_only=True)
+                         status=px.status, stage_events=stage_events,
+                         num_tokens_dev=px.recv_count)
         out = torch.empty(T, H, dtype=hidden.dtype, device=dev)
-        w = topk_weights.contiguous()
-        _lib.call("moe_ep_peer_combine", px.handle, fm._ptr(inv), fm._ptr(w), fm._code(w), T, k,
-                  fm._ptr(out), fm._ptr(px.status), stream)
+        _lib.call("moe_ep_peer_combine", px.handle, fm._ptr(inv), T, fm._ptr(out),
+                  fm._ptr(px.status), stream)
         return out
 
     def rows_received(self) -> int:
@@ -421,7 +459,8 @@ class ExpertParallelMoE:
         (token, slot) pairs (synchronises in the peer and dedup exchanges;
         `last_rows_received` counts the token rows that crossed)."""
         if self.peer is not None:
-            return int((self.peer.recv_ids >= 0).sum())
+            n = int(self.peer.recv_count.item())
+            return int((self.peer.recv_ids[:n] >= 0).sum())
         if self.dedup:
             return int((self._last_recv_eid >= 0).sum())
         return self.last_rows_received

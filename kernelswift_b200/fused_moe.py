@@ -315,7 +315,7 @@ def _cached_prepare(w1, w2, quant, compute_dtype, w1_scale, w2_scale) -> Prepare
 # ---------------------------------------------------------------------------
 
 def _problem(hidden, prep: PreparedWeights, topk_weights, topk_ids, out, status,
-             events_array=None):
+             events_array=None, num_tokens_dev=None):
     p = _lib.MoeProblem()
     p.num_tokens = hidden.shape[0]
     p.hidden_size = prep.hidden_size
@@ -337,6 +337,7 @@ def _problem(hidden, prep: PreparedWeights, topk_weights, topk_ids, out, status,
     p.status = status.data_ptr() if status is not None else None
     p.stage_events = ctypes.cast(events_array, ctypes.c_void_p) if events_array is not None \
         else None
+    p.num_tokens_dev = num_tokens_dev.data_ptr() if num_tokens_dev is not None else None
     return p
 
 
@@ -358,6 +359,17 @@ def fused_experts_launches(num_tokens: int, hidden_size: int, intermediate_size:
     n = ctypes.c_int(0)
     _lib.call("moe_fused_experts_launches", ctypes.byref(p), int(rows_only), ctypes.byref(n))
     return n.value
+
+
+def fused_moe_launches(num_tokens: int, hidden_size: int, intermediate_size: int,
+                       num_experts: int, top_k: int, quant: str = "none",
+                       dtype: torch.dtype = torch.bfloat16) -> int:
+    """Kernels fused_moe launches (answers without a GPU): the routing kernel
+    plus fused_experts' launches."""
+    if num_tokens == 0:
+        return 0
+    return 1 + fused_experts_launches(num_tokens, hidden_size, intermediate_size, num_experts,
+                                      top_k, quant, dtype)
 
 
 def fused_experts_plan(num_tokens: int, hidden_size: int, intermediate_size: int,
@@ -401,12 +413,30 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
                   a2_scale: torch.Tensor | None = None, block_shape: list[int] | None = None,
                   out: torch.Tensor | None = None, status: torch.Tensor | None = None,
                   stage_events: ctypes.Array | None = None,
-                  rows_only: bool = False, scale_format: str = "fp32") -> torch.Tensor:
+                  rows_only: bool = False, scale_format: str | None = None,
+                  router_logits: torch.Tensor | None = None,
+                  renormalize: bool = True,
+                  num_tokens_dev: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = sum_j w[t,j] * W2[e] (silu(W1g[e] x_t) * W1u[e] x_t), e = ids[t,j].
 
-    scale_format (fp8 only): "fp32" (absmax / 448 block scales, promoted per
-    k-block) or "ue8m0" (power-of-two block scales applied by the tensor
-    core; weights prepared with quant "fp8-ue8m0").
+    scale_format (fp8 only): "ue8m0" (block scales rounded up to a power of
+    two, absmax / 448 <= scale < 2 * absmax / 448, applied by the tensor
+    core; weights prepared with quant "fp8-ue8m0") or "fp32" (scale = absmax
+    / 448 exactly, applied per k-block in the epilogue). The default (None)
+    is "ue8m0" for f32/f16/bf16 weights whose hidden and intermediate sizes
+    are multiples of 128 -- the faster kernel, at the same accuracy against
+    the unquantised layer -- and "fp32" for weights given already quantised
+    to e4m3 with their fp32 block scales.
+
+    router_logits [T, E] (f32/f16/bf16): route inside the same library call
+    (moe_fused_moe): topk_weights and topk_ids are then OUTPUT buffers [T, k]
+    that the routing of base.py:44-48 fills (softmax in fp32, top-k,
+    renormalised when `renormalize`).
+
+    num_tokens_dev: a one-element int32 CUDA tensor; only the first
+    num_tokens_dev[0] tokens take part and the other rows of `out` are left
+    untouched (an expert-parallel receive buffer, sized for the worst case,
+    processed at the size it got without a host sync).
 
     rows_only (top_k == 1): rows of tokens whose expert id is dropped are left
     unspecified instead of zeroed, which lets the down GEMM write the result
@@ -434,9 +464,13 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
         raise ValueError("expected hidden_states [T, H], topk_weights/topk_ids [T, k]")
     if topk_ids.shape[0] != hidden_states.shape[0]:
         raise ValueError("topk_ids and hidden_states disagree on the token count")
-    if scale_format not in ("fp32", "ue8m0"):
-        raise ValueError("scale_format must be 'fp32' or 'ue8m0'")
+    if scale_format not in (None, "fp32", "ue8m0"):
+        raise ValueError("scale_format must be None, 'fp32' or 'ue8m0'")
     quant = "fp8" if use_fp8_w8a8 else ("int8" if use_int8_w8a8 else "none")
+    if quant == "fp8" and scale_format is None and not isinstance(w1, PreparedWeights):
+        raw = w1.dtype in (torch.float32, torch.float16, torch.bfloat16)
+        sizes = w1.dim() == 3 and w1.shape[1] % 256 == 0 and w1.shape[2] % 128 == 0
+        scale_format = "ue8m0" if raw and sizes and w1_scale is None else "fp32"
     if quant == "fp8" and scale_format == "ue8m0":
         quant = "fp8-ue8m0"
     compute = torch.float16 if hidden_states.dtype == torch.float16 else torch.bfloat16
@@ -463,12 +497,30 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
     elif (out.shape != hidden.shape or out.dtype != hidden.dtype or not out.is_contiguous()
           or out.data_ptr() % 16):
         raise ValueError("out must be a contiguous, 16-byte aligned tensor like hidden_states")
-    p = _problem(hidden, prep, tw, ti, out, status, stage_events)
+    if num_tokens_dev is not None:
+        _check_cuda("num_tokens_dev", num_tokens_dev)
+        if num_tokens_dev.dtype != torch.int32 or num_tokens_dev.numel() < 1:
+            raise ValueError("num_tokens_dev must be an int32 CUDA tensor with one element")
+    p = _problem(hidden, prep, tw, ti, out, status, stage_events, num_tokens_dev)
     lib = _lib.load()
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.moe_fused_experts_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)),
                "moe_fused_experts_workspace_size")
     ws = _workspace(hidden.device, nbytes.value)
+    if router_logits is not None:
+        if rows_only:
+            raise ValueError("rows_only takes routed ids, not router logits")
+        _check_cuda("router_logits", router_logits)
+        logits = _contig(router_logits)
+        if logits.shape != (T, prep.num_experts):
+            raise ValueError(f"router_logits must be [T, E] = [{T}, {prep.num_experts}]")
+        if tw.data_ptr() != topk_weights.data_ptr() or ti.data_ptr() != topk_ids.data_ptr():
+            raise ValueError("topk_weights / topk_ids receive the routing: pass dense, "
+                             "16-byte aligned tensors")
+        _lib.check(lib.moe_fused_moe(ctypes.byref(p), _ptr(logits), _code(logits),
+                                     int(bool(renormalize)), _ptr(ws), ws.numel(),
+                                     _stream(hidden.device)), "moe_fused_moe")
+        return out
     entry = "moe_fused_experts_rows" if rows_only else "moe_fused_experts"
     _lib.check(getattr(lib, entry)(ctypes.byref(p), _ptr(ws), ws.numel(),
                                    _stream(hidden.device)), entry)
@@ -477,10 +529,17 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
 
 def fused_moe(hidden_states: torch.Tensor, w1, w2, gating_output: torch.Tensor, topk: int,
               renormalize: bool = True, **kwargs) -> torch.Tensor:
-    """Routing + experts: the whole of base.py:35-76 as one call."""
-    topk_weights, topk_ids = fused_topk(hidden_states, gating_output, topk, renormalize,
-                                        weights_dtype=hidden_states.dtype)
-    return fused_experts(hidden_states, w1, w2, topk_weights, topk_ids, **kwargs)
+    """Routing + experts: the whole of base.py:35-76 as one library call
+    (moe_fused_moe). The routing weights are rounded to the activation dtype
+    before use, as base.py:48 casts them; the result equals fused_topk
+    followed by fused_experts bit for bit."""
+    _check_cuda("hidden_states", hidden_states)
+    T = hidden_states.shape[0]
+    dev = hidden_states.device
+    topk_weights = torch.empty(T, topk, dtype=hidden_states.dtype, device=dev)
+    topk_ids = torch.empty(T, topk, dtype=torch.int32, device=dev)
+    return fused_experts(hidden_states, w1, w2, topk_weights, topk_ids,
+                         router_logits=gating_output, renormalize=renormalize, **kwargs)
 
 
 # ---------------------------------------------------------------------------
@@ -527,20 +586,17 @@ class ModelNew(nn.Module):
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         self._last_hidden = hidden_states  # for run_out (auto_bench kernel profiling)
-        # weights in the activation dtype, as base.py:48 casts them
-        topk_weights, topk_ids = fused_topk(hidden_states, router_logits, self.top_k,
-                                            self.renormalize, weights_dtype=hidden_states.dtype)
-        return fused_experts(hidden_states, self.prepared(hidden_states.dtype), None,
-                             topk_weights, topk_ids)
+        # routing + experts in one library call; the routing weights are in
+        # the activation dtype, as base.py:48 casts them
+        return fused_moe(hidden_states, self.prepared(hidden_states.dtype), None, router_logits,
+                         self.top_k, self.renormalize)
 
     def run_out(self, router_logits: torch.Tensor, out: torch.Tensor,
                 hidden_states: torch.Tensor | None = None) -> torch.Tensor:
         """auto_bench `--profile-mode kernel` hook: forward into `out`."""
         hidden = hidden_states if hidden_states is not None else self._last_hidden
-        topk_weights, topk_ids = fused_topk(hidden, router_logits, self.top_k, self.renormalize,
-                                            weights_dtype=hidden.dtype)
-        return fused_experts(hidden, self.prepared(hidden.dtype), None, topk_weights, topk_ids,
-                             out=out)
+        return fused_moe(hidden, self.prepared(hidden.dtype), None, router_logits, self.top_k,
+                         self.renormalize, out=out)
 
 
 # ---------------------------------------------------------------------------

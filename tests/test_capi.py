@@ -39,7 +39,7 @@ def test_binding_covers_header():
 
 def test_status_strings_and_version():
     lib = _lib.load()
-    assert lib.moe_abi_version() == 1
+    assert lib.moe_abi_version() == 2
     assert _lib.status_name(_lib.MOE_OK) == "MOE_OK"
     assert _lib.status_name(_lib.MOE_ERR_TIMEOUT) == "MOE_ERR_TIMEOUT"
     assert _lib.status_name(12345) == "MOE_ERR_UNKNOWN"
@@ -174,6 +174,8 @@ def test_launch_count_query_without_gpu():
 
     assert fm.fused_experts_launches(4096, 4096, 14336, 8, 2) == 7      # 3-launch align..sum
     assert fm.fused_experts_launches(1, 2048, 768, 128, 8) == 2         # decode kernels
+    assert fm.fused_moe_launches(1, 2048, 768, 128, 8) == 3             # routing + decode
+    assert fm.fused_moe_launches(4096, 4096, 14336, 8, 2) == 8          # routing + 7
     assert fm.fused_experts_launches(64, 2048, 768, 128, 8) == 6        # split gate-up
     assert fm.fused_experts_launches(64, 7168, 2048, 256, 8, "fp8") == 6
     assert fm.fused_experts_launches(20000, 512, 256, 8, 1) == 7        # 3-launch align

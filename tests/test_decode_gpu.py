@@ -1,8 +1,10 @@
 """GPU: the decode path of moe_fused_experts (at most 16 routed rows, 16-bit
 activations, unquantised weights: two weight-streaming kernels instead of the
 align/gather/GEMM pipeline) against the fp32 oracle, with dropped slots,
-int32/int64 ids, f32/bf16 weights and fp16 activations; and the boundary
-with the tensor-core path (17 routed rows)."""
+int32/int64 ids, f32/bf16 weights and fp16 activations; the boundary with
+the tensor-core path (17 routed rows); and moe_fused_moe (routing and
+experts in one library call): bit-identical to fused_topk followed by
+fused_experts."""
 import os
 import subprocess
 import sys
@@ -34,6 +36,7 @@ def problem(T, H, I, E, k, dtype, seed):
     (1, 512, 1024, 8, 2, torch.bfloat16),     # Mixtral-like top-2
     (5, 384, 256, 8, 2, torch.float16),
     (1, 128, 32, 4, 1, torch.bfloat16),       # smallest widths the planner takes
+    (1, 2048, 768, 128, 8, torch.bfloat16),   # Qwen3-30B-A3B T=1
     (1, 256, 128, 32, 12, torch.bfloat16),    # 12 slots of one token
     (17, 256, 128, 16, 1, torch.bfloat16),    # 17 rows: tensor-core path
 ])
@@ -93,3 +96,78 @@ def run_case():
     prep = fm.prepare_weights(w1.to(dev), w2.to(dev), "none", torch.bfloat16)
     out = fm.fused_experts(hidden.to(dev), prep, None, w.to(dev), ids.to(torch.int32).to(dev))
     return out.cpu()
+
+
+ROUTE_CASES = [
+    # T, H, I, E, k, dtype, renormalize
+    (1, 2048, 768, 128, 8, torch.bfloat16, True),    # Qwen3-30B-A3B T=1
+    (2, 2048, 768, 128, 8, torch.bfloat16, True),    # 16 routed rows
+    (1, 512, 1024, 8, 2, torch.float16, True),
+    (3, 384, 256, 256, 4, torch.bfloat16, False),    # 256 experts, no renormalisation
+    (8, 256, 128, 8, 1, torch.bfloat16, True),
+    (1, 256, 128, 512, 8, torch.bfloat16, True),     # 512 experts
+    (64, 512, 256, 16, 4, torch.bfloat16, True),     # tensor-core path
+]
+
+
+@pytest.mark.parametrize("T,H,I,E,k,dtype,renorm", ROUTE_CASES,
+                         ids=[f"T{c[0]}_H{c[1]}_E{c[3]}_k{c[4]}" for c in ROUTE_CASES])
+def test_fused_moe_equals_two_calls(cuda_device, T, H, I, E, k, dtype, renorm):
+    """fused_moe (moe_fused_moe: routing inside the library call) writes the
+    same ids and weights as fused_topk and the same output as fused_topk +
+    fused_experts, bit for bit, and matches the oracle."""
+    hidden, logits, w1, w2 = problem(T, H, I, E, k, dtype, seed=T * 7 + E)
+    dev = cuda_device
+    prep = fm.prepare_weights(w1.to(dev), w2.to(dev), "none", dtype)
+    hd, ld = hidden.to(dev), logits.to(dev)
+    w_ref, ids_ref = fm.fused_topk(hd, ld, k, renorm, weights_dtype=dtype)
+    two = fm.fused_experts(hd, prep, None, w_ref, ids_ref)
+    w_out = torch.full((T, k), -1.0, dtype=dtype, device=dev)
+    ids_out = torch.full((T, k), -1, dtype=torch.int32, device=dev)
+    one = fm.fused_experts(hd, prep, None, w_out, ids_out, router_logits=ld,
+                           renormalize=renorm)
+    torch.cuda.synchronize()
+    assert torch.equal(ids_out, ids_ref) and torch.equal(w_out, w_ref)
+    assert torch.equal(one, two)
+    again = fm.fused_moe(hd, prep, None, ld, k, renorm)
+    assert torch.equal(again, one)
+    w, ids = orc.route(logits, k, renorm)
+    assert torch.equal(ids_out.cpu().long(), ids)
+    ref = orc.fused_experts(hidden, w1, w2, w, ids)
+    torch.testing.assert_close(one.float().cpu(), ref, **TOL)
+
+
+def test_fused_moe_bf16_logits_and_launch_count(cuda_device):
+    """bf16 router logits route like fused_topk on them; the fused call's
+    launch count is the routing kernel plus fused_experts' launches."""
+    T, H, I, E, k = 1, 2048, 768, 128, 8
+    hidden, logits, w1, w2 = problem(T, H, I, E, k, torch.bfloat16, seed=5)
+    dev = cuda_device
+    prep = fm.prepare_weights(w1.to(dev), w2.to(dev), "none", torch.bfloat16)
+    hd, lb = hidden.to(dev), logits.to(torch.bfloat16).to(dev)
+    w_ref, ids_ref = fm.fused_topk(hd, lb, k, weights_dtype=torch.bfloat16)
+    two = fm.fused_experts(hd, prep, None, w_ref, ids_ref)
+    assert torch.equal(fm.fused_moe(hd, prep, None, lb, k), two)
+    assert fm.fused_moe_launches(T, H, I, E, k) == 3
+    assert fm.fused_moe_launches(64, H, I, E, k) == 1 + fm.fused_experts_launches(64, H, I, E, k)
+
+
+def test_modelnew_decode_graph_replay(cuda_device):
+    """ModelNew at T=1 (routing kernel and the two decode kernels) captured in
+    a CUDA graph: replays equal eager calls bit for bit."""
+    T, H, I, E, k = 1, 2048, 768, 128, 8
+    m = fm.ModelNew(E, k, H, I).to(cuda_device)
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    with torch.no_grad():
+        m.w1.normal_(0, H ** -0.5, generator=g)
+        m.w2.normal_(0, I ** -0.5, generator=g)
+    cap = fm.CapturedMoE(m, T, H, E, dtype=torch.bfloat16, device=cuda_device)
+    for seed in (1, 2, 3):
+        gi = torch.Generator(device=cuda_device).manual_seed(seed)
+        hidden = torch.randn(T, H, generator=gi, device=cuda_device).to(torch.bfloat16)
+        logits = torch.randn(T, E, generator=gi, device=cuda_device)
+        with torch.no_grad():
+            eager = m(hidden, logits).clone()
+        out = cap(hidden, logits)
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)

@@ -7,9 +7,9 @@ by a test-only CPU backend built on the oracle. The deduplicated exchange
 second test makes one rank
 fail before its first collective and checks that the other rank's forward
 ends with an error within the process group's timeout instead of hanging. A
-third replays the peer-memory exchange's placement rule (counts matrix,
-destination offsets, combine addressing) on 2 and 4 ranks with uneven token
-counts.
+third replays the peer-memory exchange's placement rule (deduplicated
+rows, counts matrix, destination offsets, the receiver's row count, combine
+addressing) on 2 and 4 ranks with uneven token counts.
 """
 import datetime
 import os
@@ -204,10 +204,12 @@ def test_ep_rank_failure_surfaces_as_error():
 
 # ---------------------------------------------------------------------------
 # The peer-memory exchange's placement rule, restated on gloo ranks: every
-# rank learns the full counts matrix (the kernels write rows of it into each
-# other's memory; here all_gather), a sender's rows for rank d start at
-# dst_off[d] = sum of what lower ranks send to d, and the combine reads slot
-# r's result from rank d at dst_off[d] + (send position - send_start[d]).
+# rank learns the full matrix of deduplicated row counts (the kernels write
+# rows of it into each other's memory; here all_gather), a sender's rows for
+# rank d start at dst_off[d] = sum of what lower ranks send to d, the
+# receiver returns one weighted row per (token, rank) over its first n_recv
+# rows, and the combine adds, for each token, the rows of the ranks it was
+# sent to, read at dst_off[d] + (send row - send_start[d]).
 # ---------------------------------------------------------------------------
 
 def peer_worker(rank, world, port, E, k, T, H, I, result_q):
@@ -216,6 +218,8 @@ def peer_worker(rank, world, port, E, k, T, H, I, result_q):
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=30))
     try:
+        from kernelswift_b200.ep import dedup_plan
+
         w1, w2 = problem(E, H, I, seed=0)
         el = E // world
         backend = CpuBackend(w1[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el])
@@ -224,7 +228,7 @@ def peer_worker(rank, world, port, E, k, T, H, I, result_q):
         hidden = torch.randn(Tr, H, generator=g)
         logits = torch.randn(Tr, E, generator=g) + torch.linspace(0, 1.5, E)
         w, ids = orc.route(logits, k)
-        order, send_eid, inv, counts = backend.plan(ids, E, world)
+        tokens, send_eid, send_w, inv, counts = dedup_plan(ids, w, E, world)
         # counts matrix on every rank
         mat = [torch.zeros(world, dtype=torch.int64) for _ in range(world)]
         dist.all_gather(mat, counts[:world].clone())
@@ -232,41 +236,43 @@ def peer_worker(rank, world, port, E, k, T, H, I, result_q):
         send_start = torch.cat([torch.zeros(1, dtype=torch.int64), counts[:world].cumsum(0)])
         dst_off = torch.stack([mat[:rank, d].sum() for d in range(world)])
         n_recv = int(mat[:, rank].sum())
-        capacity = max(int(mat[:, d].sum()) for d in range(world))
-        # dispatch: rows land at dst_off[d] + i in rank d's receive buffer
-        rows = backend.pack(hidden, order, k)
+        capacity = (T + 3 * (world - 1)) * world      # max_tokens * world
+        # dispatch: rows, ids and weights land at dst_off[d] + i in rank d's buffer
+        rows = backend.pack(hidden, tokens, 1)
         recv = torch.zeros(capacity, H)
-        recv_id = torch.full((capacity,), -1, dtype=torch.int32)
+        recv_id = torch.full((capacity, k), -7, dtype=torch.int32)  # never read past n_recv
+        recv_w = torch.zeros(capacity, k)
         for src in range(world):
-            # every rank's placement, replayed by every rank from the matrix
             part = [torch.zeros(int(mat[src, d]), H) for d in range(world)]
-            pid = [torch.zeros(int(mat[src, d]), dtype=torch.int32) for d in range(world)]
+            pid = [torch.zeros(int(mat[src, d]), k, dtype=torch.int32) for d in range(world)]
+            pw = [torch.zeros(int(mat[src, d]), k) for d in range(world)]
             if src == rank:
                 for d in range(world):
-                    part[d] = rows[int(send_start[d]):int(send_start[d + 1])]
-                    pid[d] = send_eid[int(send_start[d]):int(send_start[d + 1])]
+                    sl = slice(int(send_start[d]), int(send_start[d + 1]))
+                    part[d], pid[d], pw[d] = rows[sl], send_eid[sl], send_w[sl]
             for d in range(world):
                 dist.broadcast(part[d], src)
                 dist.broadcast(pid[d], src)
+                dist.broadcast(pw[d], src)
             if mat[src, rank] > 0:
                 off = int(mat[:src, rank].sum())
-                recv[off:off + int(mat[src, rank])] = part[rank]
-                recv_id[off:off + int(mat[src, rank])] = pid[rank]
-        assert int((recv_id >= 0).sum()) == n_recv
-        valid = recv_id >= 0
+                n = int(mat[src, rank])
+                recv[off:off + n], recv_id[off:off + n], recv_w[off:off + n] = (
+                    part[rank], pid[rank], pw[rank])
+        # the expert pass over the first n_recv rows only
         res = torch.zeros(capacity, H)
-        res[valid] = backend.experts(recv[valid], recv_id[valid])
-        # combine: slot r reads rank d's result at dst_off[d] + (p - send_start[d])
+        res[:n_recv] = backend.experts_weighted(recv[:n_recv], recv_id[:n_recv],
+                                                recv_w[:n_recv])
         results = [torch.zeros(capacity, H) for _ in range(world)]
         dist.all_gather(results, res)
         out = torch.zeros(Tr, H)
-        for r in range(Tr * k):
-            p = int(inv[r])
-            if p < 0:
-                continue
-            d = int(torch.searchsorted(send_start[1:], p, right=True))
-            row = int(dst_off[d]) + p - int(send_start[d])
-            out[r // k] += w.reshape(-1)[r] * results[d][row]
+        for t in range(Tr):
+            for d in range(world):
+                p = int(inv[t, d])
+                if p < 0:
+                    continue
+                assert int(send_start[d]) <= p < int(send_start[d + 1])
+                out[t] += results[d][int(dst_off[d]) + p - int(send_start[d])]
         ref = orc.fused_experts(hidden, w1, w2, w, ids)
         result_q.put((rank, "ok", float((out - ref).abs().max())))
     except Exception as exc:
@@ -275,7 +281,7 @@ def peer_worker(rank, world, port, E, k, T, H, I, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,E,k", [(2, 8, 2), (4, 16, 4)])
+@pytest.mark.parametrize("world,E,k", [(2, 8, 2), (4, 16, 4), (4, 32, 8)])
 def test_peer_placement_rule_matches_oracle(world, E, k):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

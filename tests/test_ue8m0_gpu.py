@@ -194,3 +194,25 @@ def test_both_tile_widths_agree(cuda_device):
     n = int(npp.item())
     valid = (s[:n] < ids.numel()).nonzero().view(-1)
     assert torch.equal(acts[0].cpu()[valid], acts[1].cpu()[valid])
+
+
+def test_default_fp8_recipe(cuda_device):
+    """use_fp8_w8a8 without a scale format: unquantised weights take the
+    power-of-two recipe (bit-identical to scale_format="ue8m0"); weights
+    given as e4m3 with fp32 block scales take the absmax / 448 kernel."""
+    T, H, I, E, k = 60, 256, 256, 8, 2
+    w1, w2 = weights(E, H, I, seed=21, dev=cuda_device)
+    g = torch.Generator().manual_seed(22)
+    hidden = torch.randn(T, H, generator=g).to(torch.bfloat16).to(cuda_device)
+    w, ids = orc.route(torch.randn(T, E, generator=g), k)
+    w, ids = w.to(cuda_device), ids.to(cuda_device)
+    default = fm.fused_experts(hidden, w1, w2, w, ids, use_fp8_w8a8=True).clone()
+    mx = fm.fused_experts(hidden, w1, w2, w, ids, use_fp8_w8a8=True, scale_format="ue8m0")
+    assert torch.equal(default, mx)
+    q1, s1 = orc.quant_fp8_block(w1.cpu())
+    q2, s2 = orc.quant_fp8_block(w2.cpu())
+    pre = fm.fused_experts(hidden, q1.to(cuda_device), q2.to(cuda_device), w, ids,
+                           use_fp8_w8a8=True, w1_scale=s1.to(cuda_device),
+                           w2_scale=s2.to(cuda_device)).clone()
+    f32 = fm.fused_experts(hidden, w1, w2, w, ids, use_fp8_w8a8=True, scale_format="fp32")
+    assert torch.equal(pre, f32)

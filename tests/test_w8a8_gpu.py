@@ -1,5 +1,7 @@
-"""GPU: fp8 block-scaled and int8 per-channel W8A8 paths against the fp32
-dequantised oracle (relative L2 <= 5e-2)."""
+"""GPU: fp8 block-scaled (scale = absmax / 448, scale_format "fp32") and
+int8 per-channel W8A8 paths against the fp32 dequantised oracle (relative
+L2 <= 5e-2). The power-of-two scale recipe has its own tests
+(test_ue8m0_gpu.py)."""
 import pytest
 import torch
 
@@ -47,7 +49,7 @@ def check_tokens(T, ids, extra):
 def test_fp8_block_w8a8(cuda_device, name, T, H, I, E, k, extra):
     hidden, w1, w2, w, ids = problem(T, H, I, E, k, seed=T + H)
     out = fm.fused_experts(hidden, w1, w2, w.to(cuda_device), ids.to(cuda_device),
-                           use_fp8_w8a8=True, block_shape=[128, 128])
+                           use_fp8_w8a8=True, block_shape=[128, 128], scale_format="fp32")
     torch.cuda.synchronize()
     tokens = check_tokens(T, ids, extra)
     ref = oracle_on_tokens("fp8", hidden, w1, w2, w, ids, tokens)
@@ -81,7 +83,7 @@ def test_fp8_prequantised_weights_pass_through(cuda_device):
     q1, s1 = orc.quant_fp8_block(w1.cpu())
     q2, s2 = orc.quant_fp8_block(w2.cpu())
     a = fm.fused_experts(hidden, w1, w2, w.to(cuda_device), ids.to(cuda_device),
-                         use_fp8_w8a8=True).clone()
+                         use_fp8_w8a8=True, scale_format="fp32").clone()
     b = fm.fused_experts(hidden, q1.to(cuda_device), q2.to(cuda_device), w.to(cuda_device),
                          ids.to(cuda_device), use_fp8_w8a8=True, w1_scale=s1.to(cuda_device),
                          w2_scale=s2.to(cuda_device))
