@@ -393,9 +393,9 @@ def main():
             print(f"peer exchange unavailable, using NCCL: {exc}", file=sys.stderr)
             ep = make_ep("nccl")
 
-        def step(stage_arr=None):
+        def step(stage_arr=None, exchange_evs=None):
             tw, ti = fm.fused_topk(hidden, logits, k, weights_dtype=hidden.dtype)
-            return ep(hidden, tw, ti, stage_events=stage_arr)
+            return ep(hidden, tw, ti, stage_events=stage_arr, exchange_events=exchange_evs)
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -446,6 +446,15 @@ def main():
         for ev in evs:
             ev.record()  # create the events before the timed region
     stage_arrs = [fm.stage_event_array(evs) for evs in stage_evs]
+    ex_evs = None
+    if world > 1:
+        from kernelswift_b200.ep import EXCHANGE_STAGES
+        # boundaries of the exchange stages of every timed step
+        ex_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(EXCHANGE_STAGES) + 1)]
+                  for _ in range(K)]
+        for evs in ex_evs:
+            for ev in evs:
+                ev.record()
     torch.cuda.synchronize()
 
     if world > 1:
@@ -455,7 +464,10 @@ def main():
     for i in range(K):
         flush()
         starts[i].record()
-        step(stage_arrs[i])
+        if ex_evs is None:
+            step(stage_arrs[i])
+        else:
+            step(stage_arrs[i], ex_evs[i])
         ends[i].record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
@@ -466,6 +478,17 @@ def main():
     total_ms = sum(step_ms)
     stage_ms = {name: sum(evs[j].elapsed_time(evs[j + 1]) for evs in stage_evs) / K
                 for j, name in enumerate(_lib.STAGES)}
+    exchange_ms = None
+    if ex_evs is not None:
+        # per stage: the mean over the timed steps, then the max over ranks
+        # ("route" = the routing kernel, from the step's start to the plan)
+        names = ("route",) + EXCHANGE_STAGES
+        per = [sum(starts[i].elapsed_time(ex_evs[i][0]) for i in range(K)) / K]
+        per += [sum(ex_evs[i][j].elapsed_time(ex_evs[i][j + 1]) for i in range(K)) / K
+                for j in range(len(EXCHANGE_STAGES))]
+        t = torch.tensor(per, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        exchange_ms = dict(zip(names, (float(x) for x in t.tolist())))
     use_graph = args.graph and world == 1
     graph = None
     if use_graph:
@@ -688,6 +711,7 @@ def main():
                                        "nccl-dedup" if ep.dedup else "nccl")),
             "tflops": tflops,
             "stage_ms": stage_ms,
+            **({"exchange_ms": exchange_ms} if exchange_ms is not None else {}),
             "align": align_report,
             "roofline": roofline,
             "cpu_baseline": cpu,

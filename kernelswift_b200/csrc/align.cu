@@ -97,6 +97,15 @@ __device__ __forceinline__ void count_subchunk(const IdT* ids, int64_t base, int
 // Places ids[base, min(base + 1024, end)) (one per thread) at their final
 // slots. running[e] is expert e's next free slot; warp_cnt[32][E] must be
 // all zero on entry and is all zero again on exit.
+//
+// An id's slot = running[e] + (ids of e in the warps before its warp) + (its
+// rank among the lanes of its warp with the same expert). The warp leader of
+// each expert group stores the group size in warp_cnt[warp][e]; one thread
+// per expert then turns its 32-entry column into absolute bases (an
+// exclusive scan over the warps, starting at running[e]; loads are issued eight
+// at a time, independent of one another), and every id reads its base
+// with one shared-memory load. Entries of warps without the expert stay
+// zero, and each leader zeroes its own entry after its warp has read it.
 template <typename IdT>
 __device__ __forceinline__ void scatter_subchunk(const IdT* ids, int64_t base,
                                                  int64_t end, int E,
@@ -107,23 +116,28 @@ __device__ __forceinline__ void scatter_subchunk(const IdT* ids, int64_t base,
   const int e = (i < end) ? load_id(ids, i, E) : -1;
   const unsigned peers = __match_any_sync(0xffffffffu, e);
   const int rank = __popc(peers & lanemask_lt());
-  if (e >= 0 && lane == __ffs(peers) - 1) warp_cnt[warp * E + e] = __popc(peers);
-  __syncthreads();
-  if (e >= 0) {
-    int prefix = 0;
-    for (int w = 0; w < warp; ++w) prefix += warp_cnt[w * E + e];
-    sorted[running[e] + prefix + rank] = static_cast<int32_t>(i);
-  }
+  const bool leader = e >= 0 && lane == __ffs(peers) - 1;
+  if (leader) warp_cnt[warp * E + e] = __popc(peers);
   __syncthreads();
   for (int ee = tid; ee < E; ee += kThreads) {
-    int s = 0;
-#pragma unroll 8
-    for (int w = 0; w < 32; ++w) {
-      s += warp_cnt[w * E + ee];
-      warp_cnt[w * E + ee] = 0;
+    int s = running[ee];
+#pragma unroll
+    for (int w0 = 0; w0 < 32; w0 += 8) {
+      int c[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) c[u] = warp_cnt[(w0 + u) * E + ee];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (c[u] != 0) warp_cnt[(w0 + u) * E + ee] = s;
+        s += c[u];
+      }
     }
-    running[ee] += s;
+    running[ee] = s;
   }
+  __syncthreads();
+  if (e >= 0) sorted[warp_cnt[warp * E + e] + rank] = static_cast<int32_t>(i);
+  __syncwarp();
+  if (leader) warp_cnt[warp * E + e] = 0;
   __syncthreads();
 }
 

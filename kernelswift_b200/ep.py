@@ -289,6 +289,10 @@ class PeerExchange:
         self.handle = None
 
 
+# the stages of an expert-parallel step that `exchange_events` brackets
+EXCHANGE_STAGES = ("plan", "dispatch", "experts", "combine")
+
+
 class ExpertParallelMoE:
     """Fused MoE with experts sharded over the ranks of `group`.
 
@@ -333,6 +337,7 @@ class ExpertParallelMoE:
         self.exchange = exchange
         self.dedup = dedup or exchange == "peer"
         self._last_recv_eid = None
+        self._evs = None
         self.peer = None
         self.max_tokens = max_tokens
         self.last_rows_received = 0
@@ -345,9 +350,13 @@ class ExpertParallelMoE:
                                      backend.prep.hidden_size, top_k, dtype, dev, wait_limit_ms)
 
     def forward(self, hidden: torch.Tensor, topk_weights: torch.Tensor,
-                topk_ids: torch.Tensor, stage_events=None) -> torch.Tensor:
+                topk_ids: torch.Tensor, stage_events=None, exchange_events=None) -> torch.Tensor:
         """`stage_events` (fused_moe.stage_event_array) times the launches of
-        the local expert computation."""
+        the local expert computation. `exchange_events`, a list of
+        len(EXCHANGE_STAGES) + 1 torch.cuda.Event, is recorded on the current
+        stream at the boundaries of the step's exchange stages (plan,
+        dispatch, local experts, combine)."""
+        self._evs = exchange_events
         if self.peer is not None:
             return self._forward_peer(hidden, topk_weights, topk_ids, stage_events)
         if self.dedup:
@@ -356,7 +365,9 @@ class ExpertParallelMoE:
         k = topk_ids.shape[1]
         dev = hidden.device
         numel = topk_ids.numel()
+        self._mark(0)
         order, send_eid, inv, counts = self.backend.plan(topk_ids, self.num_experts, self.world)
+        self._mark(1)
         recv_counts = torch.empty(self.world, dtype=counts.dtype, device=dev)
         dist.all_to_all_single(recv_counts, counts[:self.world].contiguous(), group=self.group)
         both = torch.cat([counts, recv_counts]).cpu()  # the one host sync
@@ -376,24 +387,30 @@ class ExpertParallelMoE:
         dist.all_to_all_single(recv_eid, send_eid, recv_split, send_split, group=self.group)
 
         self.last_rows_received = n_recv
+        self._mark(2)
         if stage_events is not None:
             out_rows = self.backend.experts(recv_rows, recv_eid, stage_events=stage_events)
         else:
             out_rows = self.backend.experts(recv_rows, recv_eid)
+        self._mark(3)
         back = torch.empty(n_send, H, dtype=out_rows.dtype, device=dev)
         dist.all_to_all_single(back, out_rows, send_split, recv_split, group=self.group)
-        return self.backend.combine(back, inv, topk_weights, T, k)
+        out = self.backend.combine(back, inv, topk_weights, T, k)
+        self._mark(4)
+        return out
 
     def _forward_dedup(self, hidden, topk_weights, topk_ids, stage_events=None):
         T, H = hidden.shape
         k = topk_ids.shape[1]
         dev = hidden.device
+        self._mark(0)
         if hasattr(self.backend, "plan_dedup"):
             tokens, send_eid, send_w, inv, counts = self.backend.plan_dedup(
                 topk_ids, topk_weights, self.num_experts, self.world)
         else:
             tokens, send_eid, send_w, inv, counts = dedup_plan(topk_ids, topk_weights,
                                                                self.num_experts, self.world)
+        self._mark(1)
         recv_counts = torch.empty(self.world, dtype=counts.dtype, device=dev)
         dist.all_to_all_single(recv_counts, counts[:self.world].contiguous(), group=self.group)
         both = torch.cat([counts, recv_counts]).cpu()  # the one host sync
@@ -413,15 +430,19 @@ class ExpertParallelMoE:
         dist.all_to_all_single(recv_w, send_w, recv_split, send_split, group=self.group)
         self.last_rows_received = n_recv
         self._last_recv_eid = recv_eid
+        self._mark(2)
         if stage_events is not None:
             out_rows = self.backend.experts_weighted(recv_rows, recv_eid, recv_w,
                                                      stage_events=stage_events)
         else:
             out_rows = self.backend.experts_weighted(recv_rows, recv_eid, recv_w)
+        self._mark(3)
         back = torch.empty(tokens.numel(), H, dtype=out_rows.dtype, device=dev)
         dist.all_to_all_single(back, out_rows, send_split, recv_split, group=self.group)
         ones = torch.ones(T, self.world, dtype=torch.float32, device=dev)
-        return self.backend.combine(back, inv.reshape(-1), ones, T, self.world)
+        out = self.backend.combine(back, inv.reshape(-1), ones, T, self.world)
+        self._mark(4)
+        return out
 
     def _forward_peer(self, hidden, topk_weights, topk_ids, stage_events=None):
         px = self.peer
@@ -437,11 +458,14 @@ class ExpertParallelMoE:
         stream = fm._stream(dev)
         # a misaligned view is copied: no rank's dispatch is refused while its peers wait
         hidden = fm._contig(hidden)
+        self._mark(0)
         tokens, send_eid, send_w, inv, counts = self.backend.plan_dedup(
             topk_ids, topk_weights, self.num_experts, self.world)
+        self._mark(1)
         _lib.call("moe_ep_peer_dispatch", px.handle, fm._ptr(hidden), T, fm._ptr(tokens),
                   fm._ptr(send_eid), fm._ptr(send_w), fm._ptr(counts), fm._ptr(px.status),
                   stream)
+        self._mark(2)
         # the received rows: one per (token, this rank), k local ids and
         # weights each; only the first recv_count rows (on the device) exist
         fm.fused_experts(px.recv_rows, self.backend.prep, None, px.recv_weights, px.recv_ids,
@@ -449,10 +473,17 @@ class ExpertParallelMoE:
                          use_int8_w8a8=self.quant == "int8", out=px.result_rows,
                          status=px.status, stage_events=stage_events,
                          num_tokens_dev=px.recv_count)
+        self._mark(3)
         out = torch.empty(T, H, dtype=hidden.dtype, device=dev)
         _lib.call("moe_ep_peer_combine", px.handle, fm._ptr(inv), T, fm._ptr(out),
                   fm._ptr(px.status), stream)
+        self._mark(4)
         return out
+
+    def _mark(self, i: int) -> None:
+        """Records exchange event i of this step, if the caller passed some."""
+        if self._evs is not None:
+            self._evs[i].record()
 
     def rows_received(self) -> int:
         """Rows this rank's experts processed in the last forward, i.e. routed
