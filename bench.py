@@ -461,35 +461,46 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
+    # the timed steps carry no events besides their start and end: an event
+    # record between two kernels costs a few microseconds and breaks the
+    # programmatic overlap of the launches around it
     for i in range(K):
         flush()
         starts[i].record()
-        if ex_evs is None:
-            step(stage_arrs[i])
-        else:
-            step(stage_arrs[i], ex_evs[i])
+        step()
         ends[i].record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
-    clocks.__exit__(None, None, None)
     if world > 1:
         dist.barrier()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(step_ms)
-    stage_ms = {name: sum(evs[j].elapsed_time(evs[j + 1]) for evs in stage_evs) / K
-                for j, name in enumerate(_lib.STAGES)}
-    exchange_ms = None
-    if ex_evs is not None:
-        # per stage: the mean over the timed steps, then the max over ranks
-        # ("route" = the routing kernel, from the step's start to the plan)
-        names = ("route",) + EXCHANGE_STAGES
-        per = [sum(starts[i].elapsed_time(ex_evs[i][0]) for i in range(K)) / K]
-        per += [sum(ex_evs[i][j].elapsed_time(ex_evs[i][j + 1]) for i in range(K)) / K
-                for j in range(len(EXCHANGE_STAGES))]
-        t = torch.tensor(per, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        exchange_ms = dict(zip(names, (float(x) for x in t.tolist())))
     use_graph = args.graph and world == 1
+    stage_ms = {name: 0.0 for name in _lib.STAGES}
+    exchange_ms = None
+    if not use_graph:
+        # per-stage breakdown from K more steps, instrumented (untimed as a whole)
+        inst = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+        for i in range(K):
+            flush()
+            inst[i].record()
+            if ex_evs is None:
+                step(stage_arrs[i])
+            else:
+                step(stage_arrs[i], ex_evs[i])
+        torch.cuda.synchronize()
+        stage_ms = {name: sum(evs[j].elapsed_time(evs[j + 1]) for evs in stage_evs) / K
+                    for j, name in enumerate(_lib.STAGES)}
+        if ex_evs is not None:
+            # per stage: the mean over the instrumented steps, then the max over
+            # ranks ("route" = the routing kernel, from the step's start to the plan)
+            names = ("route",) + EXCHANGE_STAGES
+            per = [sum(inst[i].elapsed_time(ex_evs[i][0]) for i in range(K)) / K]
+            per += [sum(ex_evs[i][j].elapsed_time(ex_evs[i][j + 1]) for i in range(K)) / K
+                    for j in range(len(EXCHANGE_STAGES))]
+            t = torch.tensor(per, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            exchange_ms = dict(zip(names, (float(x) for x in t.tolist())))
     graph = None
     if use_graph:
         # The whole forward (routing + all kernels) captured once and replayed:
@@ -518,13 +529,18 @@ def main():
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize()
+        wall0 = time.perf_counter()
         for i in range(K):
             flush()
             starts[i].record()
             graph.replay()
             ends[i].record()
         torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
         total_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
+    # the clock samples cover the heat steps and every timed step (the graph
+    # replays included)
+    clocks.__exit__(None, None, None)
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -323,11 +323,18 @@ int moe_fused_experts(const moe_problem_t* p, void* workspace,
  * into p->topk_weights / p->topk_ids -- OUTPUTS here, [T, k] in
  * p->weights_dtype / p->ids_dtype -- then moe_fused_experts with those
  * weights (moe_topk_softmax's kernel, then moe_fused_experts' launches, on
- * `stream`). Workspace as for moe_fused_experts_workspace_size. Replaces
- * Model.forward (base.py:35-76).
+ * `stream`; on the decode path -- at most 16 routed rows -- with F32 logits
+ * over at most 256 experts the first decode kernel routes the tokens itself,
+ * with the same code, and no routing kernel is launched). Workspace as for
+ * moe_fused_experts_workspace_size. Replaces Model.forward (base.py:35-76).
  */
 int moe_fused_moe(const moe_problem_t* p, const void* router_logits, int logits_dtype,
                   int renormalize, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Number of kernels moe_fused_moe launches for `p` with logits of
+ * `logits_dtype` (pointers unused; answers without a GPU). No reference
+ * counterpart (measurement aid). */
+int moe_fused_moe_launches(const moe_problem_t* p, int logits_dtype, int* launches);
 
 /* moe_fused_experts for top_k == 1 where only the rows of tokens with a
  * valid expert id are wanted (the expert-parallel receive buffer): out[t] =

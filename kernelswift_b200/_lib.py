@@ -86,6 +86,7 @@ SIGNATURES = {
     "moe_fused_moe": (_int, [ctypes.POINTER(MoeProblem), _vp, _int, _int, _vp, _sz, _vp]),
     "moe_fused_experts_launches": (_int, [ctypes.POINTER(MoeProblem), _int,
                                           ctypes.POINTER(_int)]),
+    "moe_fused_moe_launches": (_int, [ctypes.POINTER(MoeProblem), _int, ctypes.POINTER(_int)]),
     "moe_fused_experts_plan": (_int, [ctypes.POINTER(MoeProblem), _vp]),
     "moe_gather_rows": (_int, [_vp, _int, _i64, _i64, _int, _vp, _vp, _i64, _i64, _int, _vp,
                                _int, _vp, _vp]),

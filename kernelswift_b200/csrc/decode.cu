@@ -7,20 +7,23 @@
 // SMs and the tensor-core path is bound by its fixed costs (seven launches,
 // pipeline fill, 128-row tiles that are almost all padding).
 //
-//   decode_gate_up_kernel  item = (routed slot, 32 rows of the regrouped w13):
-//                          16 gate rows and their 16 up rows; each warp dots
-//                          4 weight rows with the slot's token row (staged in
-//                          shared memory), then SiLU(gate) * up for 16 act
-//                          columns, rounded to the activation dtype
+//   decode_gate_up_kernel  item = (routed slot, one 32-row slice of the
+//                          regrouped w13, i.e. 16 gate rows and their 16 up
+//                          rows); each warp dots 4 weight rows with the
+//                          slot's token row (staged in shared memory), eight
+//                          16-byte loads in flight per lane, then SiLU(gate)
+//                          * up for 16 act columns, rounded to the activation
+//                          dtype. With fp32 router logits it first routes the
+//                          item's token itself (routing.cuh: the routing
+//                          kernel's code, so the same experts and weights bit
+//                          for bit); the CTA holding the first item of a
+//                          token writes that token's ids and weights.
 //   decode_down_kernel     item = (token, 8 rows of w2): each warp streams one
 //                          w2 row of every slot's expert at once, dots each
 //                          with that slot's act row (the token's act rows are
-//                          staged) and sums w_j * dot_j in slot order, in fp32;
-//                          before waiting for the gate-up kernel it has L2
-//                          prefetch the w2 rows of its first item (the ids
-//                          are already final)
-// Both run persistent grids (the CTAs that fit at once walk the items).
+//                          staged) and sums w_j * dot_j in slot order, in fp32.
 //
+// Both run persistent grids (the CTAs that fit at once walk the items).
 // Loads are 16-byte vectors, several in flight per lane. Slots whose id is
 // outside [0, E) contribute nothing. Deterministic: fixed reduction order.
 #include <algorithm>
@@ -29,12 +32,12 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "routing.cuh"
 
 namespace ksw {
 namespace {
 
 constexpr int kThreadsDec = 256;
-constexpr int kRowsGu = 32;   // w13 rows per gate-up CTA (one 32-row regroup slice)
 constexpr int kRowsDn = 8;    // w2 rows per down CTA (one per warp)
 
 template <typename T>
@@ -63,36 +66,58 @@ __device__ __forceinline__ void stage_row(T* dst, const T* src, int64_t n) {
     reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(src)[c];
 }
 
-template <typename T, typename IdT>
+constexpr int kGuRouteMaxE = 256;  // in-kernel routing: 8 logits per lane
+
+// ---------------- gate-up ----------------
+// item = (slot, 32-row slice); one CTA per item while they fit, each warp
+// dots 4 weight rows with the token row (staged in shared memory), eight
+// 16-byte loads in flight per lane. With router logits warp 0 routes the
+// item's token first (routing.cuh); the CTA holding slice 0 of a token's
+// first slot writes that token's ids and weights.
+constexpr int kRowsGuD = 32;
+
+template <typename T, typename IdT, typename Tw>
 __global__ void __launch_bounds__(kThreadsDec)
     decode_gate_up_kernel(const T* __restrict__ hidden, const T* __restrict__ w13,
-                          const IdT* __restrict__ ids, int64_t numel, int top_k, int E,
-                          int64_t H, int64_t I, T* __restrict__ act) {
+                                 IdT* __restrict__ ids, Tw* __restrict__ weights,
+                                 const float* __restrict__ logits, int renorm, int64_t numel,
+                                 int top_k, int E, int64_t H, int64_t I, T* __restrict__ act) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ uint4 smem_dec[];
   T* a = reinterpret_cast<T*>(smem_dec);  // [H] token row of the current slot
-  __shared__ float res[kRowsGu];
+  __shared__ float res[kRowsGuD];
+  __shared__ int s_sel[64];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t chunks = 2 * I / kRowsGu;
-  int64_t staged = -1;  // token whose row is in shared memory
-  // persistent CTAs walk the (slot, 32-row chunk) items, so no partial last
-  // wave of CTAs is left streaming alone
+  const int64_t chunks = 2 * I / kRowsGuD;
+  int64_t staged = -1;  // token whose row (and routing) is in shared memory
   for (int64_t item = blockIdx.x; item < numel * chunks; item += gridDim.x) {
     const int64_t slot = item / chunks;
     const int64_t chunk = item - slot * chunks;
-    const int e = valid_expert(ids, slot, E);
-    if (e < 0) continue;  // the act row of a dropped slot is never read
     const int64_t tok = slot / top_k;
     if (tok != staged) {
       __syncthreads();  // everyone is done with the previous row
+      if (logits != nullptr && warp == 0) {
+        float sel_w;
+        int sel_i;
+        route_token_warp<kGuRouteMaxE / 32>(logits + tok * E, E, top_k, renorm, lane, sel_w,
+                                            sel_i);
+        if (lane < top_k) {
+          s_sel[lane] = sel_i;
+          if (chunk == 0 && slot == tok * top_k) {
+            weights[tok * top_k + lane] = from_f32<Tw>(sel_w);
+            ids[tok * top_k + lane] = static_cast<IdT>(sel_i);
+          }
+        }
+      }
       stage_row(a, hidden + tok * H, H);
       staged = tok;
       __syncthreads();
     }
-    const T* w = w13 + (int64_t(e) * 2 * I + chunk * kRowsGu + warp * 4) * H;
+    const int e = logits != nullptr ? s_sel[slot - tok * top_k] : valid_expert(ids, slot, E);
+    if (e < 0) continue;  // the act row of a dropped slot is never read
+    const T* w = w13 + (int64_t(e) * 2 * I + chunk * kRowsGuD + warp * 4) * H;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    // two 256-column steps per iteration: 8 weight loads in flight per lane
     for (int64_t k0 = int64_t(lane) * 8; k0 < H; k0 += 512) {
       uint4 wv[2][4];
       const bool second = k0 + 256 < H;
@@ -121,7 +146,6 @@ __global__ void __launch_bounds__(kThreadsDec)
       if (lane == 0) res[warp * 4 + r] = v;
     }
     __syncthreads();
-    // rows 0-15 of the slice are gate rows, 16-31 the matching up rows
     if (threadIdx.x < 16) {
       const float g = res[threadIdx.x], u = res[16 + threadIdx.x];
       act[slot * I + chunk * 16 + threadIdx.x] = from_f32<T>(g / (1.0f + __expf(-g)) * u);
@@ -143,23 +167,6 @@ __global__ void __launch_bounds__(kThreadsDec)
   constexpr int U = KMAX >= 8 ? 1 : 8 / KMAX;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row_blocks = H / kRowsDn;
-  // The routing ids were final before the previous launch (the gate-up
-  // kernel) passed its own wait, so before waiting for it this CTA asks L2 for
-  // the w2 rows of its first item (kRowsDn contiguous rows per slot; at decode
-  // sizes most CTAs have one item); that weight stream then overlaps the
-  // gate-up kernel. Only a prefetch: the ids are read again after the wait.
-  // Kept to the many-slot instantiations (top-8 and up), whose register use
-  // it leaves as it was; in the few-slot ones it would cost occupancy.
-  if constexpr (KMAX >= 8) {
-    if (warp == 0 && lane < top_k && int64_t(blockIdx.x) < T_tokens * row_blocks) {
-      const int64_t t = int64_t(blockIdx.x) / row_blocks;
-      const int e = valid_expert(ids, t * top_k + lane, E);
-      if (e >= 0)
-        l2_prefetch_bulk(
-            w2 + (int64_t(e) * H + (int64_t(blockIdx.x) - t * row_blocks) * kRowsDn) * I,
-            uint32_t(kRowsDn * I * sizeof(T)));
-    }
-  }
   pdl_wait();
   pdl_trigger();
   extern __shared__ uint4 smem_dec[];
@@ -265,19 +272,23 @@ int launch_down(const DecodeArgs& d, cudaStream_t s) {
 template <typename T, typename IdT, typename Tw>
 int launch_decode(const DecodeArgs& d, int stage, cudaStream_t s) {
   if (stage == 0) {
+    KSW_REQUIRE(d.logits == nullptr || d.E <= kGuRouteMaxE, MOE_ERR_UNSUPPORTED,
+                "decode path: in-kernel routing takes at most 256 experts");
     const size_t smem = size_t(d.H) * sizeof(T);
-    auto k = decode_gate_up_kernel<T, IdT>;
+    auto k = decode_gate_up_kernel<T, IdT, Tw>;
     static std::atomic<size_t> granted{0};
     const int st = ensure_smem(k, smem, granted);
     if (st != MOE_OK) return st;
-    const int64_t items = d.T * d.top_k * (2 * d.I / kRowsGu);
+    const int64_t items = d.T * d.top_k * (2 * d.I / kRowsGuD);
     int64_t cap = 0;
     const int stc = grid_cap(k, smem, &cap);
     if (stc != MOE_OK) return stc;
-    KSW_LAUNCH(k, dim3(unsigned(std::min<int64_t>(items, cap))), dim3(kThreadsDec),
-               smem, s, static_cast<const T*>(d.hidden), static_cast<const T*>(d.w13),
-               static_cast<const IdT*>(d.ids), d.T * d.top_k, d.top_k, d.E, d.H, d.I,
-               static_cast<T*>(d.act));
+    KSW_LAUNCH(k, dim3(unsigned(std::min<int64_t>(items, cap))), dim3(kThreadsDec), smem, s,
+               static_cast<const T*>(d.hidden), static_cast<const T*>(d.w13),
+               static_cast<IdT*>(const_cast<void*>(d.ids)),
+               static_cast<Tw*>(const_cast<void*>(d.weights)),
+               static_cast<const float*>(d.logits), d.renorm, d.T * d.top_k, d.top_k, d.E, d.H,
+               d.I, static_cast<T*>(d.act));
     return MOE_OK;
   }
   if (d.top_k <= 1) return launch_down<T, IdT, Tw, 1>(d, s);

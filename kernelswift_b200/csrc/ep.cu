@@ -248,10 +248,14 @@ int launch_plan_multi(const IdT* ids, int64_t numel, int num_experts, int world,
 
 // ---- the deduplicated plan (moe_ep_plan_dedup): one send row per (token,
 // destination rank) holding any of the token's slots. Rows are grouped by
-// rank, tokens ascending inside a rank. One CTA walks the tokens in 1024-token
-// passes; a token's position among the rank's rows is the ballot count of
-// earlier lanes in its warp plus the totals of earlier warps and passes, so
-// the plan is deterministic. ----
+// rank, tokens ascending inside a rank. One CTA per 1024-token chunk: every
+// CTA first counts the rows of ALL tokens per rank (the ids are a few hundred
+// KB, read from L2), keeping apart the counts of the chunks before its own;
+// its rows for rank d then start at (rows of ranks < d) + (rows of rank d in
+// earlier chunks), and a token's position inside the chunk is the ballot
+// count of earlier lanes in its warp plus the totals of earlier warps. No
+// atomic decides a position, so the plan is deterministic, and it is the
+// same whatever the number of CTAs. ----
 constexpr int kDedupMaxWorld = 32;
 
 __device__ __forceinline__ float weight_as_f32(const void* w, int dtype, int64_t i) {
@@ -283,66 +287,64 @@ __global__ void __launch_bounds__(kThreads)
   pdl_wait();
   pdl_trigger();
   __shared__ int cnt[kDedupMaxWorld + 1];
+  __shared__ int pre[kDedupMaxWorld];
   __shared__ int running[kDedupMaxWorld];
   __shared__ int warp_tot[32][kDedupMaxWorld];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t my_base = int64_t(blockIdx.x) * kThreads;
   if (tid <= world) cnt[tid] = 0;
+  if (tid < world) pre[tid] = 0;
   __syncthreads();
-  // pass 1: rows per rank, and tokens with an invalid slot
+  // pass 1 (every CTA, all tokens): rows per rank, tokens with an invalid
+  // slot, and the rows of the chunks before this CTA's
   for (int64_t base = 0; base < T; base += kThreads) {
     const int64_t t = base + tid;
     const uint64_t m = t < T ? token_ranks(ids, t, k, E, e_local, world) : 0;
     for (int d = 0; d <= world; ++d) {
       const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
-      if (lane == 0 && b) atomicAdd(&cnt[d], __popc(b));
+      if (lane == 0 && b) {
+        atomicAdd(&cnt[d], __popc(b));
+        if (base < my_base && d < world) atomicAdd(&pre[d], __popc(b));
+      }
     }
   }
   __syncthreads();
   if (tid == 0) {
     int run = 0;
     for (int d = 0; d < world; ++d) {
-      running[d] = run;
+      running[d] = run + pre[d];
       run += cnt[d];
     }
   }
-  if (tid <= world) counts[tid] = cnt[tid];
+  if (blockIdx.x == 0 && tid <= world) counts[tid] = cnt[tid];
   __syncthreads();
-  // pass 2: placement
-  for (int64_t base = 0; base < T; base += kThreads) {
-    const int64_t t = base + tid;
-    const uint64_t m = t < T ? token_ranks(ids, t, k, E, e_local, world) : 0;
-    for (int d = 0; d < world; ++d) {
-      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
-      if (lane == 0) warp_tot[warp][d] = __popc(b);
+  // pass 2: placement of this CTA's chunk
+  const int64_t t = my_base + tid;
+  const uint64_t m = t < T ? token_ranks(ids, t, k, E, e_local, world) : 0;
+  for (int d = 0; d < world; ++d) {
+    const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
+    if (lane == 0) warp_tot[warp][d] = __popc(b);
+  }
+  __syncthreads();
+  for (int d = 0; d < world; ++d) {  // warp-uniform: every lane takes each ballot
+    const bool on = (m >> d) & 1u;
+    const unsigned b = __ballot_sync(0xffffffffu, on);
+    if (t >= T) continue;
+    if (!on) {
+      inv[t * world + d] = -1;
+      continue;
     }
-    __syncthreads();
-    for (int d = 0; d < world; ++d) {  // warp-uniform: every lane takes each ballot
-      const bool on = (m >> d) & 1u;
-      const unsigned b = __ballot_sync(0xffffffffu, on);
-      if (t >= T) continue;
-      if (!on) {
-        inv[t * world + d] = -1;
-        continue;
-      }
-      int prefix = 0;
-      for (int w2 = 0; w2 < warp; ++w2) prefix += warp_tot[w2][d];
-      const int pos = running[d] + prefix + __popc(b & lanemask_lt());
-      send_token[pos] = static_cast<int32_t>(t);
-      inv[t * world + d] = pos;
-      for (int j = 0; j < k; ++j) {
-        const long long v = static_cast<long long>(ids[t * k + j]);
-        const bool here = v >= 0 && v < E && v / e_local == d;
-        send_eid[int64_t(pos) * k + j] = here ? static_cast<int32_t>(v - int64_t(d) * e_local) : -1;
-        send_w[int64_t(pos) * k + j] = here ? weight_as_f32(w, w_dtype, t * k + j) : 0.0f;
-      }
+    int prefix = 0;
+    for (int w2 = 0; w2 < warp; ++w2) prefix += warp_tot[w2][d];
+    const int pos = running[d] + prefix + __popc(b & lanemask_lt());
+    send_token[pos] = static_cast<int32_t>(t);
+    inv[t * world + d] = pos;
+    for (int j = 0; j < k; ++j) {
+      const long long v = static_cast<long long>(ids[t * k + j]);
+      const bool here = v >= 0 && v < E && v / e_local == d;
+      send_eid[int64_t(pos) * k + j] = here ? static_cast<int32_t>(v - int64_t(d) * e_local) : -1;
+      send_w[int64_t(pos) * k + j] = here ? weight_as_f32(w, w_dtype, t * k + j) : 0.0f;
     }
-    __syncthreads();
-    if (tid < world) {
-      int sum = 0;
-      for (int w2 = 0; w2 < 32; ++w2) sum += warp_tot[w2][tid];
-      running[tid] += sum;
-    }
-    __syncthreads();
   }
 }
 
@@ -446,13 +448,14 @@ extern "C" int moe_ep_plan_dedup(const void* topk_ids, int ids_dtype, const void
               MOE_ERR_INVALID_ARG, "ep_plan_dedup: null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int e_local = num_experts / world;
+  const dim3 grid(unsigned(std::max<int64_t>(1, ceil_div(num_tokens, int64_t(kThreads)))));
   if (ids_dtype == MOE_DTYPE_I32)
-    KSW_LAUNCH(ep_plan_dedup_kernel<int32_t>, dim3(1), dim3(kThreads), 0, s,
+    KSW_LAUNCH(ep_plan_dedup_kernel<int32_t>, grid, dim3(kThreads), 0, s,
                static_cast<const int32_t*>(topk_ids), topk_weights, weights_dtype, num_tokens,
                top_k, num_experts, e_local, world, send_token, send_eid, send_w, inv_index,
                counts);
   else
-    KSW_LAUNCH(ep_plan_dedup_kernel<int64_t>, dim3(1), dim3(kThreads), 0, s,
+    KSW_LAUNCH(ep_plan_dedup_kernel<int64_t>, grid, dim3(kThreads), 0, s,
                static_cast<const int64_t*>(topk_ids), topk_weights, weights_dtype, num_tokens,
                top_k, num_experts, e_local, world, send_token, send_eid, send_w, inv_index,
                counts);

@@ -72,7 +72,14 @@ struct DecodeArgs {
   const void* weights;  // [T, top_k]
   void* act;            // [T*top_k, I] scratch
   void* out;            // [T, H]
+  // fp32 router logits [T, E] (E <= 256): the gate-up kernel routes the
+  // tokens itself and writes ids / weights; null when they are given
+  const void* logits = nullptr;
+  int renorm = 1;
 };
+
+// The decode kernel routes in-kernel for fp32 logits over at most this many experts.
+constexpr int kDecodeRouteMaxExperts = 256;
 
 bool decode_path_fits(int64_t T, int top_k, int64_t H, int64_t I, int act_dtype);
 bool decode_path_enabled();  // false when MOE_NO_DECODE_PATH=1

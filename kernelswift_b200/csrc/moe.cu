@@ -272,7 +272,11 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   const bool decode = P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype &&
                       p->num_tokens_dev == nullptr && decode_path_enabled() &&
                       decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype);
-  if (logits != nullptr) {
+  // fp32 logits over at most 256 experts on the decode path: the decode
+  // gate-up kernel routes the tokens itself (one launch fewer)
+  const bool route_in_decode = logits != nullptr && decode && logits_dtype == MOE_DTYPE_F32 &&
+                               P.E <= kDecodeRouteMaxExperts;
+  if (logits != nullptr && !route_in_decode) {
     st = moe_topk_softmax(logits, logits_dtype, P.T, P.E, P.k, renorm,
                           const_cast<void*>(p->topk_weights), p->weights_dtype,
                           const_cast<void*>(p->topk_ids), p->ids_dtype, stream);
@@ -315,6 +319,8 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
     d.weights = p->topk_weights;
     d.act = at<void>(workspace, P.off_act);
     d.out = rows_out != nullptr ? rows_out : p->out;
+    d.logits = route_in_decode ? logits : nullptr;
+    d.renorm = renorm;
     KSW_MARK(MOE_STAGE_ALIGN);
     KSW_MARK(MOE_STAGE_GATHER);
     KSW_MARK(MOE_STAGE_GATE_UP);
@@ -474,6 +480,29 @@ int moe_fused_moe(const moe_problem_t* p, const void* router_logits, int logits_
               MOE_ERR_INVALID_ARG, "moe_fused_moe: logits must be f32, f16 or bf16");
   return fused_experts_impl(p, workspace, workspace_bytes, stream, nullptr, router_logits,
                             logits_dtype, renormalize ? 1 : 0);
+}
+
+int moe_fused_moe_launches(const moe_problem_t* p, int logits_dtype, int* launches) {
+  KSW_REQUIRE(launches != nullptr, MOE_ERR_INVALID_ARG, "null launches pointer");
+  int n = 0;
+  int st = moe_fused_experts_launches(p, 0, &n);
+  if (st != MOE_OK) return st;
+  if (n == 0) {
+    *launches = 0;
+    return MOE_OK;
+  }
+  int sms = 148;
+  if (check_device(&sms) != MOE_OK) sms = 148;
+  Plan P;
+  st = make_plan(p, sms, &P);
+  if (st != MOE_OK) return st;
+  const bool decode = P.quant == MOE_QUANT_NONE && p->act_dtype == P.compute_dtype &&
+                      p->num_tokens_dev == nullptr && decode_path_enabled() &&
+                      decode_path_fits(P.T, P.k, P.H, P.I, p->act_dtype);
+  const bool routed_inside = decode && logits_dtype == MOE_DTYPE_F32 &&
+                             P.E <= kDecodeRouteMaxExperts;
+  *launches = n + (routed_inside ? 0 : 1);
+  return MOE_OK;
 }
 
 int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launches) {

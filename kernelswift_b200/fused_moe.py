@@ -363,13 +363,26 @@ def fused_experts_launches(num_tokens: int, hidden_size: int, intermediate_size:
 
 def fused_moe_launches(num_tokens: int, hidden_size: int, intermediate_size: int,
                        num_experts: int, top_k: int, quant: str = "none",
-                       dtype: torch.dtype = torch.bfloat16) -> int:
-    """Kernels fused_moe launches (answers without a GPU): the routing kernel
-    plus fused_experts' launches."""
-    if num_tokens == 0:
-        return 0
-    return 1 + fused_experts_launches(num_tokens, hidden_size, intermediate_size, num_experts,
-                                      top_k, quant, dtype)
+                       dtype: torch.dtype = torch.bfloat16,
+                       logits_dtype: torch.dtype = torch.float32) -> int:
+    """Kernels fused_moe launches (moe_fused_moe_launches; answers without a
+    GPU): fused_experts' launches plus the routing kernel, which the decode
+    path does not need for fp32 logits over at most 256 experts (its first
+    kernel routes the tokens itself)."""
+    p = _lib.MoeProblem()
+    p.num_tokens = num_tokens
+    p.hidden_size = hidden_size
+    p.inter_size = intermediate_size
+    p.num_experts = num_experts
+    p.top_k = top_k
+    p.act_dtype = _code(torch.empty(0, dtype=dtype))
+    p.quant = _QUANT[quant]
+    p.ids_dtype = _lib.DT_I32
+    p.weights_dtype = _code(torch.empty(0, dtype=dtype))
+    n = ctypes.c_int(0)
+    _lib.call("moe_fused_moe_launches", ctypes.byref(p),
+              _code(torch.empty(0, dtype=logits_dtype)), ctypes.byref(n))
+    return n.value
 
 
 def fused_experts_plan(num_tokens: int, hidden_size: int, intermediate_size: int,

@@ -170,11 +170,16 @@ def test_prepared_weights_cache_checks_the_source_tensors(monkeypatch):
 
 def test_launch_count_query_without_gpu():
     """moe_fused_experts_launches answers from the plan alone."""
+    import torch
+
     from kernelswift_b200 import fused_moe as fm
 
     assert fm.fused_experts_launches(4096, 4096, 14336, 8, 2) == 7      # 3-launch align..sum
     assert fm.fused_experts_launches(1, 2048, 768, 128, 8) == 2         # decode kernels
-    assert fm.fused_moe_launches(1, 2048, 768, 128, 8) == 3             # routing + decode
+    assert fm.fused_moe_launches(1, 2048, 768, 128, 8) == 2             # decode, routing inside
+    assert fm.fused_moe_launches(1, 2048, 768, 128, 8,
+                                 logits_dtype=torch.bfloat16) == 3      # routing kernel + decode
+    assert fm.fused_moe_launches(1, 256, 128, 512, 8) == 3              # 512 experts: routing kernel
     assert fm.fused_moe_launches(4096, 4096, 14336, 8, 2) == 8          # routing + 7
     assert fm.fused_experts_launches(64, 2048, 768, 128, 8) == 6        # split gate-up
     assert fm.fused_experts_launches(64, 7168, 2048, 256, 8, "fp8") == 6

@@ -139,7 +139,8 @@ def test_fused_moe_equals_two_calls(cuda_device, T, H, I, E, k, dtype, renorm):
 
 def test_fused_moe_bf16_logits_and_launch_count(cuda_device):
     """bf16 router logits route like fused_topk on them; the fused call's
-    launch count is the routing kernel plus fused_experts' launches."""
+    launch count is the routing kernel plus fused_experts' launches (fp32
+    logits on the decode path: fused_experts' launches alone)."""
     T, H, I, E, k = 1, 2048, 768, 128, 8
     hidden, logits, w1, w2 = problem(T, H, I, E, k, torch.bfloat16, seed=5)
     dev = cuda_device
@@ -148,7 +149,8 @@ def test_fused_moe_bf16_logits_and_launch_count(cuda_device):
     w_ref, ids_ref = fm.fused_topk(hd, lb, k, weights_dtype=torch.bfloat16)
     two = fm.fused_experts(hd, prep, None, w_ref, ids_ref)
     assert torch.equal(fm.fused_moe(hd, prep, None, lb, k), two)
-    assert fm.fused_moe_launches(T, H, I, E, k) == 3
+    assert fm.fused_moe_launches(T, H, I, E, k, logits_dtype=torch.bfloat16) == 3
+    assert fm.fused_moe_launches(T, H, I, E, k) == 2
     assert fm.fused_moe_launches(64, H, I, E, k) == 1 + fm.fused_experts_launches(64, H, I, E, k)
 
 

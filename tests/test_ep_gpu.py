@@ -285,20 +285,26 @@ def dsv3_worker(rank, world, port, cfg, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("quant,exchange", [("none", "peer"), ("none", "nccl"), ("fp8", "peer")])
-def test_ep_dsv3_config(cuda_device, quant, exchange):
+@pytest.mark.parametrize("quant,exchange,ranks", [("none", "peer", 2), ("none", "peer", 4),
+                                                  ("none", "peer", 8), ("none", "nccl", 0),
+                                                  ("fp8", "peer", 0)])
+def test_ep_dsv3_config(cuda_device, quant, exchange, ranks):
     """The expert-parallel DeepSeek-V3 configuration: H=7168, I=2048, 256
-    experts sharded E/N per GPU, top-8, 8192 tokens per rank (65,536 slots,
-    so the multi-CTA dispatch plan runs), on every GPU of the box up to 8.
-    Each rank checks at least 256 of its tokens against the oracle: the
-    first token of every expert its batch hits, plus 64 random tokens
-    (bf16: rtol 2e-2 / atol 2e-2; fp8: relative L2 <= 5e-2)."""
+    experts sharded E/N per GPU, top-8, 8192 tokens per rank (8192 tokens x
+    the ranks that hold a token's experts arrive per rank). bf16 over the
+    peer exchange at 2, 4 and 8 ranks (those the box has GPUs for); NCCL and
+    fp8 on every GPU of the box up to 8 (ranks = 0). Each rank checks at least
+    256 of its tokens against the oracle: the first token of every expert its
+    batch hits plus 256 random ones (bf16: rtol 2e-2 / atol 2e-2; fp8:
+    relative L2 <= 5e-2)."""
     import torch.multiprocessing as mp
 
-    world = min(torch.cuda.device_count(), 8)
+    world = ranks or min(torch.cuda.device_count(), 8)
+    if world > torch.cuda.device_count():
+        pytest.skip(f"needs {world} GPUs")
     if world < 2:
         pytest.skip("needs two GPUs: one rank would exchange nothing")
-    cfg = (256, 8, 8192, 7168, 2048, quant, exchange, 64)
+    cfg = (256, 8, 8192, 7168, 2048, quant, exchange, 256)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
