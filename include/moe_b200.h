@@ -369,7 +369,9 @@ int moe_fused_experts_plan(const moe_problem_t* p, int32_t* info);
  * dst[m] = src[sorted_token_ids[m] / top_k] for m < *num_tokens_post_pad whose
  * slot is not padding (base.py:52-58 replicate + base.py:68 gather); padding
  * rows are left untouched. top_k == 0 copies row m itself (valid rows only).
- * quant NONE: dst_dtype F16/BF16 (F32 sources are rounded).
+ * quant NONE: dst_dtype F16/BF16 (F32 sources are rounded), or F32 from
+ *   F32 rows rounded to tf32 (nearest, ties away: the operand of the tf32
+ *   GEMMs that fp32 activations use).
  * quant FP8_BLOCK: dst e4m3 + dst_scale [buffer_len, ceil(H/128)],
  *   scale = absmax/448 per 128 columns. INT8_CHANNEL: dst int8 + dst_scale
  *   [buffer_len], scale = absmax/127 per row. FP8_UE8M0: dst e4m3 +

@@ -254,7 +254,7 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 }
 
 // MMA kinds used here.
-enum MmaKind : int { kKindF16 = 0, kKindF8 = 1, kKindI8 = 2 };
+enum MmaKind : int { kKindF16 = 0, kKindF8 = 1, kKindI8 = 2, kKindTF32 = 3 };
 
 // D[tmem] (+)= A[smem] * B[smem]^T, both operands K-major.
 template <int KIND>
@@ -275,6 +275,13 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc,
             d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
+  } else if constexpr (KIND == kKindTF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
   } else {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -288,8 +295,8 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc,
 // Instruction descriptor (32 bits) for a dense MMA with K-major A and B:
 //   [4,6) D format (1 = f32, 2 = s32), [7,10) A format, [10,13) B format,
 //   [15] A major, [16] B major (0 = K-major), [17,23) N >> 3, [24,29) M >> 4.
-// A/B format: kind::f16 -> 0 f16, 1 bf16; kind::f8f6f4 -> 0 e4m3;
-// kind::i8 -> 1 signed.
+// A/B format: kind::f16 -> 0 f16, 1 bf16; kind::tf32 -> 2 tf32;
+// kind::f8f6f4 -> 0 e4m3; kind::i8 -> 1 signed.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t d_fmt,
                                                   uint32_t ab_fmt, int m,
                                                   int n) {
@@ -390,6 +397,32 @@ __device__ __forceinline__ uint32_t ue8m0_byte(float amax) {
 // 1 / scale = 2^(127 - b), exactly (b <= 253).
 __device__ __forceinline__ float ue8m0_inv_scale(uint32_t b) {
   return __uint_as_float((254u - b) << 23);
+}
+
+// fp32 -> tf32 (10 mantissa bits), round to nearest, ties away from zero;
+// the low 13 bits of the result are zero. The tf32 GEMMs take operands
+// rounded this way (the tensor core itself ignores the low bits).
+__device__ __forceinline__ float round_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+constexpr float kFp8Max = 448.0f;
+
+// Two values -> two e4m3 bytes (low byte = first value): x * inv clamped to
+// +-448, rounded to nearest even.
+__device__ __forceinline__ uint32_t to_e4m3x2(float x0, float x1, float inv) {
+  const float q0 = fminf(fmaxf(x0 * inv, -kFp8Max), kFp8Max);
+  const float q1 = fminf(fmaxf(x1 * inv, -kFp8Max), kFp8Max);
+  return uint32_t(__nv_cvt_float2_to_fp8x2(make_float2(q0, q1), __NV_SATFINITE, __NV_E4M3));
+}
+
+// Eight values -> eight e4m3 bytes in column order.
+__device__ __forceinline__ uint2 pack_e4m3x8(const float (&v)[8], float inv) {
+  const uint32_t lo = to_e4m3x2(v[0], v[1], inv) | (to_e4m3x2(v[2], v[3], inv) << 16);
+  const uint32_t hi = to_e4m3x2(v[4], v[5], inv) | (to_e4m3x2(v[6], v[7], inv) << 16);
+  return make_uint2(lo, hi);
 }
 
 // Byte offset of the scale of row r, column block kb in a scale-factor image

@@ -235,7 +235,8 @@ struct GemmCfg {
   static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM columns");
 };
 
-// KIND: kKindF16 (AB_FMT 0 = f16, 1 = bf16) or kKindI8 (AB_FMT 1 = s8).
+// KIND: kKindF16 (AB_FMT 0 = f16, 1 = bf16), kKindTF32 (AB_FMT 2, fp32
+// operands read as tf32) or kKindI8 (AB_FMT 1 = s8).
 // TOUT: element type of the gate-up output (f16/bf16).
 template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -326,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- TMA producer ----------------
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    constexpr int kColsPerKb = kKBytes / (KIND == kKindF16 ? 2 : 1);
+    constexpr int kColsPerKb = kKBytes / (KIND == kKindF16 ? 2 : KIND == kKindTF32 ? 4 : 1);
     // With early metadata the weight tiles of the first STAGES k-blocks (in
     // the order the main loop visits them) are requested before the wait
     // for the A operand's producer; those stages later get only their A tile.
@@ -496,24 +497,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                   us[4 * q4 + 2] = a_s * b4.z; us[4 * q4 + 3] = a_s * b4.w;
                 }
               }
-              uint32_t packed[8];
+              if constexpr (std::is_same<TOUT, float>::value) {
+                // fp32 activations (the down GEMM's tf32 operand, rounded
+                // to tf32 here): 16 floats per group
+                float4* dst = reinterpret_cast<float4*>(out_row + g * 16);
+                auto act_at = [&](int j) {
+                  return round_tf32(silu_mul(acc_to_f32<KIND>(gv[u][j]),
+                                             acc_to_f32<KIND>(uv[u][j])));
+                };
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float g0 = acc_to_f32<KIND>(gv[u][2 * j]);
-                float g1 = acc_to_f32<KIND>(gv[u][2 * j + 1]);
-                float u0 = acc_to_f32<KIND>(uv[u][2 * j]);
-                float u1 = acc_to_f32<KIND>(uv[u][2 * j + 1]);
-                if constexpr (kScaled) {
-                  g0 *= gs[2 * j];
-                  g1 *= gs[2 * j + 1];
-                  u0 *= us[2 * j];
-                  u1 *= us[2 * j + 1];
+                for (int j = 0; j < 4; ++j)
+                  dst[j] = make_float4(act_at(4 * j), act_at(4 * j + 1), act_at(4 * j + 2),
+                                       act_at(4 * j + 3));
+              } else {
+                uint32_t packed[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  float g0 = acc_to_f32<KIND>(gv[u][2 * j]);
+                  float g1 = acc_to_f32<KIND>(gv[u][2 * j + 1]);
+                  float u0 = acc_to_f32<KIND>(uv[u][2 * j]);
+                  float u1 = acc_to_f32<KIND>(uv[u][2 * j + 1]);
+                  if constexpr (kScaled) {
+                    g0 *= gs[2 * j];
+                    g1 *= gs[2 * j + 1];
+                    u0 *= us[2 * j];
+                    u1 *= us[2 * j + 1];
+                  }
+                  packed[j] = pack2<TOUT>(silu_mul(g0, u0), silu_mul(g1, u1));
                 }
-                packed[j] = pack2<TOUT>(silu_mul(g0, u0), silu_mul(g1, u1));
+                uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
+                dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
               }
-              uint4* dst = reinterpret_cast<uint4*>(out_row + g * 16);
-              dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-              dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
             }
           }
         }
@@ -1409,9 +1424,15 @@ struct OperandTypes {
 };
 
 int operand_types(const GroupedGemmArgs& a, OperandTypes* ot) {
+  if (a.quant == MOE_QUANT_NONE && a.compute_dtype == MOE_DTYPE_F32) {
+    // fp32 operands, multiplied as tf32 (kind::tf32)
+    ot->tma_type = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    ot->elem_bytes = 4;
+    return MOE_OK;
+  }
   if (a.quant == MOE_QUANT_NONE) {
     KSW_REQUIRE(a.compute_dtype == MOE_DTYPE_BF16 || a.compute_dtype == MOE_DTYPE_F16,
-                MOE_ERR_INVALID_ARG, "compute dtype must be bf16 or f16");
+                MOE_ERR_INVALID_ARG, "compute dtype must be bf16, f16 or f32");
     ot->tma_type = a.compute_dtype == MOE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     ot->elem_bytes = 2;
@@ -1511,6 +1532,8 @@ int gemm_gate_up_launch(const GroupedGemmArgs& a, cudaStream_t s) {
     // int8 products dequantise to bf16 activations
     return dispatch_bn<kKindI8, 1, kEpiSwiGLU, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
   }
+  if (a.compute_dtype == MOE_DTYPE_F32)
+    return dispatch_bn<kKindTF32, 2, kEpiSwiGLU, float>(bn, ta, tb, kp, grid, s);
   if (a.compute_dtype == MOE_DTYPE_BF16)
     return dispatch_bn<kKindF16, 1, kEpiSwiGLU, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
   return dispatch_bn<kKindF16, 0, kEpiSwiGLU, __half>(bn, ta, tb, kp, grid, s);
@@ -1594,6 +1617,8 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   }
   if (a.quant == MOE_QUANT_INT8_CHANNEL)
     return dispatch_bn<kKindI8, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s);
+  if (a.compute_dtype == MOE_DTYPE_F32)
+    return dispatch_bn<kKindTF32, 2, kEpiRows, float>(bn, ta, tb, kp, grid, s);
   if (a.compute_dtype == MOE_DTYPE_BF16)
     return dispatch_bn<kKindF16, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s);
   return dispatch_bn<kKindF16, 0, kEpiRows, float>(bn, ta, tb, kp, grid, s);

@@ -128,11 +128,18 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.numel = P.T * P.k;
   KSW_REQUIRE(P.numel < (int64_t(1) << 30), MOE_ERR_UNSUPPORTED, "too many tokens");
   P.L = align_buffer_len(P.numel, P.E, kBlockM);
-  P.compute_dtype = p->act_dtype == MOE_DTYPE_F16 ? MOE_DTYPE_F16 : MOE_DTYPE_BF16;
+  // 16-bit activations compute in their own dtype; fp32 activations keep
+  // fp32 operands, multiplied as tf32 (unquantised weights), or go through
+  // bf16 for the W8A8 paths
+  P.compute_dtype = p->act_dtype == MOE_DTYPE_F16 ? MOE_DTYPE_F16
+                    : p->act_dtype == MOE_DTYPE_F32 && p->quant == MOE_QUANT_NONE
+                        ? MOE_DTYPE_F32
+                        : MOE_DTYPE_BF16;
   int kbpe = 2;
   if (P.quant == MOE_QUANT_NONE) {
     P.a_dtype = P.compute_dtype;
     P.act_dtype = P.compute_dtype;
+    kbpe = int(elem_bytes(P.compute_dtype));
   } else if (P.quant == MOE_QUANT_INT8_CHANNEL) {
     P.a_dtype = MOE_DTYPE_I8;
     P.act_dtype = MOE_DTYPE_BF16;

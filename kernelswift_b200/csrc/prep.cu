@@ -16,6 +16,8 @@
 //              block is zero), q = e4m3_rn(x / scale) (exact scaling); the
 //              scale byte is written into the scale-factor image at every
 //              row of the block (its regrouped row for w13)
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace ksw {
@@ -47,7 +49,12 @@ __global__ void __launch_bounds__(256)
     const int64_t e = row / R, rs = row - e * R;
     const Tin* s = src + row * C;
     Tout* d = dst + (e * R + map_row(rs, I, regroup)) * C;
-    for (int64_t c = lane; c < C; c += 32) d[c] = from_f32<Tout>(ld(s + c));
+    for (int64_t c = lane; c < C; c += 32) {
+      if constexpr (std::is_same<Tout, float>::value)
+        d[c] = round_tf32(ld(s + c));  // fp32 weights of the tf32 GEMMs
+      else
+        d[c] = from_f32<Tout>(ld(s + c));
+    }
   }
 }
 
@@ -205,8 +212,11 @@ int prep_typed(const Tin* src, int64_t E, int64_t R, int64_t C, int64_t I,
     else if (dst_dtype == MOE_DTYPE_F16)
       prep_cast_kernel<Tin, __half><<<grid_rows(rows), 256, 0, s>>>(
           src, E, R, C, I, regroup, static_cast<__half*>(dst));
+    else if (dst_dtype == MOE_DTYPE_F32)
+      prep_cast_kernel<Tin, float><<<grid_rows(rows), 256, 0, s>>>(
+          src, E, R, C, I, regroup, static_cast<float*>(dst));
     else
-      return fail(MOE_ERR_INVALID_ARG, "prepare: dst dtype must be bf16/f16");
+      return fail(MOE_ERR_INVALID_ARG, "prepare: dst dtype must be bf16/f16/f32");
   } else if (quant == MOE_QUANT_FP8_BLOCK) {
     KSW_REQUIRE(dst_dtype == MOE_DTYPE_E4M3 && scale, MOE_ERR_INVALID_ARG,
                 "prepare: fp8 needs an e4m3 destination and a scale buffer");

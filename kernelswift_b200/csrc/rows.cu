@@ -8,6 +8,8 @@
 //                GEMM's operand).
 //   sum_topk:    out[t] = sum_s sum_j part[s, t*k + j] (the top-k reduction of
 //                base.py:75-76), in fixed order, fp32, then cast.
+#include <type_traits>
+
 #include "common.cuh"
 #include "rows.h"
 
@@ -16,7 +18,6 @@ namespace {
 
 constexpr int kWarps = 8;  // rows per CTA
 constexpr int kBatch = 4;  // loads in flight per lane in the row loops
-constexpr float kFp8Max = 448.0f;
 constexpr float kInt8Max = 127.0f;
 
 // Loads 8 consecutive elements as floats (16-byte aligned source).
@@ -97,13 +98,6 @@ __device__ __forceinline__ float quant_scale(float absmax, float qmax) {
   return s > 0.0f ? s : 1.0f;
 }
 
-// Two values -> two e4m3 bytes (low byte = first value).
-__device__ __forceinline__ uint32_t to_e4m3x2(float x0, float x1, float inv) {
-  const float q0 = fminf(fmaxf(x0 * inv, -kFp8Max), kFp8Max);
-  const float q1 = fminf(fmaxf(x1 * inv, -kFp8Max), kFp8Max);
-  return uint32_t(__nv_cvt_float2_to_fp8x2(make_float2(q0, q1), __NV_SATFINITE, __NV_E4M3));
-}
-
 __device__ __forceinline__ int8_t to_i8(float x, float inv) {
   const float q = fminf(fmaxf(x * inv, -kInt8Max), kInt8Max);
   return static_cast<int8_t>(__float2int_rn(q));
@@ -142,8 +136,14 @@ __global__ void __launch_bounds__(kWarps * 32)
       for (int u = 0; u < kBatch; ++u)
         if (h0 + u * 256 < H) load8(s + h0 + u * 256, v[u]);
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u)
+      for (int u = 0; u < kBatch; ++u) {
+        if constexpr (std::is_same<Tout, float>::value) {
+          // fp32 operand rows of the tf32 GEMMs: rounded to tf32 here
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[u][i] = round_tf32(v[u][i]);
+        }
         if (h0 + u * 256 < H) store8(d + h0 + u * 256, v[u]);
+      }
     }
   }
 }
@@ -152,12 +152,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 // Each lane handles 8 consecutive columns (one 16-byte load for 16-bit
 // sources); 16 lanes cover one 128-column group, so the group's absmax is a
 // 16-lane shuffle reduction. Requires H % 8 == 0 (checked on the host); a
-// partial last group is handled by masking lanes past H.
-__device__ __forceinline__ uint2 pack_e4m3x8(const float (&v)[8], float inv) {
-  const uint32_t lo = to_e4m3x2(v[0], v[1], inv) | (to_e4m3x2(v[2], v[3], inv) << 16);
-  const uint32_t hi = to_e4m3x2(v[4], v[5], inv) | (to_e4m3x2(v[6], v[7], inv) << 16);
-  return make_uint2(lo, hi);
-}
+// partial last group is handled by masking lanes past H (pack_e4m3x8 is in
+// common.cuh, shared with the UE8M0 gate-up epilogue).
 
 template <typename Tin>
 __global__ void __launch_bounds__(kWarps * 32)
@@ -423,7 +419,11 @@ __global__ void __launch_bounds__(256)
     }
     float out[8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) out[q] = gsum[q] / (1.0f + __expf(-gsum[q])) * usum[q];
+    for (int q = 0; q < 8; ++q) {
+      out[q] = gsum[q] / (1.0f + __expf(-gsum[q])) * usum[q];
+      // fp32 act rows are the down GEMM's tf32 operand: rounded here
+      if constexpr (std::is_same<Tout, float>::value) out[q] = round_tf32(out[q]);
+    }
     store8(act + m * I + a0, out);
   }
 }
@@ -496,6 +496,10 @@ int gather_launch(const GatherArgs& a, cudaStream_t s) {
       KSW_LAUNCH(gather_cast_kernel<float, __half>, dim3(grid), dim3(block), 0, s,
           static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
           a.max_rows, a.numel, a.src_rows, static_cast<__half*>(a.dst));
+    else if (a.src_dtype == MOE_DTYPE_F32 && a.dst_dtype == MOE_DTYPE_F32)
+      KSW_LAUNCH(gather_cast_kernel<float, float>, dim3(grid), dim3(block), 0, s,
+          static_cast<const float*>(a.src), a.H, a.top_k, a.sorted, a.num_post_pad,
+          a.max_rows, a.numel, a.src_rows, static_cast<float*>(a.dst));
     else if (a.src_dtype == MOE_DTYPE_BF16 && a.dst_dtype == MOE_DTYPE_BF16)
       KSW_LAUNCH(gather_cast_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(grid), dim3(block), 0, s,
           static_cast<const __nv_bfloat16*>(a.src), a.H, a.top_k, a.sorted,
@@ -619,8 +623,11 @@ int swiglu_reduce_launch(const float* part, int splits, int64_t numel, int64_t I
   else if (act_dtype == MOE_DTYPE_F16)
     KSW_LAUNCH(swiglu_reduce_kernel<__half>, dim3(grid), dim3(256), 0, s,
         part, splits, numel, I, sorted, num_post_pad, max_rows, static_cast<__half*>(act));
+  else if (act_dtype == MOE_DTYPE_F32)
+    KSW_LAUNCH(swiglu_reduce_kernel<float>, dim3(grid), dim3(256), 0, s,
+        part, splits, numel, I, sorted, num_post_pad, max_rows, static_cast<float*>(act));
   else
-    return fail(MOE_ERR_UNSUPPORTED, "swiglu_reduce: act dtype must be bf16/f16");
+    return fail(MOE_ERR_UNSUPPORTED, "swiglu_reduce: act dtype must be bf16/f16/f32");
   KSW_CUDA(cudaGetLastError());
   return MOE_OK;
 }

@@ -214,13 +214,26 @@ class PreparedWeights:
         return self.w13.dtype
 
 
+def compute_dtype_for(act_dtype: torch.dtype, quant: str = "none") -> torch.dtype:
+    """Operand dtype of the expert GEMMs for activations of `act_dtype`: f16
+    and bf16 compute in their own dtype; f32 activations keep f32 operands,
+    multiplied as tf32 by the tensor cores, when the weights are unquantised
+    (the W8A8 paths take bf16)."""
+    if act_dtype == torch.float16:
+        return torch.float16
+    if act_dtype == torch.float32 and quant == "none":
+        return torch.float32
+    return torch.bfloat16
+
+
 def prepare_weights(w1: torch.Tensor, w2: torch.Tensor, quant: str = "none",
                     compute_dtype: torch.dtype = torch.bfloat16,
                     w1_scale: torch.Tensor | None = None,
                     w2_scale: torch.Tensor | None = None) -> PreparedWeights:
     """Casts or quantises w1 [E, 2I, H] and w2 [E, H, I] once.
 
-    quant "none": cast to `compute_dtype` (bf16 or f16). quant "fp8": e4m3
+    quant "none": cast to `compute_dtype` (bf16, f16, or f32 for the tf32
+    GEMMs of f32 activations; see compute_dtype_for). quant "fp8": e4m3
     with one fp32 scale per 128x128 block (absmax / 448), or pass-through of
     already-e4m3 weights with `w1_scale`/`w2_scale`. quant "int8": int8 with
     one scale per output row (absmax / 127). quant "fp8-ue8m0": e4m3 with one
@@ -242,8 +255,8 @@ def prepare_weights(w1: torch.Tensor, w2: torch.Tensor, quant: str = "none",
     dev = w1.device
     q = _QUANT[quant]
     if quant == "none":
-        if compute_dtype not in (torch.bfloat16, torch.float16):
-            raise ValueError("compute_dtype must be bf16 or f16")
+        if compute_dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise ValueError("compute_dtype must be bf16, f16 or f32")
         dst_dtype = compute_dtype
         s13 = s2 = None
     elif quant == "fp8":
@@ -486,7 +499,7 @@ def fused_experts(hidden_states: torch.Tensor, w1, w2: torch.Tensor | None,
         scale_format = "ue8m0" if raw and sizes and w1_scale is None else "fp32"
     if quant == "fp8" and scale_format == "ue8m0":
         quant = "fp8-ue8m0"
-    compute = torch.float16 if hidden_states.dtype == torch.float16 else torch.bfloat16
+    compute = compute_dtype_for(hidden_states.dtype, quant)
     if isinstance(w1, PreparedWeights):
         prep = w1
         if quant == "fp8" and prep.quant == "fp8-ue8m0":
@@ -583,7 +596,7 @@ class ModelNew(nn.Module):
         objects it was made from, so a parameter replaced by a new tensor
         that happens to reuse the old address (version 0 again) is
         prepared afresh instead of matching the stale entry."""
-        compute = torch.float16 if act_dtype == torch.float16 else torch.bfloat16
+        compute = compute_dtype_for(act_dtype, quant)
         w1, w2 = self.w1, self.w2
         key = (quant, compute, w1.data_ptr(), w1._version, tuple(w1.shape), w1.dtype,
                w2.data_ptr(), w2._version, tuple(w2.shape), w2.dtype)

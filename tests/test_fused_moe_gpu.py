@@ -39,6 +39,21 @@ def test_modelnew_matches_reference_golden(cuda_device, case):
     torch.testing.assert_close(out.float().cpu(), oracle_out, **TOL)
 
 
+@pytest.mark.parametrize("name", ["toy_fp32", "cfg0_fp32", "dsv3_mini_fp32", "norenorm_fp32"])
+def test_fp32_activations_compute_in_tf32(cuda_device, name):
+    """fp32 activations keep fp32 operands (tf32 tensor-core GEMMs on operands
+    rounded to tf32, fp32 weights prepared once): the output is within 1e-3
+    relative L2 of base.py's own fp32 output (measured 5.2e-4; bf16 operands
+    gave 4.1e-3)."""
+    from cases import BY_NAME
+    case = BY_NAME[name]
+    out, _ = auto_bench_flow(case, cuda_device)
+    ref = torch.from_numpy(np.load(GOLDEN / f"{name}.npz")["out"])
+    assert out.dtype == torch.float32
+    assert orc.rel_l2(out.cpu(), ref) <= 1e-3, orc.rel_l2(out.cpu(), ref)
+    assert fm.compute_dtype_for(torch.float32) == torch.float32
+
+
 def test_state_dict_is_reference_compatible():
     m = fm.ModelNew(8, 2, 128, 64)
     assert set(m.state_dict()) == {"w1", "w2"}
