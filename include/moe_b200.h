@@ -519,13 +519,16 @@ int moe_ep_plan_dedup(const void* topk_ids, int ids_dtype, const void* topk_weig
 /* the other GPUs' buffers) and no host synchronisation.                     */
 /*                                                                          */
 /* Each rank owns one device buffer (created here, shared with the others   */
-/* through CUDA IPC handles): a control block, `capacity` received expert    */
-/* ids, `capacity` received rows and `capacity` result rows of hidden_size   */
-/* act_dtype (F16/BF16) elements. One step, all on the caller's stream:      */
-/*   moe_ep_plan -> moe_ep_peer_dispatch -> moe_fused_experts over the      */
-/*   received rows (num_tokens = capacity, top_k = 1, unit weights, ids from */
-/*   the buffer; unused slots hold id -1 and are dropped) writing the result */
-/*   rows -> moe_ep_peer_combine.                                           */
+/* through CUDA IPC handles): a control block, `capacity` x top_k received   */
+/* expert ids and weights, `capacity` received rows and `capacity` result    */
+/* rows of hidden_size act_dtype (F16/BF16) elements. A token travels to a   */
+/* rank once, with its top_k ids local to that rank (-1 for slots held       */
+/* elsewhere) and their weights. One step, all on the caller's stream:       */
+/*   moe_ep_plan_dedup -> moe_ep_peer_dispatch -> moe_fused_experts over the */
+/*   received rows (num_tokens = capacity, top_k = k, ids and weights from   */
+/*   the buffer, num_tokens_dev = the received-count word, out = the result  */
+/*   rows: each the weighted sum over the slots this rank holds)            */
+/*   -> moe_ep_peer_combine (out[t] = sum over the ranks of their rows).    */
 /* Every rank must take every step. Waits on other ranks are bounded;       */
 /* on expiry, or when a rank would receive more than `capacity` rows, the    */
 /* kernels store an error code (MOE_ERR_TIMEOUT / MOE_ERR_WORKSPACE) in the  */
