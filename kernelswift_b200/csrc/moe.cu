@@ -157,8 +157,12 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   const bool fp8 = P.quant == MOE_QUANT_FP8_BLOCK;
   const bool mx = P.quant == MOE_QUANT_FP8_UE8M0;
   const int max_bn = 256;
-  const Tiling dn =
-      choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !(fp8 || mx), max_bn);
+  // The UE8M0 kernel holds one TMEM accumulator at 256 columns and two at
+  // 128, so a 128-wide down GEMM (few k-blocks per tile) overlaps each
+  // tile's epilogue with the next tile's MMAs (DeepSeek-V3 T=4096: 1.13 ->
+  // 1.04 ms); its gate-up, with 56 k-blocks per tile, keeps 256.
+  const Tiling dn = choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !(fp8 || mx),
+                                  mx ? 128 : max_bn);
   // the split gate-up path has no fp8 epilogue (its block scales follow the
   // regrouped gate/up rows); fp8 keeps the fused SiLU*up epilogue
   const Tiling gu = choose_tiling(est_mb, P.numel, 2 * P.I, P.H * kbpe, sms, !(fp8 || mx),
