@@ -159,10 +159,14 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   const int max_bn = 256;
   // The UE8M0 kernel holds one TMEM accumulator at 256 columns and two at
   // 128, so a 128-wide down GEMM (few k-blocks per tile) overlaps each
-  // tile's epilogue with the next tile's MMAs (DeepSeek-V3 T=4096: 1.13 ->
-  // 1.04 ms); its gate-up, with 56 k-blocks per tile, keeps 256.
+  // tile's epilogue with the next tile's MMAs once the experts have rows to
+  // fill their m-blocks (DeepSeek-V3 T=4096, 128 routed rows per expert:
+  // down 1.10 -> 1.06 ms); with a few rows per expert (T=64: 2) the extra
+  // tiles cost more than the overlap gains (0.54 -> 0.58 ms), and the
+  // gate-up, with 56 k-blocks per tile, keeps 256.
+  const int dn_max_bn = mx && P.numel >= 64 * P.E ? 128 : max_bn;
   const Tiling dn = choose_tiling(est_mb, P.numel, P.H, P.I * kbpe, sms, true, !(fp8 || mx),
-                                  mx ? 128 : max_bn);
+                                  dn_max_bn);
   // the split gate-up path has no fp8 epilogue (its block scales follow the
   // regrouped gate/up rows); fp8 keeps the fused SiLU*up epilogue
   const Tiling gu = choose_tiling(est_mb, P.numel, 2 * P.I, P.H * kbpe, sms, !(fp8 || mx),
