@@ -83,11 +83,13 @@ struct KParams {
   int32_t sb_kb;
   int32_t up_offset;        // gate-up: original row of the first up row (= I)
   int32_t early_meta;       // see GroupedGemmArgs::early_meta
+  int32_t tail_halves;      // 256-wide unsplit rows epilogue: see moe_grouped_gemm_kernel
   uint64_t wait_limit_ns;
 };
 
 struct TileCoord {
   int mb, nt, ks;
+  int half;  // -1: the whole BN-wide tile; 0 / 1: its first / second 128 columns
 };
 
 // ---------------------------------------------------------------------------
@@ -176,6 +178,7 @@ __device__ void build_group_table(const int32_t* __restrict__ expert_ids, int nu
 __device__ __forceinline__ TileCoord tile_coord_tab(int t, int n_tiles, int splits,
                                                     const uint32_t* tab) {
   TileCoord c;
+  c.half = -1;
   c.ks = t % splits;
   const int u = t / splits;
   const uint32_t e = tab[u / n_tiles];
@@ -189,6 +192,7 @@ __device__ __forceinline__ TileCoord tile_coord_tab(int t, int n_tiles, int spli
 __device__ __forceinline__ TileCoord tile_coord(int t, int num_mb, int n_tiles,
                                                 int splits) {
   TileCoord c;
+  c.half = -1;
   c.ks = t % splits;
   const int u = t / splits;
   const int per_group = kGroupM * n_tiles;
@@ -238,15 +242,25 @@ struct GemmCfg {
 // KIND: kKindF16 (AB_FMT 0 = f16, 1 = bf16), kKindTF32 (AB_FMT 2, fp32
 // operands read as tf32) or kKindI8 (AB_FMT 1 = s8).
 // TOUT: element type of the gate-up output (f16/bf16).
+//
+// Tail halves (rows epilogue, BN = 256, no K split, p.tail_halves): when the
+// tiles do not fill the last wave of CTAs and the remainder R is at most half
+// the grid, those R tiles run as 2R items of 128 columns each (tmB128 loads
+// 128 weight rows, the MMA runs N = 128, the epilogue covers the item's
+// columns), so the last wave takes about half a tile-time instead of a full
+// one. Each output element keeps its K order: results are unchanged.
 template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB,
+                            const __grid_constant__ CUtensorMap tmB128,
                             const KParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::kStages;
   constexpr uint32_t D_FMT = (KIND == kKindI8) ? 2u : 1u;
   constexpr uint32_t IDESC = make_idesc(D_FMT, AB_FMT, BM, BN);
+  constexpr uint32_t IDESC_HALF = make_idesc(D_FMT, AB_FMT, BM, 128);
+  constexpr bool kHalves = (EPI == kEpiRows && BN == 256);
   constexpr bool kScaled = (KIND == kKindI8);
 
   extern __shared__ uint8_t smem_raw[];
@@ -311,12 +325,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     return use_tab ? tile_coord_tab(t, n_tiles, p.splits, gtab)
                    : tile_coord(t, num_mb, n_tiles, p.splits);
   };
-  // tile t -> its coordinates and k-block range
-  const int total_items = total_tiles;
+  // item i -> its coordinates and k-block range (tail halves: items past
+  // full_tiles are the 128-column halves of the remaining tiles)
+  int full_tiles = total_tiles;
+  if constexpr (kHalves) {
+    const int rem = total_tiles % int(gridDim.x);
+    if (p.tail_halves && p.splits == 1 && rem != 0 && 2 * rem <= int(gridDim.x))
+      full_tiles = total_tiles - rem;
+  }
+  const int total_items = full_tiles + 2 * (total_tiles - full_tiles);
   auto item = [&](int i, TileCoord& c, int& kb0, int& kb1) {
-    c = coord(i);
+    if (i < full_tiles) {
+      c = coord(i);
+    } else {
+      const int hi = i - full_tiles;
+      c = coord(full_tiles + (hi >> 1));
+      c.half = hi & 1;
+    }
     kb0 = c.ks * p.kb_per_split;
     kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+  };
+  // weight rows, tensor map and transaction bytes of an item's stages
+  auto b_first_row = [&](int e, const TileCoord& c) {
+    return e * p.n_total + c.nt * BN + (c.half > 0 ? 128 : 0);
+  };
+  auto b_map = [&](const TileCoord& c) { return c.half >= 0 ? &tmB128 : &tmB; };
+  auto stage_bytes = [&](const TileCoord& c) {
+    return uint32_t(c.half >= 0 ? kABytes + 128 * kKBytes : Cfg::kStageBytes);
   };
   if (early && !producer) {
     pdl_wait();
@@ -339,10 +374,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         item(t, c, kb0, kb1);
         const int e = __ldg(p.expert_ids + c.mb);
         if (e < 0 || e >= p.num_experts) continue;
-        const int b_row = e * p.n_total + c.nt * BN;
+        const int b_row = b_first_row(e, c);
         for (int kb = kb0; kb < kb1 && pre < uint32_t(STAGES); ++kb, ++pre) {
-          mbar_arrive_expect_tx(&full[pre], Cfg::kStageBytes);
-          tma_load_2d(sB + pre * Cfg::kBBytes, &tmB, kb * kColsPerKb, b_row, &full[pre]);
+          mbar_arrive_expect_tx(&full[pre], stage_bytes(c));
+          tma_load_2d(sB + pre * Cfg::kBBytes, b_map(c), kb * kColsPerKb, b_row, &full[pre]);
         }
       }
       pdl_wait();
@@ -359,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int e = __ldg(p.expert_ids + c.mb);
       if (e < 0 || e >= p.num_experts) continue;
       const int a_row = c.mb * BM;
-      const int b_row = e * p.n_total + c.nt * BN;
+      const int b_row = b_first_row(e, c);
       for (int kb = kb0; kb < kb1; ++kb) {
         const int kcol = kb * kColsPerKb;
         if (issued < pre) {
@@ -370,9 +405,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          mbar_arrive_expect_tx(&full[stage], stage_bytes(c));
           tma_load_2d(sA + stage * kABytes, &tmA, kcol, a_row, &full[stage]);
-          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, kcol, b_row, &full[stage]);
+          tma_load_2d(sB + stage * Cfg::kBBytes, b_map(c), kcol, b_row, &full[stage]);
         }
         ++issued;
         if (++stage == STAGES) {
@@ -408,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-      const uint32_t idesc = IDESC;
+      const uint32_t idesc = c.half >= 0 ? IDESC_HALF : IDESC;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag, limit)) {
           ok = false;
@@ -462,8 +497,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
       float a_s = 1.0f;
       if constexpr (kScaled) a_s = valid ? __ldg(p.a_scale + m) : 0.0f;
-      const float* bsc =
-          kScaled ? p.b_scale + int64_t(e) * p.n_total + c.nt * BN : nullptr;
+      const int col0 = c.nt * BN + (c.half > 0 ? 128 : 0);  // the item's first column
+      const float* bsc = kScaled ? p.b_scale + int64_t(e) * p.n_total + col0 : nullptr;
 
       if constexpr (EPI == kEpiSwiGLU) {
         constexpr int G_HALF = BN / 64;              // 32-column groups per half
@@ -535,21 +570,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         constexpr int C_HALF = BN / 32;              // 16-column chunks per half
         constexpr int CPI = C_HALF >= 4 ? 4 : C_HALF;  // chunks per TMEM wait
+        // a 128-column tail item: 4 chunks per column half
+        const int c_half = c.half >= 0 ? 4 : C_HALF;
         const float w =
             valid ? load_weight(p.row_weights, p.row_weights_dtype, r) : 0.0f;
         // weighted rows in fp32 (K-split partial sums) or the activation dtype
         TOUT* out_row = static_cast<TOUT*>(p.out) +
-                        (int64_t(c.ks) * p.numel + (valid ? r : 0)) * p.out_ld + c.nt * BN;
+                        (int64_t(c.ks) * p.numel + (valid ? r : 0)) * p.out_ld + col0;
 #pragma unroll 1
-        for (int cc = 0; cc < C_HALF; cc += CPI) {
+        for (int cc = 0; cc < c_half; cc += CPI) {
           uint32_t v[CPI][16];
 #pragma unroll
-          for (int u = 0; u < CPI; ++u) tmem_ld16(tbase + (h * C_HALF + cc + u) * 16, v[u]);
+          for (int u = 0; u < CPI; ++u) tmem_ld16(tbase + (h * c_half + cc + u) * 16, v[u]);
           tmem_ld_wait();
           if (valid) {
 #pragma unroll
             for (int u = 0; u < CPI; ++u) {
-              const int g = h * C_HALF + cc + u;
+              const int g = h * c_half + cc + u;
               float x[16];
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
@@ -1307,14 +1344,14 @@ int set_smem_once(Kern kern, size_t bytes, std::atomic<uint64_t>& done) {
 }
 
 template <int KIND, int AB_FMT, int BN, int EPI, typename TOUT>
-int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb,
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb128,
                   const KParams& kp, int grid, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
   auto kern = moe_grouped_gemm_kernel<KIND, AB_FMT, BN, EPI, TOUT>;
   static std::atomic<uint64_t> smem_set{0};
   int st = set_smem_once(kern, Cfg::kSmemBytes, smem_set);
   if (st != MOE_OK) return st;
-  KSW_LAUNCH(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, s, ta, tb, kp);
+  KSW_LAUNCH(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, s, ta, tb, tb128, kp);
   return MOE_OK;
 }
 
@@ -1374,11 +1411,14 @@ int dispatch_mx(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const KPar
 
 template <int KIND, int AB_FMT, int EPI, typename TOUT>
 int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
-                const KParams& kp, int grid, cudaStream_t s) {
+                const KParams& kp, int grid, cudaStream_t s,
+                const CUtensorMap* tb128 = nullptr) {
+  // tb128: the weights with 128-row boxes, for tail halves (kp.tail_halves)
+  const CUtensorMap& t128 = tb128 != nullptr ? *tb128 : tb;
   switch (bn) {
-    case 256: return launch_kernel<KIND, AB_FMT, 256, EPI, TOUT>(ta, tb, kp, grid, s);
-    case 128: return launch_kernel<KIND, AB_FMT, 128, EPI, TOUT>(ta, tb, kp, grid, s);
-    case 64: return launch_kernel<KIND, AB_FMT, 64, EPI, TOUT>(ta, tb, kp, grid, s);
+    case 256: return launch_kernel<KIND, AB_FMT, 256, EPI, TOUT>(ta, tb, t128, kp, grid, s);
+    case 128: return launch_kernel<KIND, AB_FMT, 128, EPI, TOUT>(ta, tb, t128, kp, grid, s);
+    case 64: return launch_kernel<KIND, AB_FMT, 64, EPI, TOUT>(ta, tb, t128, kp, grid, s);
     default: return fail(MOE_ERR_UNSUPPORTED, "unsupported block_n");
   }
 }
@@ -1458,6 +1498,16 @@ int make_maps(const GroupedGemmArgs& a, const OperandTypes& ot, int bn,
   return encode_tma_2d(tb, ot.tma_type, ot.elem_bytes, a.b, uint64_t(a.k),
                        uint64_t(a.num_experts) * uint64_t(a.n), uint64_t(a.k),
                        box_k, uint32_t(bn));
+}
+
+// MOE_NO_TAIL_HALVES=1 runs every tile of the rows GEMMs at full width (the
+// tests compare both; read once).
+bool tail_halves_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_NO_TAIL_HALVES");
+    return !(v && v[0] && v[0] != '0');
+  }();
+  return on;
 }
 
 KParams base_params(const GroupedGemmArgs& a, int elem_bytes) {
@@ -1591,6 +1641,16 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   if (st != MOE_OK) return st;
   kp.out_ld = a.n;
   const int grid = sms;
+  // 256-wide unsplit tiles of the bf16/f16/tf32/int8 kernel may run the last
+  // partial wave as 128-column halves (moe_grouped_gemm_kernel)
+  CUtensorMap tb128 = tb;
+  if (bn == 256 && kp.splits == 1 && !fp8 && !mx && tail_halves_enabled()) {
+    st = encode_tma_2d(&tb128, ot.tma_type, ot.elem_bytes, a.b, uint64_t(a.k),
+                       uint64_t(a.num_experts) * uint64_t(a.n), uint64_t(a.k),
+                       uint32_t(kKBytes / ot.elem_bytes), 128);
+    if (st != MOE_OK) return st;
+    kp.tail_halves = 1;
+  }
   KSW_REQUIRE(a.out_dtype == MOE_DTYPE_F32 || ((a.out_dtype == MOE_DTYPE_BF16 ||
                                                   a.out_dtype == MOE_DTYPE_F16) &&
                                                  kp.splits == 1 && !fp8),
@@ -1605,23 +1665,23 @@ int gemm_down_launch(const GroupedGemmArgs& a, cudaStream_t s) {
   }
   if (a.out_dtype == MOE_DTYPE_BF16) {
     if (a.quant == MOE_QUANT_INT8_CHANNEL)
-      return dispatch_bn<kKindI8, 1, kEpiRows, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
+      return dispatch_bn<kKindI8, 1, kEpiRows, __nv_bfloat16>(bn, ta, tb, kp, grid, s, &tb128);
     if (a.compute_dtype == MOE_DTYPE_BF16)
-      return dispatch_bn<kKindF16, 1, kEpiRows, __nv_bfloat16>(bn, ta, tb, kp, grid, s);
+      return dispatch_bn<kKindF16, 1, kEpiRows, __nv_bfloat16>(bn, ta, tb, kp, grid, s, &tb128);
     return fail(MOE_ERR_UNSUPPORTED, "down GEMM: bf16 rows need bf16 operands");
   }
   if (a.out_dtype == MOE_DTYPE_F16) {
     if (a.quant == MOE_QUANT_NONE && a.compute_dtype == MOE_DTYPE_F16)
-      return dispatch_bn<kKindF16, 0, kEpiRows, __half>(bn, ta, tb, kp, grid, s);
+      return dispatch_bn<kKindF16, 0, kEpiRows, __half>(bn, ta, tb, kp, grid, s, &tb128);
     return fail(MOE_ERR_UNSUPPORTED, "down GEMM: f16 rows need f16 operands");
   }
   if (a.quant == MOE_QUANT_INT8_CHANNEL)
-    return dispatch_bn<kKindI8, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s);
+    return dispatch_bn<kKindI8, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s, &tb128);
   if (a.compute_dtype == MOE_DTYPE_F32)
-    return dispatch_bn<kKindTF32, 2, kEpiRows, float>(bn, ta, tb, kp, grid, s);
+    return dispatch_bn<kKindTF32, 2, kEpiRows, float>(bn, ta, tb, kp, grid, s, &tb128);
   if (a.compute_dtype == MOE_DTYPE_BF16)
-    return dispatch_bn<kKindF16, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s);
-  return dispatch_bn<kKindF16, 0, kEpiRows, float>(bn, ta, tb, kp, grid, s);
+    return dispatch_bn<kKindF16, 1, kEpiRows, float>(bn, ta, tb, kp, grid, s, &tb128);
+  return dispatch_bn<kKindF16, 0, kEpiRows, float>(bn, ta, tb, kp, grid, s, &tb128);
 }
 
 }  // namespace ksw
