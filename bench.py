@@ -9,7 +9,8 @@ sum, over one batch of synthetic tokens (N(0,1) activations, N(0,1/fan_in)
 weights, N(0,1) router logits).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload mixtral|qwen3|dsv3|dsv3-fp8|dsv3-fp8-ue8m0|qwen3-int8] [--tokens T]
+                    [--workload cfg0|mixtral|qwen3|dsv3|dsv3-fp8|dsv3-fp8-ue8m0|qwen3-int8]
+                    [--tokens T]
 
 `value` is device time (CUDA events, inputs resident in HBM, L2 flushed
 between steps outside the timed windows, max over ranks). On one GPU a step
@@ -39,7 +40,10 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 
 WORKLOADS = {
-    # name: (H, I, E, k, quant, default T, logit bias std)
+    # name: (H, I, E, k, quant, default T, logit bias std); activations bf16
+    # except for the fp32 ones in FP32_WORKLOADS
+    # the CPU-runnable fp32 configuration (tf32 tensor-core GEMMs on the GPU)
+    "cfg0": (512, 1024, 8, 2, "none", 64, 0.0),
     "mixtral": (4096, 14336, 8, 2, "none", 4096, 0.0),
     "qwen3": (2048, 768, 128, 8, "none", 8192, 0.5),
     "dsv3": (7168, 2048, 256, 8, "none", 8192, 0.0),
@@ -48,6 +52,7 @@ WORKLOADS = {
     "dsv3-fp8-ue8m0": (7168, 2048, 256, 8, "fp8-ue8m0", 4096, 0.0),
     "qwen3-int8": (2048, 768, 128, 8, "int8", 8192, 0.5),
 }
+FP32_WORKLOADS = {"cfg0"}
 METRIC = "fused-MoE layer tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
@@ -194,7 +199,7 @@ def cpu_experts(H, I, E, k):
 
 
 def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1,
-                       min_seconds=0.0):
+                       min_seconds=0.0, act_dtype=None):
     """tokens/s of base.py's forward (oracle restatement) on the host CPU:
     median over `repeats` calls, more calls until `min_seconds` of timed work.
     Uses cpu_experts(...) of the E experts."""
@@ -204,7 +209,7 @@ def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1
     E = cpu_experts(H, I, E, k)
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
-    hidden = torch.randn(sample_tokens, H, generator=g).to(torch.bfloat16)
+    hidden = torch.randn(sample_tokens, H, generator=g).to(act_dtype or torch.bfloat16)
     logits = torch.randn(sample_tokens, E, generator=g)
     if bias:
         logits = logits + torch.randn(E, generator=g) * bias
@@ -230,7 +235,7 @@ def cpu_reference_rate(H, I, E, k, quant, bias, sample_tokens, repeats, warmup=1
 # Tokens per CPU call of each workload: one fixed sample, the same for the
 # cpu_baseline leg and the --impl reference arm, so both legs time the same
 # batch (about 0.2-1 s per call on a 16-core host).
-CPU_SAMPLE_TOKENS = {"mixtral": 2048, "qwen3": 1024, "qwen3-int8": 1024, "dsv3": 512,
+CPU_SAMPLE_TOKENS = {"cfg0": 64, "mixtral": 2048, "qwen3": 1024, "qwen3-int8": 1024, "dsv3": 512,
                      "dsv3-fp8": 512, "dsv3-fp8-ue8m0": 512}
 
 
@@ -266,20 +271,24 @@ def run_reference(args, H, I, E, k, quant, T, bias, rank):
     if rank != 0:
         return
     sample = cpu_sample_tokens(args.workload, T)
+    import torch
+    act = torch.float32 if args.workload in FP32_WORKLOADS else torch.bfloat16
     rate, med, cores, n = cpu_reference_rate(H, I, E, k, quant, bias, sample,
-                                             repeats=max(1, args.steps), warmup=max(0, args.warmup))
+                                             repeats=max(1, args.steps), warmup=max(0, args.warmup),
+                                             act_dtype=act)
+    dname = act_dtype_name(args.workload)
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": dname, "data": "synthetic",
         "config": dict(workload_config(args.workload, H, I, E, k, quant, T, args.gpus),
                        l2="not applicable: host CPU run", parallelism="single host process"),
         "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "cpu_model": cpu_model(),
                          "sample": f"{sample} tokens per step of the {args.workload} layer, "
-                                   "base.py forward restated in torch-CPU bf16 with the "
-                                   "per-call fp32->bf16 weight casts"
+                                   f"base.py forward restated in torch-CPU {dname} with the "
+                                   f"per-call fp32->{dname} weight casts"
                                    + cpu_expert_note(H, I, E, k)},
         "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -287,9 +296,14 @@ def run_reference(args, H, I, E, k, quant, T, bias, rank):
     print(json.dumps(line), flush=True)
 
 
+def act_dtype_name(name: str) -> str:
+    return "f32" if name in FP32_WORKLOADS else "bf16"
+
+
 def workload_config(name, H, I, E, k, quant, T, n, exchange=None):
     return {"workload": f"{name} MoE layer H={H} I={I} E={E} top-{k} "
-                        f"{'bf16' if quant == 'none' else quant + ' W8A8'}, {T} tokens/GPU",
+                        f"{act_dtype_name(name) if quant == 'none' else quant + ' W8A8'}, "
+                        f"{T} tokens/GPU",
             "hidden": H, "intermediate": I, "experts": E, "top_k": k, "quant": quant,
             "tokens_per_gpu": T, "global_tokens": T * n,
             "parallelism": (f"ep{n} (E/{n} experts per GPU, " + (
@@ -345,8 +359,11 @@ def main():
     from kernelswift_b200 import fused_moe as fm
 
     # ---- synthetic problem (weights N(0, 1/fan_in), tokens N(0, 1)) ----
+    act_dtype = torch.float32 if args.workload in FP32_WORKLOADS else torch.bfloat16
+    if world > 1 and act_dtype != torch.bfloat16:
+        raise SystemExit(f"{args.workload}: the expert-parallel exchange moves 16-bit rows")
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    hidden = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    hidden = torch.randn(T, H, generator=g, device=dev).to(act_dtype)
     logits = torch.randn(T, E, generator=g, device=dev)
     if bias:
         logits = logits + torch.randn(E, generator=g, device=dev) * bias
@@ -362,7 +379,7 @@ def main():
         with torch.no_grad():
             model.w1.normal_(0.0, 1.0 / math.sqrt(H), generator=g)
             model.w2.normal_(0.0, 1.0 / math.sqrt(I), generator=g)
-        prep = model.prepared(torch.bfloat16, quant)
+        prep = model.prepared(act_dtype, quant)
 
         def step(stage_arr=None):
             return fm.fused_moe(hidden, prep, None, logits, k,
@@ -510,12 +527,12 @@ def main():
             return fm.fused_moe(hd, prep, None, ld, k, use_fp8_w8a8=quant.startswith("fp8"),
                                 use_int8_w8a8=quant == "int8", stage_events=stage_arr)
 
-        graph = fm.CapturedMoE(graph_fn, T, H, E, dtype=torch.bfloat16, device=dev)
+        graph = fm.CapturedMoE(graph_fn, T, H, E, dtype=act_dtype, device=dev)
         graph.hidden.copy_(hidden)
         graph.logits.copy_(logits)
         gevs = stage_evs[0]
         gi = fm.CapturedMoE(lambda hd, ld: graph_fn(hd, ld, stage_arrs[0]), T, H, E,
-                            dtype=torch.bfloat16, device=dev)
+                            dtype=act_dtype, device=dev)
         gi.hidden.copy_(hidden)
         gi.logits.copy_(logits)
         acc = [0.0] * len(_lib.STAGES)
@@ -554,7 +571,7 @@ def main():
     if not args.no_e2e:
         h_host = hidden.cpu().pin_memory()
         l_host = logits.cpu().pin_memory()
-        out_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+        out_host = torch.empty(T, H, dtype=act_dtype).pin_memory()
         if use_graph:
             def model_call(hd, ld):
                 return graph(hd, ld)
@@ -570,7 +587,7 @@ def main():
 
         # the public host-I/O pipeline: each step's H2D and D2H copies run on
         # their own streams, overlapping the neighbouring steps' compute
-        pipe = fm.HostPipeline(model_call, T, H, E, dtype=torch.bfloat16, device=dev)
+        pipe = fm.HostPipeline(model_call, T, H, E, dtype=act_dtype, device=dev)
 
         def e2e_step():
             pipe.submit(h_host, l_host, out_host)
@@ -598,7 +615,7 @@ def main():
                "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": hidden.numel() * hidden.element_size()
                + logits.numel() * logits.element_size(),
-               "d2h_bytes_per_step": T * H * 2,
+               "d2h_bytes_per_step": T * H * hidden.element_size(),
                "path": "HostPipeline over " + (
                    "CapturedMoE (CUDA graph of fused_moe: routing + experts)" if use_graph
                    else "ModelNew.forward (drop-in module)" if world == 1 and quant == "none"
@@ -616,12 +633,16 @@ def main():
     gu_ms = stage_ms["gate_up"]
     rows = rows_per_launch[0]
     gu_flops = 4 * H * I * rows
-    w_bytes = 2 if quant == "none" else 1
+    a_bytes = torch.empty(0, dtype=act_dtype).element_size()
+    w_bytes = a_bytes if quant == "none" else 1
     e_local = E if world == 1 else E // world
     hit = experts_hit[0] if experts_hit[0] else e_local
-    gu_bytes = hit * 2 * I * H * w_bytes + rows * H * w_bytes + rows * I * 2
+    gu_bytes = hit * 2 * I * H * w_bytes + rows * H * w_bytes + rows * I * a_bytes
     tensor_peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
     tensor_note = f"bf16 dense, sustained, {peak_src}"
+    if act_dtype == torch.float32 and quant == "none":
+        tensor_peak /= 2
+        tensor_note = f"bf16 dense sustained / 2 (tf32 operand rate), {peak_src}"
     if quant != "none":
         tensor_peak *= 2
         tensor_note = f"2x bf16 dense sustained ({quant} operand rate), {peak_src}"
@@ -651,7 +672,8 @@ def main():
                                f"{gu_bytes / 1e9:.4g} GB ({hit} experts' w13 + rows in + act out) "
                                "per launch",
                 "launch_ms": gu_ms}
-    if world == 1 and quant == "none" and fm.fused_experts_plan(T, H, I, E, k)["decode_path"]:
+    if world == 1 and quant == "none" and fm.fused_experts_plan(T, H, I, E, k, quant,
+                                                                 act_dtype)["decode_path"]:
         # decode sizes: the weight-streaming gate-up kernel (its stage) reads
         # the hit experts' w13 and the token rows, writes the act rows
         dec_bytes = hit * 2 * I * H * 2 + T * H * 2 + rows * I * 2
@@ -669,11 +691,12 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sample = cpu_sample_tokens(args.workload, T)
         rate, med, cores, n = cpu_reference_rate(H, I, E, k, quant, bias, sample, repeats=3,
-                                                 min_seconds=10.0)
+                                                 min_seconds=10.0, act_dtype=act_dtype)
         cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
                "cpu_model": cpu_model(),
                "sample": f"{sample} tokens of the same layer per call, base.py forward "
-                         f"restated in torch-CPU bf16 with its per-call weight casts "
+                         f"restated in torch-CPU {act_dtype_name(args.workload)} with its "
+                         "per-call weight casts "
                          f"(median of {n} calls, {med:.2f} s each)"
                          + cpu_expert_note(H, I, E, k)}
 
@@ -698,7 +721,7 @@ def main():
     # our kernels per step: the routing kernel plus what the expert pass
     # launches for this shape (the plan's own count), plus the exchange
     if world == 1:
-        launches_per_step = fm.fused_moe_launches(T, H, I, E, k, quant)
+        launches_per_step = fm.fused_moe_launches(T, H, I, E, k, quant, act_dtype)
     elif ep.peer is not None:
         # routing, plan, dispatch, expert pass over the receive buffer
         # (top_k = k, bounded by the received count), signal, combine, step end
@@ -719,7 +742,8 @@ def main():
             "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16" if quant == "none" else ("int8" if quant == "int8" else "e4m3"),
+            "dtype": (act_dtype_name(args.workload) if quant == "none"
+                      else ("int8" if quant == "int8" else "e4m3")),
             "data": "synthetic",
             "config": workload_config(args.workload, H, I, E, k, quant, T, world,
                                       None if world == 1 else
