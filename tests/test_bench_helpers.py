@@ -21,6 +21,21 @@ def test_workloads_cover_the_configs():
     H, I, E, k, quant, T, bias = bench.WORKLOADS["mixtral"]
     assert (H, I, E, k, quant, T) == (4096, 14336, 8, 2, "none", 4096)
     assert bench.WORKLOADS["dsv3-fp8"][4] == "fp8" and bench.WORKLOADS["qwen3"][6] > 0
+    # the CPU-runnable configuration, fp32 activations
+    assert bench.WORKLOADS["cfg0"][:6] == (512, 1024, 8, 2, "none", 64)
+    assert bench.FP32_WORKLOADS == {"cfg0"} and bench.act_dtype_name("cfg0") == "f32"
+
+
+def test_reference_arm_fp32_configuration():
+    """--impl reference on the fp32 configuration times base.py's path in fp32."""
+    res = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference",
+                          "--workload", "cfg0", "--steps", "1", "--warmup", "0"],
+                         capture_output=True, text=True, timeout=600, cwd=str(ROOT),
+                         env=dict(os.environ, OMP_NUM_THREADS="4"))
+    assert res.returncode == 0, res.stderr[-2000:]
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    assert line["dtype"] == "f32" and "f32" in line["config"]["workload"]
+    assert "torch-CPU f32" in line["cpu_baseline"]["sample"] and line["value"] > 0
 
 
 def test_config_block():
