@@ -10,7 +10,7 @@
 //   decode_gate_up_kernel  item = (routed slot, one 32-row slice of the
 //                          regrouped w13, i.e. 16 gate rows and their 16 up
 //                          rows); each warp dots 4 weight rows with the
-//                          slot's token row (staged in shared memory), eight
+//                          slot's token row (staged in shared memory), 16
 //                          16-byte loads in flight per lane, then SiLU(gate)
 //                          * up for 16 act columns, rounded to the activation
 //                          dtype. With fp32 router logits it first routes the
@@ -18,10 +18,11 @@
 //                          kernel's code, so the same experts and weights bit
 //                          for bit); the CTA holding the first item of a
 //                          token writes that token's ids and weights.
-//   decode_down_kernel     item = (token, 8 rows of w2): each warp streams one
-//                          w2 row of every slot's expert at once, dots each
-//                          with that slot's act row (the token's act rows are
-//                          staged) and sums w_j * dot_j in slot order, in fp32.
+//   decode_down_kernel     item = (token, 8 rows of w2): warp j streams slot
+//                          j's 8 rows (one contiguous run of its expert) and
+//                          dots them with the slot's act row (the token's act
+//                          rows are staged); w_j * dot_j is then summed over
+//                          the slots in slot order, in fp32.
 //
 // Both run persistent grids (the CTAs that fit at once walk the items).
 // Loads are 16-byte vectors, several in flight per lane. Slots whose id is
@@ -70,7 +71,7 @@ constexpr int kGuRouteMaxE = 256;  // in-kernel routing: 8 logits per lane
 
 // ---------------- gate-up ----------------
 // item = (slot, 32-row slice); one CTA per item while they fit, each warp
-// dots 4 weight rows with the token row (staged in shared memory), eight
+// dots 4 weight rows with the token row (staged in shared memory), 16
 // 16-byte loads in flight per lane. With router logits warp 0 routes the
 // item's token first (routing.cuh); the CTA holding slice 0 of a token's
 // first slot writes that token's ids and weights.
@@ -118,17 +119,18 @@ __global__ void __launch_bounds__(kThreadsDec)
     if (e < 0) continue;  // the act row of a dropped slot is never read
     const T* w = w13 + (int64_t(e) * 2 * I + chunk * kRowsGuD + warp * 4) * H;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int64_t k0 = int64_t(lane) * 8; k0 < H; k0 += 512) {
-      uint4 wv[2][4];
-      const bool second = k0 + 256 < H;
+    // four 256-column steps of the 4 rows per iteration: 16 weight loads in
+    // flight per lane
+    for (int64_t k0 = int64_t(lane) * 8; k0 < H; k0 += 1024) {
+      uint4 wv[4][4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        wv[0][r] = *reinterpret_cast<const uint4*>(w + r * H + k0);
-        if (second) wv[1][r] = *reinterpret_cast<const uint4*>(w + r * H + k0 + 256);
-      }
+      for (int st = 0; st < 4; ++st)
 #pragma unroll
-      for (int st = 0; st < 2; ++st) {
-        if (st == 1 && !second) break;
+        for (int r = 0; r < 4; ++r)
+          if (k0 + 256 * st < H) wv[st][r] = *reinterpret_cast<const uint4*>(w + r * H + k0 + 256 * st);
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        if (k0 + 256 * st >= H) break;
         float x[8];
         unpack8<T>(*reinterpret_cast<const uint4*>(a + k0 + 256 * st), x);
 #pragma unroll
@@ -154,17 +156,22 @@ __global__ void __launch_bounds__(kThreadsDec)
   }
 }
 
-// One warp per output row; the rows of all the token's slots are streamed
-// together (one 16-byte load per slot per step, and U steps at a time when
-// there are few slots), so a warp keeps about eight loads in flight instead
-// of walking the slots one after another. KMAX >= top_k.
+// item = (token t, kRowsDn consecutive output rows h0 .. h0 + 7). Warp w
+// takes the token's slot j = w (and j = w + 8 for top-16): the 8 rows
+// w2[e_j][h0 .. h0 + 8) are one contiguous run of 8 * I elements, which the
+// warp streams with two 256-column steps of all 8 rows per iteration (16
+// sixteen-byte loads in flight per lane), dotting each row with slot j's act
+// row (staged in shared memory). The dots go to shared memory and thread r
+// sums row r over the slots in slot order, out = sum_j w_j * dot_j, in fp32.
+// Per dot the lane sums its columns in order and the warp then reduces, as
+// the gate-up kernel does. KMAX >= top_k.
 template <typename T, typename IdT, typename Tw, int KMAX>
 __global__ void __launch_bounds__(kThreadsDec)
     decode_down_kernel(const T* __restrict__ act, const T* __restrict__ w2,
                        const IdT* __restrict__ ids, const Tw* __restrict__ weights,
                        int64_t T_tokens, int top_k, int E, int64_t H, int64_t I,
                        T* __restrict__ out) {
-  constexpr int U = KMAX >= 8 ? 1 : 8 / KMAX;
+  constexpr int kWarps = kThreadsDec / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row_blocks = H / kRowsDn;
   pdl_wait();
@@ -172,10 +179,11 @@ __global__ void __launch_bounds__(kThreadsDec)
   extern __shared__ uint4 smem_dec[];
   T* a = reinterpret_cast<T*>(smem_dec);  // [top_k, I] act rows of the current token
   __shared__ int s_e[KMAX];
+  __shared__ float s_dot[KMAX][kRowsDn];
   int64_t staged = -1;
   for (int64_t item = blockIdx.x; item < T_tokens * row_blocks; item += gridDim.x) {
     const int64_t t = item / row_blocks;
-    const int64_t h = (item - t * row_blocks) * kRowsDn + warp;
+    const int64_t h0 = (item - t * row_blocks) * kRowsDn;
     if (t != staged) {
       __syncthreads();
       if (threadIdx.x < KMAX)
@@ -186,43 +194,51 @@ __global__ void __launch_bounds__(kThreadsDec)
       staged = t;
       __syncthreads();
     }
-    const T* wrow[KMAX];
+    for (int j = warp; j < top_k; j += kWarps) {
+      const int e = s_e[j];
+      if (e < 0) continue;  // a dropped slot contributes nothing
+      const T* base = w2 + (int64_t(e) * H + h0) * I;
+      const T* x = a + int64_t(j) * I;
+      float acc[kRowsDn];
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j)
-      wrow[j] = s_e[j] >= 0 ? w2 + (int64_t(s_e[j]) * H + h) * I : nullptr;
-    float acc[KMAX];
+      for (int r = 0; r < kRowsDn; ++r) acc[r] = 0.f;
+      for (int64_t k0 = int64_t(lane) * 8; k0 < I; k0 += 512) {
+        const bool second = k0 + 256 < I;
+        uint4 wv[2][kRowsDn];
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j) acc[j] = 0.f;
-    for (int64_t k0 = int64_t(lane) * 8; k0 < I; k0 += 256 * U) {
-      uint4 wv[U][KMAX];
+        for (int r = 0; r < kRowsDn; ++r) {
+          wv[0][r] = *reinterpret_cast<const uint4*>(base + r * I + k0);
+          if (second) wv[1][r] = *reinterpret_cast<const uint4*>(base + r * I + k0 + 256);
+        }
 #pragma unroll
-      for (int u = 0; u < U; ++u)
+        for (int u = 0; u < 2; ++u) {
+          if (u == 1 && !second) break;
+          float xv[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(x + k0 + 256 * u), xv);
 #pragma unroll
-        for (int j = 0; j < KMAX; ++j)
-          if (wrow[j] != nullptr && k0 + u * 256 < I)
-            wv[u][j] = *reinterpret_cast<const uint4*>(wrow[j] + k0 + u * 256);
+          for (int r = 0; r < kRowsDn; ++r) {
+            float f[8];
+            unpack8<T>(wv[u][r], f);
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        if (k0 + u * 256 >= I) break;
-#pragma unroll
-        for (int j = 0; j < KMAX; ++j) {
-          if (wrow[j] == nullptr) continue;
-          float f[8], xv[8];
-          unpack8<T>(wv[u][j], f);
-          unpack8<T>(*reinterpret_cast<const uint4*>(a + int64_t(j) * I + k0 + u * 256), xv);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) acc[j] = fmaf(f[q], xv[q], acc[j]);
+            for (int q = 0; q < 8; ++q) acc[r] = fmaf(f[q], xv[q], acc[r]);
+          }
         }
       }
-    }
-    float total = 0.f;
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j) {
-      if (wrow[j] == nullptr) continue;
-      const float dsum = warp_sum(acc[j]);
-      total = fmaf(to_f32(weights[t * top_k + j]), dsum, total);
+      for (int r = 0; r < kRowsDn; ++r) {
+        const float v = warp_sum(acc[r]);
+        if (lane == 0) s_dot[j][r] = v;
+      }
     }
-    if (lane == 0) out[t * H + h] = from_f32<T>(total);
+    __syncthreads();
+    if (threadIdx.x < kRowsDn) {
+      const int r = threadIdx.x;
+      float total = 0.f;
+      for (int j = 0; j < top_k; ++j)
+        if (s_e[j] >= 0) total = fmaf(to_f32(weights[t * top_k + j]), s_dot[j][r], total);
+      out[t * H + h0 + r] = from_f32<T>(total);
+    }
+    __syncthreads();  // s_dot is reused by the next item
   }
 }
 
