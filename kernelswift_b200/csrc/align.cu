@@ -106,11 +106,12 @@ __device__ __forceinline__ void count_subchunk(const IdT* ids, int64_t base, int
 // at a time, independent of one another), and every id reads its base
 // with one shared-memory load. Entries of warps without the expert stay
 // zero, and each leader zeroes its own entry after its warp has read it.
+// inv (optional) receives each id's slot, -1 for an id outside [0, E).
 template <typename IdT>
 __device__ __forceinline__ void scatter_subchunk(const IdT* ids, int64_t base,
                                                  int64_t end, int E,
                                                  int* running, int* warp_cnt,
-                                                 int32_t* sorted) {
+                                                 int32_t* sorted, int32_t* inv) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t i = base + tid;
   const int e = (i < end) ? load_id(ids, i, E) : -1;
@@ -135,7 +136,13 @@ __device__ __forceinline__ void scatter_subchunk(const IdT* ids, int64_t base,
     running[ee] = s;
   }
   __syncthreads();
-  if (e >= 0) sorted[warp_cnt[warp * E + e] + rank] = static_cast<int32_t>(i);
+  if (e >= 0) {
+    const int slot = warp_cnt[warp * E + e] + rank;
+    sorted[slot] = static_cast<int32_t>(i);
+    if (inv) inv[i] = slot;
+  } else if (inv && i < end) {
+    inv[i] = -1;
+  }
   __syncwarp();
   if (leader) warp_cnt[warp * E + e] = 0;
   __syncthreads();
@@ -160,7 +167,7 @@ __global__ void __launch_bounds__(kThreads)
                        int BM, int64_t L, int32_t* __restrict__ sorted,
                        int32_t* __restrict__ expert_ids,
                        int32_t* __restrict__ num_post_pad, const int32_t* valid_dev,
-                       int valid_mult) {
+                       int valid_mult, int32_t* __restrict__ inv) {
   pdl_wait();
   pdl_trigger();
   const int64_t nv = valid_ids(numel, valid_dev, valid_mult);
@@ -190,7 +197,7 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
 
   for (int64_t base = 0; base < nv; base += kThreads)
-    scatter_subchunk(ids, base, nv, E, running, warp_cnt, sorted);
+    scatter_subchunk(ids, base, nv, E, running, warp_cnt, sorted, inv);
 }
 
 template <typename IdT>
@@ -253,7 +260,7 @@ __global__ void __launch_bounds__(kThreads)
     align_scatter_kernel(const IdT* __restrict__ ids, int64_t numel, int E, int chunk,
                          const int32_t* __restrict__ chunk_base,
                          int32_t* __restrict__ sorted, const int32_t* valid_dev,
-                         int valid_mult) {
+                         int valid_mult, int32_t* __restrict__ inv) {
   pdl_wait();
   pdl_trigger();
   const int64_t nv = valid_ids(numel, valid_dev, valid_mult);
@@ -269,14 +276,14 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t end = min(nv, begin + chunk);
   if (begin >= end) return;  // nothing valid in this chunk
   for (int64_t base = begin; base < end; base += kThreads)
-    scatter_subchunk(ids, base, end, E, running, warp_cnt, sorted);
+    scatter_subchunk(ids, base, end, E, running, warp_cnt, sorted, inv);
 }
 
 template <typename IdT>
 int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
                  int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
                  int32_t* ws, int chunk, int64_t small_max, cudaStream_t s,
-                 const int32_t* valid_dev, int valid_mult) {
+                 const int32_t* valid_dev, int valid_mult, int32_t* inv) {
   if (numel <= small_max) {
     const size_t smem = size_t(2 * E + 64 + 32 * E) * sizeof(int);
     auto k = align_small_kernel<IdT>;
@@ -284,7 +291,7 @@ int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
       KSW_CUDA(cudaFuncSetAttribute(
           k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     KSW_LAUNCH(k, dim3(1), dim3(kThreads), smem, s, ids, numel, E, BM, L, sorted,
-               expert_ids, num_post_pad, valid_dev, valid_mult);
+               expert_ids, num_post_pad, valid_dev, valid_mult, inv);
     return MOE_OK;
   }
   const int nchunks = static_cast<int>(ceil_div(numel, chunk));
@@ -299,7 +306,7 @@ int launch_align(const IdT* ids, int64_t numel, int E, int BM, int64_t L,
     KSW_CUDA(cudaFuncSetAttribute(
         k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   KSW_LAUNCH(k, dim3(nchunks), dim3(kThreads), smem, s, ids, numel, E, chunk,
-             static_cast<const int32_t*>(ws), sorted, valid_dev, valid_mult);
+             static_cast<const int32_t*>(ws), sorted, valid_dev, valid_mult, inv);
   return MOE_OK;
 }
 
@@ -313,7 +320,7 @@ int align_launch_cfg(const void* ids, int ids_dtype, int64_t numel, int E, int B
                      int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
                      void* workspace, size_t ws_bytes, int chunk, int64_t small_max,
                      cudaStream_t s, const int32_t* valid_dev = nullptr,
-                     int valid_mult = 1) {
+                     int valid_mult = 1, int32_t* inv = nullptr) {
   int st = align_validate(numel, E, BM);
   if (st != MOE_OK) return st;
   KSW_REQUIRE(ids_dtype == MOE_DTYPE_I32 || ids_dtype == MOE_DTYPE_I64,
@@ -330,11 +337,11 @@ int align_launch_cfg(const void* ids, int ids_dtype, int64_t numel, int E, int B
     return launch_align(static_cast<const int32_t*>(ids), numel, E, BM, L,
                         sorted, expert_ids, num_post_pad,
                         static_cast<int32_t*>(workspace), chunk, small_max, s, valid_dev,
-                        valid_mult);
+                        valid_mult, inv);
   return launch_align(static_cast<const int64_t*>(ids), numel, E, BM, L, sorted,
                       expert_ids, num_post_pad,
                       static_cast<int32_t*>(workspace), chunk, small_max, s, valid_dev,
-                      valid_mult);
+                      valid_mult, inv);
 }
 
 }  // namespace
@@ -363,9 +370,10 @@ int align_validate(int64_t numel, int E, int BM) {
 int align_launch(const void* ids, int ids_dtype, int64_t numel, int E, int BM,
                  int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
                  void* workspace, size_t ws_bytes, cudaStream_t s, const int32_t* valid_dev,
-                 int valid_mult) {
+                 int valid_mult, int32_t* inv) {
   return align_launch_cfg(ids, ids_dtype, numel, E, BM, sorted, expert_ids, num_post_pad,
-                          workspace, ws_bytes, kChunk, kSmallMax, s, valid_dev, valid_mult);
+                          workspace, ws_bytes, kChunk, kSmallMax, s, valid_dev, valid_mult,
+                          inv);
 }
 
 }  // namespace ksw

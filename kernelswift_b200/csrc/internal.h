@@ -15,10 +15,14 @@ size_t align_workspace_bytes(int64_t numel, int E);
 int align_validate(int64_t numel, int E, int BM);
 // valid_dev (optional): only the first *valid_dev * valid_mult flat ids
 // take part; the rest are dropped like ids outside [0, E).
+// inv (optional, [numel]): receives the slot of every flat id that takes
+// part, i.e. inv[sorted[m]] = m, and -1 for ids outside [0, E); entries of
+// ids past the valid count are not written.
 int align_launch(const void* ids, int ids_dtype, int64_t numel, int E, int BM,
                  int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad,
                  void* workspace, size_t ws_bytes, cudaStream_t s,
-                 const int32_t* valid_dev = nullptr, int valid_mult = 1);
+                 const int32_t* valid_dev = nullptr, int valid_mult = 1,
+                 int32_t* inv = nullptr);
 
 // ----- gemm.cu -----
 // Row-block height of the grouped GEMMs (and the align block size they need).

@@ -36,8 +36,9 @@ struct Plan {
   int part_dtype;        // dtype of the down GEMM's weighted rows
   size_t align_ws;
   int sms;
-  size_t off_sorted, off_eids, off_npp, off_align, off_a, off_a_scale, off_act,
+  size_t off_sorted, off_eids, off_npp, off_align, off_inv, off_a, off_a_scale, off_act,
       off_act_q, off_act_scale, off_part, off_gu_part, total;
+  bool token_gather;     // gather through the align's slot map (token-major)
 };
 
 int elem_bytes(int dtype) {
@@ -48,6 +49,16 @@ int elem_bytes(int dtype) {
     case MOE_DTYPE_I64: return 8;
     default: return 0;
   }
+}
+
+// MOE_NO_TOKEN_GATHER=1 keeps the row-major gather (one source read per
+// routed row) in moe_fused_experts; the two write the same operand bytes.
+bool token_gather_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_NO_TOKEN_GATHER");
+    return !(v && v[0] && v[0] != '0');
+  }();
+  return on;
 }
 
 // Upper bound on the m-blocks a routing can use: an expert with c rows needs
@@ -205,6 +216,11 @@ int make_plan(const moe_problem_t* p, int sms, Plan* pl) {
   P.off_eids = take(size_t(P.L / kBlockM) * 4);
   P.off_npp = take(4);
   P.off_align = take(P.align_ws);
+  // the token-major gather reads each token once and writes its top_k rows
+  P.token_gather = token_gather_enabled() && P.k <= 32 &&
+                   (P.quant == MOE_QUANT_NONE || P.quant == MOE_QUANT_FP8_BLOCK ||
+                    P.quant == MOE_QUANT_FP8_UE8M0);
+  P.off_inv = take(P.token_gather ? size_t(P.numel) * 4 : 0);
   P.off_a = take(size_t(P.L) * P.H * elem_bytes(P.a_dtype));
   // per-row scales: int8 one per row, fp8 one per row per 128 columns (fp32,
   // or one byte in the scale-factor image for UE8M0)
@@ -355,8 +371,10 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   int32_t* npp = at<int32_t>(workspace, P.off_npp);
 
   KSW_MARK(MOE_STAGE_ALIGN);
+  int32_t* inv = P.token_gather ? at<int32_t>(workspace, P.off_inv) : nullptr;
   st = align_launch(p->topk_ids, p->ids_dtype, P.numel, P.E, kBlockM, sorted, eids, npp,
-                    at<void>(workspace, P.off_align), P.align_ws, s, p->num_tokens_dev, P.k);
+                    at<void>(workspace, P.off_align), P.align_ws, s, p->num_tokens_dev, P.k,
+                    inv);
   if (st != MOE_OK) return st;
 
   GatherArgs g{};
@@ -373,6 +391,8 @@ static int fused_experts_impl(const moe_problem_t* p, void* workspace, size_t wo
   g.dst = at<void>(workspace, P.off_a);
   g.dst_dtype = P.a_dtype;
   g.scale = P.quant == MOE_QUANT_NONE ? nullptr : at<float>(workspace, P.off_a_scale);
+  g.inv = inv;
+  g.src_count = p->num_tokens_dev;
   KSW_MARK(MOE_STAGE_GATHER);
   st = gather_launch(g, s);
   if (st != MOE_OK) return st;

@@ -259,6 +259,116 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// ---------------- token-major gather ----------------
+// The rows of the three kernels above, visited from the source side. With
+// the align's slot map (inv[t * top_k + j] = operand row of token t's slot
+// j, -1 for a dropped slot) one warp reads a 1024-column chunk of a token
+// once, converts or quantises it once, and stores the result into each of
+// the token's top_k operand rows: the source is read, and the e4m3
+// arithmetic done, once per token instead of once per routed row. Lane
+// geometry and per-element arithmetic are the row-major kernels' (pass u
+// covers columns c0 + 256 u + 8 lane; in fp8 modes lanes 0-15 and 16-31
+// hold two 128-column groups), so the operand rows and scales written are
+// the same bytes. Needs top_k <= 32 (one slot position per lane).
+enum { kTokCast = 0, kTokFp8 = 1, kTokUe8m0 = 2 };
+
+template <int MODE, typename Tin, typename Tout>
+__global__ void __launch_bounds__(kWarps * 32)
+    gather_tokens_kernel(const Tin* __restrict__ src, int64_t H, int top_k,
+                         const int32_t* __restrict__ inv,
+                         const int32_t* __restrict__ src_count, int64_t src_rows,
+                         int64_t max_rows, Tout* __restrict__ dst, void* __restrict__ scale,
+                         int64_t row_slices) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tokens = src_count ? min(int64_t(__ldg(src_count)), src_rows) : src_rows;
+  constexpr int64_t kCols = kBatch * 256;
+  const int64_t chunks = (H + kCols - 1) / kCols;
+  const int64_t groups = (H + 127) / 128;
+  const int64_t q_stride = row_slices * 512;
+  for (int64_t task = int64_t(blockIdx.x) * kWarps + warp; task < tokens * chunks;
+       task += int64_t(gridDim.x) * kWarps) {
+    const int64_t t = task / chunks;
+    const int64_t c0 = (task - t * chunks) * kCols;
+    const int my_pos = lane < top_k ? __ldg(inv + t * top_k + lane) : -1;
+    const Tin* s = src + t * H;
+    float v[kBatch][8];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t h = c0 + u * 256 + lane * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+      if (h < H) load8(s + h, v[u]);
+    }
+    // converted once: 16-bit rows packed, fp32 rows rounded to tf32, fp8
+    // rows packed to e4m3 with their group scale
+    uint4 packed[kBatch];
+    float sc[kBatch];
+    uint32_t sb[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if constexpr (MODE == kTokCast) {
+        if constexpr (std::is_same<Tout, float>::value) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[u][i] = round_tf32(v[u][i]);
+        } else {
+          packed[u] = make_uint4(pack2<Tout>(v[u][0], v[u][1]), pack2<Tout>(v[u][2], v[u][3]),
+                                 pack2<Tout>(v[u][4], v[u][5]), pack2<Tout>(v[u][6], v[u][7]));
+        }
+      } else {
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1)
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        float inv_s;
+        if constexpr (MODE == kTokFp8) {
+          sc[u] = quant_scale(amax, kFp8Max);
+          inv_s = 1.0f / sc[u];
+        } else {
+          sb[u] = ue8m0_byte(amax);
+          inv_s = ue8m0_inv_scale(sb[u]);
+        }
+        const uint2 q = pack_e4m3x8(v[u], inv_s);
+        packed[u] = make_uint4(q.x, q.y, 0u, 0u);
+      }
+    }
+    for (int j = 0; j < top_k; ++j) {
+      const int64_t m = __shfl_sync(0xffffffffu, my_pos, j);
+      if (m < 0 || m >= max_rows) continue;  // dropped slot (warp-uniform)
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t h = c0 + u * 256 + lane * 8;
+        if (h >= H) continue;
+        if constexpr (MODE == kTokCast) {
+          Tout* d = dst + m * H + h;
+          if constexpr (std::is_same<Tout, float>::value) {
+            reinterpret_cast<float4*>(d)[0] = make_float4(v[u][0], v[u][1], v[u][2], v[u][3]);
+            reinterpret_cast<float4*>(d)[1] = make_float4(v[u][4], v[u][5], v[u][6], v[u][7]);
+          } else {
+            *reinterpret_cast<uint4*>(d) = packed[u];
+          }
+        } else {
+          uint8_t* d = reinterpret_cast<uint8_t*>(dst) + m * H + h;
+          *reinterpret_cast<uint2*>(d) = make_uint2(packed[u].x, packed[u].y);
+          if ((lane & 15) == 0) {
+            const int64_t g = (c0 + u * 256) / 128 + (lane >> 4);
+            if constexpr (MODE == kTokFp8) {
+              static_cast<float*>(scale)[m * groups + g] = sc[u];
+            } else {
+              uint8_t* sf_row = static_cast<uint8_t*>(scale) + (m >> 7) * 512 +
+                                16 * (m & 31) + 4 * ((m & 127) >> 5);
+              sf_row[(g >> 2) * q_stride + (g & 3)] = static_cast<uint8_t>(sb[u]);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
 // ---------------- gather + int8 per row ----------------
 template <typename Tin>
 __global__ void __launch_bounds__(kWarps * 32)
@@ -473,6 +583,49 @@ int grid_for_rows(int64_t rows) {
   return int(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, kWarps), 148 * 16)));
 }
 
+template <int MODE, typename Tin, typename Tout>
+int launch_tokens_typed(const GatherArgs& a, cudaStream_t s) {
+  const int64_t tasks = a.src_rows * ceil_div(a.H, int64_t(kBatch * 256));
+  KSW_LAUNCH(gather_tokens_kernel<MODE, Tin, Tout>, dim3(grid_for_rows(tasks)),
+             dim3(kWarps * 32), 0, s, static_cast<const Tin*>(a.src), a.H, a.top_k, a.inv,
+             a.src_count, a.src_rows, a.max_rows, static_cast<Tout*>(a.dst),
+             static_cast<void*>(a.scale), a.max_rows / 128);
+  return MOE_OK;
+}
+
+template <int MODE, typename Tout>
+int launch_tokens(const GatherArgs& a, cudaStream_t s) {
+  switch (a.src_dtype) {
+    case MOE_DTYPE_F32: return launch_tokens_typed<MODE, float, Tout>(a, s);
+    case MOE_DTYPE_BF16: return launch_tokens_typed<MODE, __nv_bfloat16, Tout>(a, s);
+    case MOE_DTYPE_F16: return launch_tokens_typed<MODE, __half, Tout>(a, s);
+    default: return fail(MOE_ERR_UNSUPPORTED, "gather: unsupported source dtype");
+  }
+}
+
+// The token-major gather, for the argument sets it covers; -1 otherwise.
+int gather_tokens_launch(const GatherArgs& a, cudaStream_t s) {
+  if (!a.inv || a.top_k < 1 || a.top_k > 32) return -1;
+  if (a.quant == MOE_QUANT_NONE) {
+    const int in = a.src_dtype, out = a.dst_dtype;
+    if (in == MOE_DTYPE_F32 && out == MOE_DTYPE_BF16)
+      return launch_tokens_typed<kTokCast, float, __nv_bfloat16>(a, s);
+    if (in == MOE_DTYPE_F32 && out == MOE_DTYPE_F16)
+      return launch_tokens_typed<kTokCast, float, __half>(a, s);
+    if (in == MOE_DTYPE_F32 && out == MOE_DTYPE_F32)
+      return launch_tokens_typed<kTokCast, float, float>(a, s);
+    if (in == MOE_DTYPE_BF16 && out == MOE_DTYPE_BF16)
+      return launch_tokens_typed<kTokCast, __nv_bfloat16, __nv_bfloat16>(a, s);
+    if (in == MOE_DTYPE_F16 && out == MOE_DTYPE_F16)
+      return launch_tokens_typed<kTokCast, __half, __half>(a, s);
+    return -1;
+  }
+  if (a.quant == MOE_QUANT_FP8_BLOCK && a.scale) return launch_tokens<kTokFp8, uint8_t>(a, s);
+  if (a.quant == MOE_QUANT_FP8_UE8M0 && a.scale && a.H % 128 == 0 && a.max_rows % 128 == 0)
+    return launch_tokens<kTokUe8m0, uint8_t>(a, s);
+  return -1;
+}
+
 }  // namespace
 
 int gather_launch(const GatherArgs& a, cudaStream_t s) {
@@ -485,6 +638,12 @@ int gather_launch(const GatherArgs& a, cudaStream_t s) {
               "gather: sorted ids needed when top_k > 0");
   KSW_REQUIRE(a.H % 16 == 0 && a.H > 0, MOE_ERR_UNSUPPORTED, "gather: H % 16 != 0");
   KSW_REQUIRE(a.top_k >= 0, MOE_ERR_INVALID_ARG, "gather: top_k < 0");
+  const int tok = gather_tokens_launch(a, s);
+  if (tok >= 0) {
+    if (tok != MOE_OK) return tok;
+    KSW_CUDA(cudaGetLastError());
+    return MOE_OK;
+  }
   const int grid = grid_for_rows(a.max_rows);
   const int block = kWarps * 32;
   if (a.quant == MOE_QUANT_NONE) {

@@ -23,6 +23,12 @@ struct GatherArgs {
   int dst_dtype;                // for QUANT_NONE: F16 or BF16
   float* scale;                 // FP8: [max_rows, ceil(H/128)], INT8: [max_rows],
                                 // FP8_UE8M0: the rows' scale-factor image (bytes)
+  // Optional, for top_k in [1, 32] and quant NONE / FP8_BLOCK / FP8_UE8M0:
+  // the align's slot map (inv[t * top_k + j] = operand row, -1 = dropped),
+  // which switches to the token-major kernel (each source row read and
+  // converted once); src_count (device, optional) bounds the source rows.
+  const int32_t* inv;
+  const int32_t* src_count;
 };
 
 struct SumArgs {
