@@ -91,6 +91,10 @@ def parse_args():
                     default="auto",
                     help="expert-parallel row exchange for --gpus > 1 (auto: NVLink peer "
                          "memory; nccl-dedup: all_to_all sending a token to a rank once)")
+    ap.add_argument("--ep-chunks", type=int, default=1,
+                    help="with --ep-exchange nccl/nccl-dedup: pipeline the exchange in this "
+                         "many token chunks (deduplicated rows; each chunk's all_to_all "
+                         "overlaps the previous chunk's experts)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every step eagerly instead of replaying a CUDA graph of the "
                          "whole forward (1 GPU runs use the graph by default)")
@@ -300,7 +304,7 @@ def act_dtype_name(name: str) -> str:
     return "f32" if name in FP32_WORKLOADS else "bf16"
 
 
-def workload_config(name, H, I, E, k, quant, T, n, exchange=None):
+def workload_config(name, H, I, E, k, quant, T, n, exchange=None, chunks=1):
     return {"workload": f"{name} MoE layer H={H} I={I} E={E} top-{k} "
                         f"{act_dtype_name(name) if quant == 'none' else quant + ' W8A8'}, "
                         f"{T} tokens/GPU",
@@ -310,7 +314,8 @@ def workload_config(name, H, I, E, k, quant, T, n, exchange=None):
                 "one row per token and destination rank, moved by dispatch/combine kernels "
                 "over NVLink peer memory)"
                 if exchange == "peer" else
-                "NCCL all_to_all, one row per token and destination rank)"
+                "NCCL all_to_all, one row per token and destination rank"
+                + (f", pipelined in {chunks} token chunks)" if chunks > 1 else ")")
                 if exchange == "nccl-dedup" else "NCCL all_to_all)")) if n > 1 else "single",
             "l2": f"flushed between steps outside the timed windows ({L2_FLUSH_BYTES >> 20} MB "
                   f"write{', then a read of another ' + str(L2_FLUSH_BYTES >> 20) + ' MB that evicts the dirty lines' if L2Flush.evict else ''}); "
@@ -324,6 +329,8 @@ def active_switches() -> dict:
         v = os.environ.get(name)
         return default if not v else v[0] != "0"  # the library's reading
     return {"pdl": not on("MOE_NO_PDL", False), "decode_path": not on("MOE_NO_DECODE_PATH", False),
+            "tail_halves": not on("MOE_NO_TAIL_HALVES", False),
+            "token_gather": not on("MOE_NO_TOKEN_GATHER", False),
             "block_n": os.environ.get("MOE_BLOCK_N") or "planner"}
 
 
@@ -398,9 +405,11 @@ def main():
         w2 = torch.randn(el, H, I, generator=g, device=dev, dtype=torch.bfloat16) / math.sqrt(I)
         def make_ep(exchange):
             dedup = exchange == "nccl-dedup"
+            chunks = args.ep_chunks if exchange in ("nccl", "nccl-dedup") else 1
             return ExpertParallelMoE(w1, w2, E, k, quant=quant,
                                      exchange="nccl" if dedup else exchange,
-                                     max_tokens=T, dtype=hidden.dtype, dedup=dedup)
+                                     max_tokens=T, dtype=hidden.dtype, dedup=dedup,
+                                     chunks=chunks)
 
         try:
             ep = make_ep(args.ep_exchange)
@@ -748,7 +757,8 @@ def main():
             "config": workload_config(args.workload, H, I, E, k, quant, T, world,
                                       None if world == 1 else
                                       (ep.exchange if ep.exchange == "peer" else
-                                       "nccl-dedup" if ep.dedup else "nccl")),
+                                       "nccl-dedup" if ep.dedup else "nccl"),
+                                      1 if world == 1 else ep.chunks),
             "tflops": tflops,
             "stage_ms": stage_ms,
             **({"exchange_ms": exchange_ms} if exchange_ms is not None else {}),

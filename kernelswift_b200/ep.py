@@ -39,6 +39,17 @@ elsewhere) and their weights, the receiver runs moe_fused_experts with top_k
 (token, rank), and the source adds the rows of the ranks it used. The NCCL
 exchange does this with dedup=True; the peer exchange always does.
 
+Chunked NCCL exchange (chunks=C > 1, deduplicated rows): the tokens are cut
+into C contiguous chunks, planned up front (C plan launches, one all_to_all
+of the [world, C] count matrix, one host sync), and pipelined: chunk c+1's
+rows, ids and weights are sent (async all_to_all) before chunk c's experts
+are enqueued, and chunk c's result rows return (async) while chunk c+1's
+experts run. ProcessGroupNCCL runs the collectives on its own stream, which
+waits for the work enqueued before each collective, so the transfer of one
+chunk overlaps the expert GEMMs of the previous one. Every rank cuts its own
+tokens into the same number of chunks (a chunk may be empty), so all ranks
+issue the same collectives in the same order.
+
 With exchange="peer" (ranks on one node, 2-8 GPUs) the all_to_alls are
 replaced by two kernels that move the rows themselves over NVLink
 (`PeerExchange`, the moe_ep_peer_* entry points): dispatch stores each
@@ -306,14 +317,17 @@ class ExpertParallelMoE:
                  num_experts: int, top_k: int, group=None, quant: str = "none",
                  backend=None, exchange: str = "auto", max_tokens: int | None = None,
                  dtype: torch.dtype = torch.bfloat16, wait_limit_ms: int = 0,
-                 dedup: bool = False):
+                 dedup: bool = False, chunks: int = 1):
         """exchange: "nccl" (all_to_all), "peer" (NVLink peer memory, needs
         max_tokens: the most tokens a rank passes to one forward) or "auto"
         (peer when max_tokens is given, the CUDA backend is used and the
         group has 2-8 ranks on GPUs, else nccl). `dtype` is the row dtype of
         the peer exchange (the hidden states' dtype). dedup: send a token to
         a rank once however many of its slots the rank holds (the NCCL
-        exchange's option; the peer exchange always does)."""
+        exchange's option; the peer exchange always does). chunks > 1: the
+        NCCL exchange in that many token chunks, each chunk's transfer
+        overlapping the previous chunk's experts (implies dedup; not for the
+        peer exchange)."""
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -334,8 +348,11 @@ class ExpertParallelMoE:
                         and 2 <= self.world <= _lib.EP_MAX_RANKS else "nccl")
         if exchange not in ("nccl", "peer"):
             raise ValueError(f"unknown exchange {exchange!r}")
+        if chunks < 1 or (chunks > 1 and exchange != "nccl"):
+            raise ValueError("chunks must be >= 1, and > 1 only with the NCCL exchange")
         self.exchange = exchange
-        self.dedup = dedup or exchange == "peer"
+        self.chunks = chunks
+        self.dedup = dedup or exchange == "peer" or chunks > 1
         self._last_recv_eid = None
         self._evs = None
         self.peer = None
@@ -359,6 +376,8 @@ class ExpertParallelMoE:
         self._evs = exchange_events
         if self.peer is not None:
             return self._forward_peer(hidden, topk_weights, topk_ids, stage_events)
+        if self.chunks > 1:
+            return self._forward_chunked(hidden, topk_weights, topk_ids, stage_events)
         if self.dedup:
             return self._forward_dedup(hidden, topk_weights, topk_ids, stage_events)
         T, H = hidden.shape
@@ -442,6 +461,91 @@ class ExpertParallelMoE:
         ones = torch.ones(T, self.world, dtype=torch.float32, device=dev)
         out = self.backend.combine(back, inv.reshape(-1), ones, T, self.world)
         self._mark(4)
+        return out
+
+    def _plan_dedup(self, topk_ids, topk_weights):
+        if hasattr(self.backend, "plan_dedup"):
+            return self.backend.plan_dedup(topk_ids, topk_weights, self.num_experts, self.world)
+        return dedup_plan(topk_ids, topk_weights, self.num_experts, self.world)
+
+    def _forward_chunked(self, hidden, topk_weights, topk_ids, stage_events=None):
+        """The deduplicated NCCL exchange in self.chunks pipelined token chunks
+        (module docstring). Exchange events: 0 before the plans, 1 after them,
+        2 when chunk 0's rows have arrived, 3 after the last chunk's experts,
+        4 after the last combine."""
+        T, H = hidden.shape
+        k = topk_ids.shape[1]
+        dev = hidden.device
+        world, C = self.world, self.chunks
+        bounds = [T * c // C for c in range(C + 1)]
+        self._mark(0)
+        plans = [self._plan_dedup(topk_ids[bounds[c]:bounds[c + 1]],
+                                  topk_weights[bounds[c]:bounds[c + 1]]) for c in range(C)]
+        self._mark(1)
+        counts = torch.stack([p[4][:world + 1] for p in plans])  # [C, world + 1]
+        send_counts = counts[:, :world].t().contiguous()  # [world, C]: per destination
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        both = torch.cat([counts.reshape(-1), recv_counts.reshape(-1)]).cpu()  # one host sync
+        cnt = both[:C * (world + 1)].view(C, world + 1)
+        rcv = both[C * (world + 1):].view(world, C)
+        if int(cnt[:, world].sum()) != 0:
+            raise ValueError("expert ids out of range")
+
+        def dispatch(c):
+            tokens, send_eid, send_w, inv, _ = plans[c]
+            send_split = cnt[c, :world].tolist()
+            recv_split = rcv[:, c].tolist()
+            n_send, n_recv = sum(send_split), sum(recv_split)
+            rows = self.backend.pack(hidden[bounds[c]:bounds[c + 1]], tokens[:n_send], 1)
+            recv_rows = torch.empty(n_recv, H, dtype=hidden.dtype, device=dev)
+            recv_eid = torch.empty(n_recv, k, dtype=torch.int32, device=dev)
+            recv_w = torch.empty(n_recv, k, dtype=torch.float32, device=dev)
+            works = [dist.all_to_all_single(recv_rows, rows, recv_split, send_split,
+                                            group=self.group, async_op=True),
+                     dist.all_to_all_single(recv_eid, send_eid[:n_send], recv_split, send_split,
+                                            group=self.group, async_op=True),
+                     dist.all_to_all_single(recv_w, send_w[:n_send], recv_split, send_split,
+                                            group=self.group, async_op=True)]
+            return {"c": c, "send_split": send_split, "recv_split": recv_split, "inv": inv,
+                    "rows": recv_rows, "eid": recv_eid, "w": recv_w, "works": works,
+                    "n_send": n_send}
+
+        out = torch.empty(T, H, dtype=hidden.dtype, device=dev)
+        returning = []
+        received = []
+        nxt = dispatch(0)
+        for c in range(C):
+            cur = nxt
+            for w in cur["works"]:
+                w.wait()
+            if c == 0:
+                self._mark(2)
+            if c + 1 < C:
+                nxt = dispatch(c + 1)  # in flight during this chunk's experts
+            received.append(cur["eid"])
+            if stage_events is not None and c == 0:
+                rows = self.backend.experts_weighted(cur["rows"], cur["eid"], cur["w"],
+                                                     stage_events=stage_events)
+            else:
+                rows = self.backend.experts_weighted(cur["rows"], cur["eid"], cur["w"])
+            back = torch.empty(cur["n_send"], H, dtype=rows.dtype, device=dev)
+            work = dist.all_to_all_single(back, rows, cur["send_split"], cur["recv_split"],
+                                          group=self.group, async_op=True)
+            returning.append((cur, back, work))
+        self._mark(3)
+        for cur, back, work in returning:
+            work.wait()
+            c = cur["c"]
+            t_c = bounds[c + 1] - bounds[c]
+            if t_c == 0:
+                continue
+            ones = torch.ones(t_c, world, dtype=torch.float32, device=dev)
+            out[bounds[c]:bounds[c + 1]] = self.backend.combine(back, cur["inv"].reshape(-1),
+                                                                ones, t_c, world)
+        self._mark(4)
+        self._last_recv_eid = torch.cat(received)
+        self.last_rows_received = sum(int(e.shape[0]) for e in received)
         return out
 
     def _forward_peer(self, hidden, topk_weights, topk_ids, stage_events=None):

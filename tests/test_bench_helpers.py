@@ -41,11 +41,15 @@ def test_reference_arm_fp32_configuration():
 def test_config_block():
     cfg = bench.workload_config("mixtral", 4096, 14336, 8, 2, "none", 4096, 1)
     assert cfg["parallelism"] == "single" and cfg["tokens_per_gpu"] == 4096
-    assert "flushed" in cfg["l2"] and set(cfg["switches"]) >= {"pdl", "decode_path", "block_n"}
+    assert "flushed" in cfg["l2"] and set(cfg["switches"]) >= {"pdl", "decode_path", "tail_halves",
+                                                             "token_gather", "block_n"}
     ep = bench.workload_config("mixtral", 4096, 14336, 8, 2, "none", 4096, 8, "peer")
     assert ep["global_tokens"] == 8 * 4096 and "peer memory" in ep["parallelism"]
     dd = bench.workload_config("dsv3", 7168, 2048, 256, 8, "none", 8192, 4, "nccl-dedup")
     assert "one row per token and destination rank" in dd["parallelism"]
+    assert "chunks" not in dd["parallelism"]
+    ch = bench.workload_config("dsv3", 7168, 2048, 256, 8, "none", 8192, 4, "nccl-dedup", 3)
+    assert "pipelined in 3 token chunks" in ch["parallelism"]
 
 
 def test_cpu_baseline_memory_cap():
@@ -59,14 +63,18 @@ def test_cpu_baseline_memory_cap():
 
 
 def test_switch_record(monkeypatch):
-    for name in ("MOE_NO_PDL", "MOE_NO_DECODE_PATH", "MOE_BLOCK_N"):
+    for name in ("MOE_NO_PDL", "MOE_NO_DECODE_PATH", "MOE_NO_TAIL_HALVES",
+                 "MOE_NO_TOKEN_GATHER", "MOE_BLOCK_N"):
         monkeypatch.delenv(name, raising=False)
-    assert bench.active_switches() == {"pdl": True, "decode_path": True, "block_n": "planner"}
+    assert bench.active_switches() == {"pdl": True, "decode_path": True, "tail_halves": True,
+                                       "token_gather": True, "block_n": "planner"}
     monkeypatch.setenv("MOE_NO_PDL", "1")
     monkeypatch.setenv("MOE_NO_DECODE_PATH", "0")
+    monkeypatch.setenv("MOE_NO_TOKEN_GATHER", "1")
     monkeypatch.setenv("MOE_BLOCK_N", "128")
     sw = bench.active_switches()
     assert not sw["pdl"] and sw["decode_path"] and sw["block_n"] == "128"
+    assert sw["tail_halves"] and not sw["token_gather"]
 
 
 def test_reference_arm_json_line():

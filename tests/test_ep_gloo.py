@@ -3,8 +3,10 @@
 The exchange (split sizes, packing order, the three all_to_alls, the inverse
 permutation of the combine) runs exactly as on GPUs; the device work is done
 by a test-only CPU backend built on the oracle. The deduplicated exchange
-(one row per token and destination rank) runs its torch plan unchanged. A
-second test makes one rank
+(one row per token and destination rank) runs its torch plan unchanged, in
+one piece and pipelined in token chunks (async all_to_alls, one chunk's
+transfer in flight during the previous chunk's experts). A second test
+makes one rank
 fail before its first collective and checks that the other rank's forward
 ends with an error within the process group's timeout instead of hanging. A
 third replays the peer-memory exchange's placement rule (deduplicated
@@ -80,7 +82,7 @@ def problem(E, H, I, seed):
     return w1, w2
 
 
-def worker(rank, world, port, E, k, T, H, I, fail_rank, result_q, dedup=False):
+def worker(rank, world, port, E, k, T, H, I, fail_rank, result_q, dedup=False, chunks=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     from kernelswift_b200.ep import ExpertParallelMoE
@@ -97,13 +99,13 @@ def worker(rank, world, port, E, k, T, H, I, fail_rank, result_q, dedup=False):
         ep = ExpertParallelMoE(None, None, E, k,
                                backend=CpuBackend(w1[rank * el:(rank + 1) * el],
                                                   w2[rank * el:(rank + 1) * el]),
-                               dedup=dedup)
+                               dedup=dedup, chunks=chunks)
         if rank == fail_rank:
             raise RuntimeError("planted failure before the first collective")
         out = ep(hidden, w, ids)
         ref = orc.fused_experts(hidden, w1, w2, w, ids)
         err = float((out - ref).abs().max())
-        if dedup:
+        if dedup or chunks > 1:
             # rows received = (token, rank) pairs routed here, over all senders
             sent = torch.tensor([len({int(e) // el for e in row}) for row in ids])
             n = torch.tensor([int(sent.sum()), ep.last_rows_received])
@@ -120,12 +122,12 @@ def worker(rank, world, port, E, k, T, H, I, fail_rank, result_q, dedup=False):
             pass
 
 
-def run(world, fail_rank=-1, E=8, k=2, T=37, H=64, I=32, dedup=False):
+def run(world, fail_rank=-1, E=8, k=2, T=37, H=64, I=32, dedup=False, chunks=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
     procs = [ctx.Process(target=worker,
-                         args=(r, world, port, E, k, T, H, I, fail_rank, q, dedup))
+                         args=(r, world, port, E, k, T, H, I, fail_rank, q, dedup, chunks))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -156,6 +158,38 @@ def test_ep_dedup_matches_oracle(world, E, k):
         status, info = res[rank]
         assert status == "ok", (rank, info)
         assert info < 1e-4, (rank, info)
+
+
+@pytest.mark.parametrize("world,E,k,T,chunks", [(2, 8, 2, 37, 2), (4, 16, 4, 37, 3),
+                                                 (2, 32, 8, 2, 3)])
+def test_ep_chunked_matches_oracle(world, E, k, T, chunks):
+    """The pipelined exchange in token chunks (deduplicated rows); with T=2
+    rank 0 has fewer tokens than chunks, so one of its chunks is empty while
+    rank 1's are not, and both still issue the same collectives."""
+    res = run(world, E=E, k=k, T=T, chunks=chunks)
+    for rank in range(world):
+        status, info = res[rank]
+        assert status == "ok", (rank, info)
+        assert info < 1e-4, (rank, info)
+
+
+def test_chunks_need_the_nccl_exchange(tmp_path):
+    """chunks > 1 is the NCCL exchange's option and implies dedup."""
+    from kernelswift_b200.ep import ExpertParallelMoE
+
+    dist.init_process_group("gloo", store=dist.FileStore(str(tmp_path / "store"), 1),
+                            rank=0, world_size=1)
+    try:
+        w1, w2 = problem(4, 64, 32, seed=1)
+        be = CpuBackend(w1, w2)
+        with pytest.raises(ValueError, match="chunks"):
+            ExpertParallelMoE(None, None, 4, 2, backend=be, exchange="peer", chunks=2)
+        with pytest.raises(ValueError, match="chunks"):
+            ExpertParallelMoE(None, None, 4, 2, backend=be, chunks=0)
+        ep = ExpertParallelMoE(None, None, 4, 2, backend=be, chunks=3)
+        assert ep.dedup and ep.chunks == 3 and ep.exchange == "nccl"
+    finally:
+        dist.destroy_process_group()
 
 
 def test_dedup_plan_rows():

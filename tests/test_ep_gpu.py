@@ -1,6 +1,7 @@
 """GPU: expert parallelism, one process per GPU (never more ranks than GPUs),
 checked against the fp32 oracle on each rank's tokens: the NCCL all_to_all
-exchange and the NVLink peer-memory dispatch/combine kernels (including a
+exchange (in one piece and pipelined in token chunks) and the NVLink
+peer-memory dispatch/combine kernels (including a
 rank that never takes a step: the others' bounded waits report a timeout)."""
 import datetime
 import os
@@ -30,14 +31,14 @@ def worker(rank, world, port, cfg, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
     try:
-        E, k, T, H, I, quant, dedup = cfg
+        E, k, T, H, I, quant, dedup, chunks = cfg
         g = torch.Generator().manual_seed(0)
         w1 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
         w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
         el = E // world
         ep = ExpertParallelMoE(w1[rank * el:(rank + 1) * el].to(dev),
                                w2[rank * el:(rank + 1) * el].to(dev), E, k, quant=quant,
-                               exchange="nccl", dedup=dedup)
+                               exchange="nccl", dedup=dedup, chunks=chunks)
         gt = torch.Generator().manual_seed(10 + rank)
         hidden = torch.randn(T, H, generator=gt).to(torch.bfloat16)
         w, ids = orc.route(torch.randn(T, E, generator=gt), k)
@@ -57,16 +58,18 @@ def worker(rank, world, port, cfg, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("quant,dedup", [("none", False), ("fp8", False), ("none", True),
-                                         ("fp8-ue8m0", False)])
-def test_ep_matches_oracle(cuda_device, quant, dedup):
-    """NCCL exchange; dedup sends each token to a rank once."""
+@pytest.mark.parametrize("quant,dedup,chunks", [("none", False, 1), ("fp8", False, 1),
+                                                ("none", True, 1), ("fp8-ue8m0", False, 1),
+                                                ("none", True, 3)])
+def test_ep_matches_oracle(cuda_device, quant, dedup, chunks):
+    """NCCL exchange; dedup sends each token to a rank once; chunks > 1
+    pipelines the exchange in token chunks (async all_to_alls)."""
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs two GPUs: one rank would exchange nothing")
-    cfg = (16, 4, 200, 256, 256, quant, dedup)
+    cfg = (16, 4, 200, 256, 256, quant, dedup, chunks)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
