@@ -507,9 +507,10 @@ class ExpertParallelMoE:
                                             group=self.group, async_op=True),
                      dist.all_to_all_single(recv_w, send_w[:n_send], recv_split, send_split,
                                             group=self.group, async_op=True)]
+            # the send buffers stay referenced until the collectives are waited on
             return {"c": c, "send_split": send_split, "recv_split": recv_split, "inv": inv,
                     "rows": recv_rows, "eid": recv_eid, "w": recv_w, "works": works,
-                    "n_send": n_send}
+                    "n_send": n_send, "sent": (rows, send_eid, send_w)}
 
         out = torch.empty(T, H, dtype=hidden.dtype, device=dev)
         returning = []
@@ -532,9 +533,9 @@ class ExpertParallelMoE:
             back = torch.empty(cur["n_send"], H, dtype=rows.dtype, device=dev)
             work = dist.all_to_all_single(back, rows, cur["send_split"], cur["recv_split"],
                                           group=self.group, async_op=True)
-            returning.append((cur, back, work))
+            returning.append((cur, back, work, rows))
         self._mark(3)
-        for cur, back, work in returning:
+        for cur, back, work, _rows in returning:
             work.wait()
             c = cur["c"]
             t_c = bounds[c + 1] - bounds[c]
