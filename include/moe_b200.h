@@ -300,9 +300,14 @@ int moe_fused_experts_workspace_size(const moe_problem_t* p, size_t* bytes);
 /*
  * out[t] = sum_j topk_weights[t, j] *
  *          W2[e] . (silu(W1g[e] . x_t) * (W1u[e] . x_t)),  e = topk_ids[t, j]
- * Matmuls run on the tcgen05 tensor cores (bf16/fp16, e4m3 or int8 operands,
- * fp32/int32 accumulation in tensor memory); SiLU, scaling and the top-k sum
- * run in fp32. F32 activations are rounded to bf16 operands. With at most
+ * Matmuls run on the tcgen05 tensor cores (bf16/fp16, tf32, e4m3 or int8
+ * operands, fp32/int32 accumulation in tensor memory); SiLU, scaling and the
+ * top-k sum run in fp32. F32 activations with unquantised weights take tf32
+ * MMAs: the weights (prepared as F32) and the operand rows are rounded to
+ * tf32 (10-bit mantissa, nearest, ties away from zero) where they are
+ * written. The operand rows are gathered token by token (each token read
+ * and, for fp8, quantised once; MOE_NO_TOKEN_GATHER=1 gathers them row by
+ * row, with the same bytes). With at most
  * 16 routed rows, 16-bit activations, unquantised weights and at most 256 MB
  * of weights to stream, two weight-streaming CUDA-core kernels do the whole
  * computation instead (fp32 dot products; MOE_NO_DECODE_PATH=1 disables
