@@ -3,7 +3,10 @@
 //                (the replicate + boolean gather of base.py:52-58,68), with
 //                an optional cast (f32 -> bf16) or quantisation (e4m3 per
 //                128-column group with an fp32 or a power-of-two scale, int8
-//                per row).
+//                per row). Given the align's slot map, moe_fused_experts
+//                gathers token by token instead (gather_tokens_kernel: each
+//                source row read and converted once, stored into its top_k
+//                operand rows).
 //   quant_rows:  the same quantisations for the gate-up output (the second
 //                GEMM's operand).
 //   sum_topk:    out[t] = sum_s sum_j part[s, t*k + j] (the top-k reduction of
