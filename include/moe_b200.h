@@ -359,7 +359,9 @@ int moe_fused_experts_launches(const moe_problem_t* p, int rows_only, int* launc
 /* The plan moe_fused_experts makes for `p` (pointers unused; answers without
  * a GPU, for 148 SMs): info[0] gate-up tile width, [1] gate-up K splits,
  * [2] down tile width, [3] down K splits, [4] dtype of the down GEMM's rows,
- * [5] reserved (0), [6] 1 when the decode kernels run instead of the GEMM
+ * [5] 1 when the operand rows are gathered token by token (the align's
+ * slot map; 0 for the row-major gather, MOE_NO_TOKEN_GATHER=1, int8, or the
+ * decode kernels), [6] 1 when the decode kernels run instead of the GEMM
  * pipeline, [7] SMs planned for. No reference counterpart (inspection aid). */
 int moe_fused_experts_plan(const moe_problem_t* p, int32_t* info);
 

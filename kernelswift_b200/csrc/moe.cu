@@ -583,7 +583,7 @@ int moe_fused_experts_plan(const moe_problem_t* p, int32_t* info) {
   info[2] = P.dn_bn;
   info[3] = P.splits;
   info[4] = P.part_dtype;
-  info[5] = 0;
+  info[5] = !decode && P.token_gather ? 1 : 0;
   info[6] = decode ? 1 : 0;
   info[7] = sms;
   return MOE_OK;

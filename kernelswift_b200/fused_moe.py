@@ -401,7 +401,8 @@ def fused_moe_launches(num_tokens: int, hidden_size: int, intermediate_size: int
 def fused_experts_plan(num_tokens: int, hidden_size: int, intermediate_size: int,
                        num_experts: int, top_k: int, quant: str = "none",
                        dtype: torch.dtype = torch.bfloat16) -> dict:
-    """The tile widths and K splits fused_experts picks for this shape
+    """The tile widths and K splits fused_experts picks for this shape, and
+    whether it gathers token by token or takes the decode kernels
     (moe_fused_experts_plan; no GPU needed)."""
     p = _lib.MoeProblem()
     p.num_tokens = num_tokens
@@ -416,8 +417,8 @@ def fused_experts_plan(num_tokens: int, hidden_size: int, intermediate_size: int
     info = (ctypes.c_int32 * 8)()
     _lib.call("moe_fused_experts_plan", ctypes.byref(p), info)
     keys = ("gate_up_block_n", "gate_up_splits", "down_block_n", "down_splits",
-            "down_rows_dtype", None, "decode_path", "sms")  # info[5] is reserved
-    return {k: v for k, v in zip(keys, list(info)) if k is not None}
+            "down_rows_dtype", "token_gather", "decode_path", "sms")
+    return dict(zip(keys, list(info)))
 
 
 def stage_event_array(events) -> ctypes.Array:

@@ -204,15 +204,18 @@ def test_plan_query_without_gpu():
         assert (2 * I) % plan["gate_up_block_n"] == 0 and H % plan["down_block_n"] == 0
         assert plan["gate_up_splits"] >= 1 and plan["down_splits"] >= 1
         assert plan["sms"] == 148 and plan["decode_path"] == 0
+        assert plan["token_gather"] == (0 if quant == "int8" else 1)
         if quant.startswith("fp8"):
             assert plan["gate_up_splits"] == 1
             assert plan["gate_up_block_n"] in (128, 256) and plan["down_block_n"] in (128, 256)
-    assert fm.fused_experts_plan(1, 2048, 768, 128, 8)["decode_path"] == 1
+    decode = fm.fused_experts_plan(1, 2048, 768, 128, 8)
+    assert decode["decode_path"] == 1 and decode["token_gather"] == 0
     assert fm.fused_experts_plan(4096, 4096, 14336, 8, 2)["down_rows_dtype"] == _lib.DT_BF16
 
 
 def test_plan_switches_in_a_child_process():
-    """MOE_BLOCK_N forces the tile width it divides (fp8 keeps 128/256)."""
+    """MOE_BLOCK_N forces the tile width it divides (fp8 keeps 128/256);
+    MOE_NO_TOKEN_GATHER=1 turns the token-major gather off."""
     import json
     import subprocess
     import sys
@@ -236,6 +239,8 @@ def test_plan_switches_in_a_child_process():
     assert all(p["down_block_n"] == 128 and p["gate_up_block_n"] == 128 for p in forced)
     narrow = plans(MOE_BLOCK_N="64")
     assert narrow[0]["down_block_n"] == 64 and narrow[2]["down_block_n"] in (128, 256)
+    assert [p["token_gather"] for p in plans()] == [1, 1, 1, 0]
+    assert [p["token_gather"] for p in plans(MOE_NO_TOKEN_GATHER="1")] == [0, 0, 0, 0]
 
 
 def test_ep_plan_workspace_query_without_gpu():
